@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Throughput of one ES generation of the batched perturbed GEMM + factor replay.
+
+Workload (the reference's perturbed-GEMM microbench config): population 256,
+rank 8, a shared bf16 input x[256,4096] (N(0, 0.02)) through W[4096,4096]
+(N(0, 0.02)) plus sigma*(x A_i) B_i^T per candidate (sigma 0.01, factors from
+the threefry keys of seed 0, generation 0 onwards), every candidate's output
+[256,4096] materialised in HBM; then the fitness (N(0,1), shaped by the
+reference's centred-loss rule), factor replay of W's pseudo-gradient and an
+SGD update.  One step = one generation.  Synthetic data, fixed seeds.
+
+`python bench.py [--gpus N --steps K --warmup W]` prints one JSON line.  With
+N > 1 (one process per GPU under torch.distributed.run) the population is
+sharded across ranks, the fitness array is all-gathered (the only
+collective) and every rank replays the identical update.
+`--impl reference` times the CPU restatement of the reference's algorithm
+(the reference itself is JAX code that cannot be installed here) on this
+host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WL = dict(P=256, rank=8, M=256, K=4096, N=4096, sigma=0.01, seed=0, run_id="bench", lr=1e-3)
+METRIC = "candidate forward evals/sec"
+UNIT = "evals/s"
+WORKLOAD_NAME = ("batched perturbed GEMM + factor replay: P=256, rank=8, shared x[256,4096] bf16, "
+                 "W[4096,4096] bf16, sigma=0.01, seed 0; fitness N(0,1) centred-loss shaped; SGD update")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work per launch of each kernel (this workload)
+# ---------------------------------------------------------------------------
+def kernel_work(name: str, P_local: int):
+    P, r, M, K, N = WL["P"], WL["rank"], WL["M"], WL["K"], WL["N"]
+    if name == "lowrank_expand":      # y = xW + s (xA) B : write y bf16, read xW f32, U f32, B bf16
+        return "hbm", P_local * M * N * 2 + M * N * 4 + P_local * M * r * 4 + P_local * r * N * 2
+    if name == "replay_gemm":         # [K, P r] x [P r, N]
+        return "tensor", 2.0 * K * N * P * r
+    if name == "shared_xw":
+        return "tensor", 2.0 * M * K * N
+    if name == "lowrank_u":
+        return "tensor", 2.0 * P_local * M * K * r
+    if name == "factor_fill":         # bf16 factors written
+        return "hbm", (P + P_local) / 2 * r * (K + N) * 2
+    if name == "sgd_update":          # read W bf16 + descent f32, write W bf16
+        return "hbm", K * N * (2 + 4 + 2)
+    return None, None
+
+
+# ---------------------------------------------------------------------------
+# CPU arm: the oracle restatement of the reference on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_generation_sample(n_cand: int, seed: int = 0):
+    """Forward of n_cand candidates + their replay contribution, on the host.
+
+    Follows the reference's computation per generation: the shared x @ W once
+    (jax.vmap leaves it unbatched), then per candidate (x A) B added, then the
+    replay contraction over the sampled candidates.  Returns seconds.
+    """
+    import numpy as np
+
+    from oracle import ref
+
+    P, r, M, K, N = WL["P"], WL["rank"], WL["M"], WL["K"], WL["N"]
+    rng = np.random.default_rng(seed)
+    x = ref.round_bf16((rng.standard_normal((M, K)) * 0.02).astype(np.float32))
+    W = ref.round_bf16((rng.standard_normal((K, N)) * 0.02).astype(np.float32))
+    fitness = rng.standard_normal(P).astype(np.float32)
+    base = ref.step_key(WL["seed"], WL["run_id"], 0, 1)
+    t0 = time.perf_counter()
+    cks = ref.candidate_keys(base, range(n_cand))
+    gks = ref.group_keys(cks, 0)
+    A, B = ref.population_factors(gks, ref.MATRIX, (K, N), r, "bfloat16")
+    xw = x @ W
+    s = ref.scaled_factor(r, WL["sigma"], "bfloat16")
+    for p in range(n_cand):
+        y = xw + s * ((x @ A[p]) @ B[p])
+        y = ref.round_bf16(y)
+    shaped = ref.shape_centered_loss(fitness, WL["sigma"])[:n_cand]
+    wa = (A * shaped[:, None, None].astype(np.float32)).transpose(1, 0, 2).reshape(K, n_cand * r)
+    g = (wa @ B.reshape(n_cand * r, N)) * ref.scaled_factor(r, 1.0, "bfloat16")
+    del y, g
+    return time.perf_counter() - t0
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import ref
+
+    ref.lib()
+    n_cand = 8
+    for _ in range(max(1, min(args.warmup, 2))):
+        cpu_generation_sample(n_cand)
+    times = [cpu_generation_sample(n_cand, seed=i) for i in range(args.steps)]
+    total = sum(times)
+    value = n_cand * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD_NAME, "population": WL["P"], "rank": WL["rank"], "batch": WL["M"],
+                   "d_in": WL["K"], "d_out": WL["N"], "sample": f"{n_cand} candidates per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{n_cand} of {WL['P']} candidates per step: shared x@W, per-candidate "
+                                   "low-rank forward, replay contraction; numpy/BLAS + C threefry"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import zerograd_b200 as zg
+    from zerograd_b200 import _lib as L
+    from zerograd_b200 import _ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    L.load()
+
+    P, r, M, K, N, sigma = WL["P"], WL["rank"], WL["M"], WL["K"], WL["N"], WL["sigma"]
+    sizes = zg.compute_partition_sizes(P, [1.0] * world)
+    a = sum(sizes[:rank])
+    b = a + sizes[rank]
+    P_local = b - a
+
+    g = torch.Generator().manual_seed(WL["seed"])
+    x_host = (torch.randn(M, K, generator=g) * 0.02).to(torch.bfloat16).pin_memory()
+    W0 = (torch.randn(K, N, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    fit_host = torch.randn(P, generator=g).pin_memory()
+    x = x_host.to(dev)
+    fitness = fit_host.to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w"),))
+    ids_all = torch.arange(P, dtype=torch.int32, device=dev)
+    total_steps = args.warmup + args.steps
+
+    # per-generation candidate keys, derived up front (inputs resident)
+    keys = []
+    for gen in range(total_steps):
+        base = zg.step_key(WL["seed"], WL["run_id"], gen, manifest.version)
+        keys.append(_ops.launch_fold_in(base, ids_all))
+
+    def gather(local_losses):
+        if world == 1:
+            return local_losses
+        return zg.allgather_losses(local_losses, sizes)
+
+    def device_step(W, gen):
+        cks = keys[gen]
+        y = _ops.launch_linear(x, W, cks[a:b], 0, r, sigma, False)
+        losses = gather(fitness[a:b])
+        shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
+        d = _ops.launch_replay(shaped, cks, 0, L.ZG_MATRIX, (K, N), r, torch.bfloat16)
+        W = _ops.launch_sgd(W, d, WL["lr"])
+        del y
+        return W
+
+    def timed(step_fn, steps, W):
+        times = []
+        for i in range(steps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            W = step_fn(W, args.warmup + i)
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+        return sum(s.elapsed_time(e) for s, e in times), W
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up
+    W = W0
+    for i in range(args.warmup):
+        W = device_step(W, i)
+    barrier()
+
+    # timed (device-resident inputs)
+    n0 = L.launch_count()
+    with ClockSampler(local) as clk:
+        barrier()
+        ms, W = timed(device_step, args.steps, W0)
+        barrier()
+    launches = L.launch_count() - n0
+    ms = max_over_ranks(ms)
+    clocks = clk.summary()
+
+    # per-kernel device times (same steps, events around each launch)
+    barrier()
+    L.profile_begin(1 << 14)
+    prof_ms, _ = timed(device_step, args.steps, W0)
+    kernels = L.profile_end()
+    barrier()
+
+    # end to end through the public API: pinned host batch + fitness in, metrics out
+    opt = zg.ZeroGrad(manifest, zg.sgd(WL["lr"]), P, r, sigma, WL["seed"], WL["run_id"])
+    params = {"w": W0}
+    state = opt.init(params)
+    ids_local = torch.arange(a, b, dtype=torch.int32, device=dev)
+
+    def fwd(p, ctx, batch, rng):
+        return ctx.linear(p, ("w",), batch), None
+
+    def e2e_step(Wcur, gen):
+        nonlocal state
+        xb = x_host.to(dev, non_blocking=True)
+        fl = fit_host[a:b].to(dev, non_blocking=True)
+        y = opt.evaluate_shard({"w": Wcur}, gen, fwd, xb, ids_local)
+        losses = gather(fl)
+        newp, state, m = opt.step_from_losses(zg.ZeroGradState(gen, state.opt_state), {"w": Wcur}, losses)
+        del y
+        return newp["w"]
+
+    Wc = W0
+    for i in range(min(args.warmup, 3)):
+        Wc = e2e_step(Wc, i)
+    barrier()
+    e2e_ms, _ = timed(e2e_step, args.steps, W0)
+    e2e_ms = max_over_ranks(e2e_ms)
+    barrier()
+
+    value = P * args.steps / (ms / 1e3)
+    e2e_value = P * args.steps / (e2e_ms / 1e3)
+    if rank == 0:
+        pk = peaks()
+        top = max(kernels.items(), key=lambda kv: kv[1][1]) if kernels else None
+        roof = None
+        if top:
+            name, (n, tot) = top
+            bound, work = kernel_work(name, P_local)
+            per = tot / n / 1e3
+            if bound == "hbm":
+                ach, peak, unit = work / per / 1e9, pk["hbm_gbs"], "GB/s"
+            else:
+                ach, peak, unit = work / per / 1e12, pk["bf16_tflops"], "TFLOP/s"
+            traffic = None
+            tpath = os.path.join(ROOT, "profiles", "traffic.json")
+            if os.path.exists(tpath):
+                traffic = json.load(open(tpath)).get(name)
+            roof = {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
+                    "frac": ach / peak, "traffic": traffic, "peak_source": pk["source"],
+                    "launch_ms": tot / n, "launches": n}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "generations_per_sec": args.steps / (ms / 1e3),
+            "config": {"workload": WORKLOAD_NAME, "population": P, "rank": r, "batch": M, "d_in": K, "d_out": N,
+                       "parallelism": f"population shards x{world}, fitness allgather" if world > 1 else "1 GPU",
+                       "l2": "flushed between steps (256 MiB write outside the timed events)"},
+            "roofline": roof,
+            "kernels_ms_per_step": {k: v[1] / args.steps for k, v in sorted(kernels.items())},
+            "profiled_ms_per_step": prof_ms / args.steps,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 4 * P_local,
+                    "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms / args.steps},
+        }
+        if world == 1:
+            secs = cpu_generation_sample(8)
+            n_cand = max(1, min(64, int(8 * 15.0 / max(secs, 1e-3))))
+            secs = cpu_generation_sample(n_cand)
+            line["cpu_baseline"] = {"value": n_cand / secs, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                                    "sample": f"{n_cand} of {P} candidates of one generation (shared x@W, "
+                                              "per-candidate low-rank forward, replay contraction), numpy/BLAS "
+                                              "+ C threefry"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,214 @@
+/*
+ * zg_b200.h -- C ABI of libzgb200, the sm_100a kernels behind zerograd's
+ * population-evaluation and factor-replay path.
+ *
+ * Conventions
+ *   - Every pointer is a DEVICE pointer unless the comment says "host".
+ *   - The caller owns every buffer.  Entry points that need scratch take a
+ *     (workspace, workspace_bytes) pair; the matching *_workspace_size()
+ *     query returns the bytes required.  No entry point allocates.
+ *   - `stream` is a cudaStream_t passed as void*; all work is enqueued on it.
+ *   - Return value: ZG_OK (0) or an error code; zg_last_error() returns a
+ *     message for the calling host thread.
+ *   - Keys are uint32 pairs (jax.random key data) laid out [n, 2].
+ *     `group` >= 0: the keys are CANDIDATE keys and the kernel derives the
+ *     group key fold(candidate_key, group) itself (split(ck, n)[group] of
+ *     the partitionable threefry); `group` == -1: the keys are group keys.
+ *   - dtype codes: ZG_F32 or ZG_BF16 for the weights / activations.
+ *
+ * Each entry point names the reference interface it replaces (paths are
+ * relative to the reference project root).
+ */
+#ifndef ZG_B200_H
+#define ZG_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ZG_API __attribute__((visibility("default")))
+#else
+#define ZG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ZG_OK = 0,
+    ZG_ERR_INVALID = 1,   /* bad argument (shape, dtype, null pointer) */
+    ZG_ERR_CUDA = 2,      /* a CUDA runtime call or launch failed */
+    ZG_ERR_WORKSPACE = 3, /* workspace missing or too small */
+    ZG_ERR_UNSUPPORTED = 4
+};
+enum { ZG_F32 = 0, ZG_BF16 = 1 };
+enum { ZG_MATRIX = 0, ZG_TABLE = 1, ZG_VECTOR = 2 };
+
+/* Message of the last failing call on this host thread ("" if none). */
+ZG_API const char* zg_last_error(void);
+/* Library version string. */
+ZG_API const char* zg_version(void);
+
+/* Launch accounting.  zg_launch_count() is the number of kernels this
+ * library has launched since load (all threads).  Between
+ * zg_profile_begin() and zg_profile_end() every launch is bracketed by CUDA
+ * events on its own stream (up to `max_records` launches);
+ * zg_profile_summary() (call after the stream work completed) writes one
+ * line per kernel name, "name,launches,total_ms", into `buf`.
+ * No counterpart in the reference (it has no kernels of its own). */
+ZG_API int64_t zg_launch_count(void);
+ZG_API int zg_profile_begin(int max_records);
+ZG_API int zg_profile_end(void);
+ZG_API int zg_profile_summary(char* buf, size_t len);
+
+/* ---------------------------------------------------------------- keys -- */
+
+/* Raw threefry2x32-20 blocks: out[i] = threefry(keys[i], ctrs[i]).
+ * Replaces jax.random's threefry2x32 primitive (reached from
+ * src/zerograd/_keys.py:30,40,53,58). */
+ZG_API int zg_threefry2x32(const uint32_t* keys, const uint32_t* ctrs, uint32_t* out, int64_t n,
+                    void* stream);
+
+/* out[i] = fold_in(keys[key_stride ? i : 0], data[i]).
+ * Replaces candidate_key (src/zerograd/_keys.py:33-53) batched over a
+ * candidate-id array, the per-candidate rng fold_in
+ * (src/zerograd/_optimizer.py:175) and group_key
+ * (src/zerograd/_keys.py:56-58, with data = the group index). */
+ZG_API int zg_fold_in(const uint32_t* keys, int key_stride, const uint32_t* data, uint32_t* out,
+               int64_t n, void* stream);
+
+/* out[i] = fold_in((k0, k1), data[i]) with the key passed by value (a key
+ * computed on the host, like step_key's, needs no host-to-device copy).
+ * Replaces candidate_key (src/zerograd/_keys.py:33-53) and the
+ * per-candidate rng fold_in (src/zerograd/_optimizer.py:174-175) batched
+ * over a candidate-id array. */
+ZG_API int zg_candidate_keys(uint32_t k0, uint32_t k1, const uint32_t* data, uint32_t* out, int64_t n,
+                             void* stream);
+
+/* Random bits / float32 normals of `n` flat elements for each of `nkeys`
+ * keys: out[k, j].  Replaces jax.random.bits / jax.random.normal(float32)
+ * as called by src/zerograd/_factors.py:47,53-54,62,65-66,74. */
+ZG_API int zg_random_bits(const uint32_t* keys, int64_t nkeys, int64_t n, uint32_t* out, void* stream);
+ZG_API int zg_normal(const uint32_t* keys, int64_t nkeys, int64_t n, int dtype, void* out, void* stream);
+
+/* Population factors for one manifest entry, in the reference layouts with
+ * a leading population axis: MATRIX A[P,rows,rank], B[P,rank,cols];
+ * TABLE A[P,rows,rank], B[P,cols,rank]; VECTOR A[P,rows] (B unused).
+ * Values are the float32 draws cast to `dtype`.
+ * Replaces matrix_factors / table_factors / vector_noise
+ * (src/zerograd/_factors.py:43-74) under jax.vmap over candidates
+ * (src/zerograd/_replay.py:45,49,53). */
+ZG_API int zg_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
+                          int64_t cols, int rank, int dtype, void* A, void* B, void* stream);
+
+/* ------------------------------------------------------- forward ops -- */
+
+/* y[p] = x_p @ W + s * (x_p @ A_p) @ B_p for p in [0,P): one population-
+ * batched launch sequence.  x is [M,K] shared by all candidates
+ * (x_batched = 0) or [P,M,K] (x_batched = 1); W [K,N]; y [P,M,N]; all in
+ * `dtype`.  s = scaled_factor (sigma/sqrt(rank) rounded to dtype by the
+ * caller).  Replaces perturbed_linear / CandidateContext.linear
+ * (src/zerograd/_candidate.py:17-22,61-66) under jax.vmap. */
+ZG_API size_t zg_perturbed_linear_workspace_size(int P, int M, int K, int N, int rank, int dtype,
+                                          int x_batched);
+ZG_API int zg_perturbed_linear(const void* x, int x_batched, const void* W, const uint32_t* keys,
+                        int group, int P, int M, int K, int N, int rank, float s, int dtype,
+                        void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[p, t, :] = T[idx[t]] + s * A_p[idx[t]] @ B_p^T, T [rows, cols],
+ * idx [n_idx] (int32, shared by all candidates) or [P, n_idx]
+ * (idx_batched = 1).  A rows are regenerated in-kernel at the gathered
+ * rows.  Replaces perturbed_table_lookup / CandidateContext.table_lookup
+ * (src/zerograd/_candidate.py:25-30,68-73). */
+ZG_API size_t zg_table_lookup_workspace_size(int P, int64_t rows, int64_t cols, int rank, int dtype);
+ZG_API int zg_table_lookup(const void* T, const int32_t* idx, int idx_batched, int64_t n_idx,
+                    const uint32_t* keys, int group, int P, int64_t rows, int64_t cols,
+                    int rank, float s, int dtype, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* y[p] = x_p @ T^T + s * (x_p @ B_p) @ A_p^T with T [V, C] (table layout
+ * factors A [V,rank], B [C,rank]); x [M,C] or [P,M,C]; y [P,M,V].
+ * Replaces perturbed_tied_logits / CandidateContext.tied_logits
+ * (src/zerograd/_candidate.py:33-38,75-80). */
+ZG_API size_t zg_tied_logits_workspace_size(int P, int M, int V, int C, int rank, int dtype,
+                                     int x_batched);
+ZG_API int zg_tied_logits(const void* x, int x_batched, const void* T, const uint32_t* keys, int group,
+                   int P, int M, int V, int C, int rank, float s, int dtype, void* y,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[p, i] = v[i] + s * normal(group_key_p)[i]; v [n] or [P, n]
+ * (v_batched = 1).  Replaces perturbed_vector / CandidateContext.vector
+ * (src/zerograd/_candidate.py:41-45,82-87). */
+ZG_API int zg_perturbed_vector(const void* v, int v_batched, const uint32_t* keys, int group, int P,
+                        int64_t n, float s, int dtype, void* out, void* stream);
+
+/* --------------------------------------------- fitness / replay / update -- */
+
+/* Validates and shapes the gathered losses [P] (float32):
+ *   shaped[p] = -(l[p] - mean(l)) / (P * sigma)
+ * metrics (float32[4], device) = {mean, min, max, number of non-finite}.
+ * sigma is the Python float the reference divides by (P * sigma is formed
+ * in double precision and rounded to float32 once).
+ * Replaces shape_centered_loss + validate_losses
+ * (src/zerograd/_fitness.py:13-48) and the StepMetrics reductions
+ * (src/zerograd/_optimizer.py:237-243). */
+ZG_API int zg_shape_fitness(const float* losses, int P, double sigma, float* shaped, float* metrics,
+                     void* stream);
+
+/* Pseudo-gradient DESCENT direction of one manifest entry:
+ *   MATRIX out[rows,cols] = inv_sqrt_rank * sum_p w_p A_p @ B_p
+ *   TABLE  out[rows,cols] = inv_sqrt_rank * sum_p w_p A_p @ B_p^T
+ *   VECTOR out[rows]      = sum_p w_p n_p
+ * keys [P,2] candidate keys (group >= 0) in candidate-id order, w = the
+ * shaped fitness [P] (float32), out float32.  `inv_sqrt_rank` is
+ * scaled_factor(rank, 1.0, dtype) computed by the caller.  Factors are drawn
+ * in `dtype` exactly as in the forward pass.
+ * Replaces replay_entry (src/zerograd/_replay.py:15-54). */
+ZG_API size_t zg_replay_workspace_size(int P, int layout, int64_t rows, int64_t cols, int rank,
+                                int dtype);
+ZG_API int zg_replay(const float* shaped, const uint32_t* keys, int group, int P, int layout,
+              int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, int dtype, float* out,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused AdamW (optax.adamw: scale_by_adam -> add_decayed_weights ->
+ * scale(-lr)) on one leaf, with gradient = -descent (descent may be NULL:
+ * a non-manifest leaf, zero gradient, which still receives weight decay).
+ * Reads param / mu / nu and writes param_out / mu_out / nu_out (which may
+ * alias the inputs).  param is in `dtype`; the moments are float32.
+ * `count` is the step count AFTER increment (1 on the first step).  The
+ * hyper-parameters are the Python floats given to the transform.
+ * Replaces transform.update + optax.apply_updates
+ * (src/zerograd/_optimizer.py:233-234) and _build_pseudo_grad
+ * (src/zerograd/_optimizer.py:299-326). */
+ZG_API int zg_adamw_update(const void* param, void* param_out, int dtype, const float* descent,
+                           const float* mu, const float* nu, float* mu_out, float* nu_out,
+                           int64_t n, int count, double lr, double b1, double b2, double eps,
+                           double weight_decay, void* stream);
+
+/* Fused SGD (optax.sgd without momentum): param_out = param + (-lr) * g with
+ * g = -descent (zero when descent is NULL). */
+ZG_API int zg_sgd_update(const void* param, void* param_out, int dtype, const float* descent,
+                         int64_t n, double lr, void* stream);
+
+/* ------------------------------------------------- integer QAT linear -- */
+
+/* Integer linear with LUT activation for P candidates (no reference
+ * counterpart: the reference only has float fake quantisation,
+ * examples/train_qat_xor.py:41-50):
+ *   acc = x_p @ W (int8 x int8 -> int32, exact)
+ *   y   = acc * x_scale * w_scale[n] + s * ((x_p @ A_p) @ B_p)[m,n]   (float32)
+ *   q   = clamp(rint(y / y_scale), -128, 127);  out = lut[q + 128]   (int8)
+ * x [M,K] shared or [P,M,K]; W [K,N] int8; w_scale [N] float32; lut [256]
+ * int8; out [P,M,N] int8.  A_p/B_p are matrix factors (float32 draws) of
+ * the weight's group.  acc_out (optional, [P,M,N] int32) receives the
+ * exact accumulators. */
+ZG_API size_t zg_int8_lut_linear_workspace_size(int P, int M, int K, int N, int rank, int x_batched);
+ZG_API int zg_int8_lut_linear(const int8_t* x, int x_batched, const int8_t* W, const float* w_scale,
+                       float x_scale, float y_scale, const int8_t* lut, const uint32_t* keys,
+                       int group, int P, int M, int K, int N, int rank, float s, int8_t* out,
+                       int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,137 @@
+"""Population-batched forward ops against the float64 oracle.
+
+Tolerances: float32 rel 1e-5 (the reference's own tests use rtol/atol 1e-5);
+bf16 rel 2e-2 (bf16 outputs, float32 accumulation).
+"""
+import numpy as np
+import pytest
+import torch
+
+import zerograd_b200 as zg
+from zerograd_b200 import _ops
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: dict(rtol=1e-5, atol=1e-5), torch.bfloat16: dict(rtol=2e-2, atol=2e-2)}
+DN = {torch.float32: "float32", torch.bfloat16: "bfloat16"}
+
+
+def _u32(a, dev):
+    return torch.tensor(np.asarray(a, np.int64)).to(torch.uint32).to(dev)
+
+
+def _setup(oracle, P, group=1):
+    base = oracle.step_key(42, "test", 0, 1)
+    cks = oracle.candidate_keys(base, range(P))
+    return cks, oracle.group_keys(cks, group)
+
+
+def _rand(shape, dtype, dev, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype).to(dev)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("x_batched", [False, True])
+@pytest.mark.parametrize("dims", [(5, 8, 4, 2), (33, 70, 45, 3), (64, 128, 96, 8)])
+def test_perturbed_linear(cuda, oracle, dtype, x_batched, dims):
+    M, K, N, rank = dims
+    P, sigma = 5, 0.1
+    cks, gks = _setup(oracle, P)
+    W = _rand((K, N), dtype, cuda, 1)
+    x = _rand((P, M, K) if x_batched else (M, K), dtype, cuda, 2)
+    y = _ops.launch_linear(x, W, _u32(cks, cuda), 1, rank, sigma, x_batched)
+    xs = x.float().cpu().numpy()
+    for p in range(P):
+        want = oracle.perturbed_linear(xs[p] if x_batched else xs, W.float().cpu().numpy(), gks[p], rank, sigma, DN[dtype])
+        np.testing.assert_allclose(y[p].float().cpu().numpy(), want, **TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("x_batched", [False, True])
+def test_tied_logits(cuda, oracle, dtype, x_batched):
+    P, M, V, C, rank, sigma = 4, 9, 50, 24, 3, 0.05
+    cks, gks = _setup(oracle, P, group=0)
+    T = _rand((V, C), dtype, cuda, 3)
+    x = _rand((P, M, C) if x_batched else (M, C), dtype, cuda, 4)
+    y = _ops.launch_tied_logits(x, T, _u32(cks, cuda), 0, rank, sigma, x_batched)
+    xs = x.float().cpu().numpy()
+    for p in range(P):
+        want = oracle.perturbed_tied_logits(xs[p] if x_batched else xs, T.float().cpu().numpy(), gks[p], rank,
+                                            sigma, DN[dtype])
+        np.testing.assert_allclose(y[p].float().cpu().numpy(), want, **TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("idx_batched", [False, True])
+def test_table_lookup(cuda, oracle, dtype, idx_batched):
+    P, rows, cols, rank, sigma = 4, 40, 300, 4, 0.2
+    cks, gks = _setup(oracle, P, group=2)
+    T = _rand((rows, cols), dtype, cuda, 5)
+    g = torch.Generator().manual_seed(6)
+    idx = torch.randint(0, rows, (P, 3, 5) if idx_batched else (3, 5), generator=g).to(cuda)
+    out = _ops.launch_table_lookup(T, idx, _u32(cks, cuda), 2, rank, sigma, idx_batched)
+    ii = idx.cpu().numpy()
+    for p in range(P):
+        want = oracle.perturbed_table_lookup(T.float().cpu().numpy(), ii[p] if idx_batched else ii, gks[p], rank,
+                                             sigma, DN[dtype])
+        np.testing.assert_allclose(out[p].float().cpu().numpy(), want, **TOL[dtype])
+
+
+def test_table_lookup_negative_and_out_of_range_indices(cuda, oracle):
+    """jnp indexing: negative indices wrap, out-of-range gathers clamp."""
+    P, rows, cols, rank, sigma = 2, 10, 16, 2, 0.1
+    cks, gks = _setup(oracle, P)
+    T = _rand((rows, cols), torch.float32, cuda, 7)
+    idx = torch.tensor([-1, -10, 0, 9, 12, -13], dtype=torch.int32, device=cuda)
+    out = _ops.launch_table_lookup(T, idx, _u32(cks, cuda), 1, rank, sigma, False)
+    eff = np.array([9, 0, 0, 9, 9, 0])
+    for p in range(P):
+        want = oracle.perturbed_table_lookup(T.cpu().numpy(), eff, gks[p], rank, sigma)
+        np.testing.assert_allclose(out[p].cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_vector(cuda, oracle, dtype):
+    P, n, sigma = 7, 1000, 0.3
+    cks, gks = _setup(oracle, P, group=0)
+    v = _rand((n,), dtype, cuda, 8)
+    out = _ops.launch_vector(v, _u32(cks, cuda), 0, sigma, False)
+    for p in range(P):
+        want = oracle.perturbed_vector(v.float().cpu().numpy(), gks[p], sigma, DN[dtype])
+        np.testing.assert_allclose(out[p].float().cpu().numpy(), want, **TOL[dtype])
+
+
+def test_public_ops_take_group_keys(cuda, oracle):
+    """perturbed_* take a GROUP key, CandidateContext a candidate key + group."""
+    gk = oracle.key(1234)
+    x = _rand((3, 8), torch.float32, cuda, 9)
+    W = _rand((8, 4), torch.float32, cuda, 10)
+    y = zg.perturbed_linear(x, W, _u32(gk, cuda), 2, 0.1)
+    want = oracle.perturbed_linear(x.cpu().numpy(), W.cpu().numpy(), gk, 2, 0.1)
+    np.testing.assert_allclose(y.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+    A, B = zg.matrix_factors(_u32(gk, cuda), (8, 4), 2, dtype=torch.float32)
+    a, b = oracle.matrix_factors(gk, (8, 4), 2)
+    np.testing.assert_allclose(A.cpu().numpy(), a, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(B.cpu().numpy(), b, rtol=1e-5, atol=1e-6)
+
+
+def test_vmap_launches_one_population_op(cuda, oracle):
+    """Per-candidate code under torch.func.vmap equals the population launch."""
+    P, M, K, N, rank, sigma = 6, 4, 16, 8, 2, 0.1
+    cks, gks = _setup(oracle, P, group=0)
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w"),))
+    W = _rand((K, N), torch.float32, cuda, 11)
+    x = _rand((M, K), torch.float32, cuda, 12)
+
+    def one(ck):
+        ctx = zg.CandidateContext(manifest, ck, rank, sigma)
+        return ctx.linear({"w": W}, ("w",), x)
+
+    y = torch.func.vmap(one)(_u32(cks, cuda))
+    for p in range(P):
+        want = oracle.perturbed_linear(x.cpu().numpy(), W.cpu().numpy(), gks[p], rank, sigma)
+        np.testing.assert_allclose(y[p].cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+    # and unbatched (a single candidate) matches row 0
+    y0 = one(_u32(cks[0], cuda))
+    np.testing.assert_allclose(y0.cpu().numpy(), y[0].cpu().numpy(), rtol=0, atol=0)

@@ -1,0 +1,107 @@
+"""Factor-only forward ops of one candidate (``src/zerograd/_candidate.py``).
+
+Each op is a custom op over the C ABI; called per candidate inside
+``torch.func.vmap`` (as ``ZeroGrad`` does) it becomes one population-batched
+kernel launch.  ``CandidateContext`` passes the CANDIDATE key and the group
+index, and the kernel derives the group key itself.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _ops
+from ._factors import _validate_rank, _validate_sigma
+from ._keys import group_key
+from ._manifest import Manifest, ParameterLayout, ParameterPath, ParameterTree
+
+
+def perturbed_linear(x: torch.Tensor, weight: torch.Tensor, key: torch.Tensor, rank: int,
+                     sigma: float) -> torch.Tensor:
+    """``x @ weight + sigma/sqrt(rank) * (x @ A) @ B`` for a group key (``_candidate.py:17-22``)."""
+    if weight.ndim != 2 or x.shape[-1] != weight.shape[0]:
+        raise ValueError("linear input and [in, out] weight shapes are incompatible")
+    _validate_rank(rank)
+    _validate_sigma(sigma)
+    return _ops.linear(x, weight, key, -1, rank, sigma)
+
+
+def perturbed_table_lookup(table: torch.Tensor, indices: torch.Tensor, key: torch.Tensor, rank: int,
+                           sigma: float) -> torch.Tensor:
+    """``T[idx] + s * A[idx] @ B^T`` (``_candidate.py:25-30``)."""
+    if table.ndim != 2:
+        raise ValueError("table weights must be two-dimensional")
+    _validate_rank(rank)
+    _validate_sigma(sigma)
+    return _ops.table_lookup(table, indices, key, -1, rank, sigma)
+
+
+def perturbed_tied_logits(x: torch.Tensor, table: torch.Tensor, key: torch.Tensor, rank: int,
+                          sigma: float) -> torch.Tensor:
+    """``x @ T^T + s * (x @ B) @ A^T`` (``_candidate.py:33-38``)."""
+    if table.ndim != 2 or x.shape[-1] != table.shape[1]:
+        raise ValueError("logit input and [rows, cols] table shapes are incompatible")
+    _validate_rank(rank)
+    _validate_sigma(sigma)
+    return _ops.tied_logits(x, table, key, -1, rank, sigma)
+
+
+def perturbed_vector(vector: torch.Tensor, key: torch.Tensor, sigma: float) -> torch.Tensor:
+    """``v + sigma * noise`` (``_candidate.py:41-45``)."""
+    if vector.ndim != 1:
+        raise ValueError("vector weights must be one-dimensional")
+    _validate_sigma(sigma)
+    return _ops.vector(vector, key, -1, sigma)
+
+
+@dataclass(frozen=True, slots=True)
+class CandidateContext:
+    """Candidate-local manifest lookup and forward-op facade (``_candidate.py:48-87``)."""
+
+    manifest: Manifest
+    candidate_key: torch.Tensor
+    rank: int
+    sigma: float
+
+    def key_for(self, path: ParameterPath) -> torch.Tensor:
+        return group_key(self.candidate_key, self.manifest, self.manifest.entry(path).group)
+
+    def _group(self, path: ParameterPath) -> int:
+        return self.manifest.group_index(self.manifest.entry(path).group)
+
+    def linear(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor) -> torch.Tensor:
+        entry = self.manifest.entry(path)
+        if entry.layout is not ParameterLayout.MATRIX:
+            raise ValueError(f"{'.'.join(path)} is not a matrix entry")
+        weight = self.manifest.resolve(params, path)
+        if weight.ndim != 2 or x.shape[-1] != weight.shape[0]:
+            raise ValueError("linear input and [in, out] weight shapes are incompatible")
+        return _ops.linear(x, weight, self.candidate_key, self._group(path), self.rank, self.sigma)
+
+    def table_lookup(self, params: ParameterTree, path: ParameterPath, indices: torch.Tensor) -> torch.Tensor:
+        entry = self.manifest.entry(path)
+        if entry.layout is not ParameterLayout.TABLE:
+            raise ValueError(f"{'.'.join(path)} is not a table entry")
+        table = self.manifest.resolve(params, path)
+        if table.ndim != 2:
+            raise ValueError("table weights must be two-dimensional")
+        return _ops.table_lookup(table, indices, self.candidate_key, self._group(path), self.rank, self.sigma)
+
+    def tied_logits(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor) -> torch.Tensor:
+        entry = self.manifest.entry(path)
+        if entry.layout is not ParameterLayout.TABLE:
+            raise ValueError(f"{'.'.join(path)} is not a table entry")
+        table = self.manifest.resolve(params, path)
+        if table.ndim != 2 or x.shape[-1] != table.shape[1]:
+            raise ValueError("logit input and [rows, cols] table shapes are incompatible")
+        return _ops.tied_logits(x, table, self.candidate_key, self._group(path), self.rank, self.sigma)
+
+    def vector(self, params: ParameterTree, path: ParameterPath) -> torch.Tensor:
+        entry = self.manifest.entry(path)
+        if entry.layout is not ParameterLayout.VECTOR:
+            raise ValueError(f"{'.'.join(path)} is not a vector entry")
+        v = self.manifest.resolve(params, path)
+        if v.ndim != 1:
+            raise ValueError("vector weights must be one-dimensional")
+        return _ops.vector(v, self.candidate_key, self._group(path), self.sigma)

@@ -1,0 +1,446 @@
+"""Torch custom ops over the libzgb200 C ABI, with population vmap rules.
+
+The reference calls its forward ops per candidate inside ``jax.vmap`` over
+candidate ids (``src/zerograd/_optimizer.py:173-181``).  Here the same
+per-candidate code runs under ``torch.func.vmap``; each op below has a vmap
+rule that turns the batched candidate key into ONE population-batched
+kernel launch (an unbatched activation stays shared across candidates, the
+way vmap leaves an unbatched ``x @ W`` unbatched).
+
+Launchers (``launch_*``) are the population-form entry points: keys
+``[P, 2]`` uint32, outputs with a leading population axis.
+"""
+from __future__ import annotations
+
+import math
+import struct
+
+import torch
+
+from . import _lib as L
+
+# ---------------------------------------------------------------------------
+# scalars
+# ---------------------------------------------------------------------------
+
+
+def round_scalar(value: float, dtype: torch.dtype) -> float:
+    """A Python float converted to a scalar of ``dtype`` (float32 or bf16).
+
+    bf16 goes through float32 first, as numpy/ml_dtypes scalar conversion does.
+    """
+    f32 = struct.unpack("<f", struct.pack("<f", value))[0]
+    if dtype == torch.float32:
+        return f32
+    if dtype == torch.bfloat16:
+        u = struct.unpack("<I", struct.pack("<f", f32))[0]
+        if (u & 0x7F800000) != 0x7F800000:
+            u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+        return struct.unpack("<f", struct.pack("<I", u & 0xFFFFFFFF))[0]
+    raise TypeError(f"unsupported dtype {dtype}")
+
+
+def scaled_factor_value(rank: int, sigma: float, dtype: torch.dtype) -> float:
+    return round_scalar(sigma / math.sqrt(rank), dtype)
+
+
+def _keys2d(keys: torch.Tensor) -> torch.Tensor:
+    if keys.dtype != torch.uint32:
+        raise TypeError(f"keys must be uint32 key data, got {keys.dtype}")
+    if keys.shape[-1] != 2:
+        raise ValueError(f"keys must have a trailing dimension of 2, got {tuple(keys.shape)}")
+    return keys.reshape(-1, 2).contiguous()
+
+
+def _compute_dtype(*ts: torch.Tensor) -> torch.dtype:
+    dt = ts[0].dtype
+    for t in ts[1:]:
+        dt = torch.promote_types(dt, t.dtype)
+    L.dtype_code(dt)
+    return dt
+
+
+# ---------------------------------------------------------------------------
+# launchers (population form)
+# ---------------------------------------------------------------------------
+
+
+def _as_u32(data: torch.Tensor) -> torch.Tensor:
+    d = data.reshape(-1)
+    if d.dtype in (torch.int32, torch.uint32):
+        return d.contiguous().view(torch.uint32)
+    return d.to(torch.int64).to(torch.uint32).contiguous()
+
+
+def launch_fold_in(keys: torch.Tensor, data: torch.Tensor) -> torch.Tensor:
+    """out[i] = fold_in(keys[i] (or the single key), data[i]).
+
+    A single key held on the host is passed by value (no host-to-device copy).
+    """
+    if not keys.is_cuda and keys.numel() == 2 and data.is_cuda:
+        k = _keys2d(keys)
+        d = _as_u32(data)
+        out = torch.empty((d.numel(), 2), dtype=torch.uint32, device=data.device)
+        L.call("zg_candidate_keys", int(k[0, 0]), int(k[0, 1]), L.ptr(d), L.ptr(out), d.numel(),
+               L.stream_ptr(data.device))
+        return out
+    dev = L.require_cuda(keys, data)
+    k = _keys2d(keys)
+    d = _as_u32(data)
+    n = max(d.numel(), k.shape[0])
+    if k.shape[0] not in (1, n) or d.numel() not in (1, n):
+        raise ValueError("fold_in: keys and data counts do not broadcast")
+    if d.numel() == 1 and n > 1:
+        d = d.expand(n).contiguous()
+    out = torch.empty((n, 2), dtype=torch.uint32, device=dev)
+    L.call("zg_fold_in", L.ptr(k), int(k.shape[0] != 1), L.ptr(d), L.ptr(out), n, L.stream_ptr(dev))
+    return out
+
+
+def launch_normal(keys: torch.Tensor, n: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    dev = L.require_cuda(keys)
+    k = _keys2d(keys)
+    out = torch.empty((k.shape[0], n), dtype=dtype, device=dev)
+    L.call("zg_normal", L.ptr(k), k.shape[0], n, L.dtype_code(dtype), L.ptr(out), L.stream_ptr(dev))
+    return out
+
+
+def launch_bits(keys: torch.Tensor, n: int) -> torch.Tensor:
+    dev = L.require_cuda(keys)
+    k = _keys2d(keys)
+    out = torch.empty((k.shape[0], n), dtype=torch.uint32, device=dev)
+    L.call("zg_random_bits", L.ptr(k), k.shape[0], n, L.ptr(out), L.stream_ptr(dev))
+    return out
+
+
+def launch_factors(keys: torch.Tensor, group: int, layout: int, shape, rank: int,
+                   dtype: torch.dtype):
+    """Population factors in the reference layouts (leading P axis)."""
+    dev = L.require_cuda(keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    rows = int(shape[0])
+    if layout == L.ZG_VECTOR:
+        A = torch.empty((P, rows), dtype=dtype, device=dev)
+        L.call("zg_population_factors", L.ptr(k), group, P, layout, rows, 1, 1, L.dtype_code(dtype),
+               L.ptr(A), None, L.stream_ptr(dev))
+        return A, None
+    cols = int(shape[1])
+    A = torch.empty((P, rows, rank), dtype=dtype, device=dev)
+    B = torch.empty((P, rank, cols) if layout == L.ZG_MATRIX else (P, cols, rank), dtype=dtype, device=dev)
+    L.call("zg_population_factors", L.ptr(k), group, P, layout, rows, cols, rank, L.dtype_code(dtype),
+           L.ptr(A), L.ptr(B), L.stream_ptr(dev))
+    return A, B
+
+
+def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
+                  sigma: float, x_batched: bool) -> torch.Tensor:
+    """y[p] = x_p @ W + s (x_p @ A_p) @ B_p; x [*M, K] shared or [P, *M, K]."""
+    dev = L.require_cuda(x, weight, keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    if weight.ndim != 2 or x.ndim < 1 or x.shape[-1] != weight.shape[0]:
+        raise ValueError("linear input and [in, out] weight shapes are incompatible")
+    if x_batched and (x.ndim < 2 or x.shape[0] != P):
+        raise ValueError("batched linear input must lead with the population axis")
+    dt = _compute_dtype(x, weight)
+    x = x.to(dt).contiguous()
+    W = weight.to(dt).contiguous()
+    K, N = W.shape
+    mshape = tuple(x.shape[1:-1] if x_batched else x.shape[:-1])
+    M = math.prod(mshape)
+    y = torch.empty((P, *mshape, N), dtype=dt, device=dev)
+    if M == 0:
+        return y
+    s = scaled_factor_value(rank, sigma, weight.dtype)
+    code = L.dtype_code(dt)
+    ws = L.workspace(L.query("zg_perturbed_linear_workspace_size", P, M, K, N, rank, code, int(x_batched)), dev)
+    L.call("zg_perturbed_linear", L.ptr(x), int(x_batched), L.ptr(W), L.ptr(k), group, P, M, K, N, rank, s,
+           code, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    return y
+
+
+def launch_tied_logits(x: torch.Tensor, table: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
+                       sigma: float, x_batched: bool) -> torch.Tensor:
+    dev = L.require_cuda(x, table, keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    if table.ndim != 2 or x.ndim < 1 or x.shape[-1] != table.shape[1]:
+        raise ValueError("logit input and [rows, cols] table shapes are incompatible")
+    dt = _compute_dtype(x, table)
+    x = x.to(dt).contiguous()
+    T = table.to(dt).contiguous()
+    V, C = T.shape
+    mshape = tuple(x.shape[1:-1] if x_batched else x.shape[:-1])
+    M = math.prod(mshape)
+    y = torch.empty((P, *mshape, V), dtype=dt, device=dev)
+    if M == 0:
+        return y
+    s = scaled_factor_value(rank, sigma, table.dtype)
+    code = L.dtype_code(dt)
+    ws = L.workspace(L.query("zg_tied_logits_workspace_size", P, M, V, C, rank, code, int(x_batched)), dev)
+    L.call("zg_tied_logits", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, P, M, V, C, rank, s, code,
+           L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    return y
+
+
+def launch_table_lookup(table: torch.Tensor, indices: torch.Tensor, keys: torch.Tensor, group: int,
+                        rank: int, sigma: float, idx_batched: bool) -> torch.Tensor:
+    dev = L.require_cuda(table, indices, keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    if table.ndim != 2:
+        raise ValueError("table weights must be two-dimensional")
+    if indices.is_floating_point() or indices.dtype == torch.bool:
+        raise TypeError("table indices must be integers")
+    T = table.contiguous()
+    rows, cols = T.shape
+    ishape = tuple(indices.shape[1:] if idx_batched else indices.shape)
+    n_idx = math.prod(ishape)
+    idx = indices.to(torch.int32).contiguous()
+    out = torch.empty((P, *ishape, cols), dtype=T.dtype, device=dev)
+    if n_idx == 0:
+        return out
+    s = scaled_factor_value(rank, sigma, T.dtype)
+    code = L.dtype_code(T.dtype)
+    ws = L.workspace(L.query("zg_table_lookup_workspace_size", P, rows, cols, rank, code), dev)
+    L.call("zg_table_lookup", L.ptr(T), L.ptr(idx), int(idx_batched), n_idx, L.ptr(k), group, P, rows, cols,
+           rank, s, code, L.ptr(out), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    return out
+
+
+def launch_vector(v: torch.Tensor, keys: torch.Tensor, group: int, sigma: float, v_batched: bool) -> torch.Tensor:
+    dev = L.require_cuda(v, keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    n = v.shape[-1]
+    if (v.ndim != 1 and not v_batched) or (v_batched and v.ndim != 2):
+        raise ValueError("vector weights must be one-dimensional")
+    vv = v.contiguous()
+    out = torch.empty((P, n), dtype=v.dtype, device=dev)
+    if n == 0:
+        return out
+    s = scaled_factor_value(1, sigma, v.dtype)
+    L.call("zg_perturbed_vector", L.ptr(vv), int(v_batched), L.ptr(k), group, P, n, s, L.dtype_code(v.dtype),
+           L.ptr(out), L.stream_ptr(dev))
+    return out
+
+
+def launch_shape_fitness(losses: torch.Tensor, sigma: float):
+    """Returns (shaped [P] float32, metrics [4] float32 = mean, min, max, #non-finite)."""
+    dev = L.require_cuda(losses)
+    l32 = losses.to(torch.float32).contiguous()
+    P = l32.shape[0]
+    shaped = torch.empty(P, dtype=torch.float32, device=dev)
+    metrics = torch.empty(4, dtype=torch.float32, device=dev)
+    L.call("zg_shape_fitness", L.ptr(l32), P, float(sigma), L.ptr(shaped), L.ptr(metrics), L.stream_ptr(dev))
+    return shaped, metrics
+
+
+def launch_replay(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, layout: int, shape, rank: int,
+                  dtype: torch.dtype, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Descent direction [*shape] float32 of one entry (``_replay.py:15-54``)."""
+    dev = L.require_cuda(shaped, cand_keys)
+    k = _keys2d(cand_keys)
+    P = k.shape[0]
+    w = shaped.to(torch.float32).contiguous()
+    if w.numel() != P:
+        raise ValueError("shaped weights and candidate keys differ in length")
+    rows = int(shape[0])
+    cols = int(shape[1]) if layout != L.ZG_VECTOR else 1
+    r = rank if layout != L.ZG_VECTOR else 1
+    code = L.dtype_code(dtype)
+    if out is None:
+        out = torch.empty(tuple(int(d) for d in shape), dtype=torch.float32, device=dev)
+    inv = scaled_factor_value(r, 1.0, dtype)
+    ws = L.workspace(L.query("zg_replay_workspace_size", P, layout, rows, cols, r, code), dev)
+    L.call("zg_replay", L.ptr(w), L.ptr(k), group, P, layout, rows, cols, r, inv, code, L.ptr(out), L.ptr(ws),
+           ws.numel(), L.stream_ptr(dev))
+    return out
+
+
+def launch_adamw(param: torch.Tensor, descent: torch.Tensor | None, mu: torch.Tensor, nu: torch.Tensor,
+                 count: int, lr: float, b1: float, b2: float, eps: float, weight_decay: float):
+    dev = L.require_cuda(param, descent, mu, nu)
+    p_out = torch.empty_like(param)
+    mu_out = torch.empty_like(mu)
+    nu_out = torch.empty_like(nu)
+    d = None if descent is None else descent.to(torch.float32).contiguous()
+    L.call("zg_adamw_update", L.ptr(param.contiguous()), L.ptr(p_out), L.dtype_code(param.dtype), L.ptr(d),
+           L.ptr(mu), L.ptr(nu), L.ptr(mu_out), L.ptr(nu_out), param.numel(), count, lr, b1, b2, eps,
+           weight_decay, L.stream_ptr(dev))
+    return p_out, mu_out, nu_out
+
+
+def launch_sgd(param: torch.Tensor, descent: torch.Tensor | None, lr: float) -> torch.Tensor:
+    dev = L.require_cuda(param, descent)
+    p_out = torch.empty_like(param)
+    d = None if descent is None else descent.to(torch.float32).contiguous()
+    L.call("zg_sgd_update", L.ptr(param.contiguous()), L.ptr(p_out), L.dtype_code(param.dtype), L.ptr(d),
+           param.numel(), lr, L.stream_ptr(dev))
+    return p_out
+
+
+def launch_int8_lut_linear(x: torch.Tensor, weight: torch.Tensor, w_scale: torch.Tensor, x_scale: float,
+                           y_scale: float, lut: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
+                           sigma: float, x_batched: bool, return_acc: bool = False):
+    dev = L.require_cuda(x, weight, w_scale, lut, keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    if x.dtype != torch.int8 or weight.dtype != torch.int8 or lut.dtype != torch.int8:
+        raise TypeError("int8 linear takes int8 activations, weights and LUT")
+    if weight.ndim != 2 or x.shape[-1] != weight.shape[0] or lut.numel() != 256:
+        raise ValueError("int8 linear shapes are incompatible")
+    K, N = weight.shape
+    mshape = tuple(x.shape[1:-1] if x_batched else x.shape[:-1])
+    M = math.prod(mshape)
+    out = torch.empty((P, *mshape, N), dtype=torch.int8, device=dev)
+    acc = torch.empty((P, *mshape, N), dtype=torch.int32, device=dev) if return_acc else None
+    s = round_scalar(sigma / math.sqrt(rank), torch.float32)
+    ws = L.workspace(L.query("zg_int8_lut_linear_workspace_size", P, M, K, N, rank, int(x_batched)), dev)
+    L.call("zg_int8_lut_linear", L.ptr(x.contiguous()), int(x_batched), L.ptr(weight.contiguous()),
+           L.ptr(w_scale.to(torch.float32).contiguous()), float(x_scale), float(y_scale), L.ptr(lut.contiguous()),
+           L.ptr(k), group, P, M, K, N, rank, s, L.ptr(out), L.ptr(acc), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    return (out, acc) if return_acc else out
+
+
+# ---------------------------------------------------------------------------
+# custom ops (single-candidate semantics) + vmap rules (population launch)
+# ---------------------------------------------------------------------------
+
+_NS = "zerograd_b200"
+
+
+def _movedim0(t, d):
+    return t if d is None or d == 0 else t.movedim(d, 0)
+
+
+@torch.library.custom_op(f"{_NS}::fold_in", mutates_args=())
+def _fold_in_op(key: torch.Tensor, data: torch.Tensor) -> torch.Tensor:
+    return launch_fold_in(key, data).reshape(2)
+
+
+@torch.library.register_vmap(f"{_NS}::fold_in")
+def _fold_in_vmap(info, in_dims, key, data):
+    kd, dd = in_dims
+    key = _movedim0(key, kd)
+    data = _movedim0(data, dd)
+    return launch_fold_in(key, data), 0
+
+
+def fold_in(key: torch.Tensor, data) -> torch.Tensor:
+    if isinstance(data, int):
+        data = torch.tensor(data & 0xFFFFFFFF, dtype=torch.int64, device=key.device)
+    return _fold_in_op(key, data)
+
+
+@torch.library.custom_op(f"{_NS}::linear", mutates_args=())
+def _linear_op(x: torch.Tensor, weight: torch.Tensor, key: torch.Tensor, group: int, rank: int,
+               sigma: float) -> torch.Tensor:
+    return launch_linear(x, weight, key.reshape(1, 2), group, rank, sigma, False)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::linear")
+def _linear_vmap(info, in_dims, x, weight, key, group, rank, sigma):
+    xd, wd, kd = in_dims[:3]
+    if wd is not None:
+        raise NotImplementedError("weights batched over candidates are not supported")
+    x = _movedim0(x, xd)
+    if kd is None:
+        return launch_linear(x, weight, key.reshape(1, 2), group, rank, sigma, False)[0], 0
+    return launch_linear(x, weight, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
+
+
+@torch.library.custom_op(f"{_NS}::tied_logits", mutates_args=())
+def _tied_op(x: torch.Tensor, table: torch.Tensor, key: torch.Tensor, group: int, rank: int,
+             sigma: float) -> torch.Tensor:
+    return launch_tied_logits(x, table, key.reshape(1, 2), group, rank, sigma, False)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::tied_logits")
+def _tied_vmap(info, in_dims, x, table, key, group, rank, sigma):
+    xd, td, kd = in_dims[:3]
+    if td is not None:
+        raise NotImplementedError("tables batched over candidates are not supported")
+    x = _movedim0(x, xd)
+    if kd is None:
+        return launch_tied_logits(x, table, key.reshape(1, 2), group, rank, sigma, False)[0], 0
+    return launch_tied_logits(x, table, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
+
+
+@torch.library.custom_op(f"{_NS}::table_lookup", mutates_args=())
+def _lookup_op(table: torch.Tensor, indices: torch.Tensor, key: torch.Tensor, group: int, rank: int,
+               sigma: float) -> torch.Tensor:
+    return launch_table_lookup(table, indices, key.reshape(1, 2), group, rank, sigma, False)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::table_lookup")
+def _lookup_vmap(info, in_dims, table, indices, key, group, rank, sigma):
+    td, idd, kd = in_dims[:3]
+    if td is not None:
+        raise NotImplementedError("tables batched over candidates are not supported")
+    indices = _movedim0(indices, idd)
+    if kd is None:
+        return launch_table_lookup(table, indices, key.reshape(1, 2), group, rank, sigma, False)[0], 0
+    return launch_table_lookup(table, indices, _movedim0(key, kd), group, rank, sigma, idd is not None), 0
+
+
+@torch.library.custom_op(f"{_NS}::vector", mutates_args=())
+def _vector_op(v: torch.Tensor, key: torch.Tensor, group: int, sigma: float) -> torch.Tensor:
+    return launch_vector(v, key.reshape(1, 2), group, sigma, False)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::vector")
+def _vector_vmap(info, in_dims, v, key, group, sigma):
+    vd, kd = in_dims[:2]
+    v = _movedim0(v, vd)
+    if kd is None:
+        # shared key, batched leaf: each row gets the same noise
+        return launch_vector(v.reshape(-1, v.shape[-1]), key.reshape(1, 2).expand(v.shape[0], 2), group, sigma,
+                             True), 0
+    return launch_vector(v, _movedim0(key, kd), group, sigma, vd is not None), 0
+
+
+@torch.library.custom_op(f"{_NS}::normal", mutates_args=())
+def _normal_op(key: torch.Tensor, n: int, dtype_code: int) -> torch.Tensor:
+    return launch_normal(key.reshape(1, 2), n, torch.bfloat16 if dtype_code == L.ZG_BF16 else torch.float32)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::normal")
+def _normal_vmap(info, in_dims, key, n, dtype_code):
+    key = _movedim0(key, in_dims[0])
+    return launch_normal(key, n, torch.bfloat16 if dtype_code == L.ZG_BF16 else torch.float32), 0
+
+
+@torch.library.custom_op(f"{_NS}::bits", mutates_args=())
+def _bits_op(key: torch.Tensor, n: int) -> torch.Tensor:
+    return launch_bits(key.reshape(1, 2), n)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::bits")
+def _bits_vmap(info, in_dims, key, n):
+    return launch_bits(_movedim0(key, in_dims[0]), n), 0
+
+
+def linear(x, weight, key, group, rank, sigma):
+    return _linear_op(x, weight, key, int(group), int(rank), float(sigma))
+
+
+def tied_logits(x, table, key, group, rank, sigma):
+    return _tied_op(x, table, key, int(group), int(rank), float(sigma))
+
+
+def table_lookup(table, indices, key, group, rank, sigma):
+    return _lookup_op(table, indices, key, int(group), int(rank), float(sigma))
+
+
+def vector(v, key, group, sigma):
+    return _vector_op(v, key, int(group), float(sigma))
+
+
+def normal(key, n: int, dtype: torch.dtype = torch.float32):
+    return _normal_op(key, int(n), L.dtype_code(dtype))
+
+
+def bits(key, n: int):
+    return _bits_op(key, int(n))

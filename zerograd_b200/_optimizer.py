@@ -1,0 +1,224 @@
+"""ZeroGrad optimizer lifecycle (``src/zerograd/_optimizer.py``).
+
+Same surface as the reference: ``init``, ``evaluate_shard``,
+``step_from_losses``, ``step`` and the read-only properties.  Candidate
+evaluation runs the per-candidate ``loss_fn`` under ``torch.func.vmap`` over
+the candidate keys; every ``CandidateContext`` op inside becomes one
+population-batched kernel launch.  Completing a generation is one fused
+shaping kernel (validation + metrics), one replay per manifest entry and one
+fused update kernel per leaf, with a single device-to-host read of the
+metrics.
+"""
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Mapping
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from . import _ops
+from ._candidate import CandidateContext
+from ._fitness import _check_shape_dtype
+from ._keys import key as make_key
+from ._keys import step_key
+from ._manifest import Manifest, ParameterTree
+from ._replay import candidate_keys, replay_entry_keys
+from ._transforms import _leaves, apply_updates, is_fused, tree_get, tree_set
+
+LossFn = Callable[[ParameterTree, CandidateContext, Any, torch.Tensor], tuple[torch.Tensor, Any]]
+
+
+@dataclass(frozen=True, slots=True)
+class ZeroGradState:
+    """Immutable optimizer state: generation and transform state (``_optimizer.py:25-30``)."""
+
+    generation: int
+    opt_state: Any
+
+
+@dataclass(frozen=True, slots=True)
+class StepMetrics:
+    """Population diagnostics (``_optimizer.py:33-41``)."""
+
+    generation: int
+    mean_loss: float
+    min_loss: float
+    max_loss: float
+    population_size: int
+
+
+def _device_of(params: ParameterTree) -> torch.device:
+    for _, v in _leaves(_materialize_tree(params)):
+        if isinstance(v, torch.Tensor):
+            return v.device
+    raise ValueError("params contain no tensors")
+
+
+class ZeroGrad:
+    """Factor-only ES optimizer (``_optimizer.py:44-277``)."""
+
+    def __init__(self, manifest: Manifest, transform, population_size: int, rank: int, sigma: float, seed: int,
+                 run_id: str) -> None:
+        if not isinstance(manifest, Manifest):
+            raise TypeError("manifest must be a Manifest")
+        if not isinstance(population_size, int) or isinstance(population_size, bool) or population_size < 2:
+            raise ValueError("population_size must be an integer >= 2")
+        if not isinstance(rank, int) or isinstance(rank, bool) or rank < 1:
+            raise ValueError("rank must be a positive integer")
+        if not isinstance(sigma, float) or not math.isfinite(sigma) or sigma <= 0:
+            raise ValueError("sigma must be a finite positive float")
+        if not isinstance(seed, int) or isinstance(seed, bool):
+            raise TypeError("seed must be an integer")
+        if not isinstance(run_id, str) or not run_id:
+            raise ValueError("run_id must be a non-empty string")
+        self._manifest = manifest
+        self._transform = transform
+        self._population_size = population_size
+        self._rank = rank
+        self._sigma = sigma
+        self._seed = seed
+        self._run_id = run_id
+
+    def init(self, params: ParameterTree) -> ZeroGradState:
+        self._manifest.validate(params)
+        params = _materialize_tree(params)
+        return ZeroGradState(generation=0, opt_state=self._transform.init(params))
+
+    @property
+    def population_size(self) -> int:
+        return self._population_size
+
+    @property
+    def rank(self) -> int:
+        return self._rank
+
+    @property
+    def sigma(self) -> float:
+        return self._sigma
+
+    @property
+    def manifest(self) -> Manifest:
+        return self._manifest
+
+    @property
+    def seed(self) -> int:
+        return self._seed
+
+    @property
+    def run_id(self) -> str:
+        return self._run_id
+
+    @property
+    def transform(self):
+        return self._transform
+
+    # -- evaluation ---------------------------------------------------------
+
+    def base_key(self, generation: int) -> torch.Tensor:
+        """Host-side base key of a generation (passed to kernels by value)."""
+        return step_key(self._seed, self._run_id, generation, self._manifest.version)
+
+    def evaluate_shard(self, params: ParameterTree, generation: int, loss_fn: LossFn, batch: Any,
+                       candidate_ids, *, rng: torch.Tensor | None = None) -> torch.Tensor:
+        """Losses of a subset of candidates (``_optimizer.py:126-149``)."""
+        self._manifest.validate(params)
+        params = _materialize_tree(params)
+        return self._evaluate_shard(params, generation, loss_fn, batch, candidate_ids, rng=rng)
+
+    def _evaluate_shard(self, params, generation, loss_fn, batch, candidate_ids, *, rng=None):
+        device = _device_of(params)
+        ids = torch.as_tensor(candidate_ids, device=device)
+        if ids.ndim != 1:
+            raise ValueError("candidate_ids must be one-dimensional")
+        if rng is None:
+            rng = make_key(0)
+        cks = candidate_keys(self.base_key(generation), ids)
+        rngs = _ops.launch_fold_in(rng.reshape(1, 2), ids)
+        manifest, rank, sigma = self._manifest, self._rank, self._sigma
+
+        def evaluate_candidate(ck, crng):
+            ctx = CandidateContext(manifest, ck, rank, sigma)
+            loss, _aux = loss_fn(params, ctx, batch, crng)
+            return loss
+
+        if ids.numel() == 0:
+            return torch.empty(0, dtype=torch.float32, device=device)
+        return torch.func.vmap(evaluate_candidate)(cks, rngs)
+
+    # -- completion ---------------------------------------------------------
+
+    def step_from_losses(self, state: ZeroGradState, params: ParameterTree, losses: torch.Tensor):
+        """Complete one generation from losses in candidate-id order (``_optimizer.py:183-203``)."""
+        if not isinstance(state, ZeroGradState):
+            raise TypeError("state must be a ZeroGradState")
+        self._manifest.validate(params)
+        params = _materialize_tree(params)
+        return self._step_from_losses(state, params, losses)
+
+    def _check_losses(self, losses: torch.Tensor) -> None:
+        _check_shape_dtype(losses)
+        if losses.shape[0] != self._population_size:
+            raise ValueError(f"losses must have {self._population_size} entries, got {losses.shape[0]}")
+
+    def _step_from_losses(self, state, params, losses, cand_keys: torch.Tensor | None = None):
+        self._check_losses(losses)
+        device = _device_of(params)
+        losses = losses.to(device)
+        generation = state.generation
+        shaped, metrics = _ops.launch_shape_fitness(losses, self._sigma)
+        if cand_keys is None:
+            ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
+            cand_keys = candidate_keys(self.base_key(generation), ids)
+        descent: dict = {}
+        for entry in self._manifest.entries:
+            tree_set(descent, entry.path,
+                     replay_entry_keys(params, self._manifest, entry.path, cand_keys, shaped, self._rank))
+        if is_fused(self._transform):
+            new_params, new_opt_state = self._transform.apply(params, descent, state.opt_state)
+        else:
+            grads = _build_pseudo_grad(descent, params)
+            updates, new_opt_state = self._transform.update(grads, state.opt_state, params)
+            new_params = apply_updates(params, updates)
+        # The one host sync of a generation, after all its work is queued.  The
+        # update wrote new tensors only, so rejecting non-finite losses here
+        # leaves params and state exactly as they were.
+        m = metrics.cpu()
+        if m[3].item() > 0:
+            raise ValueError("candidate losses must be finite")
+        metrics_out = StepMetrics(generation=generation, mean_loss=float(m[0]), min_loss=float(m[1]),
+                                  max_loss=float(m[2]), population_size=self._population_size)
+        return new_params, ZeroGradState(generation=generation + 1, opt_state=new_opt_state), metrics_out
+
+    def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, loss_fn: LossFn, *,
+             rng: torch.Tensor | None = None):
+        """One generation: evaluate all candidates, then complete (``_optimizer.py:246-277``)."""
+        if not isinstance(state, ZeroGradState):
+            raise TypeError("state must be a ZeroGradState")
+        self._manifest.validate(params)
+        params = _materialize_tree(params)
+        device = _device_of(params)
+        ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
+        losses = self._evaluate_shard(params, state.generation, loss_fn, batch, ids, rng=rng)
+        return self._step_from_losses(state, params, losses)
+
+
+def _materialize_tree(params: ParameterTree) -> dict:
+    """Plain-dict copy of a Mapping tree (``_optimizer.py:280-296``)."""
+    out: dict = {}
+    for k, v in params.items():
+        out[k] = _materialize_tree(v) if isinstance(v, Mapping) else v
+    return out
+
+
+def _build_pseudo_grad(descent: dict, params: ParameterTree) -> dict:
+    """Negated descent, zeros for non-manifest leaves (``_optimizer.py:299-326``)."""
+    out: dict = {}
+    for path, v in _leaves(_materialize_tree(params)):
+        if isinstance(v, torch.Tensor):
+            d = tree_get(descent, path)
+            tree_set(out, path, -d if isinstance(d, torch.Tensor) else torch.zeros_like(v))
+        else:
+            tree_set(out, path, v)
+    return out

@@ -1,0 +1,124 @@
+"""Optimizer transforms with optax's update rules, fused on the device.
+
+The reference hands the negated replay output to an Optax transform
+(``src/zerograd/_optimizer.py:233-234``).  Optax is third-party code absent
+from the reference tree; ``adamw`` and ``sgd`` here restate optax 0.2.8's
+``adamw`` (scale_by_adam -> add_decayed_weights -> scale(-lr)) and ``sgd``
+(scale(-lr), no momentum) and run as one fused kernel per leaf that also
+applies the update.  Any object with optax's ``init`` / ``update`` protocol
+on torch tensors may be used instead (applied with :func:`apply_updates`).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from . import _ops
+
+
+def _leaves(tree, prefix=()):
+    for k, v in tree.items():
+        if isinstance(v, dict):
+            yield from _leaves(v, prefix + (k,))
+        else:
+            yield prefix + (k,), v
+
+
+def tree_get(tree, path):
+    node = tree
+    for p in path:
+        if not isinstance(node, dict) or p not in node:
+            return None
+        node = node[p]
+    return node
+
+
+def tree_set(tree, path, value):
+    node = tree
+    for p in path[:-1]:
+        node = node.setdefault(p, {})
+    node[path[-1]] = value
+
+
+@dataclass(frozen=True)
+class AdamWState:
+    count: int
+    mu: dict
+    nu: dict
+
+
+@dataclass(frozen=True)
+class adamw:
+    """``optax.adamw(learning_rate, b1, b2, eps, eps_root=0, weight_decay)``."""
+
+    learning_rate: float
+    b1: float = 0.9
+    b2: float = 0.999
+    eps: float = 1e-8
+    weight_decay: float = 1e-4
+
+    def init(self, params: dict) -> AdamWState:
+        mu, nu = {}, {}
+        for path, p in _leaves(params):
+            if isinstance(p, torch.Tensor):
+                tree_set(mu, path, torch.zeros(p.shape, dtype=torch.float32, device=p.device))
+                tree_set(nu, path, torch.zeros(p.shape, dtype=torch.float32, device=p.device))
+        return AdamWState(count=0, mu=mu, nu=nu)
+
+    def apply(self, params: dict, descent: dict, state: AdamWState):
+        """New params and state from the descent tree (missing leaf: zero gradient)."""
+        count = state.count + 1
+        new_p, mu, nu = {}, {}, {}
+        for path, p in _leaves(params):
+            if not isinstance(p, torch.Tensor):
+                tree_set(new_p, path, p)
+                continue
+            d = tree_get(descent, path)
+            pn, m, v = _ops.launch_adamw(p, d, tree_get(state.mu, path), tree_get(state.nu, path), count,
+                                         self.learning_rate, self.b1, self.b2, self.eps, self.weight_decay)
+            tree_set(new_p, path, pn)
+            tree_set(mu, path, m)
+            tree_set(nu, path, v)
+        return new_p, AdamWState(count=count, mu=mu, nu=nu)
+
+
+@dataclass(frozen=True)
+class SgdState:
+    count: int = 0
+
+
+@dataclass(frozen=True)
+class sgd:
+    """``optax.sgd(learning_rate)`` without momentum."""
+
+    learning_rate: float
+
+    def init(self, params: dict) -> SgdState:
+        return SgdState()
+
+    def apply(self, params: dict, descent: dict, state: SgdState):
+        new_p = {}
+        for path, p in _leaves(params):
+            if not isinstance(p, torch.Tensor):
+                tree_set(new_p, path, p)
+                continue
+            tree_set(new_p, path, _ops.launch_sgd(p, tree_get(descent, path), self.learning_rate))
+        return new_p, SgdState(count=state.count + 1)
+
+
+def apply_updates(params: dict, updates: dict) -> dict:
+    """``optax.apply_updates``: ``p + u`` cast back to the parameter dtype."""
+    out = {}
+    for path, p in _leaves(params):
+        u = tree_get(updates, path)
+        if isinstance(p, torch.Tensor) and u is not None:
+            tree_set(out, path, (p.to(torch.float32) + u).to(p.dtype))
+        else:
+            tree_set(out, path, p)
+    return out
+
+
+def is_fused(transform: Any) -> bool:
+    return isinstance(transform, (adamw, sgd))

@@ -1,0 +1,510 @@
+// zg_ops.cu -- population-batched forward ops, fitness shaping, replay and
+// fused optimizer updates (C ABI in include/zg_b200.h).
+//
+// Reference behaviour restated (paths relative to the reference root):
+//   perturbed_linear / table_lookup / tied_logits / vector
+//                                    src/zerograd/_candidate.py:17-45
+//   shape_centered_loss, validate_losses  src/zerograd/_fitness.py:13-48
+//   replay_entry                     src/zerograd/_replay.py:15-54
+//   _build_pseudo_grad + optax update + apply_updates
+//                                    src/zerograd/_optimizer.py:229-234,299-326
+#include <cmath>
+
+#include "zg_simt.cuh"
+#include "zg_tc.cuh"
+
+namespace zg {
+int launch_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
+                              int64_t cols, int rank, int dtype, void* A, void* B,
+                              cudaStream_t st);
+}
+
+namespace {
+
+using zg::Carver;
+using zg::SimtGemm;
+
+template <typename T, typename TO>
+int simt(const SimtGemm& g, cudaStream_t st, const char* name) {
+    return zg::launch_simt_gemm<T, TO>(g, st, name);
+}
+
+// ---------------------------------------------------------------------------
+// perturbed linear / tied logits share one plan:
+//   y[p] = x_p @ Wop + s * (x_p @ F1_p) @ F2_p
+// linear: Wop = W [K,N] (row-major), F1 = A_p [K,r], F2 = B_p [r,N]
+// tied:   Wop = T^T (T [V,C]),       F1 = B_p [C,r], F2 = A_p^T
+// ---------------------------------------------------------------------------
+struct LowRankPlan {
+    int P, M, K, N, rank, dtype, x_batched;
+    const void* x;
+    const void* Wop;
+    int64_t sWk, sWn;          // strides of Wop(k, n)
+    const void* F1;            // [P, K, r] contiguous: F1(k, j) at p*K*r + k*r + j
+    const void* F2;            // L(j, n) strides within a candidate
+    int64_t sF2b, sF2j, sF2n;
+    float s;
+    void* y;
+    float* U;                  // [P, M, r] f32 scratch
+    float* XW;                 // [M, N] f32 scratch (shared x only)
+};
+
+template <typename T>
+int run_low_rank(const LowRankPlan& q, cudaStream_t st) {
+    int rc;
+    // U[p] = x_p @ F1_p
+    {
+        SimtGemm g;
+        g.A = q.x; g.sAb = q.x_batched ? (int64_t)q.M * q.K : 0; g.sAm = q.K; g.sAko = 0; g.sAki = 1;
+        g.B = q.F1; g.sBb = (int64_t)q.K * q.rank; g.sBko = 0; g.sBki = q.rank; g.sBn = 1;
+        g.C = q.U; g.sCb = (int64_t)q.M * q.rank; g.sCm = q.rank; g.sCn = 1;
+        g.M = q.M; g.N = q.rank; g.Ko = 1; g.Ki = q.K; g.batch = q.P;
+        if ((rc = simt<T, float>(g, st, "lowrank_u"))) return rc;
+    }
+    SimtGemm g;
+    g.U = q.U; g.sUb = (int64_t)q.M * q.rank; g.sUm = q.rank; g.sUj = 1;
+    g.L = q.F2; g.sLb = q.sF2b; g.sLj = q.sF2j; g.sLn = q.sF2n;
+    g.rank = q.rank; g.lr_s = q.s;
+    g.C = q.y; g.sCb = (int64_t)q.M * q.N; g.sCm = q.N; g.sCn = 1;
+    g.M = q.M; g.N = q.N; g.batch = q.P;
+    if (!q.x_batched) {
+        // The shared product x @ Wop is computed once (as jax.vmap leaves an
+        // unbatched x @ W unbatched) and broadcast into every candidate.
+        if (!zg::tc_dense_gemm_f32out<T>(q.x, q.Wop, q.sWk, q.sWn, q.XW, q.M, q.K, q.N, st, &rc)) {
+            SimtGemm d;
+            d.A = q.x; d.sAm = q.K; d.sAki = 1;
+            d.B = q.Wop; d.sBki = q.sWk; d.sBn = q.sWn;
+            d.C = q.XW; d.sCm = q.N; d.sCn = 1;
+            d.M = q.M; d.N = q.N; d.Ko = 1; d.Ki = q.K; d.batch = 1;
+            rc = simt<T, float>(d, st, "shared_xw");
+        }
+        if (rc) return rc;
+        g.Cin = q.XW; g.sCinb = 0; g.sCinm = q.N; g.sCinn = 1;
+        g.Ko = 0; g.Ki = 0;
+    } else {
+        g.A = q.x; g.sAb = (int64_t)q.M * q.K; g.sAm = q.K; g.sAki = 1;
+        g.B = q.Wop; g.sBb = 0; g.sBki = q.sWk; g.sBn = q.sWn;
+        g.Ko = 1; g.Ki = q.K;
+    }
+    return simt<T, T>(g, st, q.x_batched ? "perturbed_gemm" : "lowrank_expand");
+}
+
+size_t low_rank_ws(int P, int M, int K, int N, int rank, int dtype, int x_batched, int64_t f1,
+                   int64_t f2) {
+    size_t es = zg::dtype_size(dtype);
+    return Carver::need({(size_t)P * f1 * es, (size_t)P * f2 * es, (size_t)P * M * rank * 4,
+                         x_batched ? 0 : (size_t)M * N * 4});
+}
+
+bool dims_ok(std::initializer_list<int64_t> v) {
+    for (int64_t d : v)
+        if (d < 1) return false;
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// table lookup: out[p,t,c] = T[row,c] + s * sum_j A_p[row,j] * B_p[c,j]
+// A rows regenerated in-kernel; B_p from the factor fill.  grid (n_idx, P).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void table_lookup_kernel(const T* __restrict__ table, const int32_t* __restrict__ idx,
+                                    int idx_batched, int64_t n_idx, const uint32_t* __restrict__ keys,
+                                    int group, int64_t rows, int64_t cols, int rank, float s,
+                                    const T* __restrict__ Bf, T* __restrict__ out) {
+    extern __shared__ float a_row[];
+    const int64_t t = blockIdx.x;
+    const int p = blockIdx.y;
+    int64_t row = idx[(idx_batched ? (int64_t)p * n_idx : 0) + t];
+    if (row < 0) row += rows;                    // numpy-style negative index
+    row = row < 0 ? 0 : (row >= rows ? rows - 1 : row);  // jnp gather clamps
+    if (threadIdx.x < rank) {
+        ZgFactorKeys fk = zg_factor_keys(keys, p, group);
+        a_row[threadIdx.x] = zg_dtype_round<T>(zg_normal(fk.a, (uint64_t)row * rank + threadIdx.x));
+    }
+    __syncthreads();
+    const T* bp = Bf + (int64_t)p * cols * rank;
+    T* o = out + ((int64_t)p * n_idx + t) * cols;
+    const T* trow = table + row * cols;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+        float lr = 0.f;
+        for (int j = 0; j < rank; ++j) lr = fmaf(a_row[j], zg_to_float(bp[c * rank + j]), lr);
+        o[c] = zg_from_float<T>(fmaf(s, lr, zg_to_float(trow[c])));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// vector: out[p,i] = v[i] + s * noise_p[i], with the reference's per-op
+// rounding to the leaf dtype (product, then sum).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void vector_kernel(const T* __restrict__ v, int v_batched, const uint32_t* __restrict__ keys,
+                              int group, int64_t n, float s, T* __restrict__ out) {
+    const int p = blockIdx.y;
+    ZgKey gk = zg_group_key(keys, p, group);
+    const T* vp = v + (v_batched ? (int64_t)p * n : 0);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float noise = zg_dtype_round<T>(zg_normal(gk, (uint64_t)i));
+        float prod = zg_dtype_round<T>(__fmul_rn(s, noise));
+        out[(int64_t)p * n + i] = zg_from_float<T>(__fadd_rn(zg_to_float(vp[i]), prod));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// fitness shaping + validation + metrics (one block)
+// ---------------------------------------------------------------------------
+__global__ void shape_fitness_kernel(const float* __restrict__ losses, int P, float denom,
+                                     float* __restrict__ shaped, float* __restrict__ metrics) {
+    __shared__ double s_sum[32];
+    __shared__ float s_min[32], s_max[32];
+    __shared__ int s_bad[32];
+    __shared__ float s_mean;
+    double sum = 0.0;
+    float mn = INFINITY, mx = -INFINITY;
+    int bad = 0;
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        float l = losses[i];
+        if (!isfinite(l)) ++bad;
+        sum += (double)l;
+        mn = fminf(mn, l);
+        mx = fmaxf(mx, l);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        bad += __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (lane == 0) { s_sum[w] = sum; s_min[w] = mn; s_max[w] = mx; s_bad[w] = bad; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double tsum = 0.0;
+        float tmn = INFINITY, tmx = -INFINITY;
+        int tbad = 0;
+        for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) {
+            tsum += s_sum[i]; tmn = fminf(tmn, s_min[i]); tmx = fmaxf(tmx, s_max[i]); tbad += s_bad[i];
+        }
+        float mean = (float)(tsum / (double)P);
+        s_mean = mean;
+        metrics[0] = mean; metrics[1] = tmn; metrics[2] = tmx; metrics[3] = (float)tbad;
+    }
+    __syncthreads();
+    const float mean = s_mean;
+    for (int i = threadIdx.x; i < P; i += blockDim.x)
+        shaped[i] = __fdiv_rn(-__fsub_rn(losses[i], mean), denom);
+}
+
+// ---------------------------------------------------------------------------
+// VECTOR replay: out[i] = sum_p w_p * noise_p[i] (noise regenerated).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void vector_replay_kernel(const float* __restrict__ w, const uint32_t* __restrict__ keys,
+                                     int group, int P, int64_t n, float* __restrict__ out) {
+    constexpr int CH = 1024;
+    __shared__ uint32_t sk[CH][2];
+    __shared__ float sw[CH];
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    float acc = 0.f;
+    for (int p0 = 0; p0 < P; p0 += CH) {
+        const int cnt = min(CH, P - p0);
+        for (int q = threadIdx.x; q < cnt; q += blockDim.x) {
+            ZgKey gk = zg_group_key(keys, p0 + q, group);
+            sk[q][0] = gk.k0; sk[q][1] = gk.k1;
+            sw[q] = w[p0 + q];
+        }
+        __syncthreads();
+        if (i < n) {
+            for (int q = 0; q < cnt; ++q) {
+                ZgKey gk = zg_make_key(sk[q][0], sk[q][1]);
+                float noise = zg_dtype_round<T>(zg_normal(gk, (uint64_t)i));
+                acc = fmaf(noise, sw[q], acc);
+            }
+        }
+        __syncthreads();
+    }
+    if (i < n) out[i] = acc;
+}
+
+// ---------------------------------------------------------------------------
+// fused optimizer updates
+// ---------------------------------------------------------------------------
+struct AdamConsts {
+    float omb1, b1, omb2, b2, bc1, bc2, eps, wd, neg_lr;
+};
+
+template <typename T>
+__global__ void adamw_kernel(const T* __restrict__ param, T* __restrict__ param_out,
+                             const float* __restrict__ descent, const float* __restrict__ mu,
+                             const float* __restrict__ nu, float* __restrict__ mu_out,
+                             float* __restrict__ nu_out, int64_t n, AdamConsts c) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float g = descent ? -descent[i] : 0.f;  // pseudo_grad = -descent
+        const float p = zg_to_float(param[i]);
+        const float m = __fadd_rn(__fmul_rn(c.omb1, g), __fmul_rn(c.b1, mu[i]));
+        const float v = __fadd_rn(__fmul_rn(c.omb2, __fmul_rn(g, g)), __fmul_rn(c.b2, nu[i]));
+        mu_out[i] = m;
+        nu_out[i] = v;
+        const float mh = __fdiv_rn(m, c.bc1);
+        const float vh = __fdiv_rn(v, c.bc2);
+        float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), c.eps));
+        u = __fadd_rn(u, __fmul_rn(c.wd, p));
+        u = __fmul_rn(u, c.neg_lr);
+        param_out[i] = zg_from_float<T>(__fadd_rn(p, u));
+    }
+}
+
+template <typename T>
+__global__ void sgd_kernel(const T* __restrict__ param, T* __restrict__ param_out,
+                           const float* __restrict__ descent, int64_t n, float neg_lr) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float g = descent ? -descent[i] : 0.f;
+        param_out[i] = zg_from_float<T>(__fadd_rn(zg_to_float(param[i]), __fmul_rn(g, neg_lr)));
+    }
+}
+
+int ew_grid(int64_t n) {
+    int64_t g = (n + 255) / 256;
+    return (int)(g < 148 * 8 ? (g < 1 ? 1 : g) : 148 * 8);
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+
+extern "C" size_t zg_perturbed_linear_workspace_size(int P, int M, int K, int N, int rank, int dtype,
+                                                     int x_batched) {
+    if (P < 1 || M < 1 || K < 1 || N < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
+    return low_rank_ws(P, M, K, N, rank, dtype, x_batched, (int64_t)K * rank, (int64_t)rank * N);
+}
+
+extern "C" int zg_perturbed_linear(const void* x, int x_batched, const void* W, const uint32_t* keys,
+                                   int group, int P, int M, int K, int N, int rank, float s, int dtype,
+                                   void* y, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dims_ok({P, M, K, N, rank}) || P > 65535)
+        return zg::fail(ZG_ERR_INVALID, "zg_perturbed_linear: bad sizes P=%d M=%d K=%d N=%d rank=%d", P, M, K, N, rank);
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_perturbed_linear: bad dtype");
+    if (!x || !W || !keys || !y) return zg::fail(ZG_ERR_INVALID, "zg_perturbed_linear: null pointer");
+    size_t need = zg_perturbed_linear_workspace_size(P, M, K, N, rank, dtype, x_batched);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_perturbed_linear: workspace %zu < %zu bytes", workspace_bytes, need);
+    cudaStream_t st = zg::as_stream(stream);
+    Carver cv(workspace, workspace_bytes);
+    size_t es = zg::dtype_size(dtype);
+    char* fa = cv.take<char>((size_t)P * K * rank * es);
+    char* fb = cv.take<char>((size_t)P * rank * N * es);
+    float* U = cv.take<float>((size_t)P * M * rank);
+    float* XW = x_batched ? nullptr : cv.take<float>((size_t)M * N);
+    int rc = zg::launch_population_factors(keys, group, P, ZG_MATRIX, K, N, rank, dtype, fa, fb, st);
+    if (rc) return rc;
+    LowRankPlan q{P, M, K, N, rank, dtype, x_batched, x, W, (int64_t)N, 1, fa, fb,
+                  (int64_t)rank * N, (int64_t)N, 1, s, y, U, XW};
+    return dtype == ZG_BF16 ? run_low_rank<__nv_bfloat16>(q, st) : run_low_rank<float>(q, st);
+}
+
+extern "C" size_t zg_tied_logits_workspace_size(int P, int M, int V, int C, int rank, int dtype,
+                                                int x_batched) {
+    if (P < 1 || M < 1 || V < 1 || C < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
+    return low_rank_ws(P, M, C, V, rank, dtype, x_batched, (int64_t)C * rank, (int64_t)V * rank);
+}
+
+extern "C" int zg_tied_logits(const void* x, int x_batched, const void* T, const uint32_t* keys, int group,
+                              int P, int M, int V, int C, int rank, float s, int dtype, void* y,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dims_ok({P, M, V, C, rank}) || P > 65535)
+        return zg::fail(ZG_ERR_INVALID, "zg_tied_logits: bad sizes");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_tied_logits: bad dtype");
+    if (!x || !T || !keys || !y) return zg::fail(ZG_ERR_INVALID, "zg_tied_logits: null pointer");
+    size_t need = zg_tied_logits_workspace_size(P, M, V, C, rank, dtype, x_batched);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_tied_logits: workspace %zu < %zu bytes", workspace_bytes, need);
+    cudaStream_t st = zg::as_stream(stream);
+    Carver cv(workspace, workspace_bytes);
+    size_t es = zg::dtype_size(dtype);
+    // table factors: A [P, V, r] (rows), B [P, C, r] (cols)
+    char* fb = cv.take<char>((size_t)P * C * rank * es);
+    char* fa = cv.take<char>((size_t)P * V * rank * es);
+    float* U = cv.take<float>((size_t)P * M * rank);
+    float* XW = x_batched ? nullptr : cv.take<float>((size_t)M * V);
+    int rc = zg::launch_population_factors(keys, group, P, ZG_TABLE, V, C, rank, dtype, fa, fb, st);
+    if (rc) return rc;
+    // Wop(k=c, n=v) = T[v*C + c];  F1 = B_p [C, r];  F2(j, v) = A_p[v*r + j]
+    LowRankPlan q{P, M, C, V, rank, dtype, x_batched, x, T, 1, (int64_t)C, fb, fa,
+                  (int64_t)V * rank, 1, (int64_t)rank, s, y, U, XW};
+    return dtype == ZG_BF16 ? run_low_rank<__nv_bfloat16>(q, st) : run_low_rank<float>(q, st);
+}
+
+extern "C" size_t zg_table_lookup_workspace_size(int P, int64_t rows, int64_t cols, int rank, int dtype) {
+    if (P < 1 || rows < 1 || cols < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
+    // B factors for every candidate; the A factor of the unused slot is tiny.
+    return Carver::need({(size_t)P * cols * rank * zg::dtype_size(dtype), 256});
+}
+
+extern "C" int zg_table_lookup(const void* T, const int32_t* idx, int idx_batched, int64_t n_idx,
+                               const uint32_t* keys, int group, int P, int64_t rows, int64_t cols,
+                               int rank, float s, int dtype, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1 || rank > 1024 || n_idx < 0 || n_idx > 2147483647)
+        return zg::fail(ZG_ERR_INVALID, "zg_table_lookup: bad sizes");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_table_lookup: bad dtype");
+    if (n_idx == 0) return ZG_OK;
+    if (!T || !idx || !keys || !out) return zg::fail(ZG_ERR_INVALID, "zg_table_lookup: null pointer");
+    size_t need = zg_table_lookup_workspace_size(P, rows, cols, rank, dtype);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_table_lookup: workspace %zu < %zu bytes", workspace_bytes, need);
+    cudaStream_t st = zg::as_stream(stream);
+    Carver cv(workspace, workspace_bytes);
+    char* fb = cv.take<char>((size_t)P * cols * rank * zg::dtype_size(dtype));
+    // Fill only B_p [cols, rank]; A rows are regenerated at the gathered
+    // rows inside the lookup kernel (rows = 0: no A elements are drawn).
+    int rc = zg::launch_population_factors(keys, group, P, ZG_TABLE, 0, cols, rank, dtype, nullptr, fb, st);
+    if (rc) return rc;
+    dim3 grid((unsigned)n_idx, P);
+    int threads = cols >= 256 ? 256 : (int)((cols + 31) / 32 * 32);
+    if (threads < rank) threads = (rank + 31) / 32 * 32;
+    size_t smem = rank * sizeof(float);
+    zg::LaunchTimer zg_lt_("table_lookup", st);
+    if (dtype == ZG_BF16)
+        table_lookup_kernel<__nv_bfloat16><<<grid, threads, smem, st>>>(
+            (const __nv_bfloat16*)T, idx, idx_batched, n_idx, keys, group, rows, cols, rank, s,
+            (const __nv_bfloat16*)fb, (__nv_bfloat16*)out);
+    else
+        table_lookup_kernel<float><<<grid, threads, smem, st>>>((const float*)T, idx, idx_batched, n_idx, keys,
+                                                                 group, rows, cols, rank, s, (const float*)fb,
+                                                                 (float*)out);
+    return zg::check_launch("zg_table_lookup");
+}
+
+extern "C" int zg_perturbed_vector(const void* v, int v_batched, const uint32_t* keys, int group, int P,
+                                   int64_t n, float s, int dtype, void* out, void* stream) {
+    if (P < 1 || P > 65535 || n < 1) return zg::fail(ZG_ERR_INVALID, "zg_perturbed_vector: bad sizes");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_perturbed_vector: bad dtype");
+    if (!v || !keys || !out) return zg::fail(ZG_ERR_INVALID, "zg_perturbed_vector: null pointer");
+    cudaStream_t st = zg::as_stream(stream);
+    int chunks = (int)((n + 255) / 256);
+    if (chunks > 1024) chunks = 1024;
+    dim3 grid(chunks, P);
+    zg::LaunchTimer zg_lt_("perturbed_vector", st);
+    if (dtype == ZG_BF16)
+        vector_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)v, v_batched, keys, group, n, s,
+                                                           (__nv_bfloat16*)out);
+    else
+        vector_kernel<float><<<grid, 256, 0, st>>>((const float*)v, v_batched, keys, group, n, s, (float*)out);
+    return zg::check_launch("zg_perturbed_vector");
+}
+
+extern "C" int zg_shape_fitness(const float* losses, int P, double sigma, float* shaped, float* metrics,
+                                void* stream) {
+    if (P < 2) return zg::fail(ZG_ERR_INVALID, "zg_shape_fitness: at least two candidate losses are required");
+    if (!(sigma > 0) || !std::isfinite(sigma)) return zg::fail(ZG_ERR_INVALID, "zg_shape_fitness: bad sigma");
+    if (!losses || !shaped || !metrics) return zg::fail(ZG_ERR_INVALID, "zg_shape_fitness: null pointer");
+    // population_size * sigma is a Python float (double) converted to the
+    // loss dtype at the division (src/zerograd/_fitness.py:34).
+    const float denom = (float)((double)P * sigma);
+    zg::LaunchTimer zg_lt_("shape_fitness", zg::as_stream(stream));
+    shape_fitness_kernel<<<1, 1024, 0, zg::as_stream(stream)>>>(losses, P, denom, shaped, metrics);
+    return zg::check_launch("zg_shape_fitness");
+}
+
+extern "C" size_t zg_replay_workspace_size(int P, int layout, int64_t rows, int64_t cols, int rank, int dtype) {
+    if (P < 1 || rows < 1 || !zg::dtype_ok(dtype)) return 0;
+    if (layout == ZG_VECTOR) return 256;
+    if (cols < 1 || rank < 1) return 0;
+    size_t es = zg::dtype_size(dtype);
+    return Carver::need({(size_t)P * rows * rank * es, (size_t)P * cols * rank * es}) +
+           zg::tc_replay_extra_workspace(P, layout, rows, cols, rank, dtype);
+}
+
+extern "C" int zg_replay(const float* shaped, const uint32_t* keys, int group, int P, int layout,
+                         int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, int dtype, float* out,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || (layout != ZG_VECTOR && (cols < 1 || rank < 1)))
+        return zg::fail(ZG_ERR_INVALID, "zg_replay: bad sizes");
+    if (layout < ZG_MATRIX || layout > ZG_VECTOR) return zg::fail(ZG_ERR_INVALID, "zg_replay: bad layout");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay: bad dtype");
+    if (!shaped || !keys || !out) return zg::fail(ZG_ERR_INVALID, "zg_replay: null pointer");
+    cudaStream_t st = zg::as_stream(stream);
+    if (layout == ZG_VECTOR) {
+        int blocks = (int)((rows + 255) / 256);
+        zg::LaunchTimer zg_lt_("replay_vector", st);
+        if (dtype == ZG_BF16)
+            vector_replay_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(shaped, keys, group, P, rows, out);
+        else
+            vector_replay_kernel<float><<<blocks, 256, 0, st>>>(shaped, keys, group, P, rows, out);
+        return zg::check_launch("zg_replay(vector)");
+    }
+    size_t need = zg_replay_workspace_size(P, layout, rows, cols, rank, dtype);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_replay: workspace %zu < %zu bytes", workspace_bytes, need);
+    Carver cv(workspace, workspace_bytes);
+    size_t es = zg::dtype_size(dtype);
+    char* fa = cv.take<char>((size_t)P * rows * rank * es);
+    char* fb = cv.take<char>((size_t)P * cols * rank * es);
+    int rc;
+    int tc_rc = 0;
+    if (zg::tc_replay(shaped, keys, group, P, layout, rows, cols, rank, inv_sqrt_rank, dtype, out, fa, fb,
+                      cv, st, &tc_rc))
+        return tc_rc;
+    rc = zg::launch_population_factors(keys, group, P, layout, rows, cols, rank, dtype, fa, fb, st);
+    if (rc) return rc;
+    SimtGemm g;
+    g.A = fa; g.sAm = rank; g.sAko = rows * (int64_t)rank; g.sAki = 1;
+    g.kscale = shaped;
+    g.B = fb;
+    if (layout == ZG_MATRIX) { g.sBko = (int64_t)rank * cols; g.sBki = cols; g.sBn = 1; }
+    else { g.sBko = cols * (int64_t)rank; g.sBki = 1; g.sBn = rank; }
+    g.C = out; g.sCm = cols; g.sCn = 1;
+    g.M = (int)rows; g.N = (int)cols; g.Ko = P; g.Ki = rank; g.batch = 1; g.alpha = inv_sqrt_rank;
+    if (rows > 2147483647 || cols > 2147483647) return zg::fail(ZG_ERR_INVALID, "zg_replay: dims too large");
+    return dtype == ZG_BF16 ? simt<__nv_bfloat16, float>(g, st, "replay_gemm") : simt<float, float>(g, st, "replay_gemm");
+}
+
+extern "C" int zg_adamw_update(const void* param, void* param_out, int dtype, const float* descent,
+                               const float* mu, const float* nu, float* mu_out, float* nu_out, int64_t n,
+                               int count, double lr, double b1, double b2, double eps, double weight_decay,
+                               void* stream) {
+    if (n < 0 || count < 1) return zg::fail(ZG_ERR_INVALID, "zg_adamw_update: bad sizes");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_adamw_update: bad dtype");
+    if (n == 0) return ZG_OK;
+    if (!param || !param_out || !mu || !nu || !mu_out || !nu_out)
+        return zg::fail(ZG_ERR_INVALID, "zg_adamw_update: null pointer");
+    // Constants as the traced float32 computation sees them: Python-float
+    // expressions rounded once to float32; bias corrections 1 - b^count in
+    // float32 (optax tree_bias_correction).
+    AdamConsts c;
+    c.omb1 = (float)(1.0 - b1); c.b1 = (float)b1;
+    c.omb2 = (float)(1.0 - b2); c.b2 = (float)b2;
+    c.bc1 = 1.0f - powf((float)b1, (float)count);
+    c.bc2 = 1.0f - powf((float)b2, (float)count);
+    c.eps = (float)eps; c.wd = (float)weight_decay; c.neg_lr = (float)(-lr);
+    cudaStream_t st = zg::as_stream(stream);
+    zg::LaunchTimer zg_lt_("adamw_update", st);
+    if (dtype == ZG_BF16)
+        adamw_kernel<__nv_bfloat16><<<ew_grid(n), 256, 0, st>>>((const __nv_bfloat16*)param, (__nv_bfloat16*)param_out,
+                                                                descent, mu, nu, mu_out, nu_out, n, c);
+    else
+        adamw_kernel<float><<<ew_grid(n), 256, 0, st>>>((const float*)param, (float*)param_out, descent, mu, nu,
+                                                        mu_out, nu_out, n, c);
+    return zg::check_launch("zg_adamw_update");
+}
+
+extern "C" int zg_sgd_update(const void* param, void* param_out, int dtype, const float* descent, int64_t n,
+                             double lr, void* stream) {
+    if (n < 0) return zg::fail(ZG_ERR_INVALID, "zg_sgd_update: bad sizes");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_sgd_update: bad dtype");
+    if (n == 0) return ZG_OK;
+    if (!param || !param_out) return zg::fail(ZG_ERR_INVALID, "zg_sgd_update: null pointer");
+    cudaStream_t st = zg::as_stream(stream);
+    zg::LaunchTimer zg_lt_("sgd_update", st);
+    if (dtype == ZG_BF16)
+        sgd_kernel<__nv_bfloat16><<<ew_grid(n), 256, 0, st>>>((const __nv_bfloat16*)param, (__nv_bfloat16*)param_out,
+                                                              descent, n, (float)(-lr));
+    else
+        sgd_kernel<float><<<ew_grid(n), 256, 0, st>>>((const float*)param, (float*)param_out, descent, n,
+                                                      (float)(-lr));
+    return zg::check_launch("zg_sgd_update");
+}
