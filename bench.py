@@ -43,8 +43,8 @@ WORKLOAD_NAME = ("batched perturbed GEMM + factor replay: P=256, rank=8, shared 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     return ap.parse_args()
 
@@ -61,55 +61,67 @@ def peaks():
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled through NVML every 5 ms
+    while the timed region runs (read-only queries)."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self, nv):
+        import torch
+
+        props = torch.cuda.get_device_properties(self.device)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        return nv.nvmlDeviceGetHandleByPciBusId(bus)
 
     def __enter__(self):
+        import threading
+
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for b, name in self.REASONS.items():
+                        if bits & b:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(2)
         return False
 
     def summary(self):
-        if not self.path or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------------------
@@ -121,12 +133,14 @@ def kernel_work(name: str, P_local: int):
         return "hbm", P_local * M * N * 2 + M * N * 4 + P_local * M * r * 4 + P_local * r * N * 2
     if name == "replay_gemm":         # [K, P r] x [P r, N]
         return "tensor", 2.0 * K * N * P * r
-    if name == "shared_xw":
+    if name in ("forward_xw_gemm", "shared_xw"):
         return "tensor", 2.0 * M * K * N
-    if name == "lowrank_u":
+    if name in ("forward_u_gemm", "lowrank_u"):
         return "tensor", 2.0 * P_local * M * K * r
-    if name == "factor_fill":         # bf16 factors written
-        return "hbm", (P + P_local) / 2 * r * (K + N) * 2
+    if name == "forward_factor_fill":  # bf16 operand written per launch (K = N here)
+        return "hbm", P_local * r * K * 2
+    if name == "replay_factor_fill":
+        return "hbm", P * r * K * 2
     if name == "sgd_update":          # read W bf16 + descent f32, write W bf16
         return "hbm", K * N * (2 + 4 + 2)
     return None, None
@@ -294,7 +308,7 @@ def run_ours(args):
 
     # timed (device-resident inputs)
     n0 = L.launch_count()
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         barrier()
         ms, W = timed(device_step, args.steps, W0)
         barrier()

@@ -61,6 +61,20 @@ ZG_API int zg_profile_begin(int max_records);
 ZG_API int zg_profile_end(void);
 ZG_API int zg_profile_summary(char* buf, size_t len);
 
+/* Error code recorded by a tensor-core kernel whose bounded wait expired
+ * (0 = none).  Synchronises the current device; `clear` resets it. */
+ZG_API int zg_device_error(int clear);
+
+/* Dense bf16 GEMM on the tcgen05 tensor cores, float32 accumulation:
+ *   D[M,N] = alpha * A[M,K] . B^T, A row-major [M,K] (lda);
+ *   B row-major [N,K] (b_mn_major = 0) or [K,N] (b_mn_major = 1) (ldb);
+ *   D row-major (ldd) in float32 (out_dtype ZG_F32) or bf16 (ZG_BF16).
+ * lda, ldb multiples of 8; A, B 16-byte aligned.  The contraction the
+ * reference expresses with jnp.einsum / @ (src/zerograd/_replay.py:47,51;
+ * src/zerograd/_candidate.py:22). */
+ZG_API int zg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn_major, void* D,
+                        int64_t ldd, int out_dtype, int M, int N, int K, float alpha, void* stream);
+
 /* ---------------------------------------------------------------- keys -- */
 
 /* Raw threefry2x32-20 blocks: out[i] = threefry(keys[i], ctrs[i]).

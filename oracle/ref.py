@@ -246,7 +246,19 @@ def perturbed_vector(v, gk, sigma, dtype="float32"):
 # --------------------------------------------------------------------------
 
 def shape_centered_loss(losses, sigma):
-    l = np.asarray(losses, np.float64)
+    """``-(l - mean(l)) / (P * sigma)`` in the loss dtype (``_fitness.py:33-34``).
+
+    For float32 losses every step is float32 as in the traced computation:
+    the mean rounded to float32 (here the correctly rounded mean), the
+    centring subtraction in float32, and P * sigma formed as a Python float
+    and rounded to float32 once at the division.
+    """
+    l = np.asarray(losses)
+    if l.dtype == np.float32:
+        mean = np.float32(l.astype(np.float64).mean())
+        centered = (l - mean).astype(np.float32)
+        return ((-centered) / np.float32(l.shape[0] * sigma)).astype(np.float32)
+    l = l.astype(np.float64)
     return -(l - l.mean()) / (l.shape[0] * sigma)
 
 

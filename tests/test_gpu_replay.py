@@ -74,4 +74,10 @@ def test_replay_larger_population(cuda, oracle, layout, shape, dtype):
     want = oracle.replay_entry(shape, layout, base, range(P), w, rank if layout != 2 else 1, 1,
                                "float32" if dtype == torch.float32 else "bfloat16")
     scale = np.abs(want).max()
-    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-5, atol=1e-5 * scale)
+    got = got.cpu().numpy()
+    if dtype == torch.float32:
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5 * scale)
+    else:
+        # bf16 leaves: the tensor-core replay rounds w_p * A_p to bf16 (rel 2^-9 per term)
+        assert np.abs(got - want).max() <= 2e-2 * scale
+        assert np.linalg.norm(got - want) <= 5e-3 * np.linalg.norm(want)

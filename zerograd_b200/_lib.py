@@ -28,6 +28,8 @@ SIGNATURES = {
     "zg_profile_begin": (_i32, [_i32]),
     "zg_profile_end": (_i32, []),
     "zg_profile_summary": (_i32, [_c.c_char_p, _sz]),
+    "zg_device_error": (_i32, [_i32]),
+    "zg_gemm_bf16": (_i32, [_vp, _i64, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i32, _f32, _vp]),
     "zg_threefry2x32": (_i32, [_vp, _vp, _vp, _i64, _vp]),
     "zg_fold_in": (_i32, [_vp, _i32, _vp, _vp, _i64, _vp]),
     "zg_candidate_keys": (_i32, [_c.c_uint32, _c.c_uint32, _vp, _vp, _i64, _vp]),

@@ -70,15 +70,12 @@ int run_low_rank(const LowRankPlan& q, cudaStream_t st) {
     if (!q.x_batched) {
         // The shared product x @ Wop is computed once (as jax.vmap leaves an
         // unbatched x @ W unbatched) and broadcast into every candidate.
-        if (!zg::tc_dense_gemm_f32out<T>(q.x, q.Wop, q.sWk, q.sWn, q.XW, q.M, q.K, q.N, st, &rc)) {
-            SimtGemm d;
-            d.A = q.x; d.sAm = q.K; d.sAki = 1;
-            d.B = q.Wop; d.sBki = q.sWk; d.sBn = q.sWn;
-            d.C = q.XW; d.sCm = q.N; d.sCn = 1;
-            d.M = q.M; d.N = q.N; d.Ko = 1; d.Ki = q.K; d.batch = 1;
-            rc = simt<T, float>(d, st, "shared_xw");
-        }
-        if (rc) return rc;
+        SimtGemm d;
+        d.A = q.x; d.sAm = q.K; d.sAki = 1;
+        d.B = q.Wop; d.sBki = q.sWk; d.sBn = q.sWn;
+        d.C = q.XW; d.sCm = q.N; d.sCn = 1;
+        d.M = q.M; d.N = q.N; d.Ko = 1; d.Ki = q.K; d.batch = 1;
+        if ((rc = simt<T, float>(d, st, "shared_xw"))) return rc;
         g.Cin = q.XW; g.sCinb = 0; g.sCinm = q.N; g.sCinn = 1;
         g.Ko = 0; g.Ki = 0;
     } else {
@@ -279,7 +276,9 @@ int ew_grid(int64_t n) {
 extern "C" size_t zg_perturbed_linear_workspace_size(int P, int M, int K, int N, int rank, int dtype,
                                                      int x_batched) {
     if (P < 1 || M < 1 || K < 1 || N < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
-    return low_rank_ws(P, M, K, N, rank, dtype, x_batched, (int64_t)K * rank, (int64_t)rank * N);
+    size_t simt_need = low_rank_ws(P, M, K, N, rank, dtype, x_batched, (int64_t)K * rank, (int64_t)rank * N);
+    size_t tc_need = (dtype == ZG_BF16 && !x_batched) ? zg::tc_shared_forward_workspace(P, M, K, N, rank) : 0;
+    return simt_need > tc_need ? simt_need : tc_need;
 }
 
 extern "C" int zg_perturbed_linear(const void* x, int x_batched, const void* W, const uint32_t* keys,
@@ -294,6 +293,10 @@ extern "C" int zg_perturbed_linear(const void* x, int x_batched, const void* W, 
         return zg::fail(ZG_ERR_WORKSPACE, "zg_perturbed_linear: workspace %zu < %zu bytes", workspace_bytes, need);
     cudaStream_t st = zg::as_stream(stream);
     Carver cv(workspace, workspace_bytes);
+    if (dtype == ZG_BF16 && !x_batched && zg::tc_shared_forward_ok(P, M, K, N, rank))
+        // W [K, N] row-major is the MN-major B operand of x @ W.
+        return zg::tc_shared_forward(x, W, true, N, keys, group, P, M, K, N, rank, /*f1: A, k*r+j*/ 0, 0,
+                                     /*f2: B, j*N+n*/ 1, 1, s, y, cv, st);
     size_t es = zg::dtype_size(dtype);
     char* fa = cv.take<char>((size_t)P * K * rank * es);
     char* fb = cv.take<char>((size_t)P * rank * N * es);
@@ -309,7 +312,9 @@ extern "C" int zg_perturbed_linear(const void* x, int x_batched, const void* W, 
 extern "C" size_t zg_tied_logits_workspace_size(int P, int M, int V, int C, int rank, int dtype,
                                                 int x_batched) {
     if (P < 1 || M < 1 || V < 1 || C < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
-    return low_rank_ws(P, M, C, V, rank, dtype, x_batched, (int64_t)C * rank, (int64_t)V * rank);
+    size_t simt_need = low_rank_ws(P, M, C, V, rank, dtype, x_batched, (int64_t)C * rank, (int64_t)V * rank);
+    size_t tc_need = (dtype == ZG_BF16 && !x_batched) ? zg::tc_shared_forward_workspace(P, M, C, V, rank) : 0;
+    return simt_need > tc_need ? simt_need : tc_need;
 }
 
 extern "C" int zg_tied_logits(const void* x, int x_batched, const void* T, const uint32_t* keys, int group,
@@ -324,6 +329,11 @@ extern "C" int zg_tied_logits(const void* x, int x_batched, const void* T, const
         return zg::fail(ZG_ERR_WORKSPACE, "zg_tied_logits: workspace %zu < %zu bytes", workspace_bytes, need);
     cudaStream_t st = zg::as_stream(stream);
     Carver cv(workspace, workspace_bytes);
+    if (dtype == ZG_BF16 && !x_batched && zg::tc_shared_forward_ok(P, M, C, V, rank))
+        // T [V, C] is the K-major B operand of x @ T^T; U = x @ B_t (B_t[c, j]:
+        // counter c*r + j), expanded through A_t[v, j] (counter v*r + j).
+        return zg::tc_shared_forward(x, T, false, C, keys, group, P, M, C, V, rank, /*f1: B*/ 1, 0,
+                                     /*f2: A*/ 0, 0, s, y, cv, st);
     size_t es = zg::dtype_size(dtype);
     // table factors: A [P, V, r] (rows), B [P, C, r] (cols)
     char* fb = cv.take<char>((size_t)P * C * rank * es);
@@ -415,8 +425,9 @@ extern "C" size_t zg_replay_workspace_size(int P, int layout, int64_t rows, int6
     if (layout == ZG_VECTOR) return 256;
     if (cols < 1 || rank < 1) return 0;
     size_t es = zg::dtype_size(dtype);
-    return Carver::need({(size_t)P * rows * rank * es, (size_t)P * cols * rank * es}) +
-           zg::tc_replay_extra_workspace(P, layout, rows, cols, rank, dtype);
+    size_t simt_need = Carver::need({(size_t)P * rows * rank * es, (size_t)P * cols * rank * es});
+    size_t tc_need = dtype == ZG_BF16 ? zg::tc_replay_workspace(P, rows, cols, rank) : 0;
+    return simt_need > tc_need ? simt_need : tc_need;
 }
 
 extern "C" int zg_replay(const float* shaped, const uint32_t* keys, int group, int P, int layout,
@@ -441,15 +452,12 @@ extern "C" int zg_replay(const float* shaped, const uint32_t* keys, int group, i
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "zg_replay: workspace %zu < %zu bytes", workspace_bytes, need);
     Carver cv(workspace, workspace_bytes);
+    if (zg::tc_replay_ok(P, rows, cols, rank, dtype))
+        return zg::tc_replay_run(shaped, keys, group, P, layout, rows, cols, rank, inv_sqrt_rank, out, cv, st);
     size_t es = zg::dtype_size(dtype);
     char* fa = cv.take<char>((size_t)P * rows * rank * es);
     char* fb = cv.take<char>((size_t)P * cols * rank * es);
-    int rc;
-    int tc_rc = 0;
-    if (zg::tc_replay(shaped, keys, group, P, layout, rows, cols, rank, inv_sqrt_rank, dtype, out, fa, fb,
-                      cv, st, &tc_rc))
-        return tc_rc;
-    rc = zg::launch_population_factors(keys, group, P, layout, rows, cols, rank, dtype, fa, fb, st);
+    int rc = zg::launch_population_factors(keys, group, P, layout, rows, cols, rank, dtype, fa, fb, st);
     if (rc) return rc;
     SimtGemm g;
     g.A = fa; g.sAm = rank; g.sAko = rows * (int64_t)rank; g.sAki = 1;

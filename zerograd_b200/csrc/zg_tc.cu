@@ -1,24 +1,444 @@
-// zg_tc.cu -- tensor-core paths (placeholder hooks: the CUDA-core path
-// handles every shape until the tcgen05 kernels are enabled).
+// zg_tc.cu -- tensor-core GEMM for sm_100a: tcgen05.mma (kind::f16, bf16 in,
+// float32 accumulate in TMEM), operands staged by TMA (no multicast) into a
+// 4-stage shared-memory ring, persistent CTAs with two TMEM accumulators so
+// the epilogue of one tile overlaps the main loop of the next.
+//
+//   D[M,N] = alpha * A[M,K] . B^T           (A K-major, row-major [M, K])
+//   B is K-major ([N, K] row-major) or MN-major ([K, N] row-major).
+//   D row-major float32 or bf16.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator +
+// MMA issuer, warps 2..5 = epilogue (TMEM -> registers -> global).  Every
+// mbarrier wait is bounded: on expiry the kernel records an error code in
+// g_zg_tc_error, drains its own TMA copies, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "zg_tc.cuh"
 
 namespace zg {
+int launch_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
+                              int64_t cols, int rank, int dtype, void* A, void* B,
+                              cudaStream_t st);
+}
 
-template <typename T>
-bool tc_dense_gemm_f32out(const void*, const void*, int64_t, int64_t, float*, int, int, int, cudaStream_t,
-                          int*) {
+__device__ unsigned int g_zg_tc_error = 0;
+
+namespace {
+
+constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false (and the error flag set) when the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023) == 1023 && *(volatile unsigned*)&g_zg_tc_error) return false;
+    }
+    atomicCAS(&g_zg_tc_error, 0u, code);
     return false;
 }
-template bool tc_dense_gemm_f32out<float>(const void*, const void*, int64_t, int64_t, float*, int, int, int,
-                                          cudaStream_t, int*);
-template bool tc_dense_gemm_f32out<__nv_bfloat16>(const void*, const void*, int64_t, int64_t, float*, int, int,
-                                                  int, cudaStream_t, int*);
 
-size_t tc_replay_extra_workspace(int, int, int64_t, int64_t, int, int) { return 0; }
+__device__ __forceinline__ bool aborted() { return *(volatile unsigned*)&g_zg_tc_error != 0; }
 
-bool tc_replay(const float*, const uint32_t*, int, int, int, int64_t, int64_t, int, float, int, float*, void*,
-               void*, Carver&, cudaStream_t, int*) {
-    return false;
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(tm), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit words: thread i gets lane (base + i), 32 columns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (sm_100 layout): start >> 4 in [0,14),
+// leading byte offset >> 4 in [16,30), stride byte offset >> 4 in [32,46),
+// version 1 in [46,48), layout type SWIZZLE_128B (2) in [61,64).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B bf16, A K-major,
+// B K-major (b_mn = 0) or MN-major (b_mn = 1), N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+struct TcArgs {
+    void* D;
+    int64_t ldd;
+    int M, N, K;
+    float alpha;
+    int out_bf16;
+    int tiles_m, tiles_n;
+};
+
+template <int BN, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs args) {
+    constexpr uint32_t A_BYTES = BM * BK * 2;
+    constexpr uint32_t B_BYTES = BN * BK * 2;
+    constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {64,128,256}
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tmem_full[2], tmem_empty[2], mma_done;
+    __shared__ uint32_t tmem_base_sh;
+
+    // 1024-byte alignment of the operand ring in the shared window (swizzle atoms)
+    const uint32_t dyn_base = smem_u32(dyn_smem);
+    uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int num_tiles = args.tiles_m * args.tiles_n;
+    const int k_blocks = (args.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 4);  // one arrive per epilogue warp
+        }
+        mbar_init(&mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t issued = 0;  // bit s: stage s has an issued load
+        uint32_t issue_parity = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1, 1)) { ok = false; break; }
+                uint8_t* sa = smem + stage * STAGE_BYTES;
+                uint8_t* sb = sa + A_BYTES;
+                mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
+                tma_load_2d(sa, &tmA, &full_bar[stage], kb * BK, tm * BM);
+                if constexpr (B_MN) {
+#pragma unroll
+                    for (int c = 0; c < BN / 64; ++c)
+                        tma_load_2d(sb + c * (64 * BK * 2), &tmB, &full_bar[stage], tn * BN + c * 64, kb * BK);
+                } else {
+                    tma_load_2d(sb, &tmB, &full_bar[stage], kb * BK, tn * BN);
+                }
+                issued |= 1u << stage;
+                issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
+        }
+        // Drain: every issued copy has landed before the CTA may exit.
+        for (int s = 0; s < STAGES; ++s)
+            if (issued & (1u << s)) {
+                for (uint32_t i = 0; i < kSpinLimit; ++i)
+                    if (mbar_try_wait(&full_bar[s], (issue_parity >> s) & 1)) break;
+            }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t IDESC = idesc_bf16(BM, BN, B_MN ? 1 : 0);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+            if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, 2)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * BN;
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                if (!mbar_wait(&full_bar[stage], phase, 3)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+                const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) {
+                    // K-major SW128: 16 bf16 of K = 32 bytes along the swizzled row.
+                    const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024);
+                    uint64_t bd;
+                    if constexpr (B_MN) {
+                        // MN-major SW128: 64-wide N blocks 8 KiB apart (LBO), 8-row K groups 1 KiB apart
+                        // (SBO); 16 K rows = 2 KiB per step.
+                        bd = smem_desc(b_addr + k * 2048, 64 * BK * 2, 1024);
+                    } else {
+                        bd = smem_desc(b_addr + k * 32, 16, 1024);
+                    }
+                    umma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit(&empty_bar[stage]);  // frees the smem stage once these MMAs complete
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
+            if (!ok) break;
+            umma_commit(&tmem_full[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+        // No MMA may still be writing TMEM when it is freed.
+        umma_commit(&mma_done);
+        for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(&mma_done, 0)) break;
+    } else if (warp >= 2) {
+        // ---------------- epilogue ----------------
+        const int quad = warp % 4;  // TMEM lanes 32*quad .. 32*quad+31
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            if (!mbar_wait(&tmem_full[acc], acc_phase, 4)) break;
+            tc_fence_after();
+            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            const int row = tm * BM + quad * 32 + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, v);
+                const int col0 = tn * BN + c0;
+                if (row < args.M) {
+                    if (args.out_bf16) {
+                        __nv_bfloat16* d = static_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd + col0;
+                        if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                __nv_bfloat162 h[4];
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    h[j] = __floats2bfloat162_rn(args.alpha * v[i + 2 * j], args.alpha * v[i + 2 * j + 1]);
+                                *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
+                            }
+                        } else {
+                            for (int i = 0; i < 32; ++i)
+                                if (col0 + i < args.N) d[i] = __float2bfloat16_rn(args.alpha * v[i]);
+                        }
+                    } else {
+                        float* d = static_cast<float*>(args.D) + (int64_t)row * args.ldd + col0;
+                        if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4)
+                                *reinterpret_cast<float4*>(d + i) =
+                                    make_float4(args.alpha * v[i], args.alpha * v[i + 1], args.alpha * v[i + 2],
+                                                args.alpha * v[i + 3]);
+                        } else {
+                            for (int i = 0; i < 32; ++i)
+                                if (col0 + i < args.N) d[i] = args.alpha * v[i];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows, inner] with leading
+// dimension `ld` elements; box {box_inner, box_rows}, 128-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_inner,
+              uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int BN, bool B_MN>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& a, cudaStream_t st, const char* name) {
+    constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return zg::fail(ZG_ERR_CUDA, "tc_gemm: shared memory attribute");
+    int tiles = a.tiles_m * a.tiles_n;
+    int grid = tiles < num_sms() ? tiles : num_sms();
+    zg::LaunchTimer zg_lt_(name, st);
+    tc_gemm_kernel<BN, B_MN><<<grid, THREADS, smem, st>>>(ta, tb, a);
+    return zg::check_launch("tc_gemm");
+}
+
+}  // namespace
+
+namespace zg {
+
+bool tc_available() {
+    static int ok = -1;
+    if (ok < 0) {
+        int dev = 0, major = 0, minor = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        ok = (major == 10 && minor == 0 && encode_fn() != nullptr) ? 1 : 0;
+    }
+    return ok == 1;
+}
+
+int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
+                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name) {
+    if (M <= 0 || N <= 0 || K <= 0) return fail(ZG_ERR_INVALID, "tc_gemm: empty problem");
+    if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+        return fail(ZG_ERR_INVALID, "tc_gemm: operands need 16-byte aligned rows");
+    // Tile width: the widest N tile that still gives every SM work.
+    int bn = 256;
+    auto tiles = [&](int b) { return ((M + BM - 1) / BM) * ((N + b - 1) / b); };
+    if (tiles(256) < num_sms()) bn = 128;
+    if (bn == 128 && tiles(128) < num_sms()) bn = 64;
+    if (b_mn_major && bn < 64) bn = 64;
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A, K, M, lda, BK, BM)) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map A");
+    bool okb = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
+    if (!okb) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
+    TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + BM - 1) / BM, (N + bn - 1) / bn};
+    if (b_mn_major) {
+        if (bn == 256) return launch_tc<256, true>(ta, tb, a, st, name);
+        if (bn == 128) return launch_tc<128, true>(ta, tb, a, st, name);
+        return launch_tc<64, true>(ta, tb, a, st, name);
+    }
+    if (bn == 256) return launch_tc<256, false>(ta, tb, a, st, name);
+    if (bn == 128) return launch_tc<128, false>(ta, tb, a, st, name);
+    return launch_tc<64, false>(ta, tb, a, st, name);
 }
 
 }  // namespace zg
+
+extern "C" int zg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn_major, void* D,
+                            int64_t ldd, int out_dtype, int M, int N, int K, float alpha, void* stream) {
+    if (!A || !B || !D) return zg::fail(ZG_ERR_INVALID, "zg_gemm_bf16: null pointer");
+    if (M < 1 || N < 1 || K < 1) return zg::fail(ZG_ERR_INVALID, "zg_gemm_bf16: bad sizes");
+    if (!zg::dtype_ok(out_dtype)) return zg::fail(ZG_ERR_INVALID, "zg_gemm_bf16: bad output dtype");
+    if (!zg::tc_available()) return zg::fail(ZG_ERR_UNSUPPORTED, "zg_gemm_bf16: needs an sm_100 device");
+    return zg::tc_gemm_bf16(A, lda, B, ldb, b_mn_major != 0, D, ldd, out_dtype == ZG_BF16, M, N, K, alpha,
+                            zg::as_stream(stream));
+}
+
+extern "C" int zg_device_error(int clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_zg_tc_error, sizeof(v)) != cudaSuccess) return -1;
+    if (clear && v) {
+        unsigned z = 0;
+        cudaMemcpyToSymbol(g_zg_tc_error, &z, sizeof(z));
+    }
+    return (int)v;
+}

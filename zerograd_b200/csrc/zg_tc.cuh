@@ -1,28 +1,40 @@
 // zg_tc.cuh -- tensor-core (tcgen05 / TMEM / TMA) paths for sm_100a.
-//
-// Each hook returns true when it handled the call (writing its status to
-// *rc), false when the shape/dtype is outside what the tensor-core kernel
-// covers, in which case the caller uses the CUDA-core path.
 #pragma once
 #include "zg_common.cuh"
 
 namespace zg {
 
-struct Carver;
+// True on a compute-capability 10.0 device with the TMA descriptor encoder.
+bool tc_available();
 
-// C[M,N] (float32, row-major) = x[M,K] (row-major) @ Wop where Wop(k,n) is
-// at W[k*sWk + n*sWn].
-template <typename T>
-bool tc_dense_gemm_f32out(const void* x, const void* W, int64_t sWk, int64_t sWn, float* C, int M,
-                          int K, int N, cudaStream_t st, int* rc);
+// D[M,N] = alpha * A[M,K] . B^T; A K-major row-major (lda), B K-major
+// [N,K] (ldb) or MN-major [K,N] (ldb); D row-major float32 or bf16 (ldd).
+// Rows of A and B must be 16-byte aligned (lda, ldb multiples of 8).
+int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
+                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name = "gemm");
 
-// Extra workspace bytes the tensor-core replay needs beyond the factor
-// buffers (0 when it is not used for this shape).
-size_t tc_replay_extra_workspace(int P, int layout, int64_t rows, int64_t cols, int rank, int dtype);
+// Factor fill in GEMM-operand layout: out[row, p*r + j] =
+// scale_p * round_dtype(normal(key_p, ctr)), ctr = row*r + j (row-major) or
+// j*rows + row (col_major); which = 0 for the A factor key, 1 for B.
+int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows, int which, int col_major,
+                 const float* scale, float extra_scale, int dtype, void* out, cudaStream_t st,
+                 const char* name = "factor_fill");
 
-// Full replay of one MATRIX/TABLE entry on the tensor cores.
-bool tc_replay(const float* shaped, const uint32_t* keys, int group, int P, int layout, int64_t rows,
-               int64_t cols, int rank, float inv_sqrt_rank, int dtype, float* out, void* fa, void* fb,
-               Carver& cv, cudaStream_t st, int* rc);
+// y[p, m, n] = XW[m, n] + s * sum_j U[m, p*r + j] * Bq[n, p*r + j].
+int lowrank_expand(const float* XW, const float* U, const void* Bq, int P, int M, int N, int rank, float s,
+                   int dtype, void* y, cudaStream_t st);
+
+// Shared-input population forward on the tensor cores (bf16).
+bool tc_shared_forward_ok(int P, int M, int K, int N, int rank);
+size_t tc_shared_forward_workspace(int P, int M, int K, int N, int rank);
+int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const uint32_t* keys, int group,
+                      int P, int M, int K, int N, int rank, int f1_which, int f1_col_major, int f2_which,
+                      int f2_col_major, float s, void* y, Carver& cv, cudaStream_t st);
+
+// Replay of one MATRIX/TABLE entry as one GEMM over the P*r axis (bf16).
+bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype);
+size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank);
+int tc_replay_run(const float* shaped, const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols,
+                  int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
 
 }  // namespace zg
