@@ -256,10 +256,12 @@ def run_ours(args):
     total_steps = args.warmup + args.steps
 
     # per-generation candidate keys, derived up front (inputs resident)
-    keys = []
+    keys, bases = [], []
     for gen in range(total_steps):
         base = zg.step_key(WL["seed"], WL["run_id"], gen, manifest.version)
-        keys.append(_ops.launch_fold_in(base, ids_all))
+        bases.append(tuple(int(v) for v in base))
+        cks = _ops.launch_fold_in(base, ids_all)
+        keys.append((cks, cks[a:b]))
 
     def gather(local_losses):
         if world == 1:
@@ -267,11 +269,17 @@ def run_ours(args):
         return zg.allgather_losses(local_losses, sizes)
 
     def device_step(W, gen):
-        cks = keys[gen]
-        y = _ops.launch_linear(x, W, cks[a:b], 0, r, sigma, False)
+        # the same sequence ZeroGrad.step runs: forward (factors kept for the
+        # generation), fitness exchange, shaping, replay (cached factors when
+        # this rank drew the whole population), update
+        cks, cks_local = keys[gen]
+        with _ops.generation_scope(bases[gen], a, P_local, cks_local):
+            y = _ops.launch_linear(x, W, cks_local, 0, r, sigma, False)
         losses = gather(fitness[a:b])
         shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
-        d = _ops.launch_replay(shaped, cks, 0, L.ZG_MATRIX, (K, N), r, torch.bfloat16)
+        d = _ops.launch_replay(shaped, cks, 0, L.ZG_MATRIX, (K, N), r, torch.bfloat16,
+                               gen=_ops._Generation(bases[gen], 0, P, cks))
+        _ops.CACHE.drop_generation(bases[gen])
         W = _ops.launch_sgd(W, d, WL["lr"])
         del y
         return W
@@ -327,7 +335,7 @@ def run_ours(args):
     opt = zg.ZeroGrad(manifest, zg.sgd(WL["lr"]), P, r, sigma, WL["seed"], WL["run_id"])
     params = {"w": W0}
     state = opt.init(params)
-    ids_local = torch.arange(a, b, dtype=torch.int32, device=dev)
+    ids_local = range(a, b)  # host-side ids: the public API keeps this range's factors for the replay
 
     def fwd(p, ctx, batch, rng):
         return ctx.linear(p, ("w",), batch), None

@@ -115,6 +115,41 @@ ZG_API int zg_normal(const uint32_t* keys, int64_t nkeys, int64_t n, int dtype, 
 ZG_API int zg_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
                           int64_t cols, int rank, int dtype, void* A, void* B, void* stream);
 
+/* Population factors of one MATRIX/TABLE entry in GEMM-operand layout,
+ * q = P * rank columns, column p*rank + j = candidate p, rank index j:
+ *   A_op[rows, q] = A_p[row, j]                       (counter row*rank + j)
+ *   B_op[cols, q] = MATRIX B_p[j, col] (counter j*cols + col) /
+ *                   TABLE  B_p[col, j] (counter col*rank + j)
+ * Either output may be NULL.  The same two buffers feed the forward pass
+ * (zg_forward_factors) and the replay (zg_replay_factors) of one
+ * generation, so each factor element is drawn once.  Replaces the
+ * matrix_factors / table_factors draws under jax.vmap
+ * (src/zerograd/_factors.py:43-67, src/zerograd/_replay.py:45,49). */
+ZG_API int zg_factor_operands(const uint32_t* keys, int group, int P, int layout, int64_t rows,
+                              int64_t cols, int rank, int dtype, void* A_op, void* B_op,
+                              void* stream);
+
+/* Shared-input population forward from operand factors (bf16, tcgen05):
+ *   y[p] = x @ Wop + s * (x @ F1_p) @ F2_p^T, x [M,K], F1 [K, P*rank],
+ *   F2 [N, P*rank], y [P, M, N].
+ * w_is_kn = 1: W is a linear weight [K, N] (F1 = A_op, F2 = B_op of its
+ * MATRIX entry); w_is_kn = 0: W is a tied table [N, K] (F1 = B_op,
+ * F2 = A_op of its TABLE entry).  Requires P*rank, K, N multiples of 8 and
+ * rank <= 32.  Replaces perturbed_linear / perturbed_tied_logits under
+ * jax.vmap (src/zerograd/_candidate.py:17-22,33-38). */
+ZG_API size_t zg_forward_factors_workspace_size(int P, int M, int N, int rank);
+ZG_API int zg_forward_factors(const void* x, const void* W, int w_is_kn, const void* F1,
+                              const void* F2, int P, int M, int K, int N, int rank, float s,
+                              void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replay from operand factors (bf16, tcgen05):
+ *   out[rows, cols] = inv_sqrt_rank * sum_q (w_{q/rank} A_op[:, q]) B_op[:, q]^T
+ * (float32).  Replaces replay_entry (src/zerograd/_replay.py:44-51). */
+ZG_API size_t zg_replay_factors_workspace_size(int P, int64_t rows, int rank);
+ZG_API int zg_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P,
+                             int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, float* out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------- forward ops -- */
 
 /* y[p] = x_p @ W + s * (x_p @ A_p) @ B_p for p in [0,P): one population-

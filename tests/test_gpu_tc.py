@@ -125,3 +125,48 @@ def test_table_replay_and_tied_logits_on_tensor_cores(cuda, oracle):
     want = oracle.replay_entry((V, C), oracle.TABLE, base, range(P), w, r, 1, "bfloat16")
     assert np.linalg.norm(got - want) <= 5e-3 * np.linalg.norm(want)
     assert L.load().zg_device_error(1) == 0
+
+
+def test_cached_factors_give_identical_results(cuda):
+    """ZeroGrad.step reuses the forward pass's factors in the replay; the
+    result is bit-identical to evaluating without the cache and replaying
+    from freshly drawn factors."""
+    import zerograd_b200 as zg
+
+    P, r, B, K, N = 32, 8, 64, 256, 128
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w"),
+                               zg.ManifestEntry(("t",), zg.ParameterLayout.TABLE, "t")))
+    g = torch.Generator().manual_seed(9)
+    params = {"w": (torch.randn(K, N, generator=g) * 0.05).to(torch.bfloat16).to(cuda),
+              "t": (torch.randn(200, N, generator=g) * 0.05).to(torch.bfloat16).to(cuda)}
+    x = (torch.randn(B, K, generator=g).to(torch.bfloat16).to(cuda), torch.randn(B, N, generator=g).to(torch.bfloat16).to(cuda))
+
+    def loss_fn(p, ctx, batch, rng):
+        h = ctx.linear(p, ("w",), batch[0])          # shared input: tensor-core path, factors cached
+        logits = ctx.tied_logits(p, ("t",), batch[1])
+        return (h.float() ** 2).mean() + (logits.float() ** 2).mean(), None
+
+    opt = zg.ZeroGrad(manifest, zg.sgd(0.1), P, r, 0.02, 0, "cache")
+    state = opt.init(params)
+    _ops.CACHE.clear()
+    h0 = _ops.CACHE.hits
+    a, _, ma = opt.step(state, params, x, loss_fn)
+    assert _ops.CACHE.hits - h0 == 2  # both entries replayed from the forward's factors
+    assert not _ops.CACHE._entries  # dropped after the update
+    losses = opt.evaluate_shard(params, 0, loss_fn, x, torch.arange(P, device=cuda))  # device ids: no cache
+    b, _, mb = opt.step_from_losses(state, params, losses)
+    for k in params:
+        assert torch.equal(a[k], b[k]), k
+    assert ma == mb
+
+
+def test_replay_factors_entry_matches_replay(cuda, oracle):
+    P, r, K, N = 64, 8, 512, 384
+    cks = _u32(oracle.candidate_keys(oracle.step_key(2, "rf", 0, 1), range(P)), cuda)
+    w = torch.randn(P, generator=torch.Generator().manual_seed(2)).to(cuda)
+    direct = _ops.launch_replay(w, cks, 1, L.ZG_MATRIX, (K, N), r, torch.bfloat16)
+    gen = _ops._Generation((7, 7), 0, P, cks)
+    A, B = _ops.operand_factors(cks, 1, L.ZG_MATRIX, K, N, r, gen)
+    cached = _ops.launch_replay(w, cks, 1, L.ZG_MATRIX, (K, N), r, torch.bfloat16, gen=gen)
+    _ops.CACHE.drop_generation((7, 7))
+    assert torch.equal(direct, cached)

@@ -133,6 +133,129 @@ def launch_factors(keys: torch.Tensor, group: int, layout: int, shape, rank: int
     return A, B
 
 
+# ---------------------------------------------------------------------------
+# generation-scoped factor cache
+# ---------------------------------------------------------------------------
+
+
+class _Generation:
+    """The candidate keys of one generation being evaluated by ZeroGrad."""
+
+    def __init__(self, base: tuple, start: int, count: int, cks: torch.Tensor):
+        self.base, self.start, self.count, self.cks = base, start, count, cks
+
+
+class FactorCache:
+    """Operand-layout factors drawn during a generation's forward pass, kept
+    (within a byte budget) for that generation's replay, so every factor
+    element is drawn once per generation.  Entries are a pure function of
+    (base key, candidate ids, group, layout, shape, rank), so reuse is exact.
+    """
+
+    def __init__(self, budget_bytes: int | None = None):
+        self.budget_bytes = budget_bytes
+        self._entries: dict = {}
+        self._bytes = 0
+        self.hits = 0
+        self.misses = 0
+        self._active: _Generation | None = None
+
+    def _budget(self, device) -> int:
+        if self.budget_bytes is None:
+            free, total = torch.cuda.mem_get_info(device)
+            self.budget_bytes = int(min(0.5 * free, 0.25 * total))
+        return self.budget_bytes
+
+    def active_for(self, keys: torch.Tensor) -> _Generation | None:
+        g = self._active
+        if g is not None and keys.data_ptr() == g.cks.data_ptr() and keys.shape[0] == g.count:
+            return g
+        return None
+
+    def get(self, key):
+        hit = self._entries.get(key)
+        if hit is not None:
+            self._entries[key] = self._entries.pop(key)  # most recent last
+            self.hits += 1
+        else:
+            self.misses += 1
+        return hit
+
+    def put(self, key, value, device) -> None:
+        nbytes = sum(t.numel() * t.element_size() for t in value)
+        budget = self._budget(device)
+        while self._entries and self._bytes + nbytes > budget:
+            _, old = self._entries.pop(next(iter(self._entries)))
+            self._bytes -= sum(t.numel() * t.element_size() for t in old)
+        if nbytes <= budget:
+            self._entries[key] = value
+            self._bytes += nbytes
+
+    def drop_generation(self, base: tuple) -> None:
+        for key in [k for k in self._entries if k[0] == base]:
+            old = self._entries.pop(key)
+            self._bytes -= sum(t.numel() * t.element_size() for t in old)
+
+    def clear(self) -> None:
+        self._entries.clear()
+        self._bytes = 0
+
+
+CACHE = FactorCache()
+
+
+class generation_scope:
+    """Context manager marking `cks` as the keys of candidates start..start+count
+    of the generation with base key words `base` (used by ZeroGrad)."""
+
+    def __init__(self, base: tuple, start: int, count: int, cks: torch.Tensor, cache: FactorCache = CACHE):
+        self.gen = _Generation(base, start, count, cks)
+        self.cache = cache
+
+    def __enter__(self):
+        self._prev = self.cache._active
+        self.cache._active = self.gen
+        return self.gen
+
+    def __exit__(self, *exc):
+        self.cache._active = self._prev
+        return False
+
+
+def _tc_ok(dev: torch.device, P: int, K: int, N: int, rank: int) -> bool:
+    return (torch.cuda.get_device_capability(dev) == (10, 0) and (P * rank) % 8 == 0 and K % 8 == 0
+            and N % 8 == 0 and rank <= 32)
+
+
+def operand_factors(keys: torch.Tensor, group: int, layout: int, rows: int, cols: int, rank: int,
+                    gen: _Generation | None = None, cache: FactorCache = CACHE):
+    """(A_op [rows, P r], B_op [cols, P r]) bf16, from the cache when the keys are
+    a generation's candidate keys."""
+    dev = keys.device
+    k = _keys2d(keys)
+    P = k.shape[0]
+    ckey = None
+    if gen is not None and group >= 0:
+        ckey = (gen.base, gen.start, gen.count, group, layout, rows, cols, rank)
+        hit = cache.get(ckey)
+        if hit is not None:
+            return hit
+    A = torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev)
+    B = torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev)
+    L.call("zg_factor_operands", L.ptr(k), group, P, layout, rows, cols, rank, L.ZG_BF16, L.ptr(A), L.ptr(B),
+           L.stream_ptr(dev))
+    if ckey is not None:
+        cache.put(ckey, (A, B), dev)
+    return A, B
+
+
+def _forward_factors(x, W, w_is_kn: bool, F1, F2, P, M, K, N, rank, s, y):
+    dev = x.device
+    ws = L.workspace(L.query("zg_forward_factors_workspace_size", P, M, N, rank), dev)
+    L.call("zg_forward_factors", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(F1), L.ptr(F2), P, M, K, N, rank, s,
+           L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+
+
 def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
                   sigma: float, x_batched: bool) -> torch.Tensor:
     """y[p] = x_p @ W + s (x_p @ A_p) @ B_p; x [*M, K] shared or [P, *M, K]."""
@@ -154,6 +277,11 @@ def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, gro
         return y
     s = scaled_factor_value(rank, sigma, weight.dtype)
     code = L.dtype_code(dt)
+    gen = CACHE.active_for(keys)
+    if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, K, N, rank):
+        A_op, B_op = operand_factors(keys, group, L.ZG_MATRIX, K, N, rank, gen)
+        _forward_factors(x, W, True, A_op, B_op, P, M, K, N, rank, s, y)
+        return y
     ws = L.workspace(L.query("zg_perturbed_linear_workspace_size", P, M, K, N, rank, code, int(x_batched)), dev)
     L.call("zg_perturbed_linear", L.ptr(x), int(x_batched), L.ptr(W), L.ptr(k), group, P, M, K, N, rank, s,
            code, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
@@ -178,6 +306,11 @@ def launch_tied_logits(x: torch.Tensor, table: torch.Tensor, keys: torch.Tensor,
         return y
     s = scaled_factor_value(rank, sigma, table.dtype)
     code = L.dtype_code(dt)
+    gen = CACHE.active_for(keys)
+    if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, C, V, rank):
+        A_op, B_op = operand_factors(keys, group, L.ZG_TABLE, V, C, rank, gen)  # A_t [V, q], B_t [C, q]
+        _forward_factors(x, T, False, B_op, A_op, P, M, C, V, rank, s, y)
+        return y
     ws = L.workspace(L.query("zg_tied_logits_workspace_size", P, M, V, C, rank, code, int(x_batched)), dev)
     L.call("zg_tied_logits", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, P, M, V, C, rank, s, code,
            L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
@@ -238,8 +371,13 @@ def launch_shape_fitness(losses: torch.Tensor, sigma: float):
 
 
 def launch_replay(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, layout: int, shape, rank: int,
-                  dtype: torch.dtype, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Descent direction [*shape] float32 of one entry (``_replay.py:15-54``)."""
+                  dtype: torch.dtype, out: torch.Tensor | None = None, gen: _Generation | None = None,
+                  cache: FactorCache = CACHE) -> torch.Tensor:
+    """Descent direction [*shape] float32 of one entry (``_replay.py:15-54``).
+
+    With `gen` (the generation whose full population the keys are), factors
+    its forward pass left in the cache are reused instead of redrawn.
+    """
     dev = L.require_cuda(shaped, cand_keys)
     k = _keys2d(cand_keys)
     P = k.shape[0]
@@ -253,6 +391,14 @@ def launch_replay(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, lay
     if out is None:
         out = torch.empty(tuple(int(d) for d in shape), dtype=torch.float32, device=dev)
     inv = scaled_factor_value(r, 1.0, dtype)
+    if gen is not None and layout != L.ZG_VECTOR and dtype == torch.bfloat16 and group >= 0:
+        hit = cache.get((gen.base, gen.start, gen.count, group, layout, rows, cols, r))
+        if hit is not None:
+            A_op, B_op = hit
+            ws = L.workspace(L.query("zg_replay_factors_workspace_size", P, rows, r), dev)
+            L.call("zg_replay_factors", L.ptr(w), L.ptr(A_op), L.ptr(B_op), P, rows, cols, r, inv, L.ptr(out),
+                   L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+            return out
     ws = L.workspace(L.query("zg_replay_workspace_size", P, layout, rows, cols, r, code), dev)
     L.call("zg_replay", L.ptr(w), L.ptr(k), group, P, layout, rows, cols, r, inv, code, L.ptr(out), L.ptr(ws),
            ws.numel(), L.stream_ptr(dev))

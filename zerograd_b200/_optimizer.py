@@ -127,14 +127,17 @@ class ZeroGrad:
         params = _materialize_tree(params)
         return self._evaluate_shard(params, generation, loss_fn, batch, candidate_ids, rng=rng)
 
-    def _evaluate_shard(self, params, generation, loss_fn, batch, candidate_ids, *, rng=None):
+    def _evaluate_shard(self, params, generation, loss_fn, batch, candidate_ids, *, rng=None, id_range=None):
         device = _device_of(params)
+        if id_range is None:
+            id_range = _host_range(candidate_ids)
         ids = torch.as_tensor(candidate_ids, device=device)
         if ids.ndim != 1:
             raise ValueError("candidate_ids must be one-dimensional")
         if rng is None:
             rng = make_key(0)
-        cks = candidate_keys(self.base_key(generation), ids)
+        base = self.base_key(generation)
+        cks = candidate_keys(base, ids)
         rngs = _ops.launch_fold_in(rng.reshape(1, 2), ids)
         manifest, rank, sigma = self._manifest, self._rank, self._sigma
 
@@ -145,7 +148,12 @@ class ZeroGrad:
 
         if ids.numel() == 0:
             return torch.empty(0, dtype=torch.float32, device=device)
-        return torch.func.vmap(evaluate_candidate)(cks, rngs)
+        if id_range is None:
+            return torch.func.vmap(evaluate_candidate)(cks, rngs)
+        # A contiguous id range known on the host: the factors drawn by the
+        # forward ops are kept for this generation's replay.
+        with _ops.generation_scope(tuple(int(v) for v in base), id_range[0], id_range[1], cks):
+            return torch.func.vmap(evaluate_candidate)(cks, rngs)
 
     # -- completion ---------------------------------------------------------
 
@@ -168,13 +176,17 @@ class ZeroGrad:
         losses = losses.to(device)
         generation = state.generation
         shaped, metrics = _ops.launch_shape_fitness(losses, self._sigma)
+        base = self.base_key(generation)
+        base_words = tuple(int(v) for v in base)
         if cand_keys is None:
             ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
-            cand_keys = candidate_keys(self.base_key(generation), ids)
+            cand_keys = candidate_keys(base, ids)
+        gen = _ops._Generation(base_words, 0, self._population_size, cand_keys)
         descent: dict = {}
         for entry in self._manifest.entries:
             tree_set(descent, entry.path,
-                     replay_entry_keys(params, self._manifest, entry.path, cand_keys, shaped, self._rank))
+                     replay_entry_keys(params, self._manifest, entry.path, cand_keys, shaped, self._rank, gen))
+        _ops.CACHE.drop_generation(base_words)
         if is_fused(self._transform):
             new_params, new_opt_state = self._transform.apply(params, descent, state.opt_state)
         else:
@@ -200,8 +212,29 @@ class ZeroGrad:
         params = _materialize_tree(params)
         device = _device_of(params)
         ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
-        losses = self._evaluate_shard(params, state.generation, loss_fn, batch, ids, rng=rng)
+        losses = self._evaluate_shard(params, state.generation, loss_fn, batch, ids, rng=rng,
+                                      id_range=(0, self._population_size))
         return self._step_from_losses(state, params, losses)
+
+
+def _host_range(candidate_ids):
+    """(start, count) when the ids are a contiguous ascending range known on
+    the host (a range, a list or a CPU tensor); None otherwise (reading a
+    device tensor would cost a synchronisation)."""
+    if isinstance(candidate_ids, range):
+        vals = candidate_ids
+    elif isinstance(candidate_ids, (list, tuple)):
+        vals = candidate_ids
+    elif isinstance(candidate_ids, torch.Tensor) and not candidate_ids.is_cuda and candidate_ids.ndim == 1:
+        vals = candidate_ids.tolist()
+    else:
+        return None
+    if len(vals) == 0:
+        return None
+    start = int(vals[0])
+    if any(int(v) != start + i for i, v in enumerate(vals)):
+        return None
+    return start, len(vals)
 
 
 def _materialize_tree(params: ParameterTree) -> dict:

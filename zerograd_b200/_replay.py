@@ -20,15 +20,19 @@ def candidate_keys(base_key: torch.Tensor, candidate_ids: torch.Tensor) -> torch
 
 
 def replay_entry_keys(params: ParameterTree, manifest: Manifest, path: ParameterPath, cand_keys: torch.Tensor,
-                      shaped_weights: torch.Tensor, rank: int) -> torch.Tensor:
-    """Descent direction of one entry (float32) from precomputed candidate keys."""
+                      shaped_weights: torch.Tensor, rank: int, gen=None) -> torch.Tensor:
+    """Descent direction of one entry (float32) from precomputed candidate keys.
+
+    `gen` names the generation whose whole population `cand_keys` are; its
+    forward-pass factors are then reused from the factor cache.
+    """
     entry = manifest.entry(path)
     parameter = manifest.resolve(params, path)
     layout = LAYOUT_CODE[entry.layout]
     group = manifest.group_index(entry.group)
     r = 1 if entry.layout is ParameterLayout.VECTOR else rank
     return _ops.launch_replay(shaped_weights, cand_keys, group, layout, tuple(parameter.shape), r,
-                              parameter.dtype)
+                              parameter.dtype, gen=gen)
 
 
 def replay_entry(params: ParameterTree, manifest: Manifest, path: ParameterPath, base_key: torch.Tensor,

@@ -159,7 +159,6 @@ __device__ __forceinline__ float zg_normal_from_bits(uint32_t bits) {
 __device__ __forceinline__ float zg_normal(const ZgKey& k, uint64_t j) {
     return zg_normal_from_bits(zg_bits(k, j));
 }
-
 // Storage helpers: the factor value of a bf16 leaf is the float32 draw cast
 // to bf16 (src/zerograd/_factors.py:48-55).
 template <typename T>

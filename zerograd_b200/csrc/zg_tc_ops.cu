@@ -78,71 +78,93 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
     }
 }
 
-// bf16 operand, r a multiple of 8 and <= EX_QC, N a multiple of 8.
-__global__ void __launch_bounds__(256)
+// Packed float32 pair FMA (sm_100): d = a * b + c on two lanes at once.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long A = *reinterpret_cast<unsigned long long*>(&a), B = *reinterpret_cast<unsigned long long*>(&b),
+                       C = *reinterpret_cast<unsigned long long*>(&c), D;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D) : "l"(A), "l"(B), "l"(C));
+    return *reinterpret_cast<float2*>(&D);
+}
+
+// bf16 factors and output, compile-time rank R (8 or 16), N % 8 == 0.
+// The factor chunk is converted to float32 once while it is staged, so the
+// inner loop is shared-memory loads and packed FMAs only.
+template <int R>
+__global__ void __launch_bounds__(256, 2)
 lowrank_expand_bf16_kernel(const float* __restrict__ XW, const float* __restrict__ U,
-                           const __nv_bfloat16* __restrict__ Bq, int P, int M, int N, int rank, float s,
-                           int p_per_split, __nv_bfloat16* __restrict__ y) {
-    __shared__ float Us[EX_BM][EX_QC + 1];
-    __shared__ __align__(16) __nv_bfloat16 Bs[EX_QC][EX_BN];  // [q][n]
+                           const __nv_bfloat16* __restrict__ Bq, int P, int M, int N, float s, int p_per_split,
+                           __nv_bfloat16* __restrict__ y) {
+    constexpr int QC = 32;         // q columns per chunk
+    constexpr int PC = QC / R;     // candidates per chunk
+    __shared__ __align__(16) float Us[EX_BM][QC + 4];
+    __shared__ __align__(16) float Bs[QC][EX_BN + 4];
     const int tid = threadIdx.x;
     const int tm = tid / 16, tn = tid % 16;
     const int m0 = blockIdx.y * EX_BM, n0 = blockIdx.x * EX_BN;
-    const int64_t ldq = (int64_t)P * rank;
-    const int pc = EX_QC / rank;  // candidates per chunk
-    const int qc = pc * rank;
-    float xw[4][8];
+    const int64_t ldq = (int64_t)P * R;
+    float2 xw[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int m = m0 + tm * 4 + i;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int n = n0 + tn * 8 + c;
-            xw[i][c] = (m < M && n < N) ? XW[(int64_t)m * N + n] : 0.f;
+        for (int c = 0; c < 4; ++c) {
+            const int n = n0 + tn * 8 + 2 * c;
+            xw[i][c] = (m < M && n < N) ? *reinterpret_cast<const float2*>(XW + (int64_t)m * N + n)
+                                        : make_float2(0.f, 0.f);
         }
     }
+    const float2 s2 = make_float2(s, s);
     const int pb = blockIdx.z * p_per_split;
     const int pe = min(P, pb + p_per_split);
-    for (int p0 = pb; p0 < pe; p0 += pc) {
-        const int np = min(pc, pe - p0);
-        const int nq = np * rank;
-        const int64_t q0 = (int64_t)p0 * rank;
+    for (int p0 = pb; p0 < pe; p0 += PC) {
+        const int np = min(PC, pe - p0);
+        const int nq = np * R;
+        const int64_t q0 = (int64_t)p0 * R;
         __syncthreads();
-        // U chunk: rows of U are contiguous in q (coalesced), smem rows padded.
-        for (int e = tid; e < EX_BM * qc; e += 256) {
-            const int mm = e / qc, qq = e % qc;
+        // U chunk [64 m x 32 q]: 16-byte loads along q, 2 per thread.
+#pragma unroll
+        for (int it = 0; it < (EX_BM * QC / 4) / 256; ++it) {
+            const int e = tid + it * 256;
+            const int mm = e / (QC / 4), c4 = e % (QC / 4);
             const int m = m0 + mm;
-            Us[mm][qq] = (m < M && qq < nq) ? U[(int64_t)m * ldq + q0 + qq] : 0.f;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m < M && c4 * 4 < nq) v = *reinterpret_cast<const float4*>(U + (int64_t)m * ldq + q0 + c4 * 4);
+            *reinterpret_cast<float4*>(&Us[mm][c4 * 4]) = v;
         }
-        // B chunk: one 16-byte load of 8 consecutive q per (n, q-group);
-        // consecutive threads take consecutive n so the transposed smem
-        // stores Bs[q][n] do not conflict.
-        for (int e = tid; e < EX_BN * (qc / 8); e += 256) {
+        // B chunk [128 n x 32 q] bf16 -> Bs[q][n] float32, consecutive threads on consecutive n.
+#pragma unroll
+        for (int it = 0; it < (EX_BN * QC / 8) / 256; ++it) {
+            const int e = tid + it * 256;
             const int nn = e % EX_BN, qg = e / EX_BN;
             const int n = n0 + nn;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (n < N && qg * 8 < nq) v = *reinterpret_cast<const uint4*>(Bq + (int64_t)n * ldq + q0 + qg * 8);
-            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+            float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (n < N && qg * 8 < nq)
+                bf16x8_to_f32(*reinterpret_cast<const uint4*>(Bq + (int64_t)n * ldq + q0 + qg * 8), f);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) Bs[qg * 8 + i][nn] = h[i];
+            for (int i = 0; i < 8; ++i) Bs[qg * 8 + i][nn] = f[i];
         }
         __syncthreads();
-        for (int pi = 0; pi < np; ++pi) {
-            float acc[4][8];
+#pragma unroll
+        for (int pi = 0; pi < PC; ++pi) {
+            if (pi >= np) break;
+            float2 acc[4][4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[i][c] = 0.f;
-#pragma unroll 4
-            for (int j = 0; j < rank; ++j) {
-                const int qq = pi * rank + j;
-                float bv[8];
-                bf16x8_to_f32(*reinterpret_cast<const uint4*>(&Bs[qq][tn * 8]), bv);
+                for (int c = 0; c < 4; ++c) acc[i][c] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < R; ++j) {
+                const int qq = pi * R + j;
+                const float4 bl = *reinterpret_cast<const float4*>(&Bs[qq][tn * 8]);
+                const float4 bh = *reinterpret_cast<const float4*>(&Bs[qq][tn * 8 + 4]);
+                const float2 b[4] = {make_float2(bl.x, bl.y), make_float2(bl.z, bl.w), make_float2(bh.x, bh.y),
+                                     make_float2(bh.z, bh.w)};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float u = Us[tm * 4 + i][qq];
+                    const float2 u2 = make_float2(u, u);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) acc[i][c] = fmaf(u, bv[c], acc[i][c]);
+                    for (int c = 0; c < 4; ++c) acc[i][c] = ffma2(u2, b[c], acc[i][c]);
                 }
             }
             const int p = p0 + pi;
@@ -153,9 +175,10 @@ lowrank_expand_bf16_kernel(const float* __restrict__ XW, const float* __restrict
                 if (m >= M || n >= N) continue;
                 __nv_bfloat162 h[4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    h[c] = __floats2bfloat162_rn(fmaf(s, acc[i][2 * c], xw[i][2 * c]),
-                                                 fmaf(s, acc[i][2 * c + 1], xw[i][2 * c + 1]));
+                for (int c = 0; c < 4; ++c) {
+                    const float2 o = ffma2(s2, acc[i][c], xw[i][c]);
+                    h[c] = __floats2bfloat162_rn(o.x, o.y);
+                }
                 *reinterpret_cast<uint4*>(y + ((int64_t)p * M + m) * N + n) = *reinterpret_cast<uint4*>(h);
             }
         }
@@ -297,10 +320,16 @@ int lowrank_expand(const float* XW, const float* U, const void* Bq, int P, int M
     dim3 grid(gx, gy, splits);
     zg::LaunchTimer zg_lt_("lowrank_expand", st);
     const int64_t ldq_bytes = (int64_t)P * rank * 2;
-    if (dtype == ZG_BF16 && rank % 8 == 0 && rank <= EX_QC && N % 8 == 0 && ldq_bytes % 16 == 0 &&
-        (reinterpret_cast<uintptr_t>(Bq) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
-        lowrank_expand_bf16_kernel<<<grid, 256, 0, st>>>(XW, U, static_cast<const __nv_bfloat16*>(Bq), P, M, N, rank,
-                                                         s, per, static_cast<__nv_bfloat16*>(y));
+    const bool fast = dtype == ZG_BF16 && (rank == 8 || rank == 16) && N % 8 == 0 && ldq_bytes % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(Bq) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(U) & 15) == 0 && (reinterpret_cast<uintptr_t>(XW) & 7) == 0;
+    if (fast) {
+        if (rank == 8)
+            lowrank_expand_bf16_kernel<8><<<grid, 256, 0, st>>>(XW, U, static_cast<const __nv_bfloat16*>(Bq), P, M, N,
+                                                                s, per, static_cast<__nv_bfloat16*>(y));
+        else
+            lowrank_expand_bf16_kernel<16><<<grid, 256, 0, st>>>(XW, U, static_cast<const __nv_bfloat16*>(Bq), P, M,
+                                                                 N, s, per, static_cast<__nv_bfloat16*>(y));
         return check_launch("lowrank_expand");
     }
     if (dtype == ZG_BF16)
@@ -312,17 +341,50 @@ int lowrank_expand(const float* XW, const float* U, const void* Bq, int P, int M
     return check_launch("lowrank_expand");
 }
 
-// Shared-x population forward on the tensor cores:
-//   y[p] = x @ Wop + s (x @ F1_p) @ F2_p^T
-// with F1 drawn as [K, P r] (row-major counter) and F2 as [N, P r]
-// (f2_col_major selects the counter order of the second factor).
-size_t tc_shared_forward_workspace(int P, int M, int K, int N, int rank) {
-    const size_t q = (size_t)P * rank;
-    return Carver::need({(size_t)K * q * 2, (size_t)N * q * 2, (size_t)M * q * 4, (size_t)M * N * 4});
+// ---------------------------------------------------------------------------
+// Operand factors of one entry: A_op[rows, P r] (A_p, counter row*r + j) and
+// B_op[cols, P r] (MATRIX: B_p[j, col], counter j*cols + col; TABLE:
+// B_p[col, j], counter col*r + j).  The forward pass and the replay of the
+// same generation use the same two buffers, so they are drawn once.
+// ---------------------------------------------------------------------------
+int factor_operands(const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols, int rank,
+                    int dtype, void* A_op, void* B_op, cudaStream_t st) {
+    int rc;
+    if (A_op && (rc = fill_operand(keys, group, P, rank, rows, 0, 0, nullptr, 1.f, dtype, A_op, st, "factor_fill")))
+        return rc;
+    if (B_op && (rc = fill_operand(keys, group, P, rank, cols, 1, layout == ZG_MATRIX ? 1 : 0, nullptr, 1.f, dtype,
+                                   B_op, st, "factor_fill")))
+        return rc;
+    return ZG_OK;
+}
+
+// Shared-x population forward on the tensor cores from operand factors:
+//   y[p] = x @ Wop + s (x @ F1_p) @ F2_p^T,  F1 [K, P r], F2 [N, P r].
+size_t tc_forward_factors_workspace(int P, int M, int N, int rank) {
+    return Carver::need({(size_t)M * P * rank * 4, (size_t)M * N * 4});
 }
 
 bool tc_shared_forward_ok(int P, int M, int K, int N, int rank) {
     return tc_available() && ((int64_t)P * rank) % 8 == 0 && K % 8 == 0 && N % 8 == 0 && rank <= 32 && M > 0;
+}
+
+int tc_forward_factors(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const void* F1, const void* F2,
+                       int P, int M, int K, int N, int rank, float s, void* y, Carver& cv, cudaStream_t st) {
+    const int64_t q = (int64_t)P * rank;
+    float* U = cv.take<float>((size_t)M * q);
+    float* XW = cv.take<float>((size_t)M * N);
+    if (!U || !XW) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
+    int rc;
+    // U[M, q] = x[M, K] . F1[K, q]   (F1 is MN-major for this product)
+    if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, false, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
+    if ((rc = tc_gemm_bf16(x, K, Wop, ldw, w_mn_major, XW, N, false, M, N, K, 1.f, st, "forward_xw_gemm")))
+        return rc;
+    return lowrank_expand(XW, U, F2, P, M, N, rank, s, ZG_BF16, y, st);
+}
+
+size_t tc_shared_forward_workspace(int P, int M, int K, int N, int rank) {
+    const size_t q = (size_t)P * rank;
+    return Carver::need({(size_t)K * q * 2, (size_t)N * q * 2}) + tc_forward_factors_workspace(P, M, N, rank) + 256;
 }
 
 int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const uint32_t* keys, int group,
@@ -331,26 +393,63 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
     const int64_t q = (int64_t)P * rank;
     __nv_bfloat16* F1 = cv.take<__nv_bfloat16>((size_t)K * q);
     __nv_bfloat16* F2 = cv.take<__nv_bfloat16>((size_t)N * q);
-    float* U = cv.take<float>((size_t)M * q);
-    float* XW = cv.take<float>((size_t)M * N);
-    if (!F1 || !F2 || !U || !XW) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
+    if (!F1 || !F2) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
     int rc;
     if ((rc = fill_operand(keys, group, P, rank, K, f1_which, f1_col_major, nullptr, 1.f, ZG_BF16, F1, st,
-                           "forward_factor_fill")))
+                           "factor_fill")))
         return rc;
     if ((rc = fill_operand(keys, group, P, rank, N, f2_which, f2_col_major, nullptr, 1.f, ZG_BF16, F2, st,
-                           "forward_factor_fill")))
+                           "factor_fill")))
         return rc;
-    // U[M, q] = x[M, K] . F1[K, q]   (F1 is MN-major for this product)
-    if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, false, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
-    if ((rc = tc_gemm_bf16(x, K, Wop, ldw, w_mn_major, XW, N, false, M, N, K, 1.f, st, "forward_xw_gemm")))
-        return rc;
-    return lowrank_expand(XW, U, F2, P, M, N, rank, s, ZG_BF16, y, st);
+    return tc_forward_factors(x, Wop, w_mn_major, ldw, F1, F2, P, M, K, N, rank, s, y, cv, st);
+}
+
+// Aw[row, q] = bf16(float(A[row, q]) * w[q / rank]): the reference's
+// weighted factor a_pop * shaped (src/zerograd/_replay.py:46) rounded to the
+// tensor-core operand type.
+__global__ void scale_operand_kernel(const __nv_bfloat16* __restrict__ A, const float* __restrict__ w, int rank,
+                                     int64_t q, int64_t total8, __nv_bfloat16* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e0 = i * 8;
+        const int64_t col0 = e0 % q;
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(A + e0), f);
+        uint4 pk;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            h[k] = __floats2bfloat162_rn(__fmul_rn(f[2 * k], w[(col0 + 2 * k) / rank]),
+                                         __fmul_rn(f[2 * k + 1], w[(col0 + 2 * k + 1) / rank]));
+        *reinterpret_cast<uint4*>(out + e0) = pk;
+    }
+}
+
+size_t tc_replay_factors_workspace(int P, int64_t rows, int rank) { return (size_t)rows * P * rank * 2 + 256; }
+
+int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
+                      int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st) {
+    const int64_t q = (int64_t)P * rank;
+    __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
+    if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
+    if (q % 8 || (reinterpret_cast<uintptr_t>(A_op) & 15)) return fail(ZG_ERR_INVALID, "tc replay: operand alignment");
+    const int64_t total8 = rows * q / 8;
+    int64_t blocks = (total8 + 255) / 256;
+    if (blocks > sm_count() * 16) blocks = sm_count() * 16;
+    {
+        zg::LaunchTimer zg_lt_("replay_scale", st);
+        scale_operand_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A_op), shaped, rank, q,
+                                                          total8, Aw);
+        int rc = check_launch("replay_scale");
+        if (rc) return rc;
+    }
+    return tc_gemm_bf16(Aw, q, B_op, q, false, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank, st,
+                        "replay_gemm");
 }
 
 size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank) {
     const size_t q = (size_t)P * rank;
-    return Carver::need({(size_t)rows * q * 2, (size_t)cols * q * 2});
+    return Carver::need({(size_t)rows * q * 2, (size_t)cols * q * 2}) + tc_replay_factors_workspace(P, rows, rank);
 }
 
 bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype) {
@@ -361,19 +460,68 @@ bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype) {
 int tc_replay_run(const float* shaped, const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols,
                   int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st) {
     const int64_t q = (int64_t)P * rank;
-    __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
-    __nv_bfloat16* Bq = cv.take<__nv_bfloat16>((size_t)cols * q);
-    if (!Aw || !Bq) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
-    int rc;
-    // weighted A: w_p * A_p[i, j] (the factor in the leaf dtype times the float32 weight)
-    if ((rc = fill_operand(keys, group, P, rank, rows, 0, 0, shaped, 1.f, ZG_BF16, Aw, st, "replay_factor_fill")))
-        return rc;
-    // B: MATRIX B_p[j, n] (counter j*cols + n), TABLE B_p[n, j] (counter n*r + j)
-    if ((rc = fill_operand(keys, group, P, rank, cols, 1, layout == ZG_MATRIX ? 1 : 0, nullptr, 1.f, ZG_BF16, Bq, st,
-                           "replay_factor_fill")))
-        return rc;
-    return tc_gemm_bf16(Aw, q, Bq, q, false, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank, st,
-                        "replay_gemm");
+    __nv_bfloat16* A_op = cv.take<__nv_bfloat16>((size_t)rows * q);
+    __nv_bfloat16* B_op = cv.take<__nv_bfloat16>((size_t)cols * q);
+    if (!A_op || !B_op) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
+    int rc = factor_operands(keys, group, P, layout, rows, cols, rank, ZG_BF16, A_op, B_op, st);
+    if (rc) return rc;
+    return tc_replay_factors(shaped, A_op, B_op, P, rows, cols, rank, inv_sqrt_rank, out, cv, st);
 }
 
 }  // namespace zg
+
+// ===========================================================================
+// C ABI: operand-layout factors, forward and replay from them
+// ===========================================================================
+
+extern "C" int zg_factor_operands(const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols,
+                                  int rank, int dtype, void* A_op, void* B_op, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1 || (layout != ZG_MATRIX && layout != ZG_TABLE))
+        return zg::fail(ZG_ERR_INVALID, "zg_factor_operands: bad sizes or layout");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_factor_operands: bad dtype");
+    if (!keys || (!A_op && !B_op)) return zg::fail(ZG_ERR_INVALID, "zg_factor_operands: null pointer");
+    return zg::factor_operands(keys, group, P, layout, rows, cols, rank, dtype, A_op, B_op, zg::as_stream(stream));
+}
+
+extern "C" size_t zg_forward_factors_workspace_size(int P, int M, int N, int rank) {
+    if (P < 1 || M < 1 || N < 1 || rank < 1) return 0;
+    return zg::tc_forward_factors_workspace(P, M, N, rank);
+}
+
+extern "C" int zg_forward_factors(const void* x, const void* W, int w_is_kn, const void* F1, const void* F2, int P,
+                                  int M, int K, int N, int rank, float s, void* y, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || M < 1 || K < 1 || N < 1 || rank < 1)
+        return zg::fail(ZG_ERR_INVALID, "zg_forward_factors: bad sizes");
+    if (!x || !W || !F1 || !F2 || !y) return zg::fail(ZG_ERR_INVALID, "zg_forward_factors: null pointer");
+    if (!zg::tc_shared_forward_ok(P, M, K, N, rank))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "zg_forward_factors: needs sm_100, P*rank, K, N multiples of 8, rank<=32");
+    size_t need = zg::tc_forward_factors_workspace(P, M, N, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_forward_factors: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    // W [K, N] (a linear weight) is the MN-major operand; T [N, K] (a tied table) the K-major one.
+    return zg::tc_forward_factors(x, W, w_is_kn != 0, w_is_kn ? N : K, F1, F2, P, M, K, N, rank, s, y, cv,
+                                  zg::as_stream(stream));
+}
+
+extern "C" size_t zg_replay_factors_workspace_size(int P, int64_t rows, int rank) {
+    if (P < 1 || rows < 1 || rank < 1) return 0;
+    return zg::tc_replay_factors_workspace(P, rows, rank);
+}
+
+extern "C" int zg_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows,
+                                 int64_t cols, int rank, float inv_sqrt_rank, float* out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1)
+        return zg::fail(ZG_ERR_INVALID, "zg_replay_factors: bad sizes");
+    if (!shaped || !A_op || !B_op || !out) return zg::fail(ZG_ERR_INVALID, "zg_replay_factors: null pointer");
+    if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "zg_replay_factors: needs sm_100 and P*rank a multiple of 8");
+    size_t need = zg::tc_replay_factors_workspace(P, rows, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_replay_factors: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::tc_replay_factors(shaped, A_op, B_op, P, rows, cols, rank, inv_sqrt_rank, out, cv,
+                                 zg::as_stream(stream));
+}
