@@ -131,7 +131,11 @@ class ZeroGrad:
         device = _device_of(params)
         if id_range is None:
             id_range = _host_range(candidate_ids)
-        ids = torch.as_tensor(candidate_ids, device=device)
+        if id_range is not None and not isinstance(candidate_ids, torch.Tensor):
+            # built on the device: a host-built id tensor would need a copy that synchronises the stream
+            ids = torch.arange(id_range[0], id_range[0] + id_range[1], dtype=torch.int32, device=device)
+        else:
+            ids = torch.as_tensor(candidate_ids, device=device)
         if ids.ndim != 1:
             raise ValueError("candidate_ids must be one-dimensional")
         if rng is None:

@@ -324,6 +324,236 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------
+// Low-rank expansion on the tensor cores, rank 8:
+//   y[p, m, n] = bf16(XW[m, n] + s * (U_p . B_p^T)[m, n])
+// U [M, P*8] bf16 (x @ A_all), B [N, P*8] bf16 (B_nq), XW [M, N] float32.
+// One M=128 N=128 K=16 MMA per candidate (the upper 8 K of each operand
+// read a zero region through the descriptor's leading byte offset); XW sits
+// in TMEM next to two accumulators; the epilogue writes bf16 into a
+// 128B-swizzled shared tile that a TMA bulk store copies out, so the global
+// writes are full lines and the kernel is bound by HBM write bandwidth.
+// Work item = (m tile, n tile, candidate chunk); persistent CTAs.
+// ---------------------------------------------------------------------------
+constexpr int EX_STAGES = 4;
+constexpr uint32_t EX_OP = 128 * 16;                       // one operand tile: 128 rows x 8 bf16
+constexpr uint32_t EX_A = 0, EX_AZ = EX_STAGES * EX_OP;    // A data, A zero half
+constexpr uint32_t EX_B = 2 * EX_STAGES * EX_OP, EX_BZ = 3 * EX_STAGES * EX_OP;
+constexpr uint32_t EX_LBO = EX_STAGES * EX_OP;             // data -> zero half, same for every stage
+constexpr uint32_t EX_STG = 32768;                         // staging, 2 buffers x (2 x 16 KiB sub-tiles)
+constexpr uint32_t EX_STG_BYTES = 128 * 128 * 2;
+constexpr uint32_t EX_SMEM = EX_STG + 2 * EX_STG_BYTES;    // 96 KiB (+ alignment)
+
+struct ExpandArgs {
+    const float* XW;
+    int M, N, P;
+    float s;
+    int tiles_m, tiles_n, chunk, chunks;
+};
+
+__device__ __forceinline__ uint64_t smem_desc_noswizzle(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // version 1, layout type 0 (no swizzle)
+    return d;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+        "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]),
+        "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
+        "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tm),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
+__device__ __forceinline__ float2 ffma2_tc(float2 a, float2 b, float2 c) {
+    unsigned long long A = *reinterpret_cast<unsigned long long*>(&a), B = *reinterpret_cast<unsigned long long*>(&b),
+                       C = *reinterpret_cast<unsigned long long*>(&c), D;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D) : "l"(A), "l"(B), "l"(C));
+    return *reinterpret_cast<float2*>(&D);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmY, const ExpandArgs a) {
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ __align__(8) uint64_t full_bar[EX_STAGES], empty_bar[EX_STAGES], tmem_full[2], tmem_empty[2],
+        stg_full[2], stg_free[2], mma_done;
+    __shared__ uint32_t tmem_base_sh;
+    const uint32_t dyn_base = smem_u32(dyn_smem);
+    uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int items = a.tiles_m * a.tiles_n * a.chunks;
+
+    // zero halves of the K=16 operands (read through the descriptors' LBO)
+    for (uint32_t i = threadIdx.x; i < EX_LBO / 16; i += THREADS) {
+        reinterpret_cast<uint4*>(smem + EX_AZ)[i] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(smem + EX_BZ)[i] = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < EX_STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], 4);
+            mbar_init(&stg_full[b], 128);
+            mbar_init(&stg_free[b], 1);
+        }
+        mbar_init(&mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(&tmem_base_sh, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer: U_p and B_p tiles ----------------
+        int stage = 0;
+        uint32_t phase = 0, issued = 0, issue_parity = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < items; t += gridDim.x) {
+            const int chunk = t % a.chunks, tile = t / a.chunks;
+            const int m0 = (tile / a.tiles_n) * 128, n0 = (tile % a.tiles_n) * 128;
+            const int p1 = min(a.P, (chunk + 1) * a.chunk);
+            for (int p = chunk * a.chunk; p < p1; ++p) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1, 11)) { ok = false; break; }
+                mbar_expect_tx(&full_bar[stage], 2 * EX_OP);
+                tma_load_2d(smem + EX_A + stage * EX_OP, &tmU, &full_bar[stage], p * 8, m0);
+                tma_load_2d(smem + EX_B + stage * EX_OP, &tmB, &full_bar[stage], p * 8, n0);
+                issued |= 1u << stage;
+                issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == EX_STAGES) { stage = 0; phase ^= 1; }
+            }
+        }
+        for (int s = 0; s < EX_STAGES; ++s)
+            if (issued & (1u << s))
+                for (uint32_t i = 0; i < kSpinLimit; ++i)
+                    if (mbar_try_wait(&full_bar[s], (issue_parity >> s) & 1)) break;
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer: one K=16 MMA per candidate ----------------
+        constexpr uint32_t IDESC = idesc_bf16(128, 128, 0);
+        int stage = 0, acc = 0;
+        uint32_t phase = 0, acc_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < items; t += gridDim.x) {
+            const int chunk = t % a.chunks;
+            const int p1 = min(a.P, (chunk + 1) * a.chunk);
+            for (int p = chunk * a.chunk; p < p1; ++p) {
+                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, 12)) { ok = false; break; }
+                tc_fence_after();
+                if (!mbar_wait(&full_bar[stage], phase, 13)) { ok = false; break; }
+                tc_fence_after();
+                const uint64_t ad = smem_desc_noswizzle(smem_u32(smem + EX_A + stage * EX_OP), EX_LBO, 128);
+                const uint64_t bd = smem_desc_noswizzle(smem_u32(smem + EX_B + stage * EX_OP), EX_LBO, 128);
+                umma_bf16(tmem_base + acc * 128, ad, bd, IDESC, 0u);
+                umma_commit(&empty_bar[stage]);
+                umma_commit(&tmem_full[acc]);
+                if (++stage == EX_STAGES) { stage = 0; phase ^= 1; }
+                if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+            }
+        }
+        umma_commit(&mma_done);
+        for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(&mma_done, 0)) break;
+    } else if (warp >= 2) {
+        // ---------------- epilogue: TMEM -> bf16 -> swizzled smem -> TMA store ----------------
+        const int quad = warp % 4;
+        const int row = quad * 32 + lane;  // TMEM lane == tile row
+        const bool issuer = (warp == 2 && lane == 0);
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const uint32_t xw_cols = tmem_base + lane_addr + 256;
+        const float2 s2 = make_float2(a.s, a.s);
+        int acc = 0, c = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < items; t += gridDim.x) {
+            const int chunk = t % a.chunks, tile = t / a.chunks;
+            const int m0 = (tile / a.tiles_n) * 128, n0 = (tile % a.tiles_n) * 128;
+            const int m = m0 + row;
+            // this row of XW into TMEM columns 256..383 (each thread owns its lane)
+#pragma unroll 1
+            for (int c0 = 0; c0 < 128; c0 += 32) {
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    const int n = n0 + c0 + i;
+                    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (m < a.M && n + 3 < a.N) f = *reinterpret_cast<const float4*>(a.XW + (int64_t)m * a.N + n);
+                    v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+                }
+                tmem_st32(xw_cols + c0, v);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            const int p1 = min(a.P, (chunk + 1) * a.chunk);
+            for (int p = chunk * a.chunk; p < p1; ++p, ++c) {
+                const int sb = c & 1;
+                const uint32_t use = (uint32_t)(c >> 1);
+                if (!mbar_wait(&tmem_full[acc], acc_phase, 14)) { ok = false; break; }
+                tc_fence_after();
+                if (!mbar_wait(&stg_free[sb], (use & 1) ^ 1, 15)) { ok = false; break; }
+                uint8_t* stg = smem + EX_STG + sb * EX_STG_BYTES;
+#pragma unroll 1
+                for (int c0 = 0; c0 < 128; c0 += 32) {
+                    float v[32], w[32];
+                    tmem_ld32(tmem_base + lane_addr + acc * 128 + c0, v);
+                    tmem_ld32(xw_cols + c0, w);
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 o = ffma2_tc(s2, make_float2(v[2 * i], v[2 * i + 1]),
+                                                  make_float2(w[2 * i], w[2 * i + 1]));
+                        __nv_bfloat162 h = __floats2bfloat162_rn(o.x, o.y);
+                        pk[i] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                    // 128B swizzle: 16-byte chunk k of a 128-byte row lives at k ^ (row % 8)
+                    uint8_t* sub = stg + (c0 / 64) * (128 * 128) + row * 128;
+                    const int ch0 = (c0 % 64) / 8;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        *reinterpret_cast<uint4*>(sub + (((ch0 + k) ^ (row & 7)) * 16)) =
+                            make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&stg_full[sb]);
+                if (issuer) {
+                    if (!mbar_wait(&stg_full[sb], use & 1, 16)) { ok = false; break; }
+                    tma_store_3d(&tmY, stg, n0, m0, p);
+                    tma_store_3d(&tmY, stg + 128 * 128, n0 + 64, m0, p);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    // the store of the previous candidate has finished reading its buffer
+                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    if (c > 0) mbar_arrive(&stg_free[sb ^ 1]);
+                }
+            }
+        }
+        if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, 512);
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -353,6 +583,32 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+bool make_map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_inner,
+                 uint32_t box_rows, CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// y [P, M, N] bf16 as a 3-D map so a tile never crosses into the next candidate.
+bool make_map_y(CUtensorMap* m, void* base, uint64_t N, uint64_t M, uint64_t P) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {N, M, P};
+    cuuint64_t strides[2] = {N * 2, M * N * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int num_sms() {
@@ -419,6 +675,43 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
     if (bn == 256) return launch_tc<256, false>(ta, tb, a, st, name);
     if (bn == 128) return launch_tc<128, false>(ta, tb, a, st, name);
     return launch_tc<64, false>(ta, tb, a, st, name);
+}
+
+}  // namespace zg
+
+namespace zg {
+
+bool tc_expand_ok(int P, int M, int N, int rank, const void* XW, const void* U, const void* Bq, const void* y) {
+    auto al = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+    return tc_available() && rank == 8 && N % 8 == 0 && M > 0 && P > 0 && al(XW, 16) && al(U, 16) && al(Bq, 16) &&
+           al(y, 16);
+}
+
+int tc_expand_r8(const float* XW, const void* U, const void* Bq, int P, int M, int N, float s, void* y,
+                 cudaStream_t st) {
+    CUtensorMap tu, tb, ty;
+    const uint64_t q = (uint64_t)P * 8;
+    if (!make_map_2d(&tu, U, q, M, q, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&tb, Bq, q, N, q, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) || !make_map_y(&ty, y, N, M, P))
+        return fail(ZG_ERR_CUDA, "tc_expand: tensor maps");
+    ExpandArgs a{XW, M, N, P, s, (M + 127) / 128, (N + 127) / 128, 0, 0};
+    const int tiles = a.tiles_m * a.tiles_n;
+    int chunks = (num_sms() * 4 + tiles - 1) / tiles;
+    if (chunks > P) chunks = P;
+    if (chunks < 1) chunks = 1;
+    a.chunk = (P + chunks - 1) / chunks;
+    a.chunks = (P + a.chunk - 1) / a.chunk;
+    const int items = tiles * a.chunks;
+    const int grid = items < num_sms() ? items : num_sms();
+    // >112 KiB so a second CTA (and its 512 TMEM columns) never shares the SM;
+    // 160 KiB also keeps every address the operand descriptors can form
+    // (start + 15 * max(LBO, SBO) + 2 KiB) inside the allocation.
+    const size_t smem = 160 * 1024 + 1024;
+    if (cudaFuncSetAttribute(expand_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return fail(ZG_ERR_CUDA, "tc_expand: shared memory attribute");
+    zg::LaunchTimer zg_lt_("lowrank_expand", st);
+    expand_tc_kernel<<<grid, THREADS, smem, st>>>(tu, tb, ty, a);
+    return check_launch("tc_expand");
 }
 
 }  // namespace zg

@@ -21,6 +21,81 @@ namespace {
 // blockDim.x threads = consecutive candidates; each thread derives its
 // candidate's key once and walks rows, writing r contiguous values.
 // ---------------------------------------------------------------------------
+// Eight independent threefry blocks advanced round by round together, so
+// the eight dependency chains interleave (the rounds of one block are a
+// serial chain of dependent integer operations).
+__device__ __forceinline__ void zg_normal_x8(const ZgKey& k, const uint64_t (&ctr)[8], float (&out)[8]) {
+    uint32_t x0[8], x1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        x0[i] = (uint32_t)(ctr[i] >> 32) + k.k0;
+        x1[i] = (uint32_t)ctr[i] + k.k1;
+    }
+    const uint32_t ks[3] = {k.k0, k.k1, k.k2};
+    constexpr int R[8] = {13, 15, 26, 6, 17, 29, 16, 24};
+#pragma unroll
+    for (int g = 0; g < 5; ++g) {
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                x0[i] += x1[i];
+                x1[i] = __funnelshift_l(x1[i], x1[i], R[(g & 1) * 4 + rr]);
+                x1[i] ^= x0[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x0[i] += ks[(g + 1) % 3];
+            x1[i] += ks[(g + 2) % 3] + (uint32_t)(g + 1);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = zg_normal_from_bits(x0[i] ^ x1[i]);
+}
+
+// Rank a multiple of 8: eight normals per step, no per-element guards.
+template <typename T, int R>
+__global__ void fill_operand_r8_kernel(const uint32_t* __restrict__ keys, int group, int P, int64_t rows, int which,
+                                       int col_major, const float* __restrict__ scale, int rows_per_block,
+                                       T* __restrict__ out) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= P) return;
+    ZgFactorKeys fk = zg_factor_keys(keys, p, group);
+    const ZgKey k = which == 0 ? fk.a : fk.b;
+    const float sc = scale ? scale[p] : 1.f;
+    const int64_t ld = (int64_t)P * R;
+    const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+    const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
+    for (int64_t row = r0; row < r1; ++row) {
+        T* dst = out + row * ld + (int64_t)p * R;
+#pragma unroll
+        for (int j0 = 0; j0 < R; j0 += 8) {
+            uint64_t ctr[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                ctr[i] = col_major ? (uint64_t)(j0 + i) * rows + row : (uint64_t)row * R + j0 + i;
+            float v[8];
+            zg_normal_x8(k, ctr, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[i] = zg_dtype_round<T>(v[i]);
+                if (scale) v[i] = __fmul_rn(v[i], sc);
+            }
+            if constexpr (sizeof(T) == 2) {
+                uint4 pk;
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                *reinterpret_cast<uint4*>(dst + j0) = pk;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dst[j0 + i] = v[i];
+            }
+        }
+    }
+}
+
 template <typename T>
 __global__ void fill_operand_kernel(const uint32_t* __restrict__ keys, int group, int P, int rank, int64_t rows,
                                     int which, int col_major, const float* __restrict__ scale, float extra_scale,
@@ -294,11 +369,32 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
     int64_t want = (int64_t)sm_count() * 16 / pblocks;
     if (want < 1) want = 1;
     int rows_per_block = (int)((rows + want - 1) / want);
-    if (rows_per_block < 8) rows_per_block = 8;  // amortise the per-thread key derivation
+    if (rows_per_block < 4) rows_per_block = 4;  // amortise the per-thread key derivation
     const int64_t yblocks = (rows + rows_per_block - 1) / rows_per_block;
     if (yblocks > 65535) return fail(ZG_ERR_INVALID, "fill_operand: too many rows");
     dim3 grid(pblocks, (unsigned)yblocks);
     zg::LaunchTimer zg_lt_(name, st);
+    const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && extra_scale == 1.f;
+    if (aligned && (rank == 8 || rank == 16)) {
+        if (dtype == ZG_BF16) {
+            if (rank == 8)
+                fill_operand_r8_kernel<__nv_bfloat16, 8><<<grid, threads, 0, st>>>(
+                    keys, group, P, rows, which, col_major, scale, rows_per_block, static_cast<__nv_bfloat16*>(out));
+            else
+                fill_operand_r8_kernel<__nv_bfloat16, 16><<<grid, threads, 0, st>>>(
+                    keys, group, P, rows, which, col_major, scale, rows_per_block, static_cast<__nv_bfloat16*>(out));
+        } else {
+            if (rank == 8)
+                fill_operand_r8_kernel<float, 8><<<grid, threads, 0, st>>>(keys, group, P, rows, which, col_major,
+                                                                           scale, rows_per_block,
+                                                                           static_cast<float*>(out));
+            else
+                fill_operand_r8_kernel<float, 16><<<grid, threads, 0, st>>>(keys, group, P, rows, which, col_major,
+                                                                            scale, rows_per_block,
+                                                                            static_cast<float*>(out));
+        }
+        return check_launch("fill_operand");
+    }
     if (dtype == ZG_BF16)
         fill_operand_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(keys, group, P, rank, rows, which, col_major,
                                                                      scale, extra_scale, rows_per_block,
@@ -375,10 +471,16 @@ int tc_forward_factors(const void* x, const void* Wop, bool w_mn_major, int64_t 
     float* XW = cv.take<float>((size_t)M * N);
     if (!U || !XW) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
     int rc;
-    // U[M, q] = x[M, K] . F1[K, q]   (F1 is MN-major for this product)
-    if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, false, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
     if ((rc = tc_gemm_bf16(x, K, Wop, ldw, w_mn_major, XW, N, false, M, N, K, 1.f, st, "forward_xw_gemm")))
         return rc;
+    if (tc_expand_ok(P, M, N, rank, XW, U, F2, y)) {
+        // U in bf16 (x @ A rounded to the leaf dtype, as the reference's bf16
+        // x @ a is) feeds the tensor-core expansion.
+        if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, true, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
+        return tc_expand_r8(XW, U, F2, P, M, N, s, y, st);
+    }
+    // U[M, q] = x[M, K] . F1[K, q]   (F1 is MN-major for this product)
+    if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, false, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
     return lowrank_expand(XW, U, F2, P, M, N, rank, s, ZG_BF16, y, st);
 }
 
