@@ -219,6 +219,25 @@ ZG_API int zg_replay(const float* shaped, const uint32_t* keys, int group, int P
               int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, int dtype, float* out,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* zg_replay for callers that cannot allocate device memory where they run
+ * the replay (a host that fixes the GPU library's memory at start-up and
+ * forbids later cudaMalloc, or a thread that must not call an allocator).
+ * Same arguments and result as zg_replay minus the workspace: the scratch
+ * is a 16 MiB buffer compiled into this library, which every GPU that loads
+ * the library holds until the process exits.  A replay whose
+ * zg_replay_workspace_size() exceeds 16 MiB is rejected with
+ * ZG_ERR_WORKSPACE.  The first call on a device looks up the buffer's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  All calls on a device share the one
+ * buffer, so calls that overlap on the GPU (different streams, or host
+ * threads racing on one device) corrupt each other's results; serialise
+ * them.  The buffer keeps the last call's contents; the replay writes every
+ * byte it reads, so nothing needs clearing.  This entry point has no
+ * counterpart in the reference. */
+ZG_API int zg_replay_noalloc(const float* shaped, const uint32_t* keys, int group, int P, int layout,
+                             int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, int dtype,
+                             float* out, void* stream);
+
 /* Fused AdamW (optax.adamw: scale_by_adam -> add_decayed_weights ->
  * scale(-lr)) on one leaf, with gradient = -descent (descent may be NULL:
  * a non-manifest leaf, zero gradient, which still receives weight decay).

@@ -55,6 +55,7 @@ SIGNATURES = {
     "zg_shape_fitness": (_i32, [_vp, _i32, _f64, _vp, _vp, _vp]),
     "zg_replay_workspace_size": (_sz, [_i32, _i32, _i64, _i64, _i32, _i32]),
     "zg_replay": (_i32, [_vp, _vp, _i32, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp, _vp, _sz, _vp]),
+    "zg_replay_noalloc": (_i32, [_vp, _vp, _i32, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp, _vp]),
     "zg_adamw_update": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _f64, _f64, _f64, _f64,
                                _f64, _vp]),
     "zg_sgd_update": (_i32, [_vp, _vp, _i32, _vp, _i64, _f64, _vp]),
