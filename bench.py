@@ -373,9 +373,12 @@ def run_ours(args):
             else:
                 ach, peak, unit = work / per / 1e12, pk["bf16_tflops"], "TFLOP/s"
             traffic = None
-            tpath = os.path.join(ROOT, "profiles", "traffic.json")
+            tpath = os.path.join(ROOT, "profiles", "traffic.txt")
             if os.path.exists(tpath):
-                traffic = json.load(open(tpath)).get(name)
+                for tl in open(tpath):
+                    parts = tl.split()
+                    if len(parts) == 2 and not tl.startswith("#") and parts[0] == name:
+                        traffic = int(parts[1])
             roof = {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                     "frac": ach / peak, "traffic": traffic, "peak_source": pk["source"],
                     "launch_ms": tot / n, "launches": n}

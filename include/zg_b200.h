@@ -142,6 +142,19 @@ ZG_API int zg_forward_factors(const void* x, const void* W, int w_is_kn, const v
                               const void* F2, int P, int M, int K, int N, int rank, float s,
                               void* y, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same forward that also draws its operand factors into F1 / F2
+ * (bf16 [K, P*rank] / [N, P*rank], kept by the caller for the replay of the
+ * generation): linear (w_is_kn = 1) F1 = A_op, F2 = B_op of the MATRIX
+ * entry; tied table (w_is_kn = 0) F1 = B_op, F2 = A_op of the TABLE entry.
+ * Internally the factor draws overlap the x @ W GEMM on a second stream
+ * joined back before return.  Workspace: zg_forward_factors_workspace_size.
+ * Replaces the factor draws plus perturbed_linear / perturbed_tied_logits
+ * under jax.vmap (src/zerograd/_candidate.py:17-38, _factors.py:43-67). */
+ZG_API int zg_forward_operands(const void* x, const void* W, int w_is_kn, const uint32_t* keys,
+                               int group, int P, int M, int K, int N, int rank, float s, void* F1,
+                               void* F2, void* y, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
 /* Replay from operand factors (bf16, tcgen05):
  *   out[rows, cols] = inv_sqrt_rank * sum_q (w_{q/rank} A_op[:, q]) B_op[:, q]^T
  * (float32).  Replaces replay_entry (src/zerograd/_replay.py:44-51). */

@@ -40,6 +40,8 @@ SIGNATURES = {
     "zg_forward_factors_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "zg_forward_factors": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
                                   _vp]),
+    "zg_forward_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp,
+                                   _vp, _sz, _vp]),
     "zg_replay_factors_workspace_size": (_sz, [_i32, _i64, _i32]),
     "zg_replay_factors": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _sz, _vp]),
     "zg_perturbed_linear_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),

@@ -256,6 +256,27 @@ def _forward_factors(x, W, w_is_kn: bool, F1, F2, P, M, K, N, rank, s, y):
            L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
 
 
+def _forward_cached(x, W, w_is_kn: bool, keys, group, layout, rows, cols, P, M, K, N, rank, s, y, gen,
+                    cache: FactorCache = CACHE):
+    """Shared-input forward whose operand factors (A_op [rows, P r], B_op
+    [cols, P r]) are kept in the cache for the generation's replay."""
+    dev = x.device
+    ckey = (gen.base, gen.start, gen.count, group, layout, rows, cols, rank)
+    hit = cache.get(ckey)
+    if hit is not None:
+        A_op, B_op = hit
+        F1, F2 = (A_op, B_op) if w_is_kn else (B_op, A_op)
+        _forward_factors(x, W, w_is_kn, F1, F2, P, M, K, N, rank, s, y)
+        return
+    A_op = torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev)
+    B_op = torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev)
+    F1, F2 = (A_op, B_op) if w_is_kn else (B_op, A_op)
+    ws = L.workspace(L.query("zg_forward_factors_workspace_size", P, M, N, rank), dev)
+    L.call("zg_forward_operands", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(_keys2d(keys)), group, P, M, K, N, rank,
+           s, L.ptr(F1), L.ptr(F2), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    cache.put(ckey, (A_op, B_op), dev)
+
+
 def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
                   sigma: float, x_batched: bool) -> torch.Tensor:
     """y[p] = x_p @ W + s (x_p @ A_p) @ B_p; x [*M, K] shared or [P, *M, K]."""
@@ -279,8 +300,7 @@ def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, gro
     code = L.dtype_code(dt)
     gen = CACHE.active_for(keys)
     if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, K, N, rank):
-        A_op, B_op = operand_factors(keys, group, L.ZG_MATRIX, K, N, rank, gen)
-        _forward_factors(x, W, True, A_op, B_op, P, M, K, N, rank, s, y)
+        _forward_cached(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y, gen)
         return y
     ws = L.workspace(L.query("zg_perturbed_linear_workspace_size", P, M, K, N, rank, code, int(x_batched)), dev)
     L.call("zg_perturbed_linear", L.ptr(x), int(x_batched), L.ptr(W), L.ptr(k), group, P, M, K, N, rank, s,
@@ -308,8 +328,8 @@ def launch_tied_logits(x: torch.Tensor, table: torch.Tensor, keys: torch.Tensor,
     code = L.dtype_code(dt)
     gen = CACHE.active_for(keys)
     if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, C, V, rank):
-        A_op, B_op = operand_factors(keys, group, L.ZG_TABLE, V, C, rank, gen)  # A_t [V, q], B_t [C, q]
-        _forward_factors(x, T, False, B_op, A_op, P, M, C, V, rank, s, y)
+        # table factors: A_t [V, q] (rows), B_t [C, q] (cols)
+        _forward_cached(x, T, False, k, group, L.ZG_TABLE, V, C, P, M, C, V, rank, s, y, gen)
         return y
     ws = L.workspace(L.query("zg_tied_logits_workspace_size", P, M, V, C, rank, code, int(x_batched)), dev)
     L.call("zg_tied_logits", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, P, M, V, C, rank, s, code,

@@ -1,7 +1,8 @@
 // zg_tc.cu -- tensor-core GEMM for sm_100a: tcgen05.mma (kind::f16, bf16 in,
 // float32 accumulate in TMEM), operands staged by TMA (no multicast) into a
-// 4-stage shared-memory ring, persistent CTAs with two TMEM accumulators so
-// the epilogue of one tile overlaps the main loop of the next.
+// 4- to 8-stage shared-memory ring (by tile width), persistent CTAs with two
+// TMEM accumulators so the epilogue of one tile overlaps the main loop of
+// the next.
 //
 //   D[M,N] = alpha * A[M,K] . B^T           (A K-major, row-major [M, K])
 //   B is K-major ([N, K] row-major) or MN-major ([K, N] row-major).
@@ -28,7 +29,12 @@ __device__ unsigned int g_zg_tc_error = 0;
 
 namespace {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BK = 64, THREADS = 192;
+
+// Operand-ring depth for a tile width: as many 64-deep K stages as fit in
+// 192 KiB (4 at BN=256, 6 at BN=128, 8 at BN=64), so narrower tiles keep
+// more bytes in flight per MMA.
+__host__ __device__ constexpr int gemm_stages(int bn) { return (192 * 1024) / (BM * BK * 2 + bn * BK * 2); }
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 // ---------------------------------------------------------------------------
@@ -161,6 +167,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     constexpr uint32_t B_BYTES = BN * BK * 2;
     constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {64,128,256}
+    constexpr int STAGES = gemm_stages(BN);
     extern __shared__ uint8_t dyn_smem[];
     __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tmem_full[2], tmem_empty[2], mma_done;
     __shared__ uint32_t tmem_base_sh;
@@ -199,18 +206,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         bool ok = true;
         for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
             const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            // Tiles start their K sweep at different blocks, so CTAs that share
+            // an operand tile do not all request the same L2 lines at once.
+            const int k_start = t % k_blocks;
             for (int kb = 0; kb < k_blocks; ++kb) {
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 1)) { ok = false; break; }
+                const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
                 uint8_t* sa = smem + stage * STAGE_BYTES;
                 uint8_t* sb = sa + A_BYTES;
                 mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
-                tma_load_2d(sa, &tmA, &full_bar[stage], kb * BK, tm * BM);
+                tma_load_2d(sa, &tmA, &full_bar[stage], kk * BK, tm * BM);
                 if constexpr (B_MN) {
 #pragma unroll
                     for (int c = 0; c < BN / 64; ++c)
-                        tma_load_2d(sb + c * (64 * BK * 2), &tmB, &full_bar[stage], tn * BN + c * 64, kb * BK);
+                        tma_load_2d(sb + c * (64 * BK * 2), &tmB, &full_bar[stage], tn * BN + c * 64, kk * BK);
                 } else {
-                    tma_load_2d(sb, &tmB, &full_bar[stage], kb * BK, tn * BN);
+                    tma_load_2d(sb, &tmB, &full_bar[stage], kk * BK, tn * BN);
                 }
                 issued |= 1u << stage;
                 issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
@@ -328,20 +339,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 //   y[p, m, n] = bf16(XW[m, n] + s * (U_p . B_p^T)[m, n])
 // U [M, P*8] bf16 (x @ A_all), B [N, P*8] bf16 (B_nq), XW [M, N] float32.
 // One M=128 N=128 K=16 MMA per candidate (the upper 8 K of each operand
-// read a zero region through the descriptor's leading byte offset); XW sits
-// in TMEM next to two accumulators; the epilogue writes bf16 into a
-// 128B-swizzled shared tile that a TMA bulk store copies out, so the global
-// writes are full lines and the kernel is bound by HBM write bandwidth.
-// Work item = (m tile, n tile, candidate chunk); persistent CTAs.
+// read a zero region through the descriptor's leading byte offset) into one
+// of four TMEM accumulators; each epilogue thread keeps its 64-column slice
+// of the XW row in registers for the whole tile, adds it with packed FMAs and
+// writes bf16 into a 128B-swizzled shared tile that a TMA bulk store copies
+// out, so the global writes are full lines and the kernel is bound by HBM
+// write bandwidth.  Work item = (m tile, n tile, candidate chunk); each
+// persistent CTA takes a contiguous run of items.
 // ---------------------------------------------------------------------------
 constexpr int EX_STAGES = 4;
 constexpr uint32_t EX_OP = 128 * 16;                       // one operand tile: 128 rows x 8 bf16
 constexpr uint32_t EX_A = 0, EX_AZ = EX_STAGES * EX_OP;    // A data, A zero half
 constexpr uint32_t EX_B = 2 * EX_STAGES * EX_OP, EX_BZ = 3 * EX_STAGES * EX_OP;
 constexpr uint32_t EX_LBO = EX_STAGES * EX_OP;             // data -> zero half, same for every stage
-constexpr uint32_t EX_STG = 32768;                         // staging, 2 buffers x (2 x 16 KiB sub-tiles)
+constexpr uint32_t EX_STG = 32768;                         // staging buffers, each 2 x 16 KiB sub-tiles
 constexpr uint32_t EX_STG_BYTES = 128 * 128 * 2;
-constexpr uint32_t EX_SMEM = EX_STG + 2 * EX_STG_BYTES;    // 96 KiB (+ alignment)
+constexpr int EX_NSTG = 4;                                 // staging buffers in flight
+constexpr int EX_NACC = 4;                                 // TMEM accumulators of 128 columns (all 512)
+constexpr uint32_t EX_SMEM = EX_STG + EX_NSTG * EX_STG_BYTES;  // 160 KiB (+ alignment)
 
 struct ExpandArgs {
     const float* XW;
@@ -383,20 +398,42 @@ __device__ __forceinline__ float2 ffma2_tc(float2 a, float2 b, float2 c) {
     return *reinterpret_cast<float2*>(&D);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+constexpr int EX_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue (2 per TMEM lane quadrant)
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+// Contiguous, balanced share of the work items for this CTA.
+__device__ __forceinline__ void ex_item_range(int items, int& t0, int& t1) {
+    const int per = items / (int)gridDim.x, rem = items % (int)gridDim.x, b = blockIdx.x;
+    t0 = b * per + min(b, rem);
+    t1 = t0 + per + (b < rem ? 1 : 0);
+}
+
+__global__ void __launch_bounds__(EX_THREADS, 1)
 expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmY, const ExpandArgs a) {
     extern __shared__ uint8_t dyn_smem[];
-    __shared__ __align__(8) uint64_t full_bar[EX_STAGES], empty_bar[EX_STAGES], tmem_full[2], tmem_empty[2],
-        stg_full[2], stg_free[2], mma_done;
+    __shared__ __align__(8) uint64_t full_bar[EX_STAGES], empty_bar[EX_STAGES], tmem_full[EX_NACC],
+        tmem_empty[EX_NACC], stg_full[EX_NSTG], stg_free[EX_NSTG], mma_done;
     __shared__ uint32_t tmem_base_sh;
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int items = a.tiles_m * a.tiles_n * a.chunks;
+    int t_begin, t_end;
+    ex_item_range(a.tiles_m * a.tiles_n * a.chunks, t_begin, t_end);
 
     // zero halves of the K=16 operands (read through the descriptors' LBO)
-    for (uint32_t i = threadIdx.x; i < EX_LBO / 16; i += THREADS) {
+    for (uint32_t i = threadIdx.x; i < EX_LBO / 16; i += EX_THREADS) {
         reinterpret_cast<uint4*>(smem + EX_AZ)[i] = make_uint4(0, 0, 0, 0);
         reinterpret_cast<uint4*>(smem + EX_BZ)[i] = make_uint4(0, 0, 0, 0);
     }
@@ -406,10 +443,12 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < EX_NACC; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 4);
-            mbar_init(&stg_full[b], 128);
+            mbar_init(&tmem_empty[b], 8);   // one arrive per epilogue warp
+        }
+        for (int b = 0; b < EX_NSTG; ++b) {
+            mbar_init(&stg_full[b], 256);   // every epilogue thread
             mbar_init(&stg_free[b], 1);
         }
         mbar_init(&mma_done, 1);
@@ -426,7 +465,7 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
         int stage = 0;
         uint32_t phase = 0, issued = 0, issue_parity = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < items; t += gridDim.x) {
+        for (int t = t_begin; ok && t < t_end; ++t) {
             const int chunk = t % a.chunks, tile = t / a.chunks;
             const int m0 = (tile / a.tiles_n) * 128, n0 = (tile % a.tiles_n) * 128;
             const int p1 = min(a.P, (chunk + 1) * a.chunk);
@@ -450,7 +489,7 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
         int stage = 0, acc = 0;
         uint32_t phase = 0, acc_phase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < items; t += gridDim.x) {
+        for (int t = t_begin; ok && t < t_end; ++t) {
             const int chunk = t % a.chunks;
             const int p1 = min(a.P, (chunk + 1) * a.chunk);
             for (int p = chunk * a.chunk; p < p1; ++p) {
@@ -464,7 +503,7 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
                 umma_commit(&empty_bar[stage]);
                 umma_commit(&tmem_full[acc]);
                 if (++stage == EX_STAGES) { stage = 0; phase ^= 1; }
-                if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+                if (++acc == EX_NACC) { acc = 0; acc_phase ^= 1; }
             }
         }
         umma_commit(&mma_done);
@@ -472,76 +511,72 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
             if (mbar_try_wait(&mma_done, 0)) break;
     } else if (warp >= 2) {
         // ---------------- epilogue: TMEM -> bf16 -> swizzled smem -> TMA store ----------------
-        const int quad = warp % 4;
-        const int row = quad * 32 + lane;  // TMEM lane == tile row
+        const int quad = warp % 4;             // TMEM lanes 32*quad..32*quad+31
+        const int half = (warp - 2) / 4;       // columns 64*half..64*half+63
+        const int row = quad * 32 + lane;      // TMEM lane == tile row
         const bool issuer = (warp == 2 && lane == 0);
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-        const uint32_t xw_cols = tmem_base + lane_addr + 256;
         const float2 s2 = make_float2(a.s, a.s);
-        int acc = 0, c = 0;
+        float2 xw[32];  // this thread's row of the XW tile, its 64 columns (constant within a tile)
+        int acc = 0, c = 0, loaded_tile = -1;
         uint32_t acc_phase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < items; t += gridDim.x) {
+        for (int t = t_begin; ok && t < t_end; ++t) {
             const int chunk = t % a.chunks, tile = t / a.chunks;
             const int m0 = (tile / a.tiles_n) * 128, n0 = (tile % a.tiles_n) * 128;
-            const int m = m0 + row;
-            // this row of XW into TMEM columns 256..383 (each thread owns its lane)
-#pragma unroll 1
-            for (int c0 = 0; c0 < 128; c0 += 32) {
-                float v[32];
+            if (tile != loaded_tile) {
+                const int m = m0 + row;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const int n = n0 + c0 + i;
+                for (int i = 0; i < 64; i += 4) {
+                    const int n = n0 + half * 64 + i;
                     float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (m < a.M && n + 3 < a.N) f = *reinterpret_cast<const float4*>(a.XW + (int64_t)m * a.N + n);
-                    v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+                    xw[i / 2] = make_float2(f.x, f.y);
+                    xw[i / 2 + 1] = make_float2(f.z, f.w);
                 }
-                tmem_st32(xw_cols + c0, v);
+                loaded_tile = tile;
             }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             const int p1 = min(a.P, (chunk + 1) * a.chunk);
             for (int p = chunk * a.chunk; p < p1; ++p, ++c) {
-                const int sb = c & 1;
-                const uint32_t use = (uint32_t)(c >> 1);
+                const int sb = c % EX_NSTG;
+                const uint32_t use = (uint32_t)(c / EX_NSTG);
                 if (!mbar_wait(&tmem_full[acc], acc_phase, 14)) { ok = false; break; }
                 tc_fence_after();
                 if (!mbar_wait(&stg_free[sb], (use & 1) ^ 1, 15)) { ok = false; break; }
-                uint8_t* stg = smem + EX_STG + sb * EX_STG_BYTES;
-#pragma unroll 1
-                for (int c0 = 0; c0 < 128; c0 += 32) {
-                    float v[32], w[32];
-                    tmem_ld32(tmem_base + lane_addr + acc * 128 + c0, v);
-                    tmem_ld32(xw_cols + c0, w);
-                    uint32_t pk[16];
+                uint8_t* sub = smem + EX_STG + sb * EX_STG_BYTES + half * (128 * 128) + row * 128;
+                uint32_t v[64];
+                tmem_ld32_nowait(tmem_base + lane_addr + acc * 128 + half * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+                tmem_ld32_nowait(tmem_base + lane_addr + acc * 128 + half * 64 + 32,
+                                 *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                uint32_t pk[32];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float2 o = ffma2_tc(s2, make_float2(v[2 * i], v[2 * i + 1]),
-                                                  make_float2(w[2 * i], w[2 * i + 1]));
-                        __nv_bfloat162 h = __floats2bfloat162_rn(o.x, o.y);
-                        pk[i] = *reinterpret_cast<uint32_t*>(&h);
-                    }
-                    // 128B swizzle: 16-byte chunk k of a 128-byte row lives at k ^ (row % 8)
-                    uint8_t* sub = stg + (c0 / 64) * (128 * 128) + row * 128;
-                    const int ch0 = (c0 % 64) / 8;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        *reinterpret_cast<uint4*>(sub + (((ch0 + k) ^ (row & 7)) * 16)) =
-                            make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+                for (int i = 0; i < 32; ++i) {
+                    const float2 o = ffma2_tc(s2, make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                              xw[i]);
+                    __nv_bfloat162 h = __floats2bfloat162_rn(o.x, o.y);
+                    pk[i] = *reinterpret_cast<uint32_t*>(&h);
                 }
+                // 128B swizzle: 16-byte chunk k of a 128-byte row lives at k ^ (row % 8)
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    *reinterpret_cast<uint4*>(sub + ((k ^ (row & 7)) * 16)) =
+                        make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tmem_empty[acc]);
-                if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+                if (++acc == EX_NACC) { acc = 0; acc_phase ^= 1; }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive(&stg_full[sb]);
                 if (issuer) {
                     if (!mbar_wait(&stg_full[sb], use & 1, 16)) { ok = false; break; }
+                    uint8_t* stg = smem + EX_STG + sb * EX_STG_BYTES;
                     tma_store_3d(&tmY, stg, n0, m0, p);
                     tma_store_3d(&tmY, stg + 128 * 128, n0 + 64, m0, p);
                     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                    // the store of the previous candidate has finished reading its buffer
-                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                    if (c > 0) mbar_arrive(&stg_free[sb ^ 1]);
+                    // all but the two newest stores have finished reading their buffers
+                    asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
+                    if (c >= 2) mbar_arrive(&stg_free[(c - 2) % EX_NSTG]);
                 }
             }
         }
@@ -624,7 +659,7 @@ int num_sms() {
 
 template <int BN, bool B_MN>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& a, cudaStream_t st, const char* name) {
-    constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+    constexpr size_t smem = (size_t)gemm_stages(BN) * (BM * BK * 2 + BN * BK * 2) + 1024;
     if (cudaFuncSetAttribute(tc_gemm_kernel<BN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return zg::fail(ZG_ERR_CUDA, "tc_gemm: shared memory attribute");
@@ -656,12 +691,17 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
     if (M <= 0 || N <= 0 || K <= 0) return fail(ZG_ERR_INVALID, "tc_gemm: empty problem");
     if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
         return fail(ZG_ERR_INVALID, "tc_gemm: operands need 16-byte aligned rows");
-    // Tile width: the widest N tile that still gives every SM work.
+    // Tile width: the persistent grid finishes after ceil(tiles / SMs) tiles
+    // per SM, each costing ~BN (narrower tiles re-read A more often, hence
+    // the small penalty); take the cheapest.
+    auto tiles = [&](int b) { return (int64_t)((M + BM - 1) / BM) * ((N + b - 1) / b); };
+    auto cost = [&](int b, double pen) {
+        return (double)((tiles(b) + num_sms() - 1) / num_sms()) * b * pen;
+    };
     int bn = 256;
-    auto tiles = [&](int b) { return ((M + BM - 1) / BM) * ((N + b - 1) / b); };
-    if (tiles(256) < num_sms()) bn = 128;
-    if (bn == 128 && tiles(128) < num_sms()) bn = 64;
-    if (b_mn_major && bn < 64) bn = 64;
+    double best = cost(256, 1.0);
+    if (cost(128, 1.3) < best) { bn = 128; best = cost(128, 1.3); }
+    if (cost(64, 1.6) < best) { bn = 64; }
     CUtensorMap ta, tb;
     if (!make_map(&ta, A, K, M, lda, BK, BM)) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map A");
     bool okb = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
@@ -696,21 +736,20 @@ int tc_expand_r8(const float* XW, const void* U, const void* Bq, int P, int M, i
         return fail(ZG_ERR_CUDA, "tc_expand: tensor maps");
     ExpandArgs a{XW, M, N, P, s, (M + 127) / 128, (N + 127) / 128, 0, 0};
     const int tiles = a.tiles_m * a.tiles_n;
-    int chunks = (num_sms() * 4 + tiles - 1) / tiles;
-    if (chunks > P) chunks = P;
+    // ~8 candidates per item: fine enough that the contiguous per-CTA shares
+    // balance to within one item, coarse enough that XW is reloaded rarely.
+    int chunks = (P + 7) / 8;
     if (chunks < 1) chunks = 1;
     a.chunk = (P + chunks - 1) / chunks;
     a.chunks = (P + a.chunk - 1) / a.chunk;
     const int items = tiles * a.chunks;
     const int grid = items < num_sms() ? items : num_sms();
-    // >112 KiB so a second CTA (and its 512 TMEM columns) never shares the SM;
-    // 160 KiB also keeps every address the operand descriptors can form
-    // (start + 15 * max(LBO, SBO) + 2 KiB) inside the allocation.
-    const size_t smem = 160 * 1024 + 1024;
+    // one CTA (and its 512 TMEM columns) per SM
+    const size_t smem = EX_SMEM + 1024;
     if (cudaFuncSetAttribute(expand_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return fail(ZG_ERR_CUDA, "tc_expand: shared memory attribute");
     zg::LaunchTimer zg_lt_("lowrank_expand", st);
-    expand_tc_kernel<<<grid, THREADS, smem, st>>>(tu, tb, ty, a);
+    expand_tc_kernel<<<grid, EX_THREADS, smem, st>>>(tu, tb, ty, a);
     return check_launch("tc_expand");
 }
 

@@ -9,6 +9,8 @@
 // The (candidate, rank) pairs q = p*r + j form the contraction axis of the
 // replay and the N axis of U, so every candidate's factors are drawn once per
 // call and the tensor cores see ordinary dense operands.
+#include <mutex>
+
 #include "zg_tc.cuh"
 
 namespace {
@@ -464,24 +466,80 @@ bool tc_shared_forward_ok(int P, int M, int K, int N, int rank) {
     return tc_available() && ((int64_t)P * rank) % 8 == 0 && K % 8 == 0 && N % 8 == 0 && rank <= 32 && M > 0;
 }
 
-int tc_forward_factors(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const void* F1, const void* F2,
-                       int P, int M, int K, int N, int rank, float s, void* y, Carver& cv, cudaStream_t st) {
+// A second stream per device for fork/join overlap inside one call: work on
+// it waits for everything queued on the caller's stream so far, and the
+// caller's stream waits for it before the call returns, so to the caller the
+// call stays one in-order unit on its own stream.  The enqueue sequence is
+// serialised per device so two host threads cannot interleave fork events.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    std::mutex mu;
+};
+
+SideStream* side_stream() {
+    static SideStream streams[64];
+    static std::mutex init_mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    SideStream& ss = streams[dev];
+    std::lock_guard<std::mutex> lk(init_mu);
+    if (!ss.s) {
+        if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+            ss.s = nullptr;
+            return nullptr;
+        }
+    }
+    return &ss;
+}
+
+// The shared-x forward, with optional factor draws.  Schedule:
+//   caller stream: [fill F1] -> U = x F1 --------------------.-> expansion
+//   side stream:          XW = x W -> [fill F2] ------------'
+// The fills are integer-ALU bound and the GEMMs tensor/L2 bound, so the two
+// streams overlap on the same SMs.
+int tc_forward_schedule(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const uint32_t* keys, int group,
+                        int f1_which, int f1_col_major, int f2_which, int f2_col_major, bool draw, const void* F1,
+                        const void* F2, int P, int M, int K, int N, int rank, float s, void* y, Carver& cv,
+                        cudaStream_t st) {
     const int64_t q = (int64_t)P * rank;
     float* U = cv.take<float>((size_t)M * q);
     float* XW = cv.take<float>((size_t)M * N);
     if (!U || !XW) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
-    int rc;
-    if ((rc = tc_gemm_bf16(x, K, Wop, ldw, w_mn_major, XW, N, false, M, N, K, 1.f, st, "forward_xw_gemm")))
-        return rc;
-    if (tc_expand_ok(P, M, N, rank, XW, U, F2, y)) {
-        // U in bf16 (x @ A rounded to the leaf dtype, as the reference's bf16
-        // x @ a is) feeds the tensor-core expansion.
-        if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, true, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
-        return tc_expand_r8(XW, U, F2, P, M, N, s, y, st);
+    const bool tc_exp = tc_expand_ok(P, M, N, rank, XW, U, F2, y);
+    SideStream* ss = side_stream();
+    if (!ss) return fail(ZG_ERR_CUDA, "tc forward: side stream");
+    int rc = ZG_OK, rc_side = ZG_OK;
+    {
+        std::lock_guard<std::mutex> lk(ss->mu);
+        if (cudaEventRecord(ss->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess)
+            return fail(ZG_ERR_CUDA, "tc forward: fork");
+        rc_side = tc_gemm_bf16(x, K, Wop, ldw, w_mn_major, XW, N, false, M, N, K, 1.f, ss->s, "forward_xw_gemm");
+        if (!rc_side && draw)
+            rc_side = fill_operand(keys, group, P, rank, N, f2_which, f2_col_major, nullptr, 1.f, ZG_BF16,
+                                   const_cast<void*>(F2), ss->s, "factor_fill");
+        if (draw)
+            rc = fill_operand(keys, group, P, rank, K, f1_which, f1_col_major, nullptr, 1.f, ZG_BF16,
+                              const_cast<void*>(F1), st, "factor_fill");
+        // U = x F1 (F1 is MN-major for this product); bf16 for the tensor-core
+        // expansion (x @ A rounded to the leaf dtype, as the reference's bf16 x @ a is)
+        if (!rc) rc = tc_gemm_bf16(x, K, F1, q, true, U, q, tc_exp, M, (int)q, K, 1.f, st, "forward_u_gemm");
+        // join unconditionally so the side stream never outlives the call
+        if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
+            return fail(ZG_ERR_CUDA, "tc forward: join");
     }
-    // U[M, q] = x[M, K] . F1[K, q]   (F1 is MN-major for this product)
-    if ((rc = tc_gemm_bf16(x, K, F1, q, true, U, q, false, M, (int)q, K, 1.f, st, "forward_u_gemm"))) return rc;
+    if (rc) return rc;
+    if (rc_side) return rc_side;
+    if (tc_exp) return tc_expand_r8(XW, U, F2, P, M, N, s, y, st);
     return lowrank_expand(XW, U, F2, P, M, N, rank, s, ZG_BF16, y, st);
+}
+
+int tc_forward_factors(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const void* F1, const void* F2,
+                       int P, int M, int K, int N, int rank, float s, void* y, Carver& cv, cudaStream_t st) {
+    return tc_forward_schedule(x, Wop, w_mn_major, ldw, nullptr, 0, 0, 0, 0, 0, false, F1, F2, P, M, K, N, rank, s,
+                               y, cv, st);
 }
 
 size_t tc_shared_forward_workspace(int P, int M, int K, int N, int rank) {
@@ -496,33 +554,36 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
     __nv_bfloat16* F1 = cv.take<__nv_bfloat16>((size_t)K * q);
     __nv_bfloat16* F2 = cv.take<__nv_bfloat16>((size_t)N * q);
     if (!F1 || !F2) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
-    int rc;
-    if ((rc = fill_operand(keys, group, P, rank, K, f1_which, f1_col_major, nullptr, 1.f, ZG_BF16, F1, st,
-                           "factor_fill")))
-        return rc;
-    if ((rc = fill_operand(keys, group, P, rank, N, f2_which, f2_col_major, nullptr, 1.f, ZG_BF16, F2, st,
-                           "factor_fill")))
-        return rc;
-    return tc_forward_factors(x, Wop, w_mn_major, ldw, F1, F2, P, M, K, N, rank, s, y, cv, st);
+    return tc_forward_schedule(x, Wop, w_mn_major, ldw, keys, group, f1_which, f1_col_major, f2_which, f2_col_major,
+                               true, F1, F2, P, M, K, N, rank, s, y, cv, st);
 }
 
 // Aw[row, q] = bf16(float(A[row, q]) * w[q / rank]): the reference's
 // weighted factor a_pop * shaped (src/zerograd/_replay.py:46) rounded to the
 // tensor-core operand type.
+// grid (column groups of 8, rows): thread = 8 consecutive columns of one row.
 __global__ void scale_operand_kernel(const __nv_bfloat16* __restrict__ A, const float* __restrict__ w, int rank,
-                                     int64_t q, int64_t total8, __nv_bfloat16* __restrict__ out) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e0 = i * 8;
-        const int64_t col0 = e0 % q;
+                                     int q, int64_t rows, __nv_bfloat16* __restrict__ out) {
+    const int col0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (col0 >= q) return;
+    float wk[8];
+    if (rank % 8 == 0) {
+        const float wc = w[col0 / rank];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wk[k] = wc;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wk[k] = w[(col0 + k) / rank];
+    }
+    for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+        const int64_t e0 = row * q + col0;
         float f[8];
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(A + e0), f);
         uint4 pk;
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-            h[k] = __floats2bfloat162_rn(__fmul_rn(f[2 * k], w[(col0 + 2 * k) / rank]),
-                                         __fmul_rn(f[2 * k + 1], w[(col0 + 2 * k + 1) / rank]));
+            h[k] = __floats2bfloat162_rn(__fmul_rn(f[2 * k], wk[2 * k]), __fmul_rn(f[2 * k + 1], wk[2 * k + 1]));
         *reinterpret_cast<uint4*>(out + e0) = pk;
     }
 }
@@ -535,13 +596,16 @@ int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, i
     __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
     if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
     if (q % 8 || (reinterpret_cast<uintptr_t>(A_op) & 15)) return fail(ZG_ERR_INVALID, "tc replay: operand alignment");
-    const int64_t total8 = rows * q / 8;
-    int64_t blocks = (total8 + 255) / 256;
-    if (blocks > sm_count() * 16) blocks = sm_count() * 16;
+    if (q > 2147483647) return fail(ZG_ERR_INVALID, "tc replay: P*rank too large");
+    const unsigned gx = (unsigned)((q / 8 + 255) / 256);
+    int64_t gy = (int64_t)sm_count() * 32 / gx;
+    if (gy < 1) gy = 1;
+    if (gy > rows) gy = rows;
+    if (gy > 65535) gy = 65535;
     {
         zg::LaunchTimer zg_lt_("replay_scale", st);
-        scale_operand_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A_op), shaped, rank, q,
-                                                          total8, Aw);
+        scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A_op), shaped,
+                                                                     rank, (int)q, rows, Aw);
         int rc = check_launch("replay_scale");
         if (rc) return rc;
     }
@@ -605,6 +669,25 @@ extern "C" int zg_forward_factors(const void* x, const void* W, int w_is_kn, con
     // W [K, N] (a linear weight) is the MN-major operand; T [N, K] (a tied table) the K-major one.
     return zg::tc_forward_factors(x, W, w_is_kn != 0, w_is_kn ? N : K, F1, F2, P, M, K, N, rank, s, y, cv,
                                   zg::as_stream(stream));
+}
+
+extern "C" int zg_forward_operands(const void* x, const void* W, int w_is_kn, const uint32_t* keys, int group, int P,
+                                   int M, int K, int N, int rank, float s, void* F1, void* F2, void* y,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || M < 1 || K < 1 || N < 1 || rank < 1)
+        return zg::fail(ZG_ERR_INVALID, "zg_forward_operands: bad sizes");
+    if (!x || !W || !keys || !F1 || !F2 || !y) return zg::fail(ZG_ERR_INVALID, "zg_forward_operands: null pointer");
+    if (!zg::tc_shared_forward_ok(P, M, K, N, rank))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "zg_forward_operands: needs sm_100, P*rank, K, N multiples of 8, rank<=32");
+    size_t need = zg::tc_forward_factors_workspace(P, M, N, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_forward_operands: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    // linear: F1 = A_op (A, counter k*r + j), F2 = B_op (B, counter j*N + n);
+    // tied table: F1 = table B_op (counter c*r + j), F2 = table A_op (counter v*r + j)
+    const bool kn = w_is_kn != 0;
+    return zg::tc_forward_schedule(x, W, kn, kn ? N : K, keys, group, kn ? 0 : 1, 0, kn ? 1 : 0, kn ? 1 : 0, true, F1,
+                                   F2, P, M, K, N, rank, s, y, cv, zg::as_stream(stream));
 }
 
 extern "C" size_t zg_replay_factors_workspace_size(int P, int64_t rows, int rank) {
