@@ -127,8 +127,16 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # algorithmic work per launch of each kernel (this workload)
 # ---------------------------------------------------------------------------
-def kernel_work(name: str, P_local: int):
+def kernel_work(name: str, P_local: int, world: int = 1):
     P, r, M, K, N = WL["P"], WL["rank"], WL["M"], WL["K"], WL["N"]
+    if name == "factor_fill":
+        # bf16 operand bytes written per launch: the forward draws A_op and B_op
+        # for this rank's candidates; with more than one rank the replay draws
+        # both for the whole population (only the local ones are cached)
+        fills = [P_local * r * K * 2, P_local * r * N * 2]
+        if world > 1:
+            fills += [P * r * K * 2, P * r * N * 2]
+        return "hbm", sum(fills) / len(fills)
     if name == "lowrank_expand":      # y = xW + s (xA) B : write y bf16, read xW f32, U f32, B bf16
         return "hbm", P_local * M * N * 2 + M * N * 4 + P_local * M * r * 4 + P_local * r * N * 2
     if name == "replay_gemm":         # [K, P r] x [P r, N]
@@ -362,11 +370,12 @@ def run_ours(args):
     e2e_value = P * args.steps / (e2e_ms / 1e3)
     if rank == 0:
         pk = peaks()
-        top = max(kernels.items(), key=lambda kv: kv[1][1]) if kernels else None
+        known = {k: v for k, v in kernels.items() if kernel_work(k, P_local, world)[0] is not None}
+        top = max(known.items(), key=lambda kv: kv[1][1]) if known else None
         roof = None
         if top:
             name, (n, tot) = top
-            bound, work = kernel_work(name, P_local)
+            bound, work = kernel_work(name, P_local, world)
             per = tot / n / 1e3
             if bound == "hbm":
                 ach, peak, unit = work / per / 1e9, pk["hbm_gbs"], "GB/s"

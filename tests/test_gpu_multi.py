@@ -1,0 +1,91 @@
+"""DistributedZeroGrad with one process per GPU (NCCL): population shards,
+fitness all-gather, replicated replay.  Every rank must end with bit-identical
+parameters, equal (float tolerance) to a single-process step.  Needs >= 2 GPUs.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _problem(dev):
+    import zerograd_b200 as zg
+
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w"),
+                               zg.ManifestEntry(("b",), zg.ParameterLayout.VECTOR, "b")))
+    g = torch.Generator().manual_seed(0)
+    params = {"w": (torch.randn(256, 128, generator=g) * 0.05).to(torch.bfloat16).to(dev),
+              "b": torch.zeros(128, dtype=torch.bfloat16).to(dev)}
+    x = torch.randn(64, 256, generator=g).to(torch.bfloat16).to(dev)
+
+    def loss_fn(p, ctx, batch, rng):
+        y = ctx.linear(p, ("w",), batch) + ctx.vector(p, ("b",))
+        return (y.float() ** 2).mean(), None
+
+    opt = zg.ZeroGrad(manifest, zg.adamw(1e-3), 48, 8, 0.02, 0, "multi")
+    return opt, params, x, loss_fn
+
+
+def _worker(rank, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import zerograd_b200 as zg
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        opt, params, x, loss_fn = _problem(dev)
+        state = opt.init(params)
+        dz = zg.DistributedZeroGrad(opt, None, loss_fn, weights=[1.0, 2.0])
+        for _ in range(2):
+            params, state, metrics = dz.step(state, params, x)
+        q.put((rank, {k: v.float().cpu() for k, v in params.items()}, dz.partition_sizes, metrics.mean_loss))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_process_group_matches_single_process():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=300) for _ in procs], key=lambda t: t[0])
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    (_, p0, sizes, m0), (_, p1, _, m1) = out
+    assert sizes == [16, 32]
+    for k in p0:
+        assert torch.equal(p0[k], p1[k]), k  # replicated replay: identical on every rank
+    # single process, same generations
+    dev = torch.device("cuda", 0)
+    opt, params, x, loss_fn = _problem(dev)
+    state = opt.init(params)
+    for _ in range(2):
+        params, state, metrics = opt.step(state, params, x, loss_fn)
+    for k in p0:
+        torch.testing.assert_close(p0[k], params[k].float().cpu(), rtol=1e-2, atol=1e-2)
+    assert m0 == m1
