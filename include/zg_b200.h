@@ -163,6 +163,40 @@ ZG_API int zg_replay_factors(const float* shaped, const void* A_op, const void* 
                              int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, float* out,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same replay with either operand given transposed: a_transposed = 1
+ * takes A as AT [P*rank, rows], b_transposed = 1 takes B as BT [P*rank, cols]
+ * (cols a multiple of 8), which is how the per-candidate-input forward keeps
+ * its input-side factor.  Replaces replay_entry
+ * (src/zerograd/_replay.py:44-51). */
+ZG_API size_t zg_replay_operands_workspace_size(int P, int64_t rows, int rank);
+ZG_API int zg_replay_operands(const float* shaped, const void* A, int a_transposed, const void* B,
+                              int b_transposed, int P, int64_t rows, int64_t cols, int rank,
+                              float inv_sqrt_rank, float* out, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* Per-candidate-input population forward (bf16, tcgen05), the hidden-layer
+ * case: x [P, M, K] (one input per candidate), y [P, M, N],
+ *   y[p] = x_p @ Wop + s * (x_p @ F1_p) @ F2_p^T
+ * with F1T [P*rank, K] (each candidate's input-side factor, K-major) and
+ * F2 [N, P*rank].  w_is_kn = 1: W is a linear weight [K, N]; F1T rows are
+ * A_p^T (A counter k*rank + j), F2 = B_op (counter j*N + n).  w_is_kn = 0:
+ * W is a tied table [N, K]; F1T rows are the table B_p^T (counter
+ * c*rank + j), F2 = the table A_op (counter v*rank + j).  rank 8 or 16; K, N
+ * multiples of 8; all pointers 16-byte aligned.  _operands draws F1T and F2
+ * (kept by the caller for the replay, which takes F1T through
+ * zg_replay_operands); _factors takes them as given.  Replaces
+ * perturbed_linear / perturbed_tied_logits under jax.vmap with a batched x
+ * (src/zerograd/_candidate.py:17-22,33-38). */
+ZG_API size_t zg_batched_forward_workspace_size(int P, int M, int K, int N, int rank);
+ZG_API int zg_batched_forward_factors(const void* x, const void* W, int w_is_kn, const void* F1T,
+                                      const void* F2, int P, int M, int K, int N, int rank, float s,
+                                      void* y, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+ZG_API int zg_batched_forward_operands(const void* x, const void* W, int w_is_kn,
+                                       const uint32_t* keys, int group, int P, int M, int K, int N,
+                                       int rank, float s, void* F1T, void* F2, void* y,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------- forward ops -- */
 
 /* y[p] = x_p @ W + s * (x_p @ A_p) @ B_p for p in [0,P): one population-

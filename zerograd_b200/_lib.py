@@ -44,7 +44,14 @@ SIGNATURES = {
                                    _vp, _sz, _vp]),
     "zg_replay_factors_workspace_size": (_sz, [_i32, _i64, _i32]),
     "zg_replay_factors": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _sz, _vp]),
-    "zg_perturbed_linear_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
+    "zg_replay_operands_workspace_size": (_sz, [_i32, _i64, _i32]),
+    "zg_replay_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "zg_batched_forward_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "zg_batched_forward_factors": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp,
+                                          _sz, _vp]),
+    "zg_batched_forward_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp,
+                                           _vp, _vp, _sz, _vp]),
+    "zg_perturbed_linear_workspace_size":(_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "zg_perturbed_linear": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32,
                                    _vp, _vp, _sz, _vp]),
     "zg_table_lookup_workspace_size": (_sz, [_i32, _i64, _i64, _i32, _i32]),

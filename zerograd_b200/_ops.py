@@ -181,6 +181,15 @@ class FactorCache:
             self.misses += 1
         return hit
 
+    def find(self, *keys):
+        """(key, value) of the first of `keys` present, counted as one hit or
+        one miss; (None, None) when none is."""
+        for key in keys:
+            if key in self._entries:
+                return key, self.get(key)
+        self.misses += 1
+        return None, None
+
     def put(self, key, value, device) -> None:
         nbytes = sum(t.numel() * t.element_size() for t in value)
         budget = self._budget(device)
@@ -277,6 +286,37 @@ def _forward_cached(x, W, w_is_kn: bool, keys, group, layout, rows, cols, P, M, 
     cache.put(ckey, (A_op, B_op), dev)
 
 
+# Cache keys of per-candidate-input forwards end with this tag: their input-side
+# factor is kept K-major ([P r, K]), so the replay reads it transposed.
+_T_TAG = "t"
+
+
+def _batched_ok(dev: torch.device, P: int, K: int, N: int, rank: int) -> bool:
+    return torch.cuda.get_device_capability(dev) == (10, 0) and rank in (8, 16) and K % 8 == 0 and N % 8 == 0
+
+
+def _forward_batched(x, W, w_is_kn: bool, keys, group, layout, rows, cols, P, M, K, N, rank, s, y, gen,
+                     cache: FactorCache = CACHE):
+    """Per-candidate-input forward (x [P, M, K]) on the tensor cores whose
+    factors (F1T [P r, K] K-major, F2 [N, P r]) are kept in the cache for the
+    generation's replay, stored in the replay's (A, B) order."""
+    dev = x.device
+    ws = L.workspace(L.query("zg_batched_forward_workspace_size", P, M, K, N, rank), dev)
+    ckey = (gen.base, gen.start, gen.count, group, layout, rows, cols, rank, _T_TAG)
+    hit = cache.get(ckey)
+    if hit is not None:
+        F1T, F2 = hit if w_is_kn else (hit[1], hit[0])
+        L.call("zg_batched_forward_factors", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(F1T), L.ptr(F2), P, M, K, N,
+               rank, s, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+        return
+    F1T = torch.empty((P * rank, K), dtype=torch.bfloat16, device=dev)
+    F2 = torch.empty((N, P * rank), dtype=torch.bfloat16, device=dev)
+    L.call("zg_batched_forward_operands", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(_keys2d(keys)), group, P, M, K,
+           N, rank, s, L.ptr(F1T), L.ptr(F2), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    # MATRIX: A^T = F1T, B_op = F2;  tied TABLE: A_op = F2, B^T = F1T
+    cache.put(ckey, (F1T, F2) if w_is_kn else (F2, F1T), dev)
+
+
 def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
                   sigma: float, x_batched: bool) -> torch.Tensor:
     """y[p] = x_p @ W + s (x_p @ A_p) @ B_p; x [*M, K] shared or [P, *M, K]."""
@@ -301,6 +341,9 @@ def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, gro
     gen = CACHE.active_for(keys)
     if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, K, N, rank):
         _forward_cached(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y, gen)
+        return y
+    if gen is not None and dt == torch.bfloat16 and x_batched and _batched_ok(dev, P, K, N, rank):
+        _forward_batched(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y, gen)
         return y
     ws = L.workspace(L.query("zg_perturbed_linear_workspace_size", P, M, K, N, rank, code, int(x_batched)), dev)
     L.call("zg_perturbed_linear", L.ptr(x), int(x_batched), L.ptr(W), L.ptr(k), group, P, M, K, N, rank, s,
@@ -330,6 +373,9 @@ def launch_tied_logits(x: torch.Tensor, table: torch.Tensor, keys: torch.Tensor,
     if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, C, V, rank):
         # table factors: A_t [V, q] (rows), B_t [C, q] (cols)
         _forward_cached(x, T, False, k, group, L.ZG_TABLE, V, C, P, M, C, V, rank, s, y, gen)
+        return y
+    if gen is not None and dt == torch.bfloat16 and x_batched and _batched_ok(dev, P, C, V, rank):
+        _forward_batched(x, T, False, k, group, L.ZG_TABLE, V, C, P, M, C, V, rank, s, y, gen)
         return y
     ws = L.workspace(L.query("zg_tied_logits_workspace_size", P, M, V, C, rank, code, int(x_batched)), dev)
     L.call("zg_tied_logits", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, P, M, V, C, rank, s, code,
@@ -412,11 +458,15 @@ def launch_replay(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, lay
         out = torch.empty(tuple(int(d) for d in shape), dtype=torch.float32, device=dev)
     inv = scaled_factor_value(r, 1.0, dtype)
     if gen is not None and layout != L.ZG_VECTOR and dtype == torch.bfloat16 and group >= 0:
-        hit = cache.get((gen.base, gen.start, gen.count, group, layout, rows, cols, r))
+        key = (gen.base, gen.start, gen.count, group, layout, rows, cols, r)
+        found, hit = cache.find(key, key + (_T_TAG,))
         if hit is not None:
-            A_op, B_op = hit
-            ws = L.workspace(L.query("zg_replay_factors_workspace_size", P, rows, r), dev)
-            L.call("zg_replay_factors", L.ptr(w), L.ptr(A_op), L.ptr(B_op), P, rows, cols, r, inv, L.ptr(out),
+            A, B = hit
+            # factors of a per-candidate-input forward: MATRIX keeps A^T, TABLE keeps B^T
+            a_t = int(found[-1] == _T_TAG and layout == L.ZG_MATRIX)
+            b_t = int(found[-1] == _T_TAG and layout == L.ZG_TABLE)
+            ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, r), dev)
+            L.call("zg_replay_operands", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r, inv, L.ptr(out),
                    L.ptr(ws), ws.numel(), L.stream_ptr(dev))
             return out
     ws = L.workspace(L.query("zg_replay_workspace_size", P, layout, rows, cols, r, code), dev)

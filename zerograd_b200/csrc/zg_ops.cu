@@ -277,7 +277,9 @@ extern "C" size_t zg_perturbed_linear_workspace_size(int P, int M, int K, int N,
                                                      int x_batched) {
     if (P < 1 || M < 1 || K < 1 || N < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
     size_t simt_need = low_rank_ws(P, M, K, N, rank, dtype, x_batched, (int64_t)K * rank, (int64_t)rank * N);
-    size_t tc_need = (dtype == ZG_BF16 && !x_batched) ? zg::tc_shared_forward_workspace(P, M, K, N, rank) : 0;
+    size_t tc_need = 0;
+    if (dtype == ZG_BF16 && !x_batched) tc_need = zg::tc_shared_forward_workspace(P, M, K, N, rank);
+    if (dtype == ZG_BF16 && x_batched) tc_need = zg::batched_forward_workspace(P, M, K, N, rank, true);
     return simt_need > tc_need ? simt_need : tc_need;
 }
 
@@ -297,6 +299,9 @@ extern "C" int zg_perturbed_linear(const void* x, int x_batched, const void* W, 
         // W [K, N] row-major is the MN-major B operand of x @ W.
         return zg::tc_shared_forward(x, W, true, N, keys, group, P, M, K, N, rank, /*f1: A, k*r+j*/ 0, 0,
                                      /*f2: B, j*N+n*/ 1, 1, s, y, cv, st);
+    if (dtype == ZG_BF16 && x_batched && zg::batched_forward_ok(P, M, K, N, rank))
+        return zg::batched_forward(x, W, true, keys, group, /*f1: A, k*r+j*/ 0, /*f2: B, j*N+n*/ 1, 1, true, nullptr,
+                                   nullptr, P, M, K, N, rank, s, y, cv, st);
     size_t es = zg::dtype_size(dtype);
     char* fa = cv.take<char>((size_t)P * K * rank * es);
     char* fb = cv.take<char>((size_t)P * rank * N * es);
@@ -313,7 +318,9 @@ extern "C" size_t zg_tied_logits_workspace_size(int P, int M, int V, int C, int 
                                                 int x_batched) {
     if (P < 1 || M < 1 || V < 1 || C < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
     size_t simt_need = low_rank_ws(P, M, C, V, rank, dtype, x_batched, (int64_t)C * rank, (int64_t)V * rank);
-    size_t tc_need = (dtype == ZG_BF16 && !x_batched) ? zg::tc_shared_forward_workspace(P, M, C, V, rank) : 0;
+    size_t tc_need = 0;
+    if (dtype == ZG_BF16 && !x_batched) tc_need = zg::tc_shared_forward_workspace(P, M, C, V, rank);
+    if (dtype == ZG_BF16 && x_batched) tc_need = zg::batched_forward_workspace(P, M, C, V, rank, true);
     return simt_need > tc_need ? simt_need : tc_need;
 }
 
@@ -334,6 +341,9 @@ extern "C" int zg_tied_logits(const void* x, int x_batched, const void* T, const
         // counter c*r + j), expanded through A_t[v, j] (counter v*r + j).
         return zg::tc_shared_forward(x, T, false, C, keys, group, P, M, C, V, rank, /*f1: B*/ 1, 0,
                                      /*f2: A*/ 0, 0, s, y, cv, st);
+    if (dtype == ZG_BF16 && x_batched && zg::batched_forward_ok(P, M, C, V, rank))
+        return zg::batched_forward(x, T, false, keys, group, /*f1: B*/ 1, /*f2: A*/ 0, 0, true, nullptr, nullptr, P, M,
+                                   C, V, rank, s, y, cv, st);
     size_t es = zg::dtype_size(dtype);
     // table factors: A [P, V, r] (rows), B [P, C, r] (cols)
     char* fb = cv.take<char>((size_t)P * C * rank * es);

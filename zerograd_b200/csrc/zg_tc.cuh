@@ -1,11 +1,43 @@
 // zg_tc.cuh -- tensor-core (tcgen05 / TMEM / TMA) paths for sm_100a.
 #pragma once
+#include <cuda.h>
+
 #include "zg_common.cuh"
 
 namespace zg {
 
 // True on a compute-capability 10.0 device with the TMA descriptor encoder.
 bool tc_available();
+
+// bf16 TMA descriptor of `rank` dimensions (innermost first), byte strides of
+// dimensions 1.., box extents; 128-byte swizzle or none; out-of-bounds
+// elements read as zero.
+bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                     const uint32_t* box, bool swizzle128);
+
+// Kernel error word of the per-candidate-input kernels (0 = none).
+int batched_error_word(int clear);
+
+// Factor fill transposed to [P r, rows]: out[p*r + j, row] =
+// round_dtype(normal(key_p, row*r + j)) (the [rows, r] row-major factor of
+// candidate p, stored K-major for the tensor cores); bf16, rank 8 or 16.
+int fill_operand_t(const uint32_t* keys, int group, int P, int rank, int64_t rows, int which, void* out,
+                   cudaStream_t st, const char* name = "factor_fill");
+
+// Per-candidate-input population forward (bf16, rank 8 or 16):
+//   y[p] = x_p @ Wop + s (x_p @ F1_p) @ F2_p^T
+// x [P, M, K]; Wop [K, N] (w_mn_major) or [N, K]; F1T [P r, K]; F2 [N, P r].
+// The two kernels of that forward:
+//   U[p, m, 0:16] = bf16(s * x_p[m] . F1_p) (columns >= rank zero)
+//   y[p] = bf16(x_p . Wop + U_p . F2_p^T)
+int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank, float s, void* U, cudaStream_t st);
+int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U, const void* F2, int P, int M, int K,
+                 int N, int rank, void* y, cudaStream_t st);
+bool batched_forward_ok(int P, int M, int K, int N, int rank);
+size_t batched_forward_workspace(int P, int M, int K, int N, int rank, bool draw);
+int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint32_t* keys, int group, int f1_which,
+                    int f2_which, int f2_col_major, bool draw, const void* F1T, const void* F2, int P, int M, int K,
+                    int N, int rank, float s, void* y, Carver& cv, cudaStream_t st);
 
 // D[M,N] = alpha * A[M,K] . B^T; A K-major row-major (lda), B K-major
 // [N,K] (ldb) or MN-major [K,N] (ldb); D row-major float32 or bf16 (ldd).
@@ -40,6 +72,10 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
 // Replay of one MATRIX/TABLE entry as one GEMM over the P*r axis (bf16).
 bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype);
 size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank);
+int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
+                      int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
+int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
+                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
 int tc_replay_run(const float* shaped, const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols,
                   int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
 

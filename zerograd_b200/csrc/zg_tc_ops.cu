@@ -98,6 +98,39 @@ __global__ void fill_operand_r8_kernel(const uint32_t* __restrict__ keys, int gr
     }
 }
 
+// Transposed fill: out[(p*R + j) * rows + row] = bf16(normal(key_p, row*R + j)).
+// Thread = 8 consecutive rows of one candidate and all R ranks, so each of
+// its R stores is 16 bytes and a warp's stores for one j are 512 contiguous
+// bytes.  grid (row groups, P).
+template <int R>
+__global__ void fill_operand_t_kernel(const uint32_t* __restrict__ keys, int group, int64_t rows, int which,
+                                      __nv_bfloat16* __restrict__ out) {
+    const int p = blockIdx.y;
+    const int64_t row0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (row0 >= rows) return;
+    ZgFactorKeys fk = zg_factor_keys(keys, p, group);
+    const ZgKey k = which == 0 ? fk.a : fk.b;
+    const bool full = row0 + 8 <= rows && (rows % 8) == 0;
+#pragma unroll 1
+    for (int j = 0; j < R; ++j) {
+        uint64_t ctr[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ctr[i] = (uint64_t)(row0 + i) * R + j;
+        float v[8];
+        zg_normal_x8(k, ctr, v);
+        __nv_bfloat16* dst = out + ((int64_t)p * R + j) * rows + row0;
+        if (full) {
+            uint4 pk;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            *reinterpret_cast<uint4*>(dst) = pk;
+        } else {
+            for (int i = 0; i < 8 && row0 + i < rows; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+        }
+    }
+}
+
 template <typename T>
 __global__ void fill_operand_kernel(const uint32_t* __restrict__ keys, int group, int P, int rank, int64_t rows,
                                     int which, int col_major, const float* __restrict__ scale, float extra_scale,
@@ -407,6 +440,22 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
     return check_launch("fill_operand");
 }
 
+int fill_operand_t(const uint32_t* keys, int group, int P, int rank, int64_t rows, int which, void* out,
+                   cudaStream_t st, const char* name) {
+    if (rank != 8 && rank != 16) return fail(ZG_ERR_INVALID, "fill_operand_t: rank must be 8 or 16");
+    if (P < 1 || P > 65535 || rows < 1) return fail(ZG_ERR_INVALID, "fill_operand_t: bad sizes");
+    const int64_t gx = ((rows + 7) / 8 + 127) / 128;
+    if (gx > 2147483647) return fail(ZG_ERR_INVALID, "fill_operand_t: too many rows");
+    dim3 grid((unsigned)gx, (unsigned)P);
+    zg::LaunchTimer zg_lt_(name, st);
+    auto* o = static_cast<__nv_bfloat16*>(out);
+    if (rank == 8)
+        fill_operand_t_kernel<8><<<grid, 128, 0, st>>>(keys, group, rows, which, o);
+    else
+        fill_operand_t_kernel<16><<<grid, 128, 0, st>>>(keys, group, rows, which, o);
+    return check_launch("fill_operand_t");
+}
+
 int lowrank_expand(const float* XW, const float* U, const void* Bq, int P, int M, int N, int rank, float s, int dtype,
                    void* y, cudaStream_t st) {
     const int gx = (N + EX_BN - 1) / EX_BN, gy = (M + EX_BM - 1) / EX_BM;
@@ -558,6 +607,54 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
                                true, F1, F2, P, M, K, N, rank, s, y, cv, st);
 }
 
+bool batched_forward_ok(int P, int M, int K, int N, int rank) {
+    return tc_available() && (rank == 8 || rank == 16) && P > 0 && M > 0 && K % 8 == 0 && N % 8 == 0 &&
+           (int64_t)P * ((M + 127) / 128) * ((N + 255) / 256) <= 2147483647LL && (int64_t)P * rank <= 2147483647LL;
+}
+
+size_t batched_forward_workspace(int P, int M, int K, int N, int rank, bool draw) {
+    const size_t q = (size_t)P * rank;
+    size_t need = Carver::need({(size_t)P * M * 16 * 2});
+    if (draw) need += Carver::need({q * K * 2, (size_t)N * q * 2});
+    return need + 256;
+}
+
+// Per-candidate-input forward.  With `draw`, the factors are drawn into F1T /
+// F2 (carved from the workspace when null) first:
+//   caller stream: [fill F1T] -> u pass --------.-> gemm
+//   side stream:   [fill F2] -------------------'
+int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint32_t* keys, int group, int f1_which,
+                    int f2_which, int f2_col_major, bool draw, const void* F1T, const void* F2, int P, int M, int K,
+                    int N, int rank, float s, void* y, Carver& cv, cudaStream_t st) {
+    const int64_t q = (int64_t)P * rank;
+    __nv_bfloat16* U = cv.take<__nv_bfloat16>((size_t)P * M * 16);
+    if (draw && !F1T) F1T = cv.take<__nv_bfloat16>((size_t)q * K);
+    if (draw && !F2) F2 = cv.take<__nv_bfloat16>((size_t)N * q);
+    if (!U || !F1T || !F2) return fail(ZG_ERR_WORKSPACE, "batched forward: workspace too small");
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!al(x) || !al(Wop) || !al(F1T) || !al(F2) || !al(y))
+        return fail(ZG_ERR_INVALID, "batched forward: operands must be 16-byte aligned");
+    int rc = ZG_OK, rc_side = ZG_OK;
+    if (draw) {
+        SideStream* ss = side_stream();
+        if (!ss) return fail(ZG_ERR_CUDA, "batched forward: side stream");
+        std::lock_guard<std::mutex> lk(ss->mu);
+        if (cudaEventRecord(ss->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess)
+            return fail(ZG_ERR_CUDA, "batched forward: fork");
+        rc_side = fill_operand(keys, group, P, rank, N, f2_which, f2_col_major, nullptr, 1.f, ZG_BF16,
+                               const_cast<void*>(F2), ss->s, "factor_fill");
+        rc = fill_operand_t(keys, group, P, rank, K, f1_which, const_cast<void*>(F1T), st, "factor_fill");
+        if (!rc) rc = batched_u_pass(x, F1T, P, M, K, rank, s, U, st);
+        if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
+            return fail(ZG_ERR_CUDA, "batched forward: join");
+    } else {
+        rc = batched_u_pass(x, F1T, P, M, K, rank, s, U, st);
+    }
+    if (rc) return rc;
+    if (rc_side) return rc_side;
+    return batched_gemm(x, Wop, w_mn_major, U, F2, P, M, K, N, rank, y, st);
+}
+
 // Aw[row, q] = bf16(float(A[row, q]) * w[q / rank]): the reference's
 // weighted factor a_pop * shaped (src/zerograd/_replay.py:46) rounded to the
 // tensor-core operand type.
@@ -588,7 +685,92 @@ __global__ void scale_operand_kernel(const __nv_bfloat16* __restrict__ A, const 
     }
 }
 
+// Transposing form: Aw[row, q] = bf16(float(AT[q, row]) * w[q / rank]) for
+// an input-side factor kept K-major as AT [P r, rows].  64 x 64 tiles through
+// shared memory so both the reads and the writes are 16-byte coalesced.
+__global__ void __launch_bounds__(256)
+scale_operand_t_kernel(const __nv_bfloat16* __restrict__ AT, const float* __restrict__ w, int rank, int q,
+                       int64_t rows, __nv_bfloat16* __restrict__ out) {
+    __shared__ float tile[64][65];
+    const int64_t r0 = (int64_t)blockIdx.x * 64;
+    const int q0 = blockIdx.y * 64;
+    const int tid = threadIdx.x;
+    // read: 64 q rows x 64 row elements, 8 per thread-chunk, 2 chunks per thread
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int e = tid + it * 256;
+        const int qq = e / 8, c8 = (e % 8) * 8;
+        const int qg = q0 + qq;
+        float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (qg < q) {
+            const float wq = w[qg / rank];
+            if (r0 + c8 + 8 <= rows) {
+                bf16x8_to_f32(*reinterpret_cast<const uint4*>(AT + (int64_t)qg * rows + r0 + c8), f);
+            } else {
+                for (int i = 0; i < 8; ++i)
+                    if (r0 + c8 + i < rows) f[i] = __bfloat162float(AT[(int64_t)qg * rows + r0 + c8 + i]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __fmul_rn(f[i], wq);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) tile[qq][c8 + i] = f[i];
+    }
+    __syncthreads();
+    // write: 64 rows x 64 q, 8 q per thread-chunk
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int e = tid + it * 256;
+        const int rr = e / 8, c8 = (e % 8) * 8;
+        const int64_t row = r0 + rr;
+        if (row >= rows || q0 + c8 >= q) continue;
+        uint4 pk;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(tile[c8 + 2 * i][rr], tile[c8 + 2 * i + 1][rr]);
+        *reinterpret_cast<uint4*>(out + row * q + q0 + c8) = pk;  // q % 8 == 0
+    }
+}
+
 size_t tc_replay_factors_workspace(int P, int64_t rows, int rank) { return (size_t)rows * P * rank * 2 + 256; }
+
+// Replay from operand factors given in either layout: A [rows, P r] or, with
+// a_t, AT [P r, rows]; B [cols, P r] or, with b_t, BT [P r, cols] (then the
+// GEMM reads it as its MN-major operand).
+int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
+                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st) {
+    const int64_t q = (int64_t)P * rank;
+    if (!a_t && !b_t) return tc_replay_factors(shaped, A, B, P, rows, cols, rank, inv_sqrt_rank, out, cv, st);
+    __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
+    if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
+    if (q % 8 || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+        return fail(ZG_ERR_INVALID, "tc replay: operand alignment");
+    if (b_t && cols % 8) return fail(ZG_ERR_INVALID, "tc replay: transposed B needs cols % 8 == 0");
+    if (q > 2147483647 || rows > 2147483647 || cols > 2147483647)
+        return fail(ZG_ERR_INVALID, "tc replay: sizes too large");
+    int rc;
+    if (a_t) {
+        const int64_t gx = (rows + 63) / 64, gy = (q + 63) / 64;
+        if (gy > 65535 || gx > 2147483647) return fail(ZG_ERR_INVALID, "tc replay: transposed A too large");
+        zg::LaunchTimer zg_lt_("replay_scale", st);
+        scale_operand_t_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(A), shaped, rank, (int)q, rows, Aw);
+        rc = check_launch("replay_scale");
+    } else {
+        const unsigned gx = (unsigned)((q / 8 + 255) / 256);
+        int64_t gy = (int64_t)sm_count() * 32 / gx;
+        if (gy < 1) gy = 1;
+        if (gy > rows) gy = rows;
+        if (gy > 65535) gy = 65535;
+        zg::LaunchTimer zg_lt_("replay_scale", st);
+        scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A), shaped,
+                                                                     rank, (int)q, rows, Aw);
+        rc = check_launch("replay_scale");
+    }
+    if (rc) return rc;
+    return tc_gemm_bf16(Aw, q, B, b_t ? cols : q, b_t, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank,
+                        st, "replay_gemm");
+}
 
 int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
                       int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st) {
@@ -709,4 +891,75 @@ extern "C" int zg_replay_factors(const float* shaped, const void* A_op, const vo
     zg::Carver cv(workspace, workspace_bytes);
     return zg::tc_replay_factors(shaped, A_op, B_op, P, rows, cols, rank, inv_sqrt_rank, out, cv,
                                  zg::as_stream(stream));
+}
+
+// ===========================================================================
+// C ABI: per-candidate-input forward, replay from either factor layout
+// ===========================================================================
+
+extern "C" size_t zg_batched_forward_workspace_size(int P, int M, int K, int N, int rank) {
+    if (P < 1 || M < 1 || K < 1 || N < 1 || rank < 1) return 0;
+    return zg::batched_forward_workspace(P, M, K, N, rank, false);
+}
+
+static int batched_args_ok(const char* who, const void* x, const void* W, const void* F1T, const void* F2,
+                           const void* y, int P, int M, int K, int N, int rank) {
+    if (P < 1 || P > 65535 || M < 1 || K < 1 || N < 1 || rank < 1) return zg::fail(ZG_ERR_INVALID, "%s: bad sizes", who);
+    if (!x || !W || !F1T || !F2 || !y) return zg::fail(ZG_ERR_INVALID, "%s: null pointer", who);
+    if (!zg::batched_forward_ok(P, M, K, N, rank))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "%s: needs sm_100, rank 8 or 16, K and N multiples of 8", who);
+    return ZG_OK;
+}
+
+extern "C" int zg_batched_forward_factors(const void* x, const void* W, int w_is_kn, const void* F1T, const void* F2,
+                                          int P, int M, int K, int N, int rank, float s, void* y, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+    int rc = batched_args_ok("zg_batched_forward_factors", x, W, F1T, F2, y, P, M, K, N, rank);
+    if (rc) return rc;
+    const size_t need = zg::batched_forward_workspace(P, M, K, N, rank, false);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_batched_forward_factors: workspace %zu < %zu bytes", workspace_bytes,
+                        need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::batched_forward(x, W, w_is_kn != 0, nullptr, 0, 0, 0, 0, false, F1T, F2, P, M, K, N, rank, s, y, cv,
+                               zg::as_stream(stream));
+}
+
+extern "C" int zg_batched_forward_operands(const void* x, const void* W, int w_is_kn, const uint32_t* keys, int group,
+                                           int P, int M, int K, int N, int rank, float s, void* F1T, void* F2,
+                                           void* y, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = batched_args_ok("zg_batched_forward_operands", x, W, F1T, F2, y, P, M, K, N, rank);
+    if (rc) return rc;
+    if (!keys) return zg::fail(ZG_ERR_INVALID, "zg_batched_forward_operands: null keys");
+    const size_t need = zg::batched_forward_workspace(P, M, K, N, rank, false);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_batched_forward_operands: workspace %zu < %zu bytes", workspace_bytes,
+                        need);
+    zg::Carver cv(workspace, workspace_bytes);
+    // linear: F1T = A (counter k*r + j), F2 = B_op (counter j*N + n);
+    // tied table: F1T = table B (counter c*r + j), F2 = table A_op (counter v*r + j)
+    const bool kn = w_is_kn != 0;
+    return zg::batched_forward(x, W, kn, keys, group, kn ? 0 : 1, kn ? 1 : 0, kn ? 1 : 0, true, F1T, F2, P, M, K, N,
+                               rank, s, y, cv, zg::as_stream(stream));
+}
+
+extern "C" size_t zg_replay_operands_workspace_size(int P, int64_t rows, int rank) {
+    if (P < 1 || rows < 1 || rank < 1) return 0;
+    return zg::tc_replay_factors_workspace(P, rows, rank);
+}
+
+extern "C" int zg_replay_operands(const float* shaped, const void* A, int a_transposed, const void* B,
+                                  int b_transposed, int P, int64_t rows, int64_t cols, int rank, float inv_sqrt_rank,
+                                  float* out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1)
+        return zg::fail(ZG_ERR_INVALID, "zg_replay_operands: bad sizes");
+    if (!shaped || !A || !B || !out) return zg::fail(ZG_ERR_INVALID, "zg_replay_operands: null pointer");
+    if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "zg_replay_operands: needs sm_100 and P*rank a multiple of 8");
+    size_t need = zg::tc_replay_factors_workspace(P, rows, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_replay_operands: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::tc_replay_operands(shaped, A, a_transposed != 0, B, b_transposed != 0, P, rows, cols, rank,
+                                  inv_sqrt_rank, out, cv, zg::as_stream(stream));
 }
