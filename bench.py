@@ -151,6 +151,10 @@ def kernel_work(name: str, P_local: int, world: int = 1):
         return "hbm", P * r * K * 2
     if name == "sgd_update":          # read W bf16 + descent f32, write W bf16
         return "hbm", K * N * (2 + 4 + 2)
+    if name == "batched_gemm":        # per-candidate x_p W + the low-rank correction U_p B_p^T
+        return "tensor", 2.0 * P_local * M * K * N + 2.0 * P_local * M * r * N
+    if name == "batched_u_pass":      # reads every x_p once (bf16), writes U (bf16, 16 columns)
+        return "hbm", P_local * M * K * 2 + P_local * M * 16 * 2
     return None, None
 
 
@@ -366,6 +370,39 @@ def run_ours(args):
     e2e_ms = max_over_ranks(e2e_ms)
     barrier()
 
+    # the hidden-layer form of the same generation: every candidate has its own
+    # input x_p [256, 4096] (seeded N(0, 0.02)), so x_p W is a batched GEMM on
+    # the tensor cores; replay reuses the forward's factors; SGD update
+    gx = torch.Generator(device=dev).manual_seed(WL["seed"] + a)
+    xb_all = (torch.randn(P_local, M, K, generator=gx, device=dev) * 0.02).to(torch.bfloat16)
+
+    def hidden_step(W, gen):
+        cks, cks_local = keys[gen]
+        with _ops.generation_scope(bases[gen], a, P_local, cks_local):
+            y = _ops.launch_linear(xb_all, W, cks_local, 0, r, sigma, True)
+        losses = gather(fitness[a:b])
+        shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
+        d = _ops.launch_replay(shaped, cks, 0, L.ZG_MATRIX, (K, N), r, torch.bfloat16,
+                               gen=_ops._Generation(bases[gen], 0, P, cks))
+        _ops.CACHE.drop_generation(bases[gen])
+        W = _ops.launch_sgd(W, d, WL["lr"])
+        del y
+        return W
+
+    h_steps = max(1, min(args.steps, 50))
+    Wh = W0
+    for i in range(args.warmup):
+        Wh = hidden_step(Wh, i)
+    barrier()
+    h_ms, _ = timed(hidden_step, h_steps, W0)
+    h_ms = max_over_ranks(h_ms)
+    barrier()
+    L.profile_begin(1 << 14)
+    timed(hidden_step, h_steps, W0)
+    h_kernels = L.profile_end()
+    barrier()
+    del xb_all
+
     value = P * args.steps / (ms / 1e3)
     e2e_value = P * args.steps / (e2e_ms / 1e3)
     if rank == 0:
@@ -407,6 +444,23 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 4 * P_local,
                     "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms / args.steps},
         }
+        hg = h_kernels.get("batched_gemm")
+        hidden = {"workload": "same generation with a per-candidate input x_p[256,4096] (seeded N(0,0.02)): "
+                              "batched perturbed GEMM on the tensor cores, replay from the forward's factors, SGD",
+                  "value": P * h_steps / (h_ms / 1e3), "unit": UNIT, "steps": h_steps,
+                  "ms_per_step": h_ms / h_steps,
+                  "kernels_ms_per_step": {k: v[1] / h_steps for k, v in sorted(h_kernels.items())}}
+        if hg:
+            per = hg[1] / hg[0] / 1e3
+            ach = kernel_work("batched_gemm", P_local, world)[1] / per / 1e12
+            hidden["roofline"] = {"kernel": "batched_gemm", "bound": "tensor", "achieved": ach,
+                                  "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+                                  "peak_source": pk["source"], "launch_ms": hg[1] / hg[0]}
+            # the whole forward (factor draws + u pass + GEMM) against the same peak
+            fwd_ms = sum(h_kernels[k][1] for k in ("batched_gemm", "batched_u_pass") if k in h_kernels) / h_steps
+            flops = 2.0 * P_local * M * K * N + 2.0 * P_local * M * r * (K + N)
+            hidden["forward_tflops"] = flops / (fwd_ms / 1e3) / 1e12
+        line["hidden_layer"] = hidden
         if world == 1:
             secs = cpu_generation_sample(8)
             n_cand = max(1, min(64, int(8 * 15.0 / max(secs, 1e-3))))

@@ -170,3 +170,35 @@ def test_replay_factors_entry_matches_replay(cuda, oracle):
     cached = _ops.launch_replay(w, cks, 1, L.ZG_MATRIX, (K, N), r, torch.bfloat16, gen=gen)
     _ops.CACHE.drop_generation((7, 7))
     assert torch.equal(direct, cached)
+
+
+@pytest.mark.parametrize("rows,cols,P", [(1024, 1024, 64),     # 32 tiles: fewer than one wave
+                                         (6400, 1024, 32),     # 200 tiles: one wave and a partial one
+                                         (4096, 4096, 256),    # 512 tiles: the bench replay
+                                         (5504, 1792, 64),     # 301 tiles, ragged rows
+                                         (1280, 768, 40)])     # 30 tiles, 320-deep contraction
+def test_replay_factors_matches_fp32(cuda, rows, cols, P):
+    """The replay GEMM over P*r matches a float32 matmul of the same weighted
+    bf16 operands, and is identical from call to call."""
+    r = 8
+    q = P * r
+    g = torch.Generator().manual_seed(rows + cols + P)
+    A = torch.randn(rows, q, generator=g).to(torch.bfloat16).to(cuda)
+    B = torch.randn(cols, q, generator=g).to(torch.bfloat16).to(cuda)
+    w = torch.randn(P, generator=g).to(cuda)
+    ws = L.workspace(L.query("zg_replay_factors_workspace_size", P, rows, r), cuda)
+
+    def run():
+        out = torch.empty((rows, cols), dtype=torch.float32, device=cuda)
+        L.call("zg_replay_factors", L.ptr(w), L.ptr(A), L.ptr(B), P, rows, cols, r, 0.5, L.ptr(out), L.ptr(ws),
+               ws.numel(), L.stream_ptr(cuda))
+        return out
+
+    a = run()
+    b = run()
+    assert L.load().zg_device_error(1) == 0
+    assert torch.equal(a, b)
+    Aw = (A.float() * w.repeat_interleave(r)[None, :]).to(torch.bfloat16).float()
+    ref = 0.5 * (Aw @ B.float().t())
+    err = (a - ref).abs().max().item()
+    assert err <= 1e-3 * ref.abs().max().item(), err
