@@ -356,6 +356,224 @@ batched_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     if (warp == 1) tmem_dealloc(tmem_base, 512);
 }
 
+// ---------------------------------------------------------------------------
+// The same GEMM on CTA pairs: 256 x 256 tiles, CTA r of the pair stages rows
+// [128 r, 128 r + 128) of the x tile and columns [128 r, 128 r + 128) of the
+// Wop tile (32 KiB per K block, 6 stages), plus its halves of the correction
+// operands (U rows, F2 rows: 8 KiB per accumulator); the leader issues the
+// M=256 N=256 MMAs, the correction included, into both CTAs' TMEM.
+// ---------------------------------------------------------------------------
+constexpr int BP_STAGES = 6;
+constexpr uint32_t BP_A = BM * BK * 2;                             // 16 KiB: 128 rows of x
+constexpr uint32_t BP_B = 128 * BK * 2;                            // 16 KiB: 128 columns of Wop
+constexpr uint32_t BP_STAGE = BP_A + BP_B;                         // 32 KiB
+constexpr uint32_t BP_CU = 128 * 16;                               // 8 K columns of 128 U rows
+constexpr uint32_t BP_CF = 128 * 16;                               // 8 K columns of 128 F2 rows
+constexpr uint32_t BP_CORR = 2 * BP_CU + 2 * BP_CF;                // 8 KiB per accumulator
+constexpr uint32_t BP_SMEM = BP_STAGES * BP_STAGE + 2 * BP_CORR;   // 208 KiB
+
+template <bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                         const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmF,
+                         const GemmArgs a) {
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ __align__(8) uint64_t full_bar[BP_STAGES], empty_bar[BP_STAGES], tmem_full[2], tmem_empty[2],
+        corr_full[2], corr_empty[2], mma_done;
+    __shared__ uint32_t tmem_base_sh;
+    const uint32_t dyn_base = smem_u32(dyn_smem);
+    uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
+    uint8_t* corr = smem + BP_STAGES * BP_STAGE;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_rank();
+    const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+    const int num_tiles = a.P * a.tiles_m * a.tiles_n;  // tiles of 256 x 256
+    const int k_blocks = (a.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < BP_STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], 8);  // 4 epilogue warps in each CTA
+            mbar_init(&corr_full[b], 1);
+            mbar_init(&corr_empty[b], 1);
+        }
+        mbar_init(&mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc_pair(&tmem_base_sh, 512);
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        int stage = 0, acc = 0;
+        uint32_t phase = 0, acc_phase = 0;
+        uint32_t issued = 0, issue_parity = 0, c_issued = 0, c_parity = 0;
+        bool ok = true;
+        const int half = (int)rank * 128;
+        for (int t = pair; ok && t < num_tiles; t += pairs) {
+            const int tn = t % a.tiles_n, rest = t / a.tiles_n;
+            const int tm = rest % a.tiles_m, p = rest / a.tiles_m;
+            if (!mbar_wait(&corr_empty[acc], acc_phase ^ 1, 51)) break;
+            uint8_t* c = corr + acc * BP_CORR;
+            if (rank == 0) mbar_expect_tx(&corr_full[acc], 2 * BP_CORR);
+            const uint32_t cb = cluster_addr(&corr_full[acc], 0);
+            tma_load_3d_pair(c, &tmU, cb, 0, tm * 256 + half, p);
+            tma_load_3d_pair(c + BP_CU, &tmU, cb, 8, tm * 256 + half, p);
+            tma_load_2d_pair(c + 2 * BP_CU, &tmF, cb, p * a.rank, tn * 256 + half);
+            tma_load_2d_pair(c + 2 * BP_CU + BP_CF, &tmF, cb, p * a.rank + 8, tn * 256 + half);
+            c_issued |= 1u << acc;
+            c_parity = (c_parity & ~(1u << acc)) | (acc_phase << acc);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+            const int k_start = t % k_blocks;
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1, 52)) { ok = false; break; }
+                const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
+                uint8_t* sa = smem + stage * BP_STAGE;
+                uint8_t* sb = sa + BP_A;
+                if (rank == 0) mbar_expect_tx(&full_bar[stage], 2 * BP_STAGE);
+                const uint32_t fb = cluster_addr(&full_bar[stage], 0);
+                tma_load_3d_pair(sa, &tmX, fb, kk * BK, tm * 256 + half, p);
+                if constexpr (B_MN) {
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+                        tma_load_2d_pair(sb + cc * (64 * BK * 2), &tmW, fb, tn * 256 + half + cc * 64, kk * BK);
+                } else {
+                    tma_load_2d_pair(sb, &tmW, fb, kk * BK, tn * 256 + half);
+                }
+                issued |= 1u << stage;
+                issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == BP_STAGES) { stage = 0; phase ^= 1; }
+            }
+        }
+        // Drain: the leader sees the bytes land on its full barriers; the peer
+        // sees its buffers released by the MMAs that consumed them.
+        for (int s = 0; s < BP_STAGES; ++s)
+            if (issued & (1u << s)) {
+                uint64_t* bar = rank == 0 ? &full_bar[s] : &empty_bar[s];
+                for (uint32_t i = 0; i < kSpinLimit; ++i)
+                    if (mbar_try_wait(bar, (issue_parity >> s) & 1)) break;
+            }
+        for (int b = 0; b < 2; ++b)
+            if (c_issued & (1u << b)) {
+                uint64_t* bar = rank == 0 ? &corr_full[b] : &corr_empty[b];
+                for (uint32_t i = 0; i < kSpinLimit; ++i)
+                    if (mbar_try_wait(bar, (c_parity >> b) & 1)) break;
+            }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---------------- MMA issuer (leader only) ----------------
+        constexpr uint32_t IDESC = idesc_bf16(256, 256, B_MN ? 1 : 0);
+        constexpr uint32_t IDESC_C = idesc_bf16(256, 256, 0);
+        int stage = 0, acc = 0;
+        uint32_t phase = 0, acc_phase = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < num_tiles; t += pairs) {
+            if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, 53)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * 256;
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                if (!mbar_wait(&full_bar[stage], phase, 54)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + stage * BP_STAGE);
+                const uint32_t b_addr = a_addr + BP_A;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) {
+                    const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                             : smem_desc(b_addr + k * 32, 16, 1024);
+                    umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit_pair(smem_u32(&empty_bar[stage]));
+                umma_commit_pair(cluster_addr(&empty_bar[stage], 1));
+                if (++stage == BP_STAGES) { stage = 0; phase ^= 1; }
+            }
+            if (!ok) break;
+            if (!mbar_wait(&corr_full[acc], acc_phase, 55)) break;
+            tc_fence_after();
+            const uint32_t c_addr = smem_u32(corr + acc * BP_CORR);
+            umma_bf16_pair(d_tmem, smem_desc_noswizzle(c_addr, BP_CU, 128),
+                           smem_desc_noswizzle(c_addr + 2 * BP_CU, BP_CF, 128), IDESC_C, 1u);
+            umma_commit_pair(smem_u32(&corr_empty[acc]));
+            umma_commit_pair(cluster_addr(&corr_empty[acc], 1));
+            umma_commit_pair(smem_u32(&tmem_full[acc]));
+            umma_commit_pair(cluster_addr(&tmem_full[acc], 1));
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+        umma_commit_pair(smem_u32(&mma_done));
+        for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(&mma_done, 0)) break;
+    } else if (warp >= 2) {
+        // ---------------- epilogue (both CTAs, own TMEM rows) ----------------
+        const int quad = warp % 4;
+        const uint32_t empty_leader = cluster_addr(&tmem_empty[0], 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = pair; t < num_tiles; t += pairs) {
+            if (!mbar_wait(&tmem_full[acc], acc_phase, 56)) break;
+            tc_fence_after();
+            const int tn = t % a.tiles_n, rest = t / a.tiles_n;
+            const int tm = rest % a.tiles_m, p = rest / a.tiles_m;
+            const int row = tm * 256 + (int)rank * 128 + quad * 32 + lane;
+            __nv_bfloat16* yrow = a.y + ((int64_t)p * a.M + row) * a.N;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 256; c0 += 32) {
+                float v[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + c0, v);
+                const int col0 = tn * 256 + c0;
+                if (row >= a.M || col0 >= a.N) continue;
+                __nv_bfloat16* d = yrow + col0;
+                if (col0 + 32 <= a.N) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        __nv_bfloat162 h[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[i + 2 * j], v[i + 2 * j + 1]);
+                        *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
+                    }
+                } else {
+                    for (int i = 0; i < 32 && col0 + i < a.N; ++i) d[i] = __float2bfloat16_rn(v[i]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
+}
+
+// CTA pairs that can be resident at once for the pair kernel (0 if unknown).
+template <bool B_MN>
+int batched_pair_slots() {
+    static int n = -1;
+    if (n < 0) {
+        constexpr size_t smem = (size_t)BP_SMEM + 1024;
+        n = 0;
+        if (cudaFuncSetAttribute(batched_gemm_pair_kernel<B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * 74, 1, 1);
+            cfg.blockDim = dim3(THREADS, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, batched_gemm_pair_kernel<B_MN>, &cfg) == cudaSuccess)
+                n = clusters;
+        }
+        cudaGetLastError();
+    }
+    return n;
+}
+
 }  // namespace
 
 namespace zg {
@@ -415,6 +633,38 @@ int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U,
     const uint32_t bf[2] = {8, BG_BN};
     ok = ok && tensor_map_bf16(&tu, U, 3, du, su, bu, false) && tensor_map_bf16(&tf, F2, 2, df, sf, bf, false);
     if (!ok) return fail(ZG_ERR_CUDA, "batched_gemm: tensor maps");
+    const int slots = w_mn_major ? batched_pair_slots<true>() : batched_pair_slots<false>();
+    const int64_t pair_tiles = (int64_t)P * ((M + 255) / 256) * ((N + 255) / 256);
+    if (slots > 0 && pair_tiles >= slots && pair_tiles <= INT_MAX) {
+        // CTA pairs: each CTA loads 128 of the 256 x / U rows and 128 of the 256 Wop / F2 columns
+        CUtensorMap tx2, tw2, tu2, tf2;
+        const uint32_t bx2[3] = {BK, BM, 1};
+        bool ok2 = tensor_map_bf16(&tx2, x, 3, dx, sx, bx2, true);
+        if (w_mn_major) {
+            const uint64_t dw[2] = {(uint64_t)N, (uint64_t)K};
+            const uint64_t sw[1] = {(uint64_t)N * 2};
+            const uint32_t bw[2] = {64, BK};
+            ok2 = ok2 && tensor_map_bf16(&tw2, Wop, 2, dw, sw, bw, true);
+        } else {
+            const uint64_t dw[2] = {(uint64_t)K, (uint64_t)N};
+            const uint64_t sw[1] = {(uint64_t)K * 2};
+            const uint32_t bw[2] = {BK, 128};
+            ok2 = ok2 && tensor_map_bf16(&tw2, Wop, 2, dw, sw, bw, true);
+        }
+        const uint32_t bu2[3] = {8, 128, 1};
+        const uint32_t bf2[2] = {8, 128};
+        ok2 = ok2 && tensor_map_bf16(&tu2, U, 3, du, su, bu2, false) && tensor_map_bf16(&tf2, F2, 2, df, sf, bf2, false);
+        if (!ok2) return fail(ZG_ERR_CUDA, "batched_gemm: tensor maps");
+        GemmArgs a2{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + 255) / 256, (N + 255) / 256};
+        const int pairs = pair_tiles < slots ? (int)pair_tiles : slots;
+        const size_t smem2 = BP_SMEM + 1024;
+        zg::LaunchTimer zg_lt_("batched_gemm", st);
+        if (w_mn_major)
+            batched_gemm_pair_kernel<true><<<2 * pairs, THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, a2);
+        else
+            batched_gemm_pair_kernel<false><<<2 * pairs, THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, a2);
+        return check_launch("batched_gemm");
+    }
     GemmArgs a{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + BM - 1) / BM, (N + BG_BN - 1) / BG_BN};
     const int64_t tiles = (int64_t)P * a.tiles_m * a.tiles_n;
     if (tiles > INT_MAX) return fail(ZG_ERR_INVALID, "batched_gemm: too many tiles");

@@ -45,6 +45,38 @@ struct TcArgs {
     int tiles_m, tiles_n;
 };
 
+// alpha * v[0..32) -> D[row, col0 .. col0+32), bounds-checked against M and N.
+__device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0, const float (&v)[32]) {
+    if (row >= args.M || col0 >= args.N) return;
+    if (args.out_bf16) {
+        __nv_bfloat16* d = static_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd + col0;
+        if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+                __nv_bfloat162 h[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    h[j] = __floats2bfloat162_rn(args.alpha * v[i + 2 * j], args.alpha * v[i + 2 * j + 1]);
+                *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
+            }
+        } else {
+            for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) d[i] = __float2bfloat16_rn(args.alpha * v[i]);
+        }
+    } else {
+        float* d = static_cast<float*>(args.D) + (int64_t)row * args.ldd + col0;
+        if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(d + i) = make_float4(args.alpha * v[i], args.alpha * v[i + 1],
+                                                                args.alpha * v[i + 2], args.alpha * v[i + 3]);
+        } else {
+            for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) d[i] = args.alpha * v[i];
+        }
+    }
+}
+
 template <int BN, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs args) {
@@ -175,37 +207,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, v);
-                const int col0 = tn * BN + c0;
-                if (row < args.M) {
-                    if (args.out_bf16) {
-                        __nv_bfloat16* d = static_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd + col0;
-                        if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 8) {
-                                __nv_bfloat162 h[4];
-#pragma unroll
-                                for (int j = 0; j < 4; ++j)
-                                    h[j] = __floats2bfloat162_rn(args.alpha * v[i + 2 * j], args.alpha * v[i + 2 * j + 1]);
-                                *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
-                            }
-                        } else {
-                            for (int i = 0; i < 32; ++i)
-                                if (col0 + i < args.N) d[i] = __float2bfloat16_rn(args.alpha * v[i]);
-                        }
-                    } else {
-                        float* d = static_cast<float*>(args.D) + (int64_t)row * args.ldd + col0;
-                        if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 4)
-                                *reinterpret_cast<float4*>(d + i) =
-                                    make_float4(args.alpha * v[i], args.alpha * v[i + 1], args.alpha * v[i + 2],
-                                                args.alpha * v[i + 3]);
-                        } else {
-                            for (int i = 0; i < 32; ++i)
-                                if (col0 + i < args.N) d[i] = args.alpha * v[i];
-                        }
-                    }
-                }
+                tc_store32(args, row, tn * BN + c0, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -217,6 +219,161 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair GEMM: 256 x 256 tiles on a cluster of two CTAs (two SMs).  CTA r
+// of the pair stages rows [128 r, 128 r + 128) of the A tile and columns
+// [128 r, 128 r + 128) of the B tile in its own shared memory; the leader
+// (r = 0) issues M=256 N=256 MMAs that read both CTAs' halves, and CTA r's
+// TMEM accumulates tile rows [128 r, 128 r + 128).  Per 64-deep K block each
+// SM stages 32 KiB instead of the 48 KiB of a one-SM 128 x 256 tile, so the
+// L2 -> SM traffic per FLOP drops by a third.
+// Barriers: full[s] (leader's; counts both CTAs' bytes), empty[s] (each CTA;
+// one commit from the leader), tmem_full[a] (each CTA; one commit),
+// tmem_empty[a] (leader's; one arrival per epilogue warp of either CTA).
+// ---------------------------------------------------------------------------
+constexpr int P2_STAGES = 6;
+constexpr uint32_t P2_A = BM * BK * 2;           // this CTA's 128 rows of the A tile
+constexpr uint32_t P2_B = 128 * BK * 2;          // this CTA's 128 columns of the B tile
+constexpr uint32_t P2_STAGE = P2_A + P2_B;       // 32 KiB
+constexpr uint32_t P2_SMEM = P2_STAGES * P2_STAGE;
+
+template <bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const TcArgs args) {
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ __align__(8) uint64_t full_bar[P2_STAGES], empty_bar[P2_STAGES], tmem_full[2], tmem_empty[2],
+        mma_done;
+    __shared__ uint32_t tmem_base_sh;
+    const uint32_t dyn_base = smem_u32(dyn_smem);
+    uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_rank();
+    const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+    const int num_tiles = args.tiles_m * args.tiles_n;
+    const int k_blocks = (args.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P2_STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 8);  // 4 epilogue warps in each CTA
+        }
+        mbar_init(&mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc_pair(&tmem_base_sh, 512);
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        int stage = 0;
+        uint32_t phase = 0, issued = 0, issue_parity = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < num_tiles; t += pairs) {
+            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            const int k_start = t % k_blocks;
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1, 21)) { ok = false; break; }
+                const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
+                uint8_t* sa = smem + stage * P2_STAGE;
+                uint8_t* sb = sa + P2_A;
+                if (rank == 0) mbar_expect_tx(&full_bar[stage], 2 * P2_STAGE);
+                const uint32_t fb = cluster_addr(&full_bar[stage], 0);
+                tma_load_2d_pair(sa, &tmA, fb, kk * BK, tm * 256 + (int)rank * 128);
+                if constexpr (B_MN) {
+#pragma unroll
+                    for (int c = 0; c < 2; ++c)
+                        tma_load_2d_pair(sb + c * (64 * BK * 2), &tmB, fb, tn * 256 + (int)rank * 128 + c * 64,
+                                         kk * BK);
+                } else {
+                    tma_load_2d_pair(sb, &tmB, fb, kk * BK, tn * 256 + (int)rank * 128);
+                }
+                issued |= 1u << stage;
+                issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == P2_STAGES) { stage = 0; phase ^= 1; }
+            }
+        }
+        // Drain: the leader sees its stages' bytes land on its full barriers;
+        // the peer sees each stage released by the MMAs that consumed it.
+        for (int s = 0; s < P2_STAGES; ++s)
+            if (issued & (1u << s)) {
+                uint64_t* bar = rank == 0 ? &full_bar[s] : &empty_bar[s];
+                for (uint32_t i = 0; i < kSpinLimit; ++i)
+                    if (mbar_try_wait(bar, (issue_parity >> s) & 1)) break;
+            }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---------------- MMA issuer (leader only) ----------------
+        constexpr uint32_t IDESC = idesc_bf16(256, 256, B_MN ? 1 : 0);
+        int stage = 0, acc = 0;
+        uint32_t phase = 0, acc_phase = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < num_tiles; t += pairs) {
+            if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, 22)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * 256;
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                if (!mbar_wait(&full_bar[stage], phase, 23)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + stage * P2_STAGE);
+                const uint32_t b_addr = a_addr + P2_A;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) {
+                    const uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                             : smem_desc(b_addr + k * 32, 16, 1024);
+                    umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                }
+                // the stage is free in both CTAs once these MMAs complete
+                umma_commit_pair(smem_u32(&empty_bar[stage]));
+                umma_commit_pair(cluster_addr(&empty_bar[stage], 1));
+                if (++stage == P2_STAGES) { stage = 0; phase ^= 1; }
+            }
+            if (!ok) break;
+            umma_commit_pair(smem_u32(&tmem_full[acc]));
+            umma_commit_pair(cluster_addr(&tmem_full[acc], 1));
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+        umma_commit_pair(smem_u32(&mma_done));
+        for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(&mma_done, 0)) break;
+    } else if (warp >= 2) {
+        // ---------------- epilogue (both CTAs, own TMEM rows) ----------------
+        const int quad = warp % 4;
+        const uint32_t empty_leader = cluster_addr(&tmem_empty[0], 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = pair; t < num_tiles; t += pairs) {
+            if (!mbar_wait(&tmem_full[acc], acc_phase, 24)) break;
+            tc_fence_after();
+            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            const int row = tm * 256 + (int)rank * 128 + quad * 32 + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 256; c0 += 32) {
+                float v[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + c0, v);
+                tc_store32(args, row, tn * 256 + c0, v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+    }
+    // All pair MMAs have completed (the leader waited on mma_done) and both
+    // CTAs' epilogues are done with TMEM before either frees it.
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -508,6 +665,39 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& a, cud
     return zg::check_launch("tc_gemm");
 }
 
+// CTA pairs that can be resident at once for the pair kernel (0 if unknown).
+template <bool B_MN>
+int pair_slots() {
+    static int n = -1;
+    if (n < 0) {
+        constexpr size_t smem = (size_t)P2_SMEM + 1024;
+        n = 0;
+        if (cudaFuncSetAttribute(tc_gemm_pair_kernel<B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+            cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * 74, 1, 1);
+            cfg.blockDim = dim3(THREADS, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel<B_MN>, &cfg) == cudaSuccess)
+                n = clusters;
+        }
+        cudaGetLastError();
+    }
+    return n;
+}
+
+template <bool B_MN>
+int launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& a, int slots, cudaStream_t st,
+                   const char* name) {
+    constexpr size_t smem = (size_t)P2_SMEM + 1024;
+    const int tiles = a.tiles_m * a.tiles_n;
+    const int pairs = tiles < slots ? tiles : slots;
+    zg::LaunchTimer zg_lt_(name, st);
+    tc_gemm_pair_kernel<B_MN><<<2 * pairs, THREADS, smem, st>>>(ta, tb, a);
+    return zg::check_launch("tc_gemm_pair");
+}
+
 }  // namespace
 
 namespace zg {
@@ -559,6 +749,16 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
     if (cost(64, 1.6) < best) { bn = 64; }
     CUtensorMap ta, tb;
     if (!make_map(&ta, A, K, M, lda, BK, BM)) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map A");
+    // At least one full wave of 256 x 256 tiles: CTA pairs (cta_group::2).
+    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const int slots = b_mn_major ? pair_slots<true>() : pair_slots<false>();
+    if (slots > 0 && pair_tiles >= slots) {
+        bool okp = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, 128);
+        if (!okp) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
+        TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + 255) / 256, (N + 255) / 256};
+        return b_mn_major ? launch_tc_pair<true>(ta, tb, a, slots, st, name)
+                          : launch_tc_pair<false>(ta, tb, a, slots, st, name);
+    }
     bool okb = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
     if (!okb) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
     TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + BM - 1) / BM, (N + bn - 1) / bn};
