@@ -53,8 +53,9 @@ def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         p = json.load(open(path))
-        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 # ---------------------------------------------------------------------------
@@ -156,6 +157,17 @@ def kernel_work(name: str, P_local: int, world: int = 1):
     if name == "batched_u_pass":      # reads every x_p once (bf16), writes U (bf16, 16 columns)
         return "hbm", P_local * M * K * 2 + P_local * M * 16 * 2
     return None, None
+
+
+def traffic_for(name: str):
+    """DRAM bytes per launch of a kernel from the committed ncu summary, or None."""
+    tpath = os.path.join(ROOT, "profiles", "traffic.txt")
+    if os.path.exists(tpath):
+        for tl in open(tpath):
+            parts = tl.split()
+            if len(parts) == 2 and not tl.startswith("#") and parts[0] == name:
+                return int(parts[1])
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -394,9 +406,12 @@ def run_ours(args):
     for i in range(args.warmup):
         Wh = hidden_step(Wh, i)
     barrier()
-    h_ms, _ = timed(hidden_step, h_steps, W0)
+    with ClockSampler(dev) as h_clk:
+        barrier()
+        h_ms, _ = timed(hidden_step, h_steps, W0)
+        barrier()
     h_ms = max_over_ranks(h_ms)
-    barrier()
+    h_clocks = h_clk.summary()
     L.profile_begin(1 << 14)
     timed(hidden_step, h_steps, W0)
     h_kernels = L.profile_end()
@@ -418,13 +433,7 @@ def run_ours(args):
                 ach, peak, unit = work / per / 1e9, pk["hbm_gbs"], "GB/s"
             else:
                 ach, peak, unit = work / per / 1e12, pk["bf16_tflops"], "TFLOP/s"
-            traffic = None
-            tpath = os.path.join(ROOT, "profiles", "traffic.txt")
-            if os.path.exists(tpath):
-                for tl in open(tpath):
-                    parts = tl.split()
-                    if len(parts) == 2 and not tl.startswith("#") and parts[0] == name:
-                        traffic = int(parts[1])
+            traffic = traffic_for(name)
             roof = {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                     "frac": ach / peak, "traffic": traffic, "peak_source": pk["source"],
                     "launch_ms": tot / n, "launches": n}
@@ -448,14 +457,19 @@ def run_ours(args):
         hidden = {"workload": "same generation with a per-candidate input x_p[256,4096] (seeded N(0,0.02)): "
                               "batched perturbed GEMM on the tensor cores, replay from the forward's factors, SGD",
                   "value": P * h_steps / (h_ms / 1e3), "unit": UNIT, "steps": h_steps,
-                  "ms_per_step": h_ms / h_steps,
+                  "ms_per_step": h_ms / h_steps, "clocks": h_clocks,
                   "kernels_ms_per_step": {k: v[1] / h_steps for k, v in sorted(h_kernels.items())}}
         if hg:
             per = hg[1] / hg[0] / 1e3
             ach = kernel_work("batched_gemm", P_local, world)[1] / per / 1e12
+            # the loop keeps the tensor cores busy for ~0.1 s, so the sustained
+            # (power-capped) peak is the matching denominator; the burst one is shown too
             hidden["roofline"] = {"kernel": "batched_gemm", "bound": "tensor", "achieved": ach,
-                                  "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
-                                  "peak_source": pk["source"], "launch_ms": hg[1] / hg[0]}
+                                  "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                                  "frac": ach / pk["bf16_tflops_sustained"],
+                                  "frac_of_burst_peak": ach / pk["bf16_tflops"],
+                                  "traffic": traffic_for("batched_gemm"),
+                                  "peak_source": pk["source"] + " (sustained)", "launch_ms": hg[1] / hg[0]}
             # the whole forward (factor draws + u pass + GEMM) against the same peak
             fwd_ms = sum(h_kernels[k][1] for k in ("batched_gemm", "batched_u_pass") if k in h_kernels) / h_steps
             flops = 2.0 * P_local * M * K * N + 2.0 * P_local * M * r * (K + N)
