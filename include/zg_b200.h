@@ -312,7 +312,7 @@ ZG_API int zg_sgd_update(const void* param, void* param_out, int dtype, const fl
  * examples/train_qat_xor.py:41-50):
  *   acc = x_p @ W (int8 x int8 -> int32, exact)
  *   y   = acc * x_scale * w_scale[n] + s * ((x_p @ A_p) @ B_p)[m,n]   (float32)
- *   q   = clamp(rint(y / y_scale), -128, 127);  out = lut[q + 128]   (int8)
+ *   q   = clamp(rint(y / y_scale), -128, 127), 0 for NaN;  out = lut[q + 128]   (int8)
  * x [M,K] shared or [P,M,K]; W [K,N] int8; w_scale [N] float32; lut [256]
  * int8; out [P,M,N] int8.  A_p/B_p are matrix factors (float32 draws) of
  * the weight's group.  acc_out (optional, [P,M,N] int32) receives the

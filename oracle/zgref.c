@@ -283,7 +283,8 @@ static void i8_range(void* c, int64_t b, int64_t e) {
             for (int j = 0; j < a->rank; ++j) lr = fmaf(u[j], a->Bf[j * N + n], lr);
             float y = fmaf((float)acc * a->x_scale, a->w_scale[n], a->s * lr);
             float qf = rintf(y / a->y_scale);
-            int q = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
+            /* a NaN pre-activation quantises to 0 (defined here; the C cast is not) */
+            int q = qf != qf ? 0 : (qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf));
             a->out[m * N + n] = a->lut[q + 128];
         }
     }

@@ -82,7 +82,7 @@ float zgo_round_bf16(float x);
  *   acc[m,n]  = sum_k x[m,k] * W[k,n]                 (int64 accumulate, exact)
  *   y         = acc * x_scale * w_scale[n] + s * sum_j u[m,j] * Bf[j,n]
  *               with u[m,j] = sum_k x[m,k] * A[k,j]    (float32 math, fixed order)
- *   q         = clamp(rint(y / y_scale), -128, 127)
+ *   q         = clamp(rint(y / y_scale), -128, 127), 0 when that is NaN
  *   out[m,n]  = lut[q + 128]
  * acc_out (optional, may be NULL) receives the int32 accumulators. */
 void zgo_int8_lut_linear(const int8_t* x, const int8_t* W, const float* w_scale,

@@ -822,7 +822,7 @@ extern "C" int zg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t l
 
 extern "C" int zg_device_error(int clear) {
     // one error word per translation unit with tensor-core kernels
-    const int a = ptx_error_word(clear), b = zg::batched_error_word(clear);
-    if (a < 0 || b < 0) return -1;
-    return a ? a : b;
+    const int a = ptx_error_word(clear), b = zg::batched_error_word(clear), c = zg::int8_error_word(clear);
+    if (a < 0 || b < 0 || c < 0) return -1;
+    return a ? a : (b ? b : c);
 }

@@ -15,8 +15,9 @@ bool tc_available();
 bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                      const uint32_t* box, bool swizzle128);
 
-// Kernel error word of the per-candidate-input kernels (0 = none).
+// Kernel error words of the per-candidate-input and int8 kernels (0 = none).
 int batched_error_word(int clear);
+int int8_error_word(int clear);
 
 // Factor fill transposed to [P r, rows]: out[p*r + j, row] =
 // round_dtype(normal(key_p, row*r + j)) (the [rows, r] row-major factor of
