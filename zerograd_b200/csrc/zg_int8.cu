@@ -14,7 +14,8 @@
 // exact int32 accumulators in TMEM) with the scale / low-rank / rint / LUT
 // steps fused into its epilogue; a CUDA-core kernel covers shapes the TMA
 // layout rules exclude (K or N not a multiple of 16).  u uses one thread per
-// (candidate, row) with the oracle's sequential order.
+// (candidate, row) with the oracle's sequential order, its input staged
+// through shared memory.
 #include <cudaTypedefs.h>
 
 #include <climits>
@@ -45,38 +46,74 @@ __global__ void int8_u_kernel(const int8_t* __restrict__ x, int x_batched, const
 }
 
 // u[p,m,0:R]: one thread per (candidate, row), the R sums advanced together
-// in k order (the oracle's order), 16-byte loads of the int8 row.
+// in k order (the oracle's order).  A block of 128 rows stages the input in
+// 128-byte K slabs through shared memory (coalesced 16-byte loads; rows
+// padded to 144 bytes so a quarter-warp's 16-byte reads hit distinct banks)
+// together with the slab's A_p rows, read as broadcasts.
+constexpr int U_ROWS = 128, U_SLAB = 128, U_PITCH = 144;
+
+// float(b) of a signed byte without the conversion unit (exact).
+__device__ __forceinline__ float s8_to_f32(uint32_t word, int byte) {
+    const int b = (int)(int8_t)(uint8_t)(word >> (8 * byte));
+    return __fsub_rn(__int_as_float(0x4B400000 + b), 12582912.0f);
+}
+
 template <int R>
-__global__ void int8_u_rows_kernel(const int8_t* __restrict__ x, int x_batched, const float* __restrict__ A, int M,
-                                   int K, float* __restrict__ U) {
-    const int p = blockIdx.y;
-    const int m = blockIdx.x * blockDim.x + threadIdx.x;
-    if (m >= M) return;
-    const int8_t* xr = x + (x_batched ? (int64_t)p * M * K : 0) + (int64_t)m * K;
-    const float* a = A + (int64_t)p * K * R;
+__global__ void __launch_bounds__(U_ROWS)
+int8_u_tile_kernel(const int8_t* __restrict__ x, int x_batched, const float* __restrict__ A, int M, int K,
+                   float* __restrict__ U) {
+    __shared__ __align__(16) int8_t xs[U_ROWS][U_PITCH];
+    __shared__ __align__(16) float as[U_SLAB][R];
+    const int p = blockIdx.y, m0 = blockIdx.x * U_ROWS, tid = threadIdx.x;
+    const int8_t* xp = x + (x_batched ? (int64_t)p * M * K : 0);
+    const float* ap = A + (int64_t)p * K * R;
+    const bool vec = (K % 16) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     float acc[R];
 #pragma unroll
     for (int j = 0; j < R; ++j) acc[j] = 0.f;
-    int k = 0;
-    if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
-        for (; k + 16 <= K; k += 16) {
-            const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-            const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+    for (int k0 = 0; k0 < K; k0 += U_SLAB) {
+        __syncthreads();
+        for (int c = tid; c < U_ROWS * (U_SLAB / 16); c += U_ROWS) {
+            const int r = c / (U_SLAB / 16), q = c % (U_SLAB / 16);
+            const int m = m0 + r, k = k0 + q * 16;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (m < M) {
+                const int8_t* src = xp + (int64_t)m * K + k;
+                if (vec && k + 16 <= K) {
+                    v = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    int8_t tmp[16];
 #pragma unroll
-            for (int kk = 0; kk < 16; ++kk) {
-                const float xv = (float)b[kk];
+                    for (int i = 0; i < 16; ++i) tmp[i] = k + i < K ? src[i] : (int8_t)0;
+                    v = *reinterpret_cast<const uint4*>(tmp);
+                }
+            }
+            *reinterpret_cast<uint4*>(&xs[r][q * 16]) = v;
+        }
+        for (int e = tid; e < U_SLAB * R; e += U_ROWS) {
+            const int kk = e / R, j = e % R;
+            as[kk][j] = k0 + kk < K ? ap[(int64_t)(k0 + kk) * R + j] : 0.f;
+        }
+        __syncthreads();
+        const int kw = K - k0 < U_SLAB ? K - k0 : U_SLAB;
+        // zero-padded bytes past K are never folded in: the loop stops at kw
+        for (int kk0 = 0; kk0 < kw; kk0 += 16) {
+            const uint4 v = *reinterpret_cast<const uint4*>(&xs[tid][kk0]);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int j = 0; j < R; ++j) acc[j] = __fmaf_rn(xv, a[(int64_t)(k + kk) * R + j], acc[j]);
+            for (int i = 0; i < 16; ++i) {
+                if (kk0 + i < kw) {
+                    const float xv = s8_to_f32(w[i / 4], i % 4);
+#pragma unroll
+                    for (int j = 0; j < R; ++j) acc[j] = __fmaf_rn(xv, as[kk0 + i][j], acc[j]);
+                }
             }
         }
     }
-    for (; k < K; ++k) {
-        const float xv = (float)xr[k];
+    if (m0 + tid < M) {
 #pragma unroll
-        for (int j = 0; j < R; ++j) acc[j] = __fmaf_rn(xv, a[(int64_t)k * R + j], acc[j]);
+        for (int j = 0; j < R; ++j) U[((int64_t)p * M + m0 + tid) * R + j] = acc[j];
     }
-#pragma unroll
-    for (int j = 0; j < R; ++j) U[((int64_t)p * M + m) * R + j] = acc[j];
 }
 
 constexpr int BM = 64, BN = 64, BK = 32, THREADS = 256;
@@ -158,7 +195,6 @@ constexpr uint32_t I8_A = I8_BM * I8_BK;              // 16 KiB
 constexpr uint32_t I8_B = I8_BN * I8_BK;              // 32 KiB: two 128-column blocks
 constexpr uint32_t I8_STAGE = I8_A + I8_B;            // 48 KiB
 constexpr uint32_t I8_SMEM = I8_STAGES * I8_STAGE;    // 192 KiB
-constexpr int I8_MAX_RANK = 16;
 
 // Instruction descriptor, kind::i8: D s32, A and B signed 8-bit, A K-major,
 // B MN-major (b_mn = 1), N >> 3, M >> 4.
@@ -187,14 +223,12 @@ __device__ __forceinline__ float s32_to_f32_rn(int a) {
     return __fmaf_rn(hf, 65536.0f, lf);
 }
 
-// clamp((int)rintf(v), -128, 127) with (int)NaN = 0: adding 1.5 * 2^23
-// rounds v to the nearest integer (ties to even) in the low mantissa bits
-// for |v| < 2^22; larger magnitudes and infinities land on the right side
-// of the clamp.
+// clamp((int)rintf(v), -128, 127) with (int)NaN = 0.  Clamping to the
+// integer bounds first commutes with rounding; adding 1.5 * 2^23 then rounds
+// to the nearest integer (ties to even) into the low mantissa bits.
 __device__ __forceinline__ int rint_clamp_s8(float v) {
-    if (v != v) return 0;
-    const int q = __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
-    return min(max(q, -128), 127);
+    const float c = v != v ? 0.f : fminf(fmaxf(v, -128.f), 127.f);
+    return __float_as_int(__fadd_rn(c, 12582912.0f)) - 0x4B400000;
 }
 
 struct I8Args {
@@ -224,8 +258,9 @@ __device__ __forceinline__ bool epi8_all(bool v) {
     return out != 0;
 }
 
-// POW2: y_scale is a power of two, so y / y_scale is exactly y * y_inv.
-template <bool POW2>
+// R: the perturbation rank; POW2: y_scale is a power of two, so y / y_scale
+// is exactly y * y_inv.
+template <int R, bool POW2>
 __global__ void __launch_bounds__(I8_THREADS, 1)
 int8_lut_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                    const I8Args a) {
@@ -235,7 +270,7 @@ int8_lut_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constan
     __shared__ uint32_t tmem_base_sh;
     __shared__ int8_t slut[256];
     __shared__ __align__(16) float s_wsc[I8_BN];
-    __shared__ __align__(16) float s_b[I8_MAX_RANK][I8_BN];
+    __shared__ __align__(16) float s_b[R][I8_BN];
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -356,14 +391,13 @@ int8_lut_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constan
             for (int p = p0; p < p1; ++p) {
                 epi8_bar();  // previous candidate's reads of s_b are done (and s_wsc written)
                 const float* bp = a.Bf + (int64_t)p * a.rank * a.N;
-                for (int e = et; e < a.rank * I8_BN; e += 256) {
+                for (int e = et; e < R * I8_BN; e += 256) {
                     const int j = e / I8_BN, nl = e % I8_BN, n = n0 + nl;
                     s_b[j][nl] = n < a.N ? bp[(int64_t)j * a.N + n] : 0.f;
                 }
-                float ur[I8_MAX_RANK];
+                float ur[R];
 #pragma unroll
-                for (int j = 0; j < I8_MAX_RANK; ++j)
-                    ur[j] = (j < a.rank && row < a.M) ? a.U[((int64_t)p * a.M + row) * a.rank + j] : 0.f;
+                for (int j = 0; j < R; ++j) ur[j] = row < a.M ? a.U[((int64_t)p * a.M + row) * R + j] : 0.f;
                 epi8_bar();
 #pragma unroll 1
                 for (int c0 = 0; c0 < 128; c0 += 32) {
@@ -378,14 +412,12 @@ int8_lut_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constan
                         const float4 w4 = *reinterpret_cast<const float4*>(&s_wsc[nl0 + i4]);
                         float lr[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int j = 0; j < I8_MAX_RANK; ++j) {
-                            if (j < a.rank) {
-                                const float4 b4 = *reinterpret_cast<const float4*>(&s_b[j][nl0 + i4]);
-                                lr[0] = __fmaf_rn(ur[j], b4.x, lr[0]);
-                                lr[1] = __fmaf_rn(ur[j], b4.y, lr[1]);
-                                lr[2] = __fmaf_rn(ur[j], b4.z, lr[2]);
-                                lr[3] = __fmaf_rn(ur[j], b4.w, lr[3]);
-                            }
+                        for (int j = 0; j < R; ++j) {
+                            const float4 b4 = *reinterpret_cast<const float4*>(&s_b[j][nl0 + i4]);
+                            lr[0] = __fmaf_rn(ur[j], b4.x, lr[0]);
+                            lr[1] = __fmaf_rn(ur[j], b4.y, lr[1]);
+                            lr[2] = __fmaf_rn(ur[j], b4.z, lr[2]);
+                            lr[3] = __fmaf_rn(ur[j], b4.w, lr[3]);
                         }
                         const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
                         uint32_t word = 0;
@@ -489,7 +521,17 @@ int launch_int8_tc(const int8_t* x, int x_batched, const int8_t* W, const I8Args
     if (tiles > INT_MAX) return zg::fail(ZG_ERR_INVALID, "int8 tc: too many tiles");
     const int grid = tiles < sm_count_i8() ? (int)tiles : sm_count_i8();
     const size_t smem = I8_SMEM + 1024;
-    auto kern = a.y_inv != 0.f ? int8_lut_tc_kernel<true> : int8_lut_tc_kernel<false>;
+    using Kern = void (*)(const CUtensorMap, const CUtensorMap, const I8Args);
+    Kern kern = nullptr;
+    const bool p2 = a.y_inv != 0.f;
+    switch (a.rank) {
+        case 1: kern = p2 ? int8_lut_tc_kernel<1, true> : int8_lut_tc_kernel<1, false>; break;
+        case 2: kern = p2 ? int8_lut_tc_kernel<2, true> : int8_lut_tc_kernel<2, false>; break;
+        case 4: kern = p2 ? int8_lut_tc_kernel<4, true> : int8_lut_tc_kernel<4, false>; break;
+        case 8: kern = p2 ? int8_lut_tc_kernel<8, true> : int8_lut_tc_kernel<8, false>; break;
+        case 16: kern = p2 ? int8_lut_tc_kernel<16, true> : int8_lut_tc_kernel<16, false>; break;
+        default: return zg::fail(ZG_ERR_INVALID, "int8 tc: rank %d", a.rank);
+    }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return zg::fail(ZG_ERR_CUDA, "int8 tc: shared memory attribute");
     zg::LaunchTimer zg_lt_("int8_lut_gemm", st);
@@ -530,13 +572,13 @@ extern "C" int zg_int8_lut_linear(const int8_t* x, int x_batched, const int8_t* 
     if (rc) return rc;
     {
         zg::LaunchTimer zg_lt_("int8_u", st);
-        dim3 rgrid((unsigned)((M + 127) / 128), P);
+        dim3 rgrid((unsigned)((M + U_ROWS - 1) / U_ROWS), P);
         switch (rank) {
-            case 1: int8_u_rows_kernel<1><<<rgrid, 128, 0, st>>>(x, x_batched, fa, M, K, U); break;
-            case 2: int8_u_rows_kernel<2><<<rgrid, 128, 0, st>>>(x, x_batched, fa, M, K, U); break;
-            case 4: int8_u_rows_kernel<4><<<rgrid, 128, 0, st>>>(x, x_batched, fa, M, K, U); break;
-            case 8: int8_u_rows_kernel<8><<<rgrid, 128, 0, st>>>(x, x_batched, fa, M, K, U); break;
-            case 16: int8_u_rows_kernel<16><<<rgrid, 128, 0, st>>>(x, x_batched, fa, M, K, U); break;
+            case 1: int8_u_tile_kernel<1><<<rgrid, U_ROWS, 0, st>>>(x, x_batched, fa, M, K, U); break;
+            case 2: int8_u_tile_kernel<2><<<rgrid, U_ROWS, 0, st>>>(x, x_batched, fa, M, K, U); break;
+            case 4: int8_u_tile_kernel<4><<<rgrid, U_ROWS, 0, st>>>(x, x_batched, fa, M, K, U); break;
+            case 8: int8_u_tile_kernel<8><<<rgrid, U_ROWS, 0, st>>>(x, x_batched, fa, M, K, U); break;
+            case 16: int8_u_tile_kernel<16><<<rgrid, U_ROWS, 0, st>>>(x, x_batched, fa, M, K, U); break;
             default: {
                 int64_t n = (int64_t)M * rank;
                 dim3 grid((unsigned)((n + 127) / 128), P);
@@ -547,7 +589,8 @@ extern "C" int zg_int8_lut_linear(const int8_t* x, int x_batched, const int8_t* 
     }
     // tensor cores when the TMA layout rules hold (16-byte aligned rows)
     const bool al = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0;
-    if (zg::tc_available() && K % 16 == 0 && N % 16 == 0 && rank <= I8_MAX_RANK && al) {
+    const bool tc_rank = rank == 1 || rank == 2 || rank == 4 || rank == 8 || rank == 16;
+    if (zg::tc_available() && K % 16 == 0 && N % 16 == 0 && tc_rank && al) {
         int e2 = 0;
         const float mant = frexpf(y_scale, &e2);
         const float y_inv = (mant == 0.5f && e2 > -125 && e2 < 126) ? ldexpf(1.f, 1 - e2) : 0.f;
