@@ -6,8 +6,9 @@ rank 8, a shared bf16 input x[256,4096] (N(0, 0.02)) through W[4096,4096]
 (N(0, 0.02)) plus sigma*(x A_i) B_i^T per candidate (sigma 0.01, factors from
 the threefry keys of seed 0, generation 0 onwards), every candidate's output
 [256,4096] materialised in HBM; then the fitness (N(0,1), shaped by the
-reference's centred-loss rule), factor replay of W's pseudo-gradient and an
-SGD update.  One step = one generation.  Synthetic data, fixed seeds.
+reference's centred-loss rule), factor replay of W's pseudo-gradient with the
+SGD update applied in the replay GEMM's epilogue.  One step = one generation.
+Synthetic data, fixed seeds.
 
 `python bench.py [--gpus N --steps K --warmup W]` prints one JSON line.  With
 N > 1 (one process per GPU under torch.distributed.run) the population is
@@ -170,6 +171,59 @@ def traffic_for(name: str):
     return None
 
 
+def int8_layer_section(dev, args):
+    """The integer QAT MLP's 4096 -> 4096 layer (batch 512 int8 inputs per
+    candidate, P=512, rank 4): int8 x int8 -> int32 on the tensor cores, the
+    float32 low-rank term, rint and the 256-entry tanh LUT in the epilogue.
+    Seeded synthetic int8 inputs/weights (U[-127,127]), per-channel scales
+    U[0.5,1.5]/127.  Inputs (1 GiB) exceed L2, so no flush is needed."""
+    import torch
+
+    import zerograd_b200 as zg
+    from zerograd_b200 import _lib as L
+    from zerograd_b200 import _ops
+
+    P8, M8, K8, N8, r8 = 512, 512, 4096, 4096, 4
+    g = torch.Generator(device=dev).manual_seed(3)
+    x8 = torch.randint(-127, 128, (P8, M8, K8), generator=g, device=dev, dtype=torch.int8)
+    W8 = torch.randint(-127, 128, (K8, N8), generator=g, device=dev, dtype=torch.int8)
+    ws8 = (torch.rand(N8, generator=g, device=dev) + 0.5) / 127
+    q = torch.arange(-128, 128, dtype=torch.float64, device=dev)
+    lut = torch.round(127 * torch.tanh(q / 32)).to(torch.int8)
+    keys8 = _ops.launch_fold_in(zg.step_key(0, "qat", 0, 1), torch.arange(P8, dtype=torch.int32, device=dev))
+
+    def run():
+        return _ops.launch_int8_lut_linear(x8, W8, ws8, 1 / 127, 1 / 32, lut, keys8, 1, r8, 0.01, True)
+
+    for _ in range(max(3, min(args.warmup, 5))):
+        run()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record()
+        for _ in range(steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    L.profile_begin()
+    for _ in range(steps):
+        run()
+    kern = L.profile_end()
+    pk = peaks()
+    ops = 2.0 * P8 * M8 * K8 * N8
+    gm = kern["int8_lut_gemm"][1] / kern["int8_lut_gemm"][0]
+    peak = 2.0 * pk["bf16_tflops"]  # dense int8 issues at twice the bf16 rate
+    return {"workload": "int8 QAT layer 4096->4096, P=512, batch 512 per candidate, rank 4, tanh LUT",
+            "ms_per_layer": ms, "candidate_layers_per_sec": P8 / (ms / 1e3), "clocks": clk.summary(),
+            "kernels_ms": {k: v[1] / v[0] for k, v in sorted(kern.items())},
+            "roofline": {"kernel": "int8_lut_gemm", "bound": "tensor", "achieved": ops / (gm / 1e3) / 1e12,
+                         "peak": peak, "unit": "TOP/s", "frac": ops / (gm / 1e3) / 1e12 / peak,
+                         "peak_source": "2x measured bf16 dense (no measured int8 figure)",
+                         "launch_ms": gm}}
+
+
 # ---------------------------------------------------------------------------
 # CPU arm: the oracle restatement of the reference on a bounded sample
 # ---------------------------------------------------------------------------
@@ -301,10 +355,10 @@ def run_ours(args):
             y = _ops.launch_linear(x, W, cks_local, 0, r, sigma, False)
         losses = gather(fitness[a:b])
         shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
-        d = _ops.launch_replay(shaped, cks, 0, L.ZG_MATRIX, (K, N), r, torch.bfloat16,
-                               gen=_ops._Generation(bases[gen], 0, P, cks))
+        # replay with the SGD step in the replay GEMM's epilogue (what ZeroGrad.step runs)
+        W, _, _ = _ops.launch_replay_step(shaped, cks, 0, L.ZG_MATRIX, W, r, {"kind": "sgd", "lr": WL["lr"]},
+                                          gen=_ops._Generation(bases[gen], 0, P, cks))
         _ops.CACHE.drop_generation(bases[gen])
-        W = _ops.launch_sgd(W, d, WL["lr"])
         del y
         return W
 
@@ -394,10 +448,10 @@ def run_ours(args):
             y = _ops.launch_linear(xb_all, W, cks_local, 0, r, sigma, True)
         losses = gather(fitness[a:b])
         shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
-        d = _ops.launch_replay(shaped, cks, 0, L.ZG_MATRIX, (K, N), r, torch.bfloat16,
-                               gen=_ops._Generation(bases[gen], 0, P, cks))
+        # replay with the SGD step in the replay GEMM's epilogue (what ZeroGrad.step runs)
+        W, _, _ = _ops.launch_replay_step(shaped, cks, 0, L.ZG_MATRIX, W, r, {"kind": "sgd", "lr": WL["lr"]},
+                                          gen=_ops._Generation(bases[gen], 0, P, cks))
         _ops.CACHE.drop_generation(bases[gen])
-        W = _ops.launch_sgd(W, d, WL["lr"])
         del y
         return W
 
@@ -475,6 +529,8 @@ def run_ours(args):
             flops = 2.0 * P_local * M * K * N + 2.0 * P_local * M * r * (K + N)
             hidden["forward_tflops"] = flops / (fwd_ms / 1e3) / 1e12
         line["hidden_layer"] = hidden
+        if world == 1:
+            line["int8_qat_layer"] = int8_layer_section(dev, args)
         if world == 1:
             secs = cpu_generation_sample(8)
             n_cand = max(1, min(64, int(8 * 15.0 / max(secs, 1e-3))))

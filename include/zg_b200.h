@@ -174,6 +174,30 @@ ZG_API int zg_replay_operands(const float* shaped, const void* A, int a_transpos
                               float inv_sqrt_rank, float* out, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Replay with the optimizer step fused into the replay GEMM's epilogue
+ * (bf16 operands as for zg_replay_operands): the descent d of every element
+ * of the entry's parameter [rows, cols] is formed in float32 and consumed in
+ * place by the step, so it never round-trips through memory:
+ *   SGD:   param_out = param + (-lr) * (-d)                (optax.sgd)
+ *   AdamW: mu_out, nu_out, param_out as zg_adamw_update   (optax.adamw)
+ * on the pseudo-gradient -d, bit-identical to zg_replay_operands followed by
+ * zg_sgd_update / zg_adamw_update.  param in `dtype` (float32 or bf16),
+ * moments float32, all [rows, cols] row-major; descent_out (optional) also
+ * receives d.  Workspace: zg_replay_operands_workspace_size.  Replaces
+ * replay_entry + transform.update + apply_updates
+ * (src/zerograd/_replay.py:44-54, src/zerograd/_optimizer.py:229-234). */
+ZG_API int zg_replay_sgd(const float* shaped, const void* A, int a_transposed, const void* B,
+                         int b_transposed, int P, int64_t rows, int64_t cols, int rank,
+                         float inv_sqrt_rank, const void* param, void* param_out, int dtype,
+                         double lr, float* descent_out, void* workspace, size_t workspace_bytes,
+                         void* stream);
+ZG_API int zg_replay_adamw(const float* shaped, const void* A, int a_transposed, const void* B,
+                           int b_transposed, int P, int64_t rows, int64_t cols, int rank,
+                           float inv_sqrt_rank, const void* param, void* param_out, int dtype,
+                           const float* mu, const float* nu, float* mu_out, float* nu_out, int count,
+                           double lr, double b1, double b2, double eps, double weight_decay,
+                           float* descent_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Per-candidate-input population forward (bf16, tcgen05), the hidden-layer
  * case: x [P, M, K] (one input per candidate), y [P, M, N],
  *   y[p] = x_p @ Wop + s * (x_p @ F1_p) @ F2_p^T

@@ -475,6 +475,57 @@ def launch_replay(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, lay
     return out
 
 
+def _replay_operands_for(cand_keys, group, layout, rows, cols, rank, gen, cache):
+    """(A, a_transposed, B, b_transposed) bf16 replay operands of one entry:
+    the forward's cached factors when present, else freshly drawn."""
+    if gen is not None and group >= 0:
+        key = (gen.base, gen.start, gen.count, group, layout, rows, cols, rank)
+        found, hit = cache.find(key, key + (_T_TAG,))
+        if hit is not None:
+            t = found[-1] == _T_TAG
+            return hit[0], int(t and layout == L.ZG_MATRIX), hit[1], int(t and layout == L.ZG_TABLE)
+    A, B = operand_factors(cand_keys, group, layout, rows, cols, rank)
+    return A, 0, B, 0
+
+
+def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, layout: int, param: torch.Tensor,
+                       rank: int, step: dict, gen: _Generation | None = None, cache: FactorCache = CACHE):
+    """Replay of one MATRIX/TABLE entry with the optimizer step fused into the
+    replay GEMM's epilogue (bf16 parameters on the tensor cores).  `step`:
+    {"kind": "sgd", "lr"} or {"kind": "adamw", "lr", "b1", "b2", "eps",
+    "weight_decay", "count", "mu", "nu"}.  Returns (new param, new mu, new nu)
+    -- the moments None for SGD -- or None when the fused path does not apply
+    (the caller then replays and updates separately, with identical results)."""
+    dev = L.require_cuda(shaped, cand_keys, param)
+    k = _keys2d(cand_keys)
+    P = k.shape[0]
+    if (layout == L.ZG_VECTOR or param.dtype != torch.bfloat16 or param.ndim != 2 or not param.is_contiguous()
+            or torch.cuda.get_device_capability(dev) != (10, 0) or (P * rank) % 8 != 0):
+        return None
+    rows, cols = (int(d) for d in param.shape)
+    w = shaped.to(torch.float32).contiguous()
+    if w.numel() != P:
+        raise ValueError("shaped weights and candidate keys differ in length")
+    A, a_t, B, b_t = _replay_operands_for(k, group, layout, rows, cols, rank, gen, cache)
+    if b_t and cols % 8:
+        return None
+    inv = scaled_factor_value(rank, 1.0, param.dtype)
+    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, rank), dev)
+    out = torch.empty_like(param)
+    st = L.stream_ptr(dev)
+    if step["kind"] == "sgd":
+        L.call("zg_replay_sgd", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, rank, inv, L.ptr(param),
+               L.ptr(out), L.ZG_BF16, float(step["lr"]), None, L.ptr(ws), ws.numel(), st)
+        return out, None, None
+    mu_out = torch.empty_like(step["mu"])
+    nu_out = torch.empty_like(step["nu"])
+    L.call("zg_replay_adamw", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, rank, inv, L.ptr(param),
+           L.ptr(out), L.ZG_BF16, L.ptr(step["mu"].contiguous()), L.ptr(step["nu"].contiguous()), L.ptr(mu_out),
+           L.ptr(nu_out), int(step["count"]), float(step["lr"]), float(step["b1"]), float(step["b2"]),
+           float(step["eps"]), float(step["weight_decay"]), None, L.ptr(ws), ws.numel(), st)
+    return out, mu_out, nu_out
+
+
 def launch_adamw(param: torch.Tensor, descent: torch.Tensor | None, mu: torch.Tensor, nu: torch.Tensor,
                  count: int, lr: float, b1: float, b2: float, eps: float, weight_decay: float):
     dev = L.require_cuda(param, descent, mu, nu)

@@ -24,7 +24,7 @@ from ._fitness import _check_shape_dtype
 from ._keys import key as make_key
 from ._keys import step_key
 from ._manifest import Manifest, ParameterTree
-from ._replay import candidate_keys, replay_entry_keys
+from ._replay import candidate_keys, replay_entry_keys, replay_entry_step
 from ._transforms import _leaves, apply_updates, is_fused, tree_get, tree_set
 
 LossFn = Callable[[ParameterTree, CandidateContext, Any, torch.Tensor], tuple[torch.Tensor, Any]]
@@ -187,12 +187,21 @@ class ZeroGrad:
             cand_keys = candidate_keys(base, ids)
         gen = _ops._Generation(base_words, 0, self._population_size, cand_keys)
         descent: dict = {}
+        fused = is_fused(self._transform)
+        done: dict = {}
         for entry in self._manifest.entries:
+            if fused:
+                # the optimizer step in the replay GEMM's epilogue (bf16 MATRIX/TABLE)
+                res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank,
+                                        self._transform.step_spec(state.opt_state, entry.path), gen)
+                if res is not None:
+                    done[tuple(entry.path)] = res
+                    continue
             tree_set(descent, entry.path,
                      replay_entry_keys(params, self._manifest, entry.path, cand_keys, shaped, self._rank, gen))
         _ops.CACHE.drop_generation(base_words)
-        if is_fused(self._transform):
-            new_params, new_opt_state = self._transform.apply(params, descent, state.opt_state)
+        if fused:
+            new_params, new_opt_state = self._transform.apply(params, descent, state.opt_state, done)
         else:
             grads = _build_pseudo_grad(descent, params)
             updates, new_opt_state = self._transform.update(grads, state.opt_state, params)

@@ -35,6 +35,19 @@ def replay_entry_keys(params: ParameterTree, manifest: Manifest, path: Parameter
                               parameter.dtype, gen=gen)
 
 
+def replay_entry_step(params: ParameterTree, manifest: Manifest, path: ParameterPath, cand_keys: torch.Tensor,
+                      shaped_weights: torch.Tensor, rank: int, step: dict, gen=None):
+    """Replay of one entry with the optimizer step fused in: (param, mu, nu)
+    or None where the fused form does not apply (VECTOR entries, float32
+    leaves), in which case the caller replays and steps separately."""
+    entry = manifest.entry(path)
+    if entry.layout is ParameterLayout.VECTOR:
+        return None
+    parameter = manifest.resolve(params, path)
+    return _ops.launch_replay_step(shaped_weights, cand_keys, manifest.group_index(entry.group),
+                                   LAYOUT_CODE[entry.layout], parameter, rank, step, gen=gen)
+
+
 def replay_entry(params: ParameterTree, manifest: Manifest, path: ParameterPath, base_key: torch.Tensor,
                  candidate_ids: torch.Tensor, shaped_weights: torch.Tensor, rank: int) -> torch.Tensor:
     """``_replay.py:15-54``."""

@@ -67,13 +67,27 @@ class adamw:
                 tree_set(nu, path, torch.zeros(p.shape, dtype=torch.float32, device=p.device))
         return AdamWState(count=0, mu=mu, nu=nu)
 
-    def apply(self, params: dict, descent: dict, state: AdamWState):
-        """New params and state from the descent tree (missing leaf: zero gradient)."""
+    def step_spec(self, state: AdamWState, path) -> dict:
+        """The step of one leaf, for a replay that applies it in its epilogue."""
+        return {"kind": "adamw", "lr": self.learning_rate, "b1": self.b1, "b2": self.b2, "eps": self.eps,
+                "weight_decay": self.weight_decay, "count": state.count + 1, "mu": tree_get(state.mu, path),
+                "nu": tree_get(state.nu, path)}
+
+    def apply(self, params: dict, descent: dict, state: AdamWState, done: dict | None = None):
+        """New params and state from the descent tree (missing leaf: zero
+        gradient); `done` maps leaf paths already stepped by a fused replay to
+        their (param, mu, nu)."""
         count = state.count + 1
         new_p, mu, nu = {}, {}, {}
         for path, p in _leaves(params):
             if not isinstance(p, torch.Tensor):
                 tree_set(new_p, path, p)
+                continue
+            if done and path in done:
+                pn, m, v = done[path]
+                tree_set(new_p, path, pn)
+                tree_set(mu, path, m)
+                tree_set(nu, path, v)
                 continue
             d = tree_get(descent, path)
             pn, m, v = _ops.launch_adamw(p, d, tree_get(state.mu, path), tree_get(state.nu, path), count,
@@ -98,11 +112,17 @@ class sgd:
     def init(self, params: dict) -> SgdState:
         return SgdState()
 
-    def apply(self, params: dict, descent: dict, state: SgdState):
+    def step_spec(self, state: SgdState, path) -> dict:
+        return {"kind": "sgd", "lr": self.learning_rate}
+
+    def apply(self, params: dict, descent: dict, state: SgdState, done: dict | None = None):
         new_p = {}
         for path, p in _leaves(params):
             if not isinstance(p, torch.Tensor):
                 tree_set(new_p, path, p)
+                continue
+            if done and path in done:
+                tree_set(new_p, path, done[path][0])
                 continue
             tree_set(new_p, path, _ops.launch_sgd(p, tree_get(descent, path), self.learning_rate))
         return new_p, SgdState(count=state.count + 1)

@@ -12,6 +12,7 @@
 
 #include "zg_simt.cuh"
 #include "zg_tc.cuh"
+#include "zg_update.cuh"
 
 namespace zg {
 int launch_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
@@ -226,29 +227,19 @@ __global__ void vector_replay_kernel(const float* __restrict__ w, const uint32_t
 // ---------------------------------------------------------------------------
 // fused optimizer updates
 // ---------------------------------------------------------------------------
-struct AdamConsts {
-    float omb1, b1, omb2, b2, bc1, bc2, eps, wd, neg_lr;
-};
-
 template <typename T>
 __global__ void adamw_kernel(const T* __restrict__ param, T* __restrict__ param_out,
                              const float* __restrict__ descent, const float* __restrict__ mu,
                              const float* __restrict__ nu, float* __restrict__ mu_out,
-                             float* __restrict__ nu_out, int64_t n, AdamConsts c) {
+                             float* __restrict__ nu_out, int64_t n, zg::AdamConsts c) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float g = descent ? -descent[i] : 0.f;  // pseudo_grad = -descent
-        const float p = zg_to_float(param[i]);
-        const float m = __fadd_rn(__fmul_rn(c.omb1, g), __fmul_rn(c.b1, mu[i]));
-        const float v = __fadd_rn(__fmul_rn(c.omb2, __fmul_rn(g, g)), __fmul_rn(c.b2, nu[i]));
+        float m, v;
+        const float pn = zg::adamw_step(zg_to_float(param[i]), g, mu[i], nu[i], c, m, v);
         mu_out[i] = m;
         nu_out[i] = v;
-        const float mh = __fdiv_rn(m, c.bc1);
-        const float vh = __fdiv_rn(v, c.bc2);
-        float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), c.eps));
-        u = __fadd_rn(u, __fmul_rn(c.wd, p));
-        u = __fmul_rn(u, c.neg_lr);
-        param_out[i] = zg_from_float<T>(__fadd_rn(p, u));
+        param_out[i] = zg_from_float<T>(pn);
     }
 }
 
@@ -258,7 +249,7 @@ __global__ void sgd_kernel(const T* __restrict__ param, T* __restrict__ param_ou
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float g = descent ? -descent[i] : 0.f;
-        param_out[i] = zg_from_float<T>(__fadd_rn(zg_to_float(param[i]), __fmul_rn(g, neg_lr)));
+        param_out[i] = zg_from_float<T>(zg::sgd_step(zg_to_float(param[i]), g, neg_lr));
     }
 }
 
@@ -490,15 +481,7 @@ extern "C" int zg_adamw_update(const void* param, void* param_out, int dtype, co
     if (n == 0) return ZG_OK;
     if (!param || !param_out || !mu || !nu || !mu_out || !nu_out)
         return zg::fail(ZG_ERR_INVALID, "zg_adamw_update: null pointer");
-    // Constants as the traced float32 computation sees them: Python-float
-    // expressions rounded once to float32; bias corrections 1 - b^count in
-    // float32 (optax tree_bias_correction).
-    AdamConsts c;
-    c.omb1 = (float)(1.0 - b1); c.b1 = (float)b1;
-    c.omb2 = (float)(1.0 - b2); c.b2 = (float)b2;
-    c.bc1 = 1.0f - powf((float)b1, (float)count);
-    c.bc2 = 1.0f - powf((float)b2, (float)count);
-    c.eps = (float)eps; c.wd = (float)weight_decay; c.neg_lr = (float)(-lr);
+    const zg::AdamConsts c = zg::adam_consts(count, lr, b1, b2, eps, weight_decay);
     cudaStream_t st = zg::as_stream(stream);
     zg::LaunchTimer zg_lt_("adamw_update", st);
     if (dtype == ZG_BF16)

@@ -70,9 +70,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, ui
         : "memory");
 }
 
-// 32 lanes x 16 columns of 32-bit words (waits for the load).
+// 32 lanes x 16 columns of 32-bit words (waits for the load).  The TMEM
+// loads are warp-collective (.sync.aligned): every wrapper first reconverges
+// the warp, and callers keep all 32 lanes on the same call site.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -187,6 +190,7 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_bar) {
 // 32 lanes x 32 columns of 32-bit words: thread i gets lane (base + i), 32 columns.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -255,6 +259,7 @@ __device__ __forceinline__ float2 ffma2_tc(float2 a, float2 b, float2 c) {
 
 
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"

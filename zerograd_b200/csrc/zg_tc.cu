@@ -19,6 +19,7 @@
 
 #include "zg_ptx.cuh"
 #include "zg_tc.cuh"
+#include "zg_update.cuh"
 
 namespace zg {
 int launch_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
@@ -43,10 +44,120 @@ struct TcArgs {
     float alpha;
     int out_bf16;
     int tiles_m, tiles_n;
+    zg::FusedStep step;  // optimizer step on the float32 result (kind 0: none)
 };
 
+// The optimizer step on d = alpha * v[0..n) of row `row`, columns col0..:
+// parameters (and AdamW moments) read and written at the same positions, in
+// groups of 8 elements (16-byte bf16 / 2 x 16-byte float32 accesses) when the
+// row segment is aligned, element by element at a ragged edge.
+__device__ __forceinline__ void tc_step8(const zg::FusedStep& st, int64_t e0, const float* d, int n, bool vec) {
+    float p[8], mu[8], nu[8];
+    if (vec) {
+        if (st.param_bf16) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(st.param) + e0);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                p[2 * i] = __uint_as_float(w[i] << 16);
+                p[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+            }
+        } else {
+            const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(st.param) + e0);
+            const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(st.param) + e0 + 4);
+            p[0] = a.x; p[1] = a.y; p[2] = a.z; p[3] = a.w; p[4] = b.x; p[5] = b.y; p[6] = b.z; p[7] = b.w;
+        }
+        if (st.kind == zg::ZG_STEP_ADAMW) {
+            const float4 m0 = *reinterpret_cast<const float4*>(st.mu + e0), m1 = *reinterpret_cast<const float4*>(st.mu + e0 + 4);
+            const float4 v0 = *reinterpret_cast<const float4*>(st.nu + e0), v1 = *reinterpret_cast<const float4*>(st.nu + e0 + 4);
+            mu[0] = m0.x; mu[1] = m0.y; mu[2] = m0.z; mu[3] = m0.w; mu[4] = m1.x; mu[5] = m1.y; mu[6] = m1.z; mu[7] = m1.w;
+            nu[0] = v0.x; nu[1] = v0.y; nu[2] = v0.z; nu[3] = v0.w; nu[4] = v1.x; nu[5] = v1.y; nu[6] = v1.z; nu[7] = v1.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            p[i] = 0.f;
+            mu[i] = nu[i] = 0.f;
+            if (i < n) {
+                p[i] = st.param_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(st.param)[e0 + i])
+                                     : static_cast<const float*>(st.param)[e0 + i];
+                if (st.kind == zg::ZG_STEP_ADAMW) {
+                    mu[i] = st.mu[e0 + i];
+                    nu[i] = st.nu[e0 + i];
+                }
+            }
+        }
+    }
+    float pn[8], m[8], vv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float g = -d[i];  // pseudo-gradient
+        if (st.kind == zg::ZG_STEP_SGD) {
+            pn[i] = zg::sgd_step(p[i], g, st.c.neg_lr);
+        } else {
+            pn[i] = zg::adamw_step(p[i], g, mu[i], nu[i], st.c, m[i], vv[i]);
+        }
+    }
+    if (vec) {
+        if (st.param_bf16) {
+            uint4 o;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(pn[2 * i], pn[2 * i + 1]);
+            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(st.param_out) + e0) = o;
+        } else {
+            float* q = static_cast<float*>(st.param_out) + e0;
+            *reinterpret_cast<float4*>(q) = make_float4(pn[0], pn[1], pn[2], pn[3]);
+            *reinterpret_cast<float4*>(q + 4) = make_float4(pn[4], pn[5], pn[6], pn[7]);
+        }
+        if (st.kind == zg::ZG_STEP_ADAMW) {
+            *reinterpret_cast<float4*>(st.mu_out + e0) = make_float4(m[0], m[1], m[2], m[3]);
+            *reinterpret_cast<float4*>(st.mu_out + e0 + 4) = make_float4(m[4], m[5], m[6], m[7]);
+            *reinterpret_cast<float4*>(st.nu_out + e0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            *reinterpret_cast<float4*>(st.nu_out + e0 + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (i < n) {
+                if (st.param_bf16)
+                    static_cast<__nv_bfloat16*>(st.param_out)[e0 + i] = __float2bfloat16_rn(pn[i]);
+                else
+                    static_cast<float*>(st.param_out)[e0 + i] = pn[i];
+                if (st.kind == zg::ZG_STEP_ADAMW) {
+                    st.mu_out[e0 + i] = m[i];
+                    st.nu_out[e0 + i] = vv[i];
+                }
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tc_step32(const TcArgs& args, int row, int col0, const float (&v)[32]) {
+    const zg::FusedStep& st = args.step;
+    const int n = min(32, args.N - col0);
+    const int64_t base = (int64_t)row * st.ldp + col0;
+    const int esz = st.param_bf16 ? 2 : 4;
+    // 16-byte aligned groups of 8 in every array touched
+    const bool al = ((reinterpret_cast<uintptr_t>(st.param) + base * esz) & 15) == 0 &&
+                    ((reinterpret_cast<uintptr_t>(st.param_out) + base * esz) & 15) == 0 &&
+                    (st.kind != zg::ZG_STEP_ADAMW ||
+                     (((reinterpret_cast<uintptr_t>(st.mu) | reinterpret_cast<uintptr_t>(st.nu) |
+                        reinterpret_cast<uintptr_t>(st.mu_out) | reinterpret_cast<uintptr_t>(st.nu_out)) +
+                       base * 4) & 15) == 0);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        float d[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[i] = args.alpha * v[8 * g + i];
+        const int ng = n - 8 * g;
+        if (ng <= 0) break;
+        tc_step8(st, base + 8 * g, d, ng, al && ng >= 8);
+    }
+}
+
 // alpha * v[0..32) -> D[row, col0 .. col0+32), bounds-checked against M and N.
-__device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0, const float (&v)[32]) {
+__device__ __forceinline__ void tc_store32_d(const TcArgs& args, int row, int col0, const float (&v)[32]) {
     if (row >= args.M || col0 >= args.N) return;
     if (args.out_bf16) {
         __nv_bfloat16* d = static_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd + col0;
@@ -74,6 +185,63 @@ __device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0
             for (int i = 0; i < 32; ++i)
                 if (col0 + i < args.N) d[i] = args.alpha * v[i];
         }
+    }
+}
+
+// The epilogue's store of 32 columns: the fused optimizer step (if any) and
+// D (which may be null when the step consumes the result).
+__device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0, const float (&v)[32]) {
+    if (row >= args.M || col0 >= args.N) return;
+    if (args.step.kind != zg::ZG_STEP_NONE) tc_step32(args, row, col0, v);
+    if (args.D) tc_store32_d(args, row, col0, v);
+}
+
+// One tile row of an epilogue: TMEM columns [0, W) of this thread's lane ->
+// D and/or the fused optimizer step.  For an SGD step on an aligned bf16 row
+// segment every parameter load of the row is issued before the first TMEM
+// read, so their latency is paid once per tile, not once per 32 columns.
+template <int W>
+__device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int col_base, uint32_t tacc) {
+    const zg::FusedStep& st = args.step;
+    const int64_t base = (int64_t)row * st.ldp + col_base;
+    const bool lane_fast = st.kind == zg::ZG_STEP_SGD && st.param_bf16 && row < args.M && col_base + W <= args.N &&
+                           ((reinterpret_cast<uintptr_t>(st.param) + base * 2) & 15) == 0 &&
+                           ((reinterpret_cast<uintptr_t>(st.param_out) + base * 2) & 15) == 0;
+    // tcgen05.ld is warp-collective (.sync.aligned): the whole warp takes one
+    // path, so a ragged tile (rows past M in some lanes) uses the general one
+    if (__all_sync(0xffffffffu, lane_fast)) {
+        uint4 pre[W / 8];
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(st.param) + base);
+#pragma unroll
+        for (int i = 0; i < W / 8; ++i) pre[i] = src[i];
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(st.param_out) + base);
+#pragma unroll
+        for (int c = 0; c < W / 32; ++c) {
+            float v[32];
+            tmem_ld32(tacc + c * 32, v);
+            if (args.D) tc_store32_d(args, row, col_base + c * 32, v);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const uint4 raw = pre[c * 4 + g];
+                const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+                uint4 o;
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float d0 = args.alpha * v[8 * g + 2 * i], d1 = args.alpha * v[8 * g + 2 * i + 1];
+                    h[i] = __floats2bfloat162_rn(zg::sgd_step(__uint_as_float(w[i] << 16), -d0, st.c.neg_lr),
+                                                 zg::sgd_step(__uint_as_float(w[i] & 0xFFFF0000u), -d1, st.c.neg_lr));
+                }
+                dst[c * 4 + g] = o;
+            }
+        }
+        return;
+    }
+#pragma unroll 1
+    for (int c0 = 0; c0 < W; c0 += 32) {
+        float v[32];
+        tmem_ld32(tacc + c0, v);
+        tc_store32(args, row, col_base + c0, v);
     }
 }
 
@@ -203,12 +371,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_after();
             const int tm = t / args.tiles_n, tn = t % args.tiles_n;
             const int row = tm * BM + quad * 32 + lane;
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                float v[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, v);
-                tc_store32(args, row, tn * BN + c0, v);
-            }
+            tc_epilogue_row<BN>(args, row, tn * BN, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[acc]);
@@ -356,12 +519,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             tc_fence_after();
             const int tm = t / args.tiles_n, tn = t % args.tiles_n;
             const int row = tm * 256 + (int)rank * 128 + quad * 32 + lane;
-#pragma unroll 1
-            for (int c0 = 0; c0 < 256; c0 += 32) {
-                float v[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + c0, v);
-                tc_store32(args, row, tn * 256 + c0, v);
-            }
+            tc_epilogue_row<256>(args, row, tn * 256, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
@@ -732,8 +890,11 @@ bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t*
 }
 
 int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
-                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name) {
+                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name,
+                 const FusedStep* step) {
     if (M <= 0 || N <= 0 || K <= 0) return fail(ZG_ERR_INVALID, "tc_gemm: empty problem");
+    if (!D && !(step && step->kind != ZG_STEP_NONE)) return fail(ZG_ERR_INVALID, "tc_gemm: no output");
+    const FusedStep no_step{};
     if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
         return fail(ZG_ERR_INVALID, "tc_gemm: operands need 16-byte aligned rows");
     // Tile width: the persistent grid finishes after ceil(tiles / SMs) tiles
@@ -755,13 +916,15 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
     if (slots > 0 && pair_tiles >= slots) {
         bool okp = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, 128);
         if (!okp) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
-        TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + 255) / 256, (N + 255) / 256};
+        TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + 255) / 256, (N + 255) / 256, no_step};
+        if (step) a.step = *step;
         return b_mn_major ? launch_tc_pair<true>(ta, tb, a, slots, st, name)
                           : launch_tc_pair<false>(ta, tb, a, slots, st, name);
     }
     bool okb = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
     if (!okb) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
-    TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + BM - 1) / BM, (N + bn - 1) / bn};
+    TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + BM - 1) / BM, (N + bn - 1) / bn, no_step};
+    if (step) a.step = *step;
     if (b_mn_major) {
         if (bn == 256) return launch_tc<256, true>(ta, tb, a, st, name);
         if (bn == 128) return launch_tc<128, true>(ta, tb, a, st, name);

@@ -3,6 +3,7 @@
 #include <cuda.h>
 
 #include "zg_common.cuh"
+#include "zg_update.cuh"
 
 namespace zg {
 
@@ -43,8 +44,11 @@ int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint3
 // D[M,N] = alpha * A[M,K] . B^T; A K-major row-major (lda), B K-major
 // [N,K] (ldb) or MN-major [K,N] (ldb); D row-major float32 or bf16 (ldd).
 // Rows of A and B must be 16-byte aligned (lda, ldb multiples of 8).
+// With `step`, the epilogue also applies that optimizer step to the float32
+// result (D may then be null).
 int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
-                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name = "gemm");
+                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name = "gemm",
+                 const FusedStep* step = nullptr);
 
 // Factor fill in GEMM-operand layout: out[row, p*r + j] =
 // scale_p * round_dtype(normal(key_p, ctr)), ctr = row*r + j (row-major) or
@@ -74,9 +78,11 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
 bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype);
 size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank);
 int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
-                      int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
+                      int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st,
+                      const FusedStep* step = nullptr);
 int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
-                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
+                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st,
+                       const FusedStep* step = nullptr);
 int tc_replay_run(const float* shaped, const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols,
                   int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st);
 

@@ -738,9 +738,10 @@ size_t tc_replay_factors_workspace(int P, int64_t rows, int rank) { return (size
 // a_t, AT [P r, rows]; B [cols, P r] or, with b_t, BT [P r, cols] (then the
 // GEMM reads it as its MN-major operand).
 int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
-                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st) {
+                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st,
+                       const FusedStep* step) {
     const int64_t q = (int64_t)P * rank;
-    if (!a_t && !b_t) return tc_replay_factors(shaped, A, B, P, rows, cols, rank, inv_sqrt_rank, out, cv, st);
+    if (!a_t && !b_t) return tc_replay_factors(shaped, A, B, P, rows, cols, rank, inv_sqrt_rank, out, cv, st, step);
     __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
     if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
     if (q % 8 || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
@@ -769,11 +770,11 @@ int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void*
     }
     if (rc) return rc;
     return tc_gemm_bf16(Aw, q, B, b_t ? cols : q, b_t, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank,
-                        st, "replay_gemm");
+                        st, "replay_gemm", step);
 }
 
 int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
-                      int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st) {
+                      int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st, const FusedStep* step) {
     const int64_t q = (int64_t)P * rank;
     __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
     if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
@@ -792,7 +793,7 @@ int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, i
         if (rc) return rc;
     }
     return tc_gemm_bf16(Aw, q, B_op, q, false, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank, st,
-                        "replay_gemm");
+                        "replay_gemm", step);
 }
 
 size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank) {
@@ -962,4 +963,63 @@ extern "C" int zg_replay_operands(const float* shaped, const void* A, int a_tran
     zg::Carver cv(workspace, workspace_bytes);
     return zg::tc_replay_operands(shaped, A, a_transposed != 0, B, b_transposed != 0, P, rows, cols, rank,
                                   inv_sqrt_rank, out, cv, zg::as_stream(stream));
+}
+
+// ===========================================================================
+// C ABI: replay with the optimizer step fused into its GEMM epilogue
+// ===========================================================================
+
+static int replay_step(const char* who, const float* shaped, const void* A, int a_t, const void* B, int b_t, int P,
+                       int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const zg::FusedStep& step,
+                       float* descent_out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1) return zg::fail(ZG_ERR_INVALID, "%s: bad sizes", who);
+    if (!shaped || !A || !B || !step.param || !step.param_out) return zg::fail(ZG_ERR_INVALID, "%s: null pointer", who);
+    if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "%s: needs sm_100 and P*rank a multiple of 8", who);
+    size_t need = zg::tc_replay_factors_workspace(P, rows, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::tc_replay_operands(shaped, A, a_t != 0, B, b_t != 0, P, rows, cols, rank, inv_sqrt_rank, descent_out,
+                                  cv, zg::as_stream(stream), &step);
+}
+
+extern "C" int zg_replay_sgd(const float* shaped, const void* A, int a_transposed, const void* B, int b_transposed,
+                             int P, int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const void* param,
+                             void* param_out, int dtype, double lr, float* descent_out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay_sgd: bad dtype");
+    zg::FusedStep st{};
+    st.kind = zg::ZG_STEP_SGD;
+    st.param_bf16 = dtype == ZG_BF16;
+    st.ldp = cols;
+    st.param = param;
+    st.param_out = param_out;
+    st.c.neg_lr = (float)(-lr);
+    return replay_step("zg_replay_sgd", shaped, A, a_transposed, B, b_transposed, P, rows, cols, rank, inv_sqrt_rank,
+                       st, descent_out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int zg_replay_adamw(const float* shaped, const void* A, int a_transposed, const void* B, int b_transposed,
+                               int P, int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const void* param,
+                               void* param_out, int dtype, const float* mu, const float* nu, float* mu_out,
+                               float* nu_out, int count, double lr, double b1, double b2, double eps,
+                               double weight_decay, float* descent_out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: bad dtype");
+    if (count < 1) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: count must be >= 1");
+    if (!mu || !nu || !mu_out || !nu_out) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: null moment");
+    zg::FusedStep st{};
+    st.kind = zg::ZG_STEP_ADAMW;
+    st.param_bf16 = dtype == ZG_BF16;
+    st.ldp = cols;
+    st.param = param;
+    st.param_out = param_out;
+    st.mu = mu;
+    st.nu = nu;
+    st.mu_out = mu_out;
+    st.nu_out = nu_out;
+    st.c = zg::adam_consts(count, lr, b1, b2, eps, weight_decay);
+    return replay_step("zg_replay_adamw", shaped, A, a_transposed, B, b_transposed, P, rows, cols, rank,
+                       inv_sqrt_rank, st, descent_out, workspace, workspace_bytes, stream);
 }
