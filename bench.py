@@ -346,11 +346,20 @@ def run_ours(args):
             return local_losses
         return zg.allgather_losses(local_losses, sizes)
 
+    replay_entries = [(0, L.ZG_MATRIX, K, N, r)]
+
+    def prefetch(gen):
+        # a shard's process replays the whole population: its replay factors
+        # are drawn on a second stream while the shard's forward runs
+        if world > 1:
+            _ops.prefetch_replay_factors(_ops._Generation(bases[gen], 0, P, keys[gen][0]), replay_entries)
+
     def device_step(W, gen):
         # the same sequence ZeroGrad.step runs: forward (factors kept for the
         # generation), fitness exchange, shaping, replay (cached factors when
         # this rank drew the whole population), update
         cks, cks_local = keys[gen]
+        prefetch(gen)
         with _ops.generation_scope(bases[gen], a, P_local, cks_local):
             y = _ops.launch_linear(x, W, cks_local, 0, r, sigma, False)
         losses = gather(fitness[a:b])
@@ -422,7 +431,7 @@ def run_ours(args):
         nonlocal state
         xb = x_host.to(dev, non_blocking=True)
         fl = fit_host[a:b].to(dev, non_blocking=True)
-        y = opt.evaluate_shard({"w": Wcur}, gen, fwd, xb, ids_local)
+        y = opt.evaluate_shard({"w": Wcur}, gen, fwd, xb, ids_local, prefetch_replay=world > 1)
         losses = gather(fl)
         newp, state, m = opt.step_from_losses(zg.ZeroGradState(gen, state.opt_state), {"w": Wcur}, losses)
         del y
@@ -444,6 +453,7 @@ def run_ours(args):
 
     def hidden_step(W, gen):
         cks, cks_local = keys[gen]
+        prefetch(gen)
         with _ops.generation_scope(bases[gen], a, P_local, cks_local):
             y = _ops.launch_linear(xb_all, W, cks_local, 0, r, sigma, True)
         losses = gather(fitness[a:b])

@@ -102,6 +102,9 @@ class DeviceShard:
         self._loss_fn = loss_fn
         self.name = name or f"shard-{self.device.type}"
         self._candidate_ids: torch.Tensor | None = None
+        # True when this process also replays the whole population (one
+        # process per GPU): the shard then prefetches the replay's factors
+        self.replays = False
 
     def evaluate(self, params: ParameterTree, batch: Any, candidate_ids: torch.Tensor, generation: int,
                  rng: torch.Tensor | None = None) -> ShardResult:
@@ -109,10 +112,14 @@ class DeviceShard:
             rng = make_key(0)
         params_d = _to_device(_materialize_tree(params), self.device)
         batch_d = _to_device(batch, self.device)
-        ids_d = torch.as_tensor(candidate_ids).to(self.device)
+        # host-side ids: a contiguous range is then known without a device sync,
+        # so the forward's factors are kept for this process's replay
+        ids_h = torch.as_tensor(candidate_ids)
+        ids = ids_h if ids_h.device.type == "cpu" else ids_h.to(self.device)
         with torch.cuda.device(self.device) if self.device.type == "cuda" else _null():
-            losses = self._optimizer.evaluate_shard(params_d, generation, self._loss_fn, batch_d, ids_d,
-                                                    rng=rng.to(self.device))
+            self._optimizer.manifest.validate(params_d)
+            losses = self._optimizer._evaluate_shard(params_d, generation, self._loss_fn, batch_d, ids,
+                                                     rng=rng.to(self.device), prefetch_replay=self.replays)
         return ShardResult(candidate_ids=candidate_ids, losses=losses)
 
     @property
@@ -169,6 +176,7 @@ class DistributedZeroGrad:
         self._weights = list(weights) if weights else [1.0] * n
         if self._pg_mode:
             self._shards = [DeviceShard(self._devices[0], optimizer, loss_fn, name=f"rank-{self._rank}")]
+            self._shards[0].replays = True
         else:
             self._shards = [DeviceShard(d, optimizer, loss_fn, name=f"worker-{i}-{d.type}")
                             for i, d in enumerate(self._devices)]

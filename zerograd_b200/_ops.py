@@ -12,6 +12,7 @@ Launchers (``launch_*``) are the population-form entry points: keys
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import struct
 
@@ -155,6 +156,7 @@ class FactorCache:
     def __init__(self, budget_bytes: int | None = None):
         self.budget_bytes = budget_bytes
         self._entries: dict = {}
+        self._ready: dict = {}  # key -> event: entry drawn on another stream, not yet waited for
         self._bytes = 0
         self.hits = 0
         self.misses = 0
@@ -177,6 +179,13 @@ class FactorCache:
         if hit is not None:
             self._entries[key] = self._entries.pop(key)  # most recent last
             self.hits += 1
+            ev = self._ready.pop(key, None)
+            if ev is not None:
+                # drawn on a second stream: order this stream after the draws
+                cur = torch.cuda.current_stream(hit[0].device)
+                cur.wait_event(ev)
+                for t in hit:
+                    t.record_stream(cur)
         else:
             self.misses += 1
         return hit
@@ -190,23 +199,32 @@ class FactorCache:
         self.misses += 1
         return None, None
 
-    def put(self, key, value, device) -> None:
+    def __contains__(self, key) -> bool:
+        return key in self._entries
+
+    def put(self, key, value, device, ready=None) -> None:
         nbytes = sum(t.numel() * t.element_size() for t in value)
         budget = self._budget(device)
         while self._entries and self._bytes + nbytes > budget:
-            _, old = self._entries.pop(next(iter(self._entries)))
+            old_key = next(iter(self._entries))
+            old = self._entries.pop(old_key)
+            self._ready.pop(old_key, None)
             self._bytes -= sum(t.numel() * t.element_size() for t in old)
         if nbytes <= budget:
             self._entries[key] = value
             self._bytes += nbytes
+            if ready is not None:
+                self._ready[key] = ready
 
     def drop_generation(self, base: tuple) -> None:
         for key in [k for k in self._entries if k[0] == base]:
             old = self._entries.pop(key)
+            self._ready.pop(key, None)
             self._bytes -= sum(t.numel() * t.element_size() for t in old)
 
     def clear(self) -> None:
         self._entries.clear()
+        self._ready.clear()
         self._bytes = 0
 
 
@@ -234,6 +252,46 @@ class generation_scope:
 def _tc_ok(dev: torch.device, P: int, K: int, N: int, rank: int) -> bool:
     return (torch.cuda.get_device_capability(dev) == (10, 0) and (P * rank) % 8 == 0 and K % 8 == 0
             and N % 8 == 0 and rank <= 32)
+
+
+_PREFETCH_STREAMS: dict = {}
+
+
+def _prefetch_stream(dev: torch.device) -> torch.cuda.Stream:
+    s = _PREFETCH_STREAMS.get(dev)
+    if s is None:
+        s = torch.cuda.Stream(device=dev)
+        _PREFETCH_STREAMS[dev] = s
+    return s
+
+
+def prefetch_replay_factors(gen: _Generation, entries, cache: FactorCache = CACHE) -> None:
+    """Draw, on a second stream, the operand factors of `entries` -- (group,
+    layout, rows, cols, rank) of bf16 MATRIX/TABLE entries -- for the whole
+    population whose candidate keys are ``gen.cks``, and keep them in the
+    cache under gen's key.  A shard's replay needs every candidate's factors
+    but its forward pass draws only its own; started with the generation,
+    these draws (integer-ALU work) overlap the forward's GEMMs, and the
+    replay waits for them only when it uses them."""
+    dev = gen.cks.device
+    side = _prefetch_stream(dev)
+    main = torch.cuda.current_stream(dev)
+    side.wait_stream(main)  # the candidate keys come from this stream
+    k = _keys2d(gen.cks)
+    k.record_stream(side)
+    P = k.shape[0]
+    for group, layout, rows, cols, rank in entries:
+        key = (gen.base, gen.start, gen.count, group, layout, rows, cols, rank)
+        if key in cache or group < 0:
+            continue
+        with torch.cuda.stream(side):
+            A = torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev)
+            B = torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev)
+            L.call("zg_factor_operands", L.ptr(k), group, P, layout, rows, cols, rank, L.ZG_BF16, L.ptr(A),
+                   L.ptr(B), ctypes.c_void_p(side.cuda_stream))
+            ev = torch.cuda.Event()
+            ev.record(side)
+        cache.put(key, (A, B), dev, ready=ev)
 
 
 def operand_factors(keys: torch.Tensor, group: int, layout: int, rows: int, cols: int, rank: int,

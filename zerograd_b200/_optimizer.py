@@ -23,7 +23,7 @@ from ._candidate import CandidateContext
 from ._fitness import _check_shape_dtype
 from ._keys import key as make_key
 from ._keys import step_key
-from ._manifest import Manifest, ParameterTree
+from ._manifest import LAYOUT_CODE, Manifest, ParameterLayout, ParameterTree
 from ._replay import candidate_keys, replay_entry_keys, replay_entry_step
 from ._transforms import _leaves, apply_updates, is_fused, tree_get, tree_set
 
@@ -121,17 +121,25 @@ class ZeroGrad:
         return step_key(self._seed, self._run_id, generation, self._manifest.version)
 
     def evaluate_shard(self, params: ParameterTree, generation: int, loss_fn: LossFn, batch: Any,
-                       candidate_ids, *, rng: torch.Tensor | None = None) -> torch.Tensor:
-        """Losses of a subset of candidates (``_optimizer.py:126-149``)."""
+                       candidate_ids, *, rng: torch.Tensor | None = None,
+                       prefetch_replay: bool = False) -> torch.Tensor:
+        """Losses of a subset of candidates (``_optimizer.py:126-149``).
+
+        ``prefetch_replay`` (an addition to the reference signature): this
+        process will also replay the whole population (one process per GPU),
+        so for a contiguous shard the replay's factors are drawn on a second
+        stream while the shard's forward runs."""
         self._manifest.validate(params)
         params = _materialize_tree(params)
-        return self._evaluate_shard(params, generation, loss_fn, batch, candidate_ids, rng=rng)
+        return self._evaluate_shard(params, generation, loss_fn, batch, candidate_ids, rng=rng,
+                                    prefetch_replay=prefetch_replay)
 
-    def _evaluate_shard(self, params, generation, loss_fn, batch, candidate_ids, *, rng=None, id_range=None):
+    def _evaluate_shard(self, params, generation, loss_fn, batch, candidate_ids, *, rng=None, id_range=None,
+                        prefetch_replay=False):
         device = _device_of(params)
         if id_range is None:
             id_range = _host_range(candidate_ids)
-        if id_range is not None and not isinstance(candidate_ids, torch.Tensor):
+        if id_range is not None:
             # built on the device: a host-built id tensor would need a copy that synchronises the stream
             ids = torch.arange(id_range[0], id_range[0] + id_range[1], dtype=torch.int32, device=device)
         else:
@@ -154,10 +162,30 @@ class ZeroGrad:
             return torch.empty(0, dtype=torch.float32, device=device)
         if id_range is None:
             return torch.func.vmap(evaluate_candidate)(cks, rngs)
+        base_words = tuple(int(v) for v in base)
+        if prefetch_replay and id_range[1] < self._population_size:
+            # a shard whose process also replays the whole population: its
+            # replay factors are drawn on a second stream while the forward runs
+            self._prefetch_replay(params, base, base_words, device)
         # A contiguous id range known on the host: the factors drawn by the
         # forward ops are kept for this generation's replay.
-        with _ops.generation_scope(tuple(int(v) for v in base), id_range[0], id_range[1], cks):
+        with _ops.generation_scope(base_words, id_range[0], id_range[1], cks):
             return torch.func.vmap(evaluate_candidate)(cks, rngs)
+
+    def _prefetch_replay(self, params, base, base_words, device) -> None:
+        entries = []
+        for entry in self._manifest.entries:
+            if entry.layout is ParameterLayout.VECTOR:
+                continue
+            p = self._manifest.resolve(params, entry.path)
+            if isinstance(p, torch.Tensor) and p.dtype == torch.bfloat16 and p.ndim == 2:
+                entries.append((self._manifest.group_index(entry.group), LAYOUT_CODE[entry.layout],
+                                int(p.shape[0]), int(p.shape[1]), self._rank))
+        if not entries or torch.cuda.get_device_capability(device) != (10, 0):
+            return
+        ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
+        gen = _ops._Generation(base_words, 0, self._population_size, candidate_keys(base, ids))
+        _ops.prefetch_replay_factors(gen, entries)
 
     # -- completion ---------------------------------------------------------
 
