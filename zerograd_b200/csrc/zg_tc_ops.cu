@@ -672,17 +672,40 @@ __global__ void scale_operand_kernel(const __nv_bfloat16* __restrict__ A, const 
 #pragma unroll
         for (int k = 0; k < 8; ++k) wk[k] = w[(col0 + k) / rank];
     }
-    for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-        const int64_t e0 = row * q + col0;
-        float f[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(A + e0), f);
-        uint4 pk;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+    // four rows per thread per pass, their loads issued together, so enough
+    // bytes are in flight per SM to run at HBM rate
+    const int64_t gy = gridDim.y;
+    for (int64_t r0 = blockIdx.y; r0 < rows; r0 += 4 * gy) {
+        uint4 v[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            h[k] = __floats2bfloat162_rn(__fmul_rn(f[2 * k], wk[2 * k]), __fmul_rn(f[2 * k + 1], wk[2 * k + 1]));
-        *reinterpret_cast<uint4*>(out + e0) = pk;
+        for (int u = 0; u < 4; ++u) {
+            const int64_t row = r0 + u * gy;
+            if (row < rows) v[u] = *reinterpret_cast<const uint4*>(A + row * q + col0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t row = r0 + u * gy;
+            if (row >= rows) break;
+            float f[8];
+            bf16x8_to_f32(v[u], f);
+            uint4 pk;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                h[k] = __floats2bfloat162_rn(__fmul_rn(f[2 * k], wk[2 * k]), __fmul_rn(f[2 * k + 1], wk[2 * k + 1]));
+            *reinterpret_cast<uint4*>(out + row * q + col0) = pk;
+        }
     }
+}
+
+// Grid rows for scale_operand_kernel: about 8 resident blocks per SM, each
+// thread covering at least four rows.
+int64_t scale_grid_rows(unsigned gx, int64_t rows) {
+    int64_t gy = (int64_t)sm_count() * 8 / gx;
+    if (gy > (rows + 3) / 4) gy = (rows + 3) / 4;
+    if (gy < 1) gy = 1;
+    if (gy > 65535) gy = 65535;
+    return gy;
 }
 
 // Transposing form: Aw[row, q] = bf16(float(AT[q, row]) * w[q / rank]) for
@@ -759,10 +782,7 @@ int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void*
         rc = check_launch("replay_scale");
     } else {
         const unsigned gx = (unsigned)((q / 8 + 255) / 256);
-        int64_t gy = (int64_t)sm_count() * 32 / gx;
-        if (gy < 1) gy = 1;
-        if (gy > rows) gy = rows;
-        if (gy > 65535) gy = 65535;
+        const int64_t gy = scale_grid_rows(gx, rows);
         zg::LaunchTimer zg_lt_("replay_scale", st);
         scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A), shaped,
                                                                      rank, (int)q, rows, Aw);
@@ -781,10 +801,7 @@ int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, i
     if (q % 8 || (reinterpret_cast<uintptr_t>(A_op) & 15)) return fail(ZG_ERR_INVALID, "tc replay: operand alignment");
     if (q > 2147483647) return fail(ZG_ERR_INVALID, "tc replay: P*rank too large");
     const unsigned gx = (unsigned)((q / 8 + 255) / 256);
-    int64_t gy = (int64_t)sm_count() * 32 / gx;
-    if (gy < 1) gy = 1;
-    if (gy > rows) gy = rows;
-    if (gy > 65535) gy = 65535;
+    const int64_t gy = scale_grid_rows(gx, rows);
     {
         zg::LaunchTimer zg_lt_("replay_scale", st);
         scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A_op), shaped,
