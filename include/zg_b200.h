@@ -198,6 +198,24 @@ ZG_API int zg_replay_adamw(const float* shaped, const void* A, int a_transposed,
                            double lr, double b1, double b2, double eps, double weight_decay,
                            float* descent_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Tied logits fused with softmax cross-entropy (bf16, tcgen05): for each
+ * candidate p and row m
+ *   logits = bf16(x_p @ T^T + s * (x_p @ B_p) @ A_p^T)    (perturbed_tied_logits)
+ *   loss[p, m] = logsumexp_v logits[m, v] - logits[m, labels[m]]   (float32)
+ * without materialising the [P, M, V] logits: a pair of SMs sweeps the whole
+ * vocabulary for a 256-row block, keeping each row's running max and sum of
+ * exponentials in registers.  T [V, C] (the tied table), x [M, C] shared
+ * (x_batched = 0) or [P, M, C]; labels [M] int32 (shared by the candidates);
+ * loss [P, M].  A label outside [0, V) gives a NaN loss.  rank 8 or 16; C a
+ * multiple of 8; x and T 16-byte aligned.  Replaces perturbed_tied_logits
+ * (src/zerograd/_candidate.py:33-38) followed by a cross-entropy over the
+ * logits in the loss function. */
+ZG_API size_t zg_tied_logits_ce_workspace_size(int P, int M, int V, int C, int rank);
+ZG_API int zg_tied_logits_ce(const void* x, int x_batched, const void* T, const uint32_t* keys,
+                             int group, const int32_t* labels, int P, int M, int V, int C,
+                             int rank, float s, float* loss, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Per-candidate-input population forward (bf16, tcgen05), the hidden-layer
  * case: x [P, M, K] (one input per candidate), y [P, M, N],
  *   y[p] = x_p @ Wop + s * (x_p @ F1_p) @ F2_p^T

@@ -236,6 +236,18 @@ def perturbed_tied_logits(x, T, gk, rank, sigma, dtype="float32"):
     return x @ np.asarray(T, np.float64).T + s * np.einsum("...c,cr,vr->...v", x, b, a)
 
 
+def tied_logits_cross_entropy(x, T, gk, rank, sigma, labels, dtype="bfloat16"):
+    """Per-row cross-entropy of the tied logits rounded to the leaf dtype
+    (what tied_logits returns), log-sum-exp in float64."""
+    logits = perturbed_tied_logits(x, T, gk, rank, sigma, dtype)
+    logits = cast(logits, dtype).astype(np.float64)
+    mx = logits.max(axis=-1, keepdims=True)
+    lse = mx[..., 0] + np.log(np.exp(logits - mx).sum(axis=-1))
+    lab = np.asarray(labels, np.int64)
+    picked = np.take_along_axis(logits, lab[..., None], axis=-1)[..., 0]
+    return lse - picked
+
+
 def perturbed_vector(v, gk, sigma, dtype="float32"):
     s = scaled_factor(1, sigma, dtype)
     return np.asarray(v, np.float64) + s * vector_noise(gk, v.shape, dtype)

@@ -16,9 +16,11 @@ from ._manifest import Manifest, ManifestEntry, ParameterLayout, ParameterPath, 
 from ._optimizer import StepMetrics, ZeroGrad, ZeroGradState
 from ._replay import replay, replay_entry
 from ._transforms import adamw, apply_updates, sgd
-from . import random
+from . import checkpoint, random
+from .checkpoint import EarlyStopping, load_checkpoint, save_checkpoint
 
 __all__ = [
+    "EarlyStopping", "load_checkpoint", "save_checkpoint", "checkpoint",
     "CandidateContext", "CalibrationResult", "DeviceShard", "DistributedZeroGrad", "Manifest", "ManifestEntry",
     "ParameterLayout", "ParameterPath", "ParameterTree", "ShardResult", "StepMetrics", "ZeroGrad",
     "ZeroGradState", "adamw", "allgather_losses", "apply_updates", "candidate_key", "compute_partition_sizes",

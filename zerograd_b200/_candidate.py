@@ -97,6 +97,22 @@ class CandidateContext:
             raise ValueError("logit input and [rows, cols] table shapes are incompatible")
         return _ops.tied_logits(x, table, self.candidate_key, self._group(path), self.rank, self.sigma)
 
+    def tied_logits_cross_entropy(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor,
+                                  labels: torch.Tensor) -> torch.Tensor:
+        """Per-row softmax cross-entropy of ``tied_logits(params, path, x)``
+        against integer ``labels`` (float32, shape of x without its last axis),
+        computed without materialising the [rows, vocabulary] logits: the
+        logits are the bf16 values tied_logits returns, the log-sum-exp runs
+        in float32.  An addition to the reference's context (which leaves the
+        cross-entropy to the loss function); bf16 tables, rank 8 or 16."""
+        entry = self.manifest.entry(path)
+        if entry.layout is not ParameterLayout.TABLE:
+            raise ValueError(f"{'.'.join(path)} is not a table entry")
+        table = self.manifest.resolve(params, path)
+        if table.ndim != 2 or x.shape[-1] != table.shape[1]:
+            raise ValueError("logit input and [rows, cols] table shapes are incompatible")
+        return _ops.tied_logits_ce(x, table, labels, self.candidate_key, self._group(path), self.rank, self.sigma)
+
     def vector(self, params: ParameterTree, path: ParameterPath) -> torch.Tensor:
         entry = self.manifest.entry(path)
         if entry.layout is not ParameterLayout.VECTOR:

@@ -50,6 +50,9 @@ SIGNATURES = {
                              _vp, _sz, _vp]),
     "zg_replay_adamw": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _i32, _vp, _vp,
                                _vp, _vp, _i32, _f64, _f64, _f64, _f64, _f64, _vp, _vp, _sz, _vp]),
+    "zg_tied_logits_ce_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "zg_tied_logits_ce": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
+                                 _vp]),
     "zg_batched_forward_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "zg_batched_forward_factors": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp,
                                           _sz, _vp]),

@@ -441,6 +441,39 @@ def launch_tied_logits(x: torch.Tensor, table: torch.Tensor, keys: torch.Tensor,
     return y
 
 
+def launch_tied_logits_ce(x: torch.Tensor, table: torch.Tensor, labels: torch.Tensor, keys: torch.Tensor,
+                          group: int, rank: int, sigma: float, x_batched: bool) -> torch.Tensor:
+    """Per-row cross-entropy of the tied logits, [P, *rows] float32, without
+    materialising the logits (bf16 table and input, rank 8 or 16)."""
+    dev = L.require_cuda(x, table, labels, keys)
+    k = _keys2d(keys)
+    P = k.shape[0]
+    if table.ndim != 2 or x.shape[-1] != table.shape[1]:
+        raise ValueError("logit input and [rows, cols] table shapes are incompatible")
+    if x_batched and (x.ndim < 2 or x.shape[0] != P):
+        raise ValueError("batched logit input must lead with the population axis")
+    mshape = tuple(x.shape[1:-1] if x_batched else x.shape[:-1])
+    if tuple(labels.shape) != mshape:
+        raise ValueError(f"labels of shape {tuple(labels.shape)} do not match the rows {mshape}")
+    if labels.dtype not in (torch.int32, torch.int64):
+        raise TypeError("labels must be integer class indices")
+    if table.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise TypeError("the fused tied-logits cross-entropy takes bf16 tables and inputs")
+    x = x.contiguous()
+    T = table.contiguous()
+    V, C = T.shape
+    M = math.prod(mshape)
+    loss = torch.empty((P, *mshape), dtype=torch.float32, device=dev)
+    if M == 0:
+        return loss
+    s = scaled_factor_value(rank, sigma, table.dtype)
+    lab = labels.to(torch.int32).contiguous()
+    ws = L.workspace(L.query("zg_tied_logits_ce_workspace_size", P, M, V, C, rank), dev)
+    L.call("zg_tied_logits_ce", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, L.ptr(lab), P, M, V, C, rank,
+           s, L.ptr(loss), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+    return loss
+
+
 def launch_table_lookup(table: torch.Tensor, indices: torch.Tensor, keys: torch.Tensor, group: int,
                         rank: int, sigma: float, idx_batched: bool) -> torch.Tensor:
     dev = L.require_cuda(table, indices, keys)
@@ -693,6 +726,23 @@ def _tied_vmap(info, in_dims, x, table, key, group, rank, sigma):
     return launch_tied_logits(x, table, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
 
 
+@torch.library.custom_op(f"{_NS}::tied_logits_ce", mutates_args=())
+def _tied_ce_op(x: torch.Tensor, table: torch.Tensor, labels: torch.Tensor, key: torch.Tensor, group: int,
+                rank: int, sigma: float) -> torch.Tensor:
+    return launch_tied_logits_ce(x, table, labels, key.reshape(1, 2), group, rank, sigma, False)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::tied_logits_ce")
+def _tied_ce_vmap(info, in_dims, x, table, labels, key, group, rank, sigma):
+    xd, td, ld, kd = in_dims[:4]
+    if td is not None or ld is not None:
+        raise NotImplementedError("tables and labels batched over candidates are not supported")
+    x = _movedim0(x, xd)
+    if kd is None:
+        return launch_tied_logits_ce(x, table, labels, key.reshape(1, 2), group, rank, sigma, False)[0], 0
+    return launch_tied_logits_ce(x, table, labels, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
+
+
 @torch.library.custom_op(f"{_NS}::table_lookup", mutates_args=())
 def _lookup_op(table: torch.Tensor, indices: torch.Tensor, key: torch.Tensor, group: int, rank: int,
                sigma: float) -> torch.Tensor:
@@ -753,6 +803,10 @@ def linear(x, weight, key, group, rank, sigma):
 
 def tied_logits(x, table, key, group, rank, sigma):
     return _tied_op(x, table, key, int(group), int(rank), float(sigma))
+
+
+def tied_logits_ce(x, table, labels, key, group, rank, sigma):
+    return _tied_ce_op(x, table, labels, key, int(group), int(rank), float(sigma))
 
 
 def table_lookup(table, indices, key, group, rank, sigma):

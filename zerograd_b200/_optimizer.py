@@ -244,6 +244,20 @@ class ZeroGrad:
                                   max_loss=float(m[2]), population_size=self._population_size)
         return new_params, ZeroGradState(generation=generation + 1, opt_state=new_opt_state), metrics_out
 
+    def catch_up(self, state: ZeroGradState, params: ParameterTree, loss_history) -> tuple:
+        """Replay a loss history: one ``step_from_losses`` per recorded
+        generation, from ``state.generation`` on.  No forward pass runs: a
+        generation's update needs only its losses and its seed-derived keys,
+        so a node that joins late (or restarts from an older checkpoint)
+        reaches the cluster's parameters bit for bit (the reference's
+        ``add_node`` catch-up, ``_fault_tolerant.py:148-158``).  Returns the
+        new (params, state) and the last generation's metrics (None for an
+        empty history)."""
+        metrics = None
+        for losses in loss_history:
+            params, state, metrics = self.step_from_losses(state, params, torch.as_tensor(losses))
+        return params, state, metrics
+
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, loss_fn: LossFn, *,
              rng: torch.Tensor | None = None):
         """One generation: evaluate all candidates, then complete (``_optimizer.py:246-277``)."""

@@ -52,6 +52,7 @@ struct UPassArgs {
     __nv_bfloat16* U;
     int M, K, P, rank, tiles_m;
     float s;
+    int x_batched;  // 0: one input shared by every candidate
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -93,7 +94,7 @@ batched_u_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 31)) { ok = false; break; }
                 uint8_t* sx = smem + stage * UP_STAGE;
                 mbar_expect_tx(&full_bar[stage], UP_STAGE);
-                tma_load_3d(sx, &tmX, &full_bar[stage], kb * BK, tm * BM, p);
+                tma_load_3d(sx, &tmX, &full_bar[stage], kb * BK, tm * BM, a.x_batched ? p : 0);
                 tma_load_2d(sx + UP_X, &tmF, &full_bar[stage], kb * BK, p * a.rank);
                 issued |= 1u << stage;
                 issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
@@ -580,11 +581,12 @@ namespace zg {
 
 int batched_error_word(int clear) { return ptx_error_word(clear); }
 
-int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank, float s, void* U, cudaStream_t st) {
+int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank, float s, void* U, cudaStream_t st,
+                   bool x_batched) {
     if ((rank != 8 && rank != 16) || K % 8 || P < 1 || M < 1)
         return fail(ZG_ERR_INVALID, "batched_u_pass: rank 8 or 16 and K a multiple of 8");
     CUtensorMap tx, tf;
-    const uint64_t dx[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)P};
+    const uint64_t dx[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)(x_batched ? P : 1)};
     const uint64_t sx[2] = {(uint64_t)K * 2, (uint64_t)M * K * 2};
     const uint32_t bx[3] = {BK, BM, 1};
     const uint64_t df[2] = {(uint64_t)K, (uint64_t)P * rank};
@@ -592,7 +594,7 @@ int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank
     const uint32_t bf[2] = {BK, 16};
     if (!tensor_map_bf16(&tx, x, 3, dx, sx, bx, true) || !tensor_map_bf16(&tf, F1T, 2, df, sf, bf, true))
         return fail(ZG_ERR_CUDA, "batched_u_pass: tensor maps");
-    UPassArgs a{static_cast<__nv_bfloat16*>(U), M, K, P, rank, (M + BM - 1) / BM, s};
+    UPassArgs a{static_cast<__nv_bfloat16*>(U), M, K, P, rank, (M + BM - 1) / BM, s, x_batched ? 1 : 0};
     const int64_t tiles = (int64_t)P * a.tiles_m;
     if (tiles > INT_MAX) return fail(ZG_ERR_INVALID, "batched_u_pass: too many tiles");
     const int grid = tiles < sm_count_b() ? (int)tiles : sm_count_b();

@@ -19,6 +19,7 @@ bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t*
 // Kernel error words of the per-candidate-input and int8 kernels (0 = none).
 int batched_error_word(int clear);
 int int8_error_word(int clear);
+int ce_error_word(int clear);
 
 // Factor fill transposed to [P r, rows]: out[p*r + j, row] =
 // round_dtype(normal(key_p, row*r + j)) (the [rows, r] row-major factor of
@@ -32,7 +33,8 @@ int fill_operand_t(const uint32_t* keys, int group, int P, int rank, int64_t row
 // The two kernels of that forward:
 //   U[p, m, 0:16] = bf16(s * x_p[m] . F1_p) (columns >= rank zero)
 //   y[p] = bf16(x_p . Wop + U_p . F2_p^T)
-int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank, float s, void* U, cudaStream_t st);
+int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank, float s, void* U, cudaStream_t st,
+                   bool x_batched = true);
 int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U, const void* F2, int P, int M, int K,
                  int N, int rank, void* y, cudaStream_t st);
 bool batched_forward_ok(int P, int M, int K, int N, int rank);
