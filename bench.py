@@ -224,6 +224,48 @@ def int8_layer_section(dev, args):
                          "launch_ms": gm}}
 
 
+def tied_ce_section(dev, args):
+    """The decoder LM's tied output layer with its cross-entropy (vocabulary
+    32000, width 768, 16 sequences x 256 tokens per candidate, rank 16): 16
+    candidates of the population, each with its own hidden states (seeded
+    N(0,1) bf16, table N(0, 0.02)), logits never materialised."""
+    import torch
+
+    import zerograd_b200 as zg
+    from zerograd_b200 import _lib as L
+    from zerograd_b200 import _ops
+
+    P, M, V, C, r = 16, 16 * 256, 32000, 768, 16
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(P, M, C, generator=g, device=dev).to(torch.bfloat16)
+    T = (torch.randn(V, C, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    labels = torch.randint(0, V, (M,), generator=g, device=dev)
+    keys = _ops.launch_fold_in(zg.step_key(0, "lm", 0, 1), torch.arange(P, dtype=torch.int32, device=dev))
+
+    def run():
+        return _ops.launch_tied_logits_ce(x, T, labels, keys, 0, r, 0.01, True)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 10))
+    L.profile_begin()
+    for _ in range(steps):
+        run()
+    kern = L.profile_end()
+    pk = peaks()
+    ce = kern["tied_ce"][1] / kern["tied_ce"][0]
+    flops = 2.0 * P * M * V * C + 2.0 * P * M * r * V  # x . T^T and the low-rank term
+    return {"workload": "tied logits + softmax cross-entropy, V=32000, C=768, 4096 tokens per candidate, "
+                        "rank 16, 16 candidates, per-candidate hidden states",
+            "kernels_ms": {k: v[1] / v[0] for k, v in sorted(kern.items())},
+            "candidates_per_sec": P / (sum(v[1] / v[0] for v in kern.values()) / 1e3),
+            "roofline": {"kernel": "tied_ce", "bound": "tensor", "achieved": flops / (ce / 1e3) / 1e12,
+                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": flops / (ce / 1e3) / 1e12 / pk["bf16_tflops"], "peak_source": pk["source"],
+                         "launch_ms": ce}}
+
+
 # ---------------------------------------------------------------------------
 # CPU arm: the oracle restatement of the reference on a bounded sample
 # ---------------------------------------------------------------------------
@@ -541,6 +583,7 @@ def run_ours(args):
         line["hidden_layer"] = hidden
         if world == 1:
             line["int8_qat_layer"] = int8_layer_section(dev, args)
+            line["lm_tied_ce"] = tied_ce_section(dev, args)
         if world == 1:
             secs = cpu_generation_sample(8)
             n_cand = max(1, min(64, int(8 * 15.0 / max(secs, 1e-3))))

@@ -98,3 +98,24 @@ def test_step_with_fused_cross_entropy(cuda):
     new, _, m = opt.step(state, params, tokens, loss_fn)
     assert np.isfinite(m.mean_loss)
     assert L.load().zg_device_error(1) == 0
+
+
+def test_tied_ce_lm_slice(cuda, oracle):
+    """The decoder LM's output layer (V=32000, C=768, 4096 tokens, rank 16)
+    for 16 candidates with their own hidden states; rows 0..7 of candidates 0
+    and 15 against the oracle."""
+    P, M, V, C, r, sigma = 16, 4096, 32000, 768, 16, 0.01
+    cks = oracle.candidate_keys(oracle.step_key(0, "lm", 0, 1), range(P))
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(P, M, C, generator=g, device=cuda).to(torch.bfloat16)
+    T = (torch.randn(V, C, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    labels = torch.randint(0, V, (M,), generator=g, device=cuda)
+    loss = _ops.launch_tied_logits_ce(x, T, labels, _u32(cks, cuda), 0, r, sigma, True)
+    assert L.load().zg_device_error(1) == 0
+    Ts = T.float().cpu().numpy().astype(np.float64)
+    lab = labels.cpu().numpy()[:8]
+    for p in (0, 15):
+        xs = x[p, :8].float().cpu().numpy().astype(np.float64)
+        want = oracle.tied_logits_cross_entropy(xs, Ts, oracle.fold_in(cks[p], 0), r, sigma, lab)
+        np.testing.assert_allclose(loss[p, :8].cpu().numpy(), want, rtol=1e-2, atol=3e-2)
+    assert torch.isfinite(loss).all()

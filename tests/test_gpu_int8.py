@@ -112,3 +112,27 @@ def test_int8_rounding_and_clamp_edges(cuda, oracle, y_scale):
         o, a = oracle.int8_lut_linear(x[p], W, w_scale, 1.0 / 127, y_scale, lut, A, B, float(s))
         np.testing.assert_array_equal(acc[p].cpu().numpy(), a)
         np.testing.assert_array_equal(out[p].cpu().numpy(), o)
+
+
+def test_int8_qat_layer_64_candidates(cuda, oracle):
+    """The same layer with 64 candidates (inputs and outputs larger than L2),
+    checked on the first 8 rows of candidates 0, 31 and 63."""
+    from zerograd_b200 import _lib as L
+
+    P, M, K, N, rank, sigma = 64, 512, 4096, 4096, 4, 0.05
+    rng = np.random.default_rng(13)
+    x = rng.integers(-127, 128, (P, M, K), dtype=np.int8)
+    W = rng.integers(-127, 128, (K, N), dtype=np.int8)
+    w_scale = (rng.uniform(0.5, 1.5, N) / 127).astype(np.float32)
+    lut = oracle.tanh_lut()
+    cks = oracle.candidate_keys(oracle.step_key(13, "qat", 0, 1), range(P))
+    gks = oracle.group_keys(cks, 1)
+    out = _ops.launch_int8_lut_linear(torch.tensor(x).to(cuda), torch.tensor(W).to(cuda),
+                                      torch.tensor(w_scale).to(cuda), 1.0 / 127, 1.0 / 32,
+                                      torch.tensor(lut).to(cuda), _u32(cks, cuda), 1, rank, sigma, True)
+    assert L.load().zg_device_error(1) == 0
+    s = np.float32(sigma / np.sqrt(rank))
+    for p in (0, 31, 63):
+        A, B = oracle.matrix_factors(gks[p], (K, N), rank)
+        o, _ = oracle.int8_lut_linear(x[p][:8], W, w_scale, 1.0 / 127, 1.0 / 32, lut, A, B, float(s))
+        np.testing.assert_array_equal(out[p].cpu().numpy()[:8], o)
