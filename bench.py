@@ -249,16 +249,17 @@ def tied_ce_section(dev, args):
         run()
     torch.cuda.synchronize()
     steps = max(1, min(args.steps, 10))
-    L.profile_begin()
-    for _ in range(steps):
-        run()
-    kern = L.profile_end()
+    with ClockSampler(dev) as clk:
+        L.profile_begin()
+        for _ in range(steps):
+            run()
+        kern = L.profile_end()
     pk = peaks()
     ce = kern["tied_ce"][1] / kern["tied_ce"][0]
     flops = 2.0 * P * M * V * C + 2.0 * P * M * r * V  # x . T^T and the low-rank term
     return {"workload": "tied logits + softmax cross-entropy, V=32000, C=768, 4096 tokens per candidate, "
                         "rank 16, 16 candidates, per-candidate hidden states",
-            "kernels_ms": {k: v[1] / v[0] for k, v in sorted(kern.items())},
+            "kernels_ms": {k: v[1] / v[0] for k, v in sorted(kern.items())}, "clocks": clk.summary(),
             "candidates_per_sec": P / (sum(v[1] / v[0] for v in kern.values()) / 1e3),
             "roofline": {"kernel": "tied_ce", "bound": "tensor", "achieved": flops / (ce / 1e3) / 1e12,
                          "peak": pk["bf16_tflops"], "unit": "TFLOP/s",

@@ -25,7 +25,8 @@ def _u32(a, dev):
 
 @pytest.mark.parametrize("P,M,V,C,r,x_batched", [(6, 300, 1000, 256, 8, True),    # ragged rows and vocabulary
                                                   (4, 64, 600, 128, 16, False),   # shared input, rank 16
-                                                  (3, 512, 4096, 512, 8, True)])  # whole 256-blocks
+                                                  (3, 512, 4096, 512, 8, True),   # whole 256-blocks
+                                                  (1, 100, 200, 128, 8, False)])  # one tile: one range
 def test_tied_ce_matches_oracle(cuda, oracle, P, M, V, C, r, x_batched):
     sigma, group = 0.05, 1
     cks = oracle.candidate_keys(oracle.step_key(2, "ce", 0, 1), range(P))

@@ -8,7 +8,9 @@
 // by a float32 cross-entropy over the bf16 logits, without ever writing the
 // [P, M, V] logits: a CTA pair owns one (candidate, 256-row block) and sweeps
 // every 256-column block of the vocabulary; each epilogue thread owns one row
-// and keeps its running max, sum of exponentials and label logit in registers.
+// and keeps its running max, sum of exponentials and label logit in registers
+// (two epilogue warps per TMEM lane quadrant, each over half of every column
+// block; the two halves of a row merge through shared memory at the end).
 // U_p = bf16(s x_p . B_p) comes from the u pass of the per-candidate-input
 // forward (table B kept K-major as F1T); F2 = the table A in operand layout.
 // A label outside [0, V) yields a NaN loss.
@@ -20,7 +22,7 @@
 
 namespace {
 
-constexpr int THREADS = 192, BK = 64;
+constexpr int THREADS = 320, BK = 64;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int CE_STAGES = 6;
 constexpr uint32_t CE_A = 128 * BK * 2;                            // 16 KiB: this CTA's 128 rows of x
 constexpr uint32_t CE_B = 128 * BK * 2;                            // 16 KiB: this CTA's 128 rows of T
@@ -33,8 +35,115 @@ constexpr uint32_t CE_SMEM = CE_STAGES * CE_STAGE + 2 * CE_CORR;   // 208 KiB
 struct CeArgs {
     float* loss;            // [P, M]
     const int32_t* labels;  // [M]
+    float4* partial;        // [pairs, 2, 256]: (max, sum of exp, label logit, flags) of units cut by a pair's range
     int M, V, C, P, rank, tiles_m, tiles_n, x_batched;
 };
+
+// Schedule of the (unit, 256-column block) tiles over G CTA pairs.  Whole
+// units go out in rounds, unit k G + g to pair g, so that all pairs sweep the
+// vocabulary together and each table tile is fetched from DRAM about once per
+// round; the tiles of the remaining units, r = (unit - rounds G) tiles_n + tn,
+// are split into contiguous balanced ranges, pair g owning [RT g / G, RT (g+1) / G).
+__host__ __device__ __forceinline__ int64_t range_begin(int64_t T, int g, int G) { return T * g / G; }
+__host__ __device__ __forceinline__ int pair_of_tile(int64_t t, int64_t T, int G) {
+    return (int)(((int64_t)G * (t + 1) - 1) / T);
+}
+
+struct CeSched {
+    int g, G, tiles_n, rounds;
+    int64_t round_tiles, rb, re;  // rounds * tiles_n; this pair's remainder range [rb, re)
+    __device__ CeSched(int g_, int G_, int units, int tiles_n_) : g(g_), G(G_), tiles_n(tiles_n_) {
+        rounds = units / G;
+        round_tiles = (int64_t)rounds * tiles_n;
+        const int64_t rt = (int64_t)(units - rounds * G) * tiles_n;
+        rb = range_begin(rt, g, G);
+        re = range_begin(rt, g + 1, G);
+    }
+    __device__ int64_t count() const { return round_tiles + (re - rb); }
+    __device__ void at(int64_t j, int& u, int& tn) const {
+        if (j < round_tiles) {
+            u = (int)(j / tiles_n) * G + g;
+            tn = (int)(j % tiles_n);
+        } else {
+            const int64_t t = rb + (j - round_tiles);
+            u = rounds * G + (int)(t / tiles_n);
+            tn = (int)(t % tiles_n);
+        }
+    }
+    // whole in this pair: a round unit, or a remainder unit inside [rb, re)
+    __device__ bool whole(int u) const {
+        if (u < rounds * G) return true;
+        const int64_t t0 = (int64_t)(u - rounds * G) * tiles_n;
+        return t0 >= rb && t0 + tiles_n <= re;
+    }
+};
+
+// Flags of a partial record.
+constexpr int kFound = 1, kOk = 2;
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x by the hardware approximation (exp(y) is evaluated as 2^(y log2 e)).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 32 lanes x 64 columns of float32 accumulators, loaded and waited for in one
+// statement so no use of the registers can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+    uint32_t r[64];
+    __syncwarp();
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Rounds 64 float32 logits to bf16 in place (round to nearest even, as the
+// tied-logits output does) and returns their maximum.
+__device__ __forceinline__ float round_bf16_max64(float (&v)[64]) {
+    __nv_bfloat162 m[8];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        m[i % 8] = i < 8 ? b : __hmax2(m[i % 8], b);
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(&b);
+        v[2 * i] = __uint_as_float(u << 16);
+        v[2 * i + 1] = __uint_as_float(u & 0xffff0000u);
+    }
+    m[0] = __hmax2(__hmax2(m[0], m[1]), __hmax2(m[2], m[3]));
+    m[4] = __hmax2(__hmax2(m[4], m[5]), __hmax2(m[6], m[7]));
+    m[0] = __hmax2(m[0], m[4]);
+    return fmaxf(__low2float(m[0]), __high2float(m[0]));
+}
+
+// sum_i exp(v[i] - vmax) with four independent partial sums.
+__device__ __forceinline__ float sum_exp64(const float (&v)[64], float vmax) {
+    const float t = vmax * kLog2e;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 64; ++i) s[i % 4] += ex2_approx(fmaf(v[i], kLog2e, -t));
+    return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmT,
@@ -51,6 +160,8 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     const uint32_t rank = cluster_rank();
     const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
     const int units = a.P * a.tiles_m;  // (candidate, 256-row block)
+    const CeSched sch(pair, pairs, units, a.tiles_n);
+    const int64_t n_mine = sch.count();
     const int k_blocks = (a.C + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -60,7 +171,7 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 8);  // 4 epilogue warps in each CTA
+            mbar_init(&tmem_empty[b], 16);  // 8 epilogue warps in each CTA
             mbar_init(&corr_full[b], 1);
             mbar_init(&corr_empty[b], 1);
         }
@@ -80,10 +191,12 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         uint32_t issued = 0, issue_parity = 0, c_issued = 0, c_parity = 0;
         bool ok = true;
         const int half = (int)rank * 128;
-        for (int u = pair; ok && u < units; u += pairs) {
+        for (int64_t j = 0; ok && j < n_mine; ++j) {
+            int u, tn;
+            sch.at(j, u, tn);
             const int p = u / a.tiles_m, tm = u % a.tiles_m;
             const int zx = a.x_batched ? p : 0;
-            for (int tn = 0; ok && tn < a.tiles_n; ++tn) {
+            {
                 if (!mbar_wait(&corr_empty[acc], acc_phase ^ 1, 71)) { ok = false; break; }
                 uint8_t* c = corr + acc * CE_CORR;
                 if (rank == 0) mbar_expect_tx(&corr_full[acc], 2 * CE_CORR);
@@ -95,7 +208,7 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
                 c_issued |= 1u << acc;
                 c_parity = (c_parity & ~(1u << acc)) | (acc_phase << acc);
                 if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-                const int k_start = (u * a.tiles_n + tn) % k_blocks;
+                const int k_start = (int)(((int64_t)u * a.tiles_n + tn) % k_blocks);
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!mbar_wait(&empty_bar[stage], phase ^ 1, 72)) { ok = false; break; }
                     const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
@@ -130,8 +243,8 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         int stage = 0, acc = 0;
         uint32_t phase = 0, acc_phase = 0;
         bool ok = true;
-        for (int u = pair; ok && u < units; u += pairs) {
-            for (int tn = 0; ok && tn < a.tiles_n; ++tn) {
+        for (int64_t j = 0; ok && j < n_mine; ++j) {
+            {
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, 73)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * 256;
@@ -167,57 +280,98 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             if (mbar_try_wait(&mma_done, 0)) break;
     } else if (warp >= 2) {
         // ---------------- epilogue: online log-sum-exp over the vocabulary ----------------
-        // Thread = one row of this CTA's 128; per 32-column chunk: the chunk's
-        // max and sum of exponentials, merged into the row's running pair.
-        const int quad = warp % 4;
+        // Thread = one row of this CTA's 128 and one half (128 columns) of
+        // every 256-column block; per 64-column chunk: the chunk's max and sum
+        // of exponentials, merged into the running pair of the row half.  At
+        // the last tile of a unit in this pair's range the halves merge; a
+        // unit the range holds whole gets its loss, a cut one a partial record.
+        __shared__ float s_half[2][4][128];  // second halves' (max, sum, label logit, flags), by parity
+        const int quad = warp % 4, half = (warp - 2) / 4, r = quad * 32 + lane;
         const uint32_t empty_leader = cluster_addr(&tmem_empty[0], 0);
-        int acc = 0;
+        const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + half * 128;
+        const int first_cut = sch.rounds * pairs + (int)(sch.rb / a.tiles_n);  // first remainder unit
+        int acc = 0, parity = 0, label = -1, row = 0;
         uint32_t acc_phase = 0;
-        bool ok = true;
-        for (int u = pair; u < units; u += pairs) {
-            const int p = u / a.tiles_m, tm = u % a.tiles_m;
-            const int row = tm * 256 + (int)rank * 128 + quad * 32 + lane;
-            // a label outside [0, V) never matches a column: its loss is NaN
-            int label = row < a.M ? a.labels[row] : -1;
-            if (label >= a.V) label = -1;
-            float run_max = -INFINITY, run_sum = 0.f, label_logit = 0.f;
-            bool found = false;
-            for (int tn = 0; tn < a.tiles_n; ++tn) {
-                ok = ok && mbar_wait(&tmem_full[acc], acc_phase, 76);
-                if (ok) {
-                    tc_fence_after();
+        bool ok = true, found = false;
+        float run_max = -INFINITY, run_sum = 0.f, label_logit = 0.f;
+        for (int64_t j = 0; j < n_mine; ++j) {
+            int u, tn;
+            sch.at(j, u, tn);
+            if (tn == 0 || j == sch.round_tiles) {
+                row = (u % a.tiles_m) * 256 + (int)rank * 128 + r;
+                // a label outside [0, V) never matches a column: its loss is NaN
+                label = row < a.M ? a.labels[row] : -1;
+                if (label >= a.V) label = -1;
+                run_max = -INFINITY;
+                run_sum = 0.f;
+                label_logit = 0.f;
+                found = false;
+            }
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(&tmem_full[acc], acc_phase, 76));
+            if (ok) {
+                tc_fence_after();
 #pragma unroll 1
-                    for (int c0 = 0; c0 < 256; c0 += 32) {
-                        float v[32];
-                        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + c0, v);
-                        const int col0 = tn * 256 + c0;
-                        float cmax = -INFINITY;
+                for (int c0 = 0; c0 < 128; c0 += 64) {
+                    const int col0 = tn * 256 + half * 128 + c0;
+                    if (col0 >= a.V) break;  // the rest of this block is past the vocabulary
+                    float v[64];
+                    tmem_ld64(t_row + acc * 256 + c0, v);
+                    float cmax = round_bf16_max64(v);  // v now holds the bf16 logits
+                    if (col0 + 64 > a.V) {
+                        cmax = -INFINITY;
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            // the logit tied_logits would return: float32 accumulator rounded to bf16
-                            v[i] = col0 + i < a.V ? __bfloat162float(__float2bfloat16_rn(v[i])) : -INFINITY;
+                        for (int i = 0; i < 64; ++i) {
+                            if (col0 + i >= a.V) v[i] = -INFINITY;
                             cmax = fmaxf(cmax, v[i]);
-                            if (col0 + i == label) {
+                        }
+                    }
+                    const unsigned li = (unsigned)(label - col0);
+                    if (__any_sync(0xffffffffu, li < 64u)) {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i)
+                            if (li == (unsigned)i) {
                                 label_logit = v[i];
                                 found = true;
                             }
-                        }
-                        if (cmax == -INFINITY) continue;  // every column past V
-                        float csum = 0.f;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) csum += expf(v[i] - cmax);
-                        const float m = fmaxf(run_max, cmax);
-                        run_sum = run_sum * expf(run_max - m) + csum * expf(cmax - m);
-                        run_max = m;
+                    }
+                    const float csum = sum_exp64(v, cmax);
+                    const float m = fmaxf(run_max, cmax);
+                    run_sum = run_sum * ex2_approx((run_max - m) * kLog2e) + csum * ex2_approx((cmax - m) * kLog2e);
+                    run_max = m;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0 && ok) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+            if (tn == a.tiles_n - 1 || j == n_mine - 1) {
+                if (half == 1) {
+                    s_half[parity][0][r] = run_max;
+                    s_half[parity][1][r] = run_sum;
+                    s_half[parity][2][r] = label_logit;
+                    s_half[parity][3][r] = (float)((found ? kFound : 0) | (ok ? kOk : 0));
+                }
+                epi_bar();
+                if (half == 0) {
+                    const float m1 = s_half[parity][0][r], s1 = s_half[parity][1][r];
+                    const int f1 = (int)s_half[parity][3][r];
+                    const int flags = ((found || (f1 & kFound)) ? kFound : 0) | ((ok && (f1 & kOk)) ? kOk : 0);
+                    const float m = fmaxf(run_max, m1);
+                    const float sum =
+                        run_sum * ex2_approx((run_max - m) * kLog2e) + s1 * ex2_approx((m1 - m) * kLog2e);
+                    const float lab = found ? label_logit : s_half[parity][2][r];
+                    if (sch.whole(u)) {
+                        if ((flags & kOk) && row < a.M)
+                            a.loss[(int64_t)(u / a.tiles_m) * a.M + row] =
+                                (flags & kFound) ? m + logf(sum) - lab : __int_as_float(0x7fc00000);
+                    } else {
+                        const int slot = u == first_cut ? 0 : 1;
+                        a.partial[((int64_t)pair * 2 + slot) * 256 + (int)rank * 128 + r] =
+                            make_float4(m, sum, lab, (float)flags);
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0 && ok) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
-                if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+                parity ^= 1;
             }
-            if (ok && row < a.M)
-                a.loss[(int64_t)p * a.M + row] = found ? run_max + logf(run_sum) - label_logit : __int_as_float(0x7fc00000);
         }
     }
     tc_fence_before();
@@ -225,6 +379,45 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     tc_fence_after();
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
+
+// Loss of every unit that the pair ranges cut, from the records of the pairs
+// that share it, merged the way the epilogue merges the two halves of a row.
+__global__ void tied_ce_merge_kernel(const float4* __restrict__ partial, float* __restrict__ loss, int M, int tiles_m,
+                                     int tiles_n, int units, int pairs) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)units * 256) return;
+    const int u = (int)(idx / 256), lr = (int)(idx % 256);
+    const int row = (u % tiles_m) * 256 + lr;
+    if (row >= M) return;
+    const int rounds = units / pairs, ur = u - rounds * pairs;
+    if (ur < 0) return;  // a round unit: written whole by its pair
+    const int64_t rt = (int64_t)(units - rounds * pairs) * tiles_n;
+    const int g_lo = pair_of_tile((int64_t)ur * tiles_n, rt, pairs);
+    const int g_hi = pair_of_tile((int64_t)(ur + 1) * tiles_n - 1, rt, pairs);
+    if (g_lo == g_hi) return;  // held whole by one range: written by the main kernel
+    const int slot_lo = range_begin(rt, g_lo, pairs) / tiles_n == ur ? 0 : 1;
+    float m = -INFINITY;
+    for (int g = g_lo; g <= g_hi; ++g)
+        if (range_begin(rt, g + 1, pairs) > range_begin(rt, g, pairs))
+            m = fmaxf(m, partial[((int64_t)g * 2 + (g == g_lo ? slot_lo : 0)) * 256 + lr].x);
+    float sum = 0.f, lab = 0.f;
+    int flags = kOk;
+    for (int g = g_lo; g <= g_hi; ++g) {
+        if (range_begin(rt, g + 1, pairs) == range_begin(rt, g, pairs)) continue;  // an empty range
+        const float4 rec = partial[((int64_t)g * 2 + (g == g_lo ? slot_lo : 0)) * 256 + lr];
+        const int f = (int)rec.w;
+        sum += rec.y * ex2_approx((rec.x - m) * kLog2e);
+        if (f & kFound) {
+            lab = rec.z;
+            flags |= kFound;
+        }
+        if (!(f & kOk)) flags &= ~kOk;
+    }
+    if (flags & kOk)
+        loss[(int64_t)(u / tiles_m) * M + row] = (flags & kFound) ? m + logf(sum) - lab : __int_as_float(0x7fc00000);
+}
+
+constexpr int kMaxPairs = 256;  // bound on the pairs of one launch (sizes the partial records)
 
 }  // namespace
 
@@ -237,7 +430,8 @@ bool tied_ce_ok(int P, int M, int V, int C, int rank) {
 
 size_t tied_ce_workspace(int P, int M, int V, int C, int rank) {
     const size_t q = (size_t)P * rank;
-    return Carver::need({(size_t)P * M * 16 * 2, q * C * 2, (size_t)V * q * 2}) + 256;
+    return Carver::need({(size_t)P * M * 16 * 2, q * C * 2, (size_t)V * q * 2, (size_t)kMaxPairs * 2 * 256 * 16}) +
+           256;
 }
 
 // CTA pairs that can be resident at once (0 if unknown).
@@ -266,7 +460,8 @@ int tied_ce(const void* x, int x_batched, const void* T, const uint32_t* keys, i
     __nv_bfloat16* U = cv.take<__nv_bfloat16>((size_t)P * M * 16);
     __nv_bfloat16* F1T = cv.take<__nv_bfloat16>((size_t)q * C);
     __nv_bfloat16* F2 = cv.take<__nv_bfloat16>((size_t)V * q);
-    if (!U || !F1T || !F2) return fail(ZG_ERR_WORKSPACE, "tied_ce: workspace too small");
+    float4* partial = cv.take<float4>((size_t)kMaxPairs * 2 * 256);
+    if (!U || !F1T || !F2 || !partial) return fail(ZG_ERR_WORKSPACE, "tied_ce: workspace too small");
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!al(x) || !al(T)) return fail(ZG_ERR_INVALID, "tied_ce: x and T must be 16-byte aligned");
     // table factors: F2 = A_op [V, q] (counter v*r + j), F1T = B^T [q, C] (counter c*r + j)
@@ -292,13 +487,23 @@ int tied_ce(const void* x, int x_batched, const void* T, const uint32_t* keys, i
     if (!tensor_map_bf16(&tx, x, 3, dx, sx, bx, true) || !tensor_map_bf16(&tt, T, 2, dt, stt, bt, true) ||
         !tensor_map_bf16(&tu, U, 3, du, su, bu, false) || !tensor_map_bf16(&tf, F2, 2, df, sf, bf, false))
         return fail(ZG_ERR_CUDA, "tied_ce: tensor maps");
-    CeArgs a{loss, labels, M, V, C, P, rank, (M + 255) / 256, (V + 255) / 256, x_batched != 0};
-    const int64_t units = (int64_t)P * a.tiles_m;
-    const int pairs = units < slots ? (int)units : slots;
+    CeArgs a{loss, labels, partial, M, V, C, P, rank, (M + 255) / 256, (V + 255) / 256, x_batched != 0};
+    const int units = P * a.tiles_m;
+    const int64_t n_tiles = (int64_t)units * a.tiles_n;
+    int pairs = slots < kMaxPairs ? slots : kMaxPairs;
+    if (n_tiles < pairs) pairs = (int)n_tiles;
     const size_t smem = (size_t)CE_SMEM + 1024;
-    zg::LaunchTimer zg_lt_("tied_ce", st);
-    tied_ce_pair_kernel<<<2 * pairs, THREADS, smem, st>>>(tx, tt, tu, tf, a);
-    return check_launch("tied_ce");
+    {
+        zg::LaunchTimer zg_lt_("tied_ce", st);
+        tied_ce_pair_kernel<<<2 * pairs, THREADS, smem, st>>>(tx, tt, tu, tf, a);
+        if (int e = check_launch("tied_ce")) return e;
+    }
+    if (units % pairs == 0) return 0;  // every unit went out whole in a round
+    zg::LaunchTimer zg_lt_("tied_ce_merge", st);
+    const int64_t n = (int64_t)units * 256;
+    tied_ce_merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partial, loss, M, a.tiles_m, a.tiles_n, units,
+                                                                     pairs);
+    return check_launch("tied_ce_merge");
 }
 
 int ce_error_word(int clear) { return ptx_error_word(clear); }
