@@ -221,6 +221,8 @@ def int8_layer_section(dev, args):
             "roofline": {"kernel": "int8_lut_gemm", "bound": "tensor", "achieved": ops / (gm / 1e3) / 1e12,
                          "peak": peak, "unit": "TOP/s", "frac": ops / (gm / 1e3) / 1e12 / peak,
                          "peak_source": "2x measured bf16 dense (no measured int8 figure)",
+                         "traffic": (traffic_for("int8_lut_gemm_p64") * P8 // 64
+                                     if traffic_for("int8_lut_gemm_p64") else None),
                          "launch_ms": gm}}
 
 
@@ -264,7 +266,7 @@ def tied_ce_section(dev, args):
             "roofline": {"kernel": "tied_ce", "bound": "tensor", "achieved": flops / (ce / 1e3) / 1e12,
                          "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": flops / (ce / 1e3) / 1e12 / pk["bf16_tflops"], "peak_source": pk["source"],
-                         "launch_ms": ce}}
+                         "traffic": traffic_for("tied_ce"), "launch_ms": ce}}
 
 
 # ---------------------------------------------------------------------------
