@@ -463,7 +463,9 @@ def run_ours(args):
     kernels = L.profile_end()
     barrier()
 
-    # end to end through the public API: pinned host batch + fitness in, metrics out
+    # end to end through the public API: the batch copied in from pinned host
+    # memory every generation, the step's metrics read back.  Eager form:
+    # evaluate_shard + (all-gather) + step_from_losses, the fitness from the host.
     opt = zg.ZeroGrad(manifest, zg.sgd(WL["lr"]), P, r, sigma, WL["seed"], WL["run_id"])
     params = {"w": W0}
     state = opt.init(params)
@@ -486,9 +488,36 @@ def run_ours(args):
     for i in range(min(args.warmup, 3)):
         Wc = e2e_step(Wc, i)
     barrier()
-    e2e_ms, _ = timed(e2e_step, args.steps, W0)
+    eager_ms, _ = timed(e2e_step, args.steps, W0)
+    eager_ms = max_over_ranks(eager_ms)
+    barrier()
+
+    # Captured form (ZeroGrad.capture / CapturedGeneration): the generation as
+    # one CUDA graph -- every candidate's output [256, 4096] materialised, its
+    # loss one element of that output, the fitness all-gather in the graph
+    # with more than one rank -- replayed with the batch copied in from
+    # pinned host memory and the metrics read back every generation.
+    def fwd_loss(p, ctx, batch, rng):
+        return ctx.linear(p, ("w",), batch)[0, 0].float(), None
+
+    cg = zg.CapturedGeneration(opt, {"w": W0}, fwd_loss, x, state=opt.init({"w": W0}),
+                               candidate_range=(a, P_local) if world > 1 else None,
+                               gather=(lambda l: zg.allgather_losses(l, sizes)) if world > 1 else None)
+    cstate = opt.init({"w": W0})
+
+    def captured_step(Wcur, gen):
+        nonlocal cstate
+        _, cstate, _ = cg.step(zg.ZeroGradState(gen, cstate.opt_state), x_host)
+        return Wcur
+
+    for i in range(min(args.warmup, 3)):
+        captured_step(None, i)
+    barrier()
+    e2e_ms, _ = timed(captured_step, args.steps, None)
     e2e_ms = max_over_ranks(e2e_ms)
     barrier()
+    del cg  # holds NCCL work with more than one rank: released before the process group
+    torch.cuda.synchronize()
 
     # the hidden-layer form of the same generation: every candidate has its own
     # input x_p [256, 4096] (seeded N(0, 0.02)), so x_p W is a batched GEMM on
@@ -529,6 +558,7 @@ def run_ours(args):
 
     value = P * args.steps / (ms / 1e3)
     e2e_value = P * args.steps / (e2e_ms / 1e3)
+    eager_value = P * args.steps / (eager_ms / 1e3)
     if rank == 0:
         pk = peaks()
         known = {k: v for k, v in kernels.items() if kernel_work(k, P_local, world)[0] is not None}
@@ -559,8 +589,12 @@ def run_ours(args):
             "profiled_ms_per_step": prof_ms / args.steps,
             "gpu_launches": launches,
             "clocks": clocks,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 4 * P_local,
-                    "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms / args.steps},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 8,
+                    "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms / args.steps,
+                    "api": "ZeroGrad.capture -> CapturedGeneration.step (the generation as one CUDA graph)"},
+            "e2e_eager": {"value": eager_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 4 * P_local,
+                          "d2h_bytes_per_step": 16, "ms_per_step": eager_ms / args.steps,
+                          "api": "evaluate_shard + step_from_losses (fitness from the host)"},
         }
         hg = h_kernels.get("batched_gemm")
         hidden = {"workload": "same generation with a per-candidate input x_p[256,4096] (seeded N(0,0.02)): "

@@ -265,3 +265,22 @@ def test_cpu_tensors_fail_loudly():
 
     with pytest.raises(ZgLibraryError):
         zg.perturbed_linear(torch.zeros(2, 4), torch.zeros(4, 3), zg.step_key(0, "r", 0, 1), 2, 0.1)
+
+
+def test_capture_refusals():
+    """A captured generation needs sgd (adamw's bias correction is a
+    per-step host value) and CUDA parameters; shards need a gather."""
+    from zerograd_b200._graph import CapturedGeneration
+    from zerograd_b200._lib import ZgLibraryError
+
+    m = _manifest()
+    params = {"linear": {"weight": torch.zeros(4, 3)}, "table": {"embed": torch.zeros(5, 3)},
+              "vector": {"scale": torch.zeros(3)}}
+    loss = lambda p, ctx, batch, rng: (torch.zeros(()), None)  # noqa: E731
+    with pytest.raises(NotImplementedError):
+        zg.ZeroGrad(m, zg.adamw(1e-3), 4, 2, 0.1, 0, "r").capture(params, loss, torch.zeros(2, 4))
+    opt = zg.ZeroGrad(m, zg.sgd(0.1), 4, 2, 0.1, 0, "r")
+    with pytest.raises(ZgLibraryError):
+        opt.capture(params, loss, torch.zeros(2, 4))
+    with pytest.raises(ValueError):
+        CapturedGeneration(opt, params, loss, torch.zeros(2, 4), candidate_range=(0, 2))

@@ -1,0 +1,88 @@
+"""A generation captured as a CUDA graph (ZeroGrad.capture) against the eager
+ZeroGrad.step of the same generations: bit-identical parameters and equal
+metrics; a generation with non-finite losses raises and leaves the captured
+parameters untouched."""
+import pytest
+import torch
+
+import zerograd_b200 as zg
+from zerograd_b200 import _lib as L
+
+pytestmark = pytest.mark.gpu
+
+
+def _small(dev):
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w"),
+                               zg.ManifestEntry(("b",), zg.ParameterLayout.VECTOR, "b")))
+    g = torch.Generator().manual_seed(3)
+    params = {"w": (torch.randn(256, 128, generator=g) * 0.05).to(torch.bfloat16).to(dev),
+              "b": (torch.randn(128, generator=g) * 0.01).to(torch.bfloat16).to(dev)}
+    batches = [torch.randn(64, 256, generator=g).to(torch.bfloat16).to(dev) for _ in range(4)]
+
+    def loss_fn(p, ctx, batch, rng):
+        y = ctx.linear(p, ("w",), batch) + ctx.vector(p, ("b",))
+        return (y.float() ** 2).mean(), None
+
+    return manifest, params, batches, loss_fn
+
+
+def test_captured_generations_match_eager(cuda):
+    manifest, params, batches, loss_fn = _small(cuda)
+    opt = zg.ZeroGrad(manifest, zg.sgd(0.05), 48, 8, 0.02, 0, "graph")
+    cg = opt.capture(params, loss_fn, batches[0])
+    pe, se = params, opt.init(params)
+    sc = opt.init(params)
+    n0 = L.launch_count()
+    for g in range(4):
+        pe, se, me = opt.step(se, pe, batches[g], loss_fn)
+        pc, sc, mc = cg.step(sc, batches[g])
+        assert sc.generation == se.generation == g + 1
+        for k in pe:
+            assert torch.equal(pc[k], pe[k]), (g, k)
+        assert (mc.mean_loss, mc.min_loss, mc.max_loss) == (me.mean_loss, me.min_loss, me.max_loss)
+    assert L.load().zg_device_error(1) == 0
+    assert L.launch_count() > n0
+
+
+def test_captured_generation_rejects_nonfinite_losses(cuda):
+    manifest, params, batches, loss_fn = _small(cuda)
+    opt = zg.ZeroGrad(manifest, zg.sgd(0.05), 32, 8, 0.02, 1, "graph-nan")
+    cg = opt.capture(params, loss_fn, batches[0])
+    state = opt.init(params)
+    _, state, _ = cg.step(state, batches[1])
+    before = {k: v.clone() for k, v in cg.params.items()}
+    bad = batches[2].clone()
+    bad[5, 7] = float("nan")
+    with pytest.raises(ValueError, match="finite"):
+        cg.step(state, bad)
+    for k in before:
+        assert torch.equal(cg.params[k], before[k])
+    # the next good generation proceeds from the unchanged parameters
+    pc, _, m = cg.step(state, batches[3])
+    pe, _, me = opt.step(state, before, batches[3], loss_fn)
+    for k in pe:
+        assert torch.equal(pc[k], pe[k])
+
+
+def test_captured_bench_generation(cuda):
+    """The perturbed-GEMM generation (P=256, rank 8, shared x[256,4096],
+    W[4096,4096] bf16, SGD) with a one-element loss per candidate."""
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w"),))
+    g = torch.Generator(device=cuda).manual_seed(0)
+    W = (torch.randn(4096, 4096, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    xs = [(torch.randn(256, 4096, generator=g, device=cuda) * 0.02).to(torch.bfloat16) for _ in range(2)]
+
+    def loss_fn(p, ctx, batch, rng):
+        y = ctx.linear(p, ("w",), batch)
+        return y[0, 0].float(), None
+
+    opt = zg.ZeroGrad(manifest, zg.sgd(1e-3), 256, 8, 0.01, 0, "bench")
+    cg = opt.capture({"w": W}, loss_fn, xs[0])
+    pe, se = {"w": W}, opt.init({"w": W})
+    sc = se
+    for i in range(2):
+        pe, se, me = opt.step(se, pe, xs[i], loss_fn)
+        pc, sc, mc = cg.step(sc, xs[i])
+        assert torch.equal(pc["w"], pe["w"])
+        assert mc.mean_loss == me.mean_loss
+    assert L.load().zg_device_error(1) == 0

@@ -89,3 +89,56 @@ def test_process_group_matches_single_process():
     for k in p0:
         torch.testing.assert_close(p0[k], params[k].float().cpu(), rtol=1e-2, atol=1e-2)
     assert m0 == m1
+
+
+def _worker_captured(rank, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import zerograd_b200 as zg
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        opt, params, x, loss_fn = _problem(dev)
+        opt = zg.ZeroGrad(opt.manifest, zg.sgd(0.05), 48, 8, 0.02, 0, "multi-graph")
+        dz = zg.DistributedZeroGrad(opt, None, loss_fn, weights=[1.0, 2.0])
+        cg = dz.capture(params, x)
+        pe, se = params, opt.init(params)
+        sc = opt.init(params)
+        same = True
+        for g in range(3):
+            xg = x * (1.0 + 0.25 * g)
+            pe, se, me = dz.step(se, pe, xg)
+            pc, sc, mc = cg.step(sc, xg)
+            same = same and all(torch.equal(pc[k], pe[k]) for k in pe) and mc.mean_loss == me.mean_loss
+        q.put((rank, same, {k: v.float().cpu() for k, v in pc.items()}))
+        del cg  # the graph holds NCCL work: released before the process group
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_captured_process_group_generation():
+    """Each rank captures its shard's forward, the NCCL fitness all-gather and
+    the replicated completion; replays match the eager steps bit for bit."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_captured, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=300) for _ in procs], key=lambda t: t[0])
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    (_, same0, p0), (_, same1, p1) = out
+    assert same0 and same1
+    for k in p0:
+        assert torch.equal(p0[k], p1[k]), k

@@ -219,6 +219,26 @@ class DistributedZeroGrad:
         return self._optimizer.init(params)
 
     # -- one generation -----------------------------------------------------
+    def capture(self, params: ParameterTree, batch: Any, *, state: ZeroGradState | None = None,
+                rng: torch.Tensor | None = None, warmup: int = 2):
+        """The generation ``step`` runs in process-group mode, captured as a
+        CUDA graph: this process's shard of the forward, the fitness
+        all-gather (NCCL, in the graph) and the replicated completion.  Every
+        rank must capture together.  Release the returned object before the
+        process group is destroyed."""
+        from ._graph import CapturedGeneration
+
+        if not self._pg_mode:
+            raise NotImplementedError("capture is for process-group mode (one process per GPU)")
+        if self._closed:
+            raise RuntimeError("coordinator has been shut down")
+        a, b = shard_ranges(self._partition_sizes)[self._rank]
+        sizes, group = list(self._partition_sizes), self._group
+        return CapturedGeneration(self._optimizer, _to_device(_materialize_tree(params), self._devices[0]),
+                                  self._loss_fn, batch, state=state, candidate_range=(a, b - a),
+                                  gather=lambda local: allgather_losses(local, sizes, group), rng=rng,
+                                  warmup=warmup)
+
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, *, rng: torch.Tensor | None = None):
         if rng is None:
             rng = make_key(0)

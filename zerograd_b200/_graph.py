@@ -1,0 +1,176 @@
+"""One ES generation captured as a CUDA graph.
+
+``ZeroGrad.step`` issues every kernel of a generation from Python: the
+candidate keys, each context op under ``vmap``, the fitness shaping, the
+factor replay and the optimizer step, about half a millisecond of host work
+for a few hundred microseconds of GPU work at the perturbed-GEMM size.  A
+:class:`CapturedGeneration` records that launch sequence once and replays
+it for every later generation.  What changes between generations is data,
+not launches:
+
+* the base key ``step_key(seed, run_id, generation, version)`` is copied
+  into a device buffer before each replay, and the captured candidate keys
+  are derived from that buffer in the graph (every factor draw, forward and
+  replay kernel reads keys from device memory);
+* the batch is copied into the captured batch buffers (from pinned host
+  memory, or from the device);
+* the parameters live in captured buffers; the graph writes the updated
+  parameters to its own output buffers, which are copied back after the
+  losses have been checked, so a generation with non-finite losses leaves
+  the parameters as they were and raises, as ``step_from_losses`` does.
+
+Each replay gives the same bits as the eager ``evaluate_shard`` +
+``step_from_losses`` of the same generation.  Capturable optimizers are the
+ones whose kernels take no per-generation host value: ``sgd``.  (AdamW's bias
+correction 1 - b^t is a host value that changes every step.)
+
+With a process group, ``gather`` (the fitness all-gather) is captured in the
+graph as well, and each process captures its own shard of candidates.
+"""
+from __future__ import annotations
+
+from typing import Any, Callable
+
+import torch
+from torch.utils import _pytree as pytree
+
+from . import _lib as L
+from . import _ops
+from ._manifest import ParameterTree
+from ._transforms import _leaves, tree_get
+
+
+def _clone_tree(tree):
+    return pytree.tree_map(lambda t: t.clone() if isinstance(t, torch.Tensor) else t, tree)
+
+
+class CapturedGeneration:
+    """A generation of ``optimizer`` (evaluate + complete) as a CUDA graph.
+
+    Build it with :meth:`ZeroGrad.capture`.  :meth:`step` then runs one
+    generation: ``params, state, metrics = cg.step(state, batch)``.  The
+    returned parameters are the captured buffers themselves: the next
+    ``step`` updates them in place (clone them to keep a generation).
+    """
+
+    def __init__(self, optimizer, params: ParameterTree, loss_fn: Callable, batch: Any, *, state=None,
+                 candidate_range: tuple[int, int] | None = None,
+                 gather: Callable[[torch.Tensor], torch.Tensor] | None = None,
+                 rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2):
+        from ._optimizer import ZeroGradState, _device_of, _materialize_tree
+        from ._transforms import sgd
+
+        if not isinstance(optimizer.transform, sgd):
+            raise NotImplementedError("capture needs an optimizer whose kernels take no per-generation host "
+                                      "value: sgd (adamw's bias correction changes every step)")
+        optimizer.manifest.validate(params)
+        self._opt = optimizer
+        self._gather = gather
+        self._rng = rng
+        P = optimizer.population_size
+        self._range = candidate_range if candidate_range is not None else (0, P)
+        if gather is None and self._range != (0, P):
+            raise ValueError("a shard of the population needs a gather of the losses")
+        self.device = _device_of(params)
+        dev = self.device
+        if dev.type != "cuda":
+            raise L.ZgLibraryError("capture runs on CUDA devices only; there is no CPU fallback")
+        self._params = _clone_tree(_materialize_tree(params))
+        self._batch = _clone_tree(batch)
+        self._loss_fn = loss_fn
+        self._prefetch = prefetch_replay
+        self._base_host = torch.empty(2, dtype=torch.uint32).pin_memory()
+        self._base_dev = torch.empty((1, 2), dtype=torch.uint32, device=dev)
+        self._ids = torch.arange(P, dtype=torch.int32, device=dev)
+        g0 = state.generation if state is not None else 0
+        opt_state0 = state.opt_state if state is not None else optimizer.init(self._params).opt_state
+        self._state_cls = ZeroGradState
+
+        # warm-up outside the graph: first-call setup (kernel attributes, the
+        # factor-cache budget, the communicator) must not happen in a capture
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for i in range(max(1, warmup)):
+                self._set_base(g0 + i)
+                self._generation(g0 + i, opt_state0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+
+        self._graph = torch.cuda.CUDAGraph()
+        self._set_base(g0)
+        with torch.cuda.graph(self._graph):
+            capture_stream = L.stream_ptr(dev).value
+            self._out = self._generation(g0, opt_state0)
+        torch.cuda.synchronize(dev)
+        optimizer._forget_keys(capture_stream)
+
+    def _set_base(self, generation: int) -> None:
+        self._base_host.copy_(self._opt.base_key(generation))
+        self._base_dev.copy_(self._base_host.view(1, 2), non_blocking=True)
+
+    def _generation(self, generation: int, opt_state):
+        """The launch sequence of one generation, keys read from the device
+        base-key buffer."""
+        opt, dev, (start, count) = self._opt, self.device, self._range
+        P = opt.population_size
+        cks_all = _ops.launch_fold_in(self._base_dev, self._ids)
+        opt._seed_keys(generation, 0, P, dev, cks_all)
+        if (start, count) != (0, P):
+            opt._seed_keys(generation, start, count, dev, cks_all[start:start + count])
+        losses = opt._evaluate_shard(self._params, generation, self._loss_fn, self._batch,
+                                     range(start, start + count), rng=self._rng,
+                                     prefetch_replay=self._prefetch)
+        if self._gather is not None:
+            losses = self._gather(losses.to(torch.float32))
+        state = self._state_cls(generation, opt_state)
+        new_params, new_opt_state, metrics = opt._complete(state, self._params, losses, cand_keys=cks_all)
+        return new_params, new_opt_state, metrics
+
+    @property
+    def params(self) -> ParameterTree:
+        """The captured parameter buffers (the current parameters)."""
+        return self._params
+
+    def load_params(self, params: ParameterTree) -> None:
+        """Copy `params` (same tree and shapes) into the captured buffers."""
+        for path, t in _leaves(self._params):
+            t.copy_(tree_get(params, path), non_blocking=True)
+
+    def step(self, state, batch: Any = None):
+        """One generation: copy `batch` (if given) into the captured batch,
+        replay the graph, check the losses, and update the parameters.
+        Returns (params, new state, metrics) like ``ZeroGrad.step``."""
+        if not isinstance(state, self._state_cls):
+            raise TypeError("state must be a ZeroGradState")
+        if batch is not None:
+            dst = pytree.tree_leaves(self._batch)
+            src = pytree.tree_leaves(batch)
+            if len(dst) != len(src):
+                raise ValueError("batch does not match the captured batch's structure")
+            for d, s in zip(dst, src):
+                if isinstance(d, torch.Tensor):
+                    if tuple(s.shape) != tuple(d.shape):
+                        raise ValueError(f"batch leaf of shape {tuple(s.shape)}; captured {tuple(d.shape)}")
+                    d.copy_(s, non_blocking=True)
+        self._set_base(state.generation)
+        self._graph.replay()
+        new_params, new_opt_state, metrics = self._out
+        m = self._opt._metrics(state.generation, metrics)  # raises before the parameters change
+        for path, t in _leaves(self._params):
+            t.copy_(tree_get(new_params, path), non_blocking=True)
+        opt_state = _advance_state(state.opt_state, new_opt_state)
+        return self._params, self._state_cls(state.generation + 1, opt_state), m
+
+
+def _advance_state(old, captured):
+    """The optimizer state after one replay: the captured generation's host
+    fields advanced from `old` (sgd keeps only a counter)."""
+    from ._transforms import SgdState
+
+    if isinstance(old, SgdState):
+        return SgdState(count=old.count + 1)
+    return captured
+
+
+__all__ = ["CapturedGeneration"]

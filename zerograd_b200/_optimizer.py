@@ -11,6 +11,7 @@ metrics.
 """
 from __future__ import annotations
 
+import collections
 import math
 from collections.abc import Callable, Mapping
 from dataclasses import dataclass
@@ -18,6 +19,7 @@ from typing import Any
 
 import torch
 
+from . import _lib as L
 from . import _ops
 from ._candidate import CandidateContext
 from ._fitness import _check_shape_dtype
@@ -80,6 +82,39 @@ class ZeroGrad:
         self._sigma = sigma
         self._seed = seed
         self._run_id = run_id
+        # Per-generation host and device keys, reused by the calls of one
+        # generation (evaluate, prefetch, completion): (tag, device, stream) -> tensor
+        self._keys_memo: collections.OrderedDict = collections.OrderedDict()
+
+    def _memo(self, tag, device: torch.device, make):
+        """A key tensor of this optimizer, computed once per (tag, device,
+        stream): device keys are only read on the stream that wrote them."""
+        k = (tag, device, L.stream_ptr(device).value if device.type == "cuda" else None)
+        v = self._keys_memo.get(k)
+        if v is None:
+            v = make()
+            self._keys_memo[k] = v
+            while len(self._keys_memo) > 16:
+                self._keys_memo.popitem(last=False)
+        return v
+
+    def _seed_keys(self, generation: int, start: int, count: int, device: torch.device, cks: torch.Tensor) -> None:
+        """Use `cks` as the candidate keys of ids [start, start + count) of a
+        generation on the current stream (a captured generation derives them
+        from its device base-key buffer)."""
+        self._keys_memo[(("ck", generation, start, count), device, L.stream_ptr(device).value)] = cks
+
+    def _forget_keys(self, stream_value) -> None:
+        """Drop the keys kept for one stream (a finished capture's)."""
+        for k in [k for k in self._keys_memo if k[2] == stream_value]:
+            del self._keys_memo[k]
+
+    def _candidate_keys_range(self, generation: int, start: int, count: int, device: torch.device):
+        """Candidate keys of ids [start, start + count) of a generation."""
+        def make():
+            ids = torch.arange(start, start + count, dtype=torch.int32, device=device)
+            return candidate_keys(self.base_key(generation), ids)
+        return self._memo(("ck", generation, start, count), device, make)
 
     def init(self, params: ParameterTree) -> ZeroGradState:
         self._manifest.validate(params)
@@ -118,7 +153,9 @@ class ZeroGrad:
 
     def base_key(self, generation: int) -> torch.Tensor:
         """Host-side base key of a generation (passed to kernels by value)."""
-        return step_key(self._seed, self._run_id, generation, self._manifest.version)
+        cpu = torch.device("cpu")
+        return self._memo(("base", generation, self._manifest.version), cpu,
+                          lambda: step_key(self._seed, self._run_id, generation, self._manifest.version)).clone()
 
     def evaluate_shard(self, params: ParameterTree, generation: int, loss_fn: LossFn, batch: Any,
                        candidate_ids, *, rng: torch.Tensor | None = None,
@@ -139,18 +176,26 @@ class ZeroGrad:
         device = _device_of(params)
         if id_range is None:
             id_range = _host_range(candidate_ids)
+        base = self.base_key(generation)
         if id_range is not None:
-            # built on the device: a host-built id tensor would need a copy that synchronises the stream
-            ids = torch.arange(id_range[0], id_range[0] + id_range[1], dtype=torch.int32, device=device)
+            # keys built on the device (a host-built id tensor would need a
+            # copy that synchronises the stream), once per generation and range
+            start, count = id_range
+            cks = self._candidate_keys_range(generation, start, count, device)
+            if rng is None:
+                def make_rngs():
+                    ids = torch.arange(start, start + count, dtype=torch.int32, device=device)
+                    return _ops.launch_fold_in(make_key(0).reshape(1, 2), ids)
+                rngs = self._memo(("rng", start, count), device, make_rngs)
+            else:
+                ids = torch.arange(start, start + count, dtype=torch.int32, device=device)
+                rngs = _ops.launch_fold_in(rng.reshape(1, 2), ids)
         else:
             ids = torch.as_tensor(candidate_ids, device=device)
-        if ids.ndim != 1:
-            raise ValueError("candidate_ids must be one-dimensional")
-        if rng is None:
-            rng = make_key(0)
-        base = self.base_key(generation)
-        cks = candidate_keys(base, ids)
-        rngs = _ops.launch_fold_in(rng.reshape(1, 2), ids)
+            if ids.ndim != 1:
+                raise ValueError("candidate_ids must be one-dimensional")
+            cks = candidate_keys(base, ids)
+            rngs = _ops.launch_fold_in((make_key(0) if rng is None else rng).reshape(1, 2), ids)
         manifest, rank, sigma = self._manifest, self._rank, self._sigma
 
         def evaluate_candidate(ck, crng):
@@ -158,7 +203,7 @@ class ZeroGrad:
             loss, _aux = loss_fn(params, ctx, batch, crng)
             return loss
 
-        if ids.numel() == 0:
+        if cks.shape[0] == 0:
             return torch.empty(0, dtype=torch.float32, device=device)
         if id_range is None:
             return torch.func.vmap(evaluate_candidate)(cks, rngs)
@@ -166,13 +211,13 @@ class ZeroGrad:
         if prefetch_replay and id_range[1] < self._population_size:
             # a shard whose process also replays the whole population: its
             # replay factors are drawn on a second stream while the forward runs
-            self._prefetch_replay(params, base, base_words, device)
+            self._prefetch_replay(params, generation, base_words, device)
         # A contiguous id range known on the host: the factors drawn by the
         # forward ops are kept for this generation's replay.
         with _ops.generation_scope(base_words, id_range[0], id_range[1], cks):
             return torch.func.vmap(evaluate_candidate)(cks, rngs)
 
-    def _prefetch_replay(self, params, base, base_words, device) -> None:
+    def _prefetch_replay(self, params, generation, base_words, device) -> None:
         entries = []
         for entry in self._manifest.entries:
             if entry.layout is ParameterLayout.VECTOR:
@@ -183,9 +228,8 @@ class ZeroGrad:
                                 int(p.shape[0]), int(p.shape[1]), self._rank))
         if not entries or torch.cuda.get_device_capability(device) != (10, 0):
             return
-        ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
-        gen = _ops._Generation(base_words, 0, self._population_size, candidate_keys(base, ids))
-        _ops.prefetch_replay_factors(gen, entries)
+        cks = self._candidate_keys_range(generation, 0, self._population_size, device)
+        _ops.prefetch_replay_factors(_ops._Generation(base_words, 0, self._population_size, cks), entries)
 
     # -- completion ---------------------------------------------------------
 
@@ -203,6 +247,27 @@ class ZeroGrad:
             raise ValueError(f"losses must have {self._population_size} entries, got {losses.shape[0]}")
 
     def _step_from_losses(self, state, params, losses, cand_keys: torch.Tensor | None = None):
+        new_params, new_opt_state, metrics = self._complete(state, params, losses, cand_keys)
+        # The one host sync of a generation, after all its work is queued.  The
+        # update wrote new tensors only, so rejecting non-finite losses here
+        # leaves params and state exactly as they were.
+        return new_params, ZeroGradState(generation=state.generation + 1, opt_state=new_opt_state), \
+            self._metrics(state.generation, metrics)
+
+    def _metrics(self, generation: int, metrics: torch.Tensor) -> StepMetrics:
+        """Host metrics from the shaping kernel's [mean, min, max, non-finite
+        count]; raises on non-finite losses (``_fitness.py:37-48``)."""
+        m = metrics.cpu()
+        if m[3].item() > 0:
+            raise ValueError("candidate losses must be finite")
+        return StepMetrics(generation=generation, mean_loss=float(m[0]), min_loss=float(m[1]),
+                           max_loss=float(m[2]), population_size=self._population_size)
+
+    def _complete(self, state, params, losses, cand_keys: torch.Tensor | None = None):
+        """Device part of a generation's completion, all queued on the
+        current stream with no host synchronisation: shaping, replay and the
+        optimizer step.  Returns (new params, new optimizer state, device
+        metrics [mean, min, max, non-finite count])."""
         self._check_losses(losses)
         device = _device_of(params)
         losses = losses.to(device)
@@ -211,8 +276,7 @@ class ZeroGrad:
         base = self.base_key(generation)
         base_words = tuple(int(v) for v in base)
         if cand_keys is None:
-            ids = torch.arange(self._population_size, dtype=torch.int32, device=device)
-            cand_keys = candidate_keys(base, ids)
+            cand_keys = self._candidate_keys_range(generation, 0, self._population_size, device)
         gen = _ops._Generation(base_words, 0, self._population_size, cand_keys)
         descent: dict = {}
         fused = is_fused(self._transform)
@@ -234,15 +298,7 @@ class ZeroGrad:
             grads = _build_pseudo_grad(descent, params)
             updates, new_opt_state = self._transform.update(grads, state.opt_state, params)
             new_params = apply_updates(params, updates)
-        # The one host sync of a generation, after all its work is queued.  The
-        # update wrote new tensors only, so rejecting non-finite losses here
-        # leaves params and state exactly as they were.
-        m = metrics.cpu()
-        if m[3].item() > 0:
-            raise ValueError("candidate losses must be finite")
-        metrics_out = StepMetrics(generation=generation, mean_loss=float(m[0]), min_loss=float(m[1]),
-                                  max_loss=float(m[2]), population_size=self._population_size)
-        return new_params, ZeroGradState(generation=generation + 1, opt_state=new_opt_state), metrics_out
+        return new_params, new_opt_state, metrics
 
     def catch_up(self, state: ZeroGradState, params: ParameterTree, loss_history) -> tuple:
         """Replay a loss history: one ``step_from_losses`` per recorded
@@ -257,6 +313,16 @@ class ZeroGrad:
         for losses in loss_history:
             params, state, metrics = self.step_from_losses(state, params, torch.as_tensor(losses))
         return params, state, metrics
+
+    def capture(self, params: ParameterTree, loss_fn: LossFn, batch: Any, *, state: ZeroGradState | None = None,
+                rng: torch.Tensor | None = None, warmup: int = 2):
+        """The generation ``step`` runs, captured as a CUDA graph
+        (:class:`CapturedGeneration`): replaying it costs one graph launch
+        instead of the per-op host work.  `params` and `batch` give the
+        shapes and the initial values; the graph keeps its own copies."""
+        from ._graph import CapturedGeneration
+
+        return CapturedGeneration(self, params, loss_fn, batch, state=state, rng=rng, warmup=warmup)
 
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, loss_fn: LossFn, *,
              rng: torch.Tensor | None = None):
@@ -277,8 +343,10 @@ def _host_range(candidate_ids):
     the host (a range, a list or a CPU tensor); None otherwise (reading a
     device tensor would cost a synchronisation)."""
     if isinstance(candidate_ids, range):
-        vals = candidate_ids
-    elif isinstance(candidate_ids, (list, tuple)):
+        if len(candidate_ids) == 0 or (candidate_ids.step != 1 and len(candidate_ids) > 1):
+            return None
+        return candidate_ids.start, len(candidate_ids)
+    if isinstance(candidate_ids, (list, tuple)):
         vals = candidate_ids
     elif isinstance(candidate_ids, torch.Tensor) and not candidate_ids.is_cuda and candidate_ids.ndim == 1:
         vals = candidate_ids.tolist()
