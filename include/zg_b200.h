@@ -347,6 +347,13 @@ ZG_API int zg_adamw_update(const void* param, void* param_out, int dtype, const 
 ZG_API int zg_sgd_update(const void* param, void* param_out, int dtype, const float* descent,
                          int64_t n, double lr, void* stream);
 
+/* Copy `bytes` from src to dst when *flag == 0 (a float count), else leave
+ * dst as it is.  A captured generation writes its update back with this,
+ * the flag being the non-finite count that zg_shape_fitness wrote to
+ * metrics[3]: losses that are not all finite change no parameter
+ * (_fitness.py:37-48 rejects them before any state changes). */
+ZG_API int zg_copy_if_zero(void* dst, const void* src, size_t bytes, const float* flag, void* stream);
+
 /* ------------------------------------------------- integer QAT linear -- */
 
 /* Integer linear with LUT activation for P candidates (no reference

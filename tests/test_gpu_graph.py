@@ -86,3 +86,44 @@ def test_captured_bench_generation(cuda):
         assert torch.equal(pc["w"], pe["w"])
         assert mc.mean_loss == me.mean_loss
     assert L.load().zg_device_error(1) == 0
+
+
+def test_enqueued_generations_match_eager(cuda):
+    """Generations queued back to back; a non-finite one in the middle is
+    rejected (its result raises) and the next starts from unchanged params."""
+    manifest, params, batches, loss_fn = _small(cuda)
+    opt = zg.ZeroGrad(manifest, zg.sgd(0.05), 48, 8, 0.02, 2, "graph-queue")
+    cg = opt.capture(params, loss_fn, batches[0])
+    bad = batches[2].clone()
+    bad[0, 0] = float("inf")
+    seq = [batches[0], batches[1], bad, batches[3]]
+    state = opt.init(params)
+    pending = []
+    for b in seq:
+        _, state, p = cg.enqueue(state, b)
+        pending.append(p)
+    got = cg.params
+    pe, se = params, opt.init(params)
+    for i, b in enumerate(seq):
+        if i == 2:
+            with pytest.raises(ValueError, match="finite"):
+                pending[i].result()
+            se = zg.ZeroGradState(se.generation + 1, se.opt_state)  # the queue moved on a generation
+            continue
+        pe, se, me = opt.step(se, pe, b, loss_fn)
+        assert pending[i].result().mean_loss == me.mean_loss
+    for k in pe:
+        assert torch.equal(got[k], pe[k])
+
+
+@pytest.mark.parametrize("nbytes,offset", [(4096 * 4096 * 2, 0), (1001, 0), (4099, 3)])
+def test_copy_if_zero(cuda, nbytes, offset):
+    from zerograd_b200 import _ops
+
+    src = torch.randint(0, 255, (nbytes + offset,), dtype=torch.uint8, device=cuda)[offset:]
+    for flag, copies in ((0.0, True), (2.0, False), (float("nan"), False)):
+        dst = torch.zeros(nbytes + offset, dtype=torch.uint8, device=cuda)[offset:]
+        _ops.launch_copy_if_zero(dst, src, torch.tensor([flag], device=cuda))
+        assert torch.equal(dst, src) == copies
+        if not copies:
+            assert int(dst.sum()) == 0

@@ -15,9 +15,15 @@ not launches:
 * the batch is copied into the captured batch buffers (from pinned host
   memory, or from the device);
 * the parameters live in captured buffers; the graph writes the updated
-  parameters to its own output buffers, which are copied back after the
-  losses have been checked, so a generation with non-finite losses leaves
-  the parameters as they were and raises, as ``step_from_losses`` does.
+  parameters to its own output buffers and copies them back at its end,
+  on the device, only when the shaping kernel counted no non-finite loss:
+  a rejected generation leaves the parameters as they were, and ``step``
+  raises as ``step_from_losses`` does.
+
+``step`` reads the metrics back every generation (a synchronisation, as the
+reference's ``float(jnp.mean(losses))``); ``enqueue`` queues a generation
+and returns a handle whose ``result()`` does that read later, so successive
+generations keep the GPU busy.
 
 Each replay gives the same bits as the eager ``evaluate_shard`` +
 ``step_from_losses`` of the same generation.  Capturable optimizers are the
@@ -78,8 +84,9 @@ class CapturedGeneration:
         self._params = _clone_tree(_materialize_tree(params))
         self._batch = _clone_tree(batch)
         self._loss_fn = loss_fn
-        self._prefetch = prefetch_replay
-        self._base_host = torch.empty(2, dtype=torch.uint32).pin_memory()
+        # a shard replays the whole population: its replay factors are drawn
+        # on a second stream (a parallel branch of the graph) during the forward
+        self._prefetch = prefetch_replay or self._range != (0, P)
         self._base_dev = torch.empty((1, 2), dtype=torch.uint32, device=dev)
         self._ids = torch.arange(P, dtype=torch.int32, device=dev)
         g0 = state.generation if state is not None else 0
@@ -93,23 +100,29 @@ class CapturedGeneration:
         with torch.cuda.stream(side):
             for i in range(max(1, warmup)):
                 self._set_base(g0 + i)
-                self._generation(g0 + i, opt_state0)
+                self._generation(g0 + i, opt_state0, copy_back=False)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
 
         self._graph = torch.cuda.CUDAGraph()
         self._set_base(g0)
+        n0 = L.launch_count()
         with torch.cuda.graph(self._graph):
             capture_stream = L.stream_ptr(dev).value
-            self._out = self._generation(g0, opt_state0)
+            self._out = self._generation(g0, opt_state0, copy_back=True)
         torch.cuda.synchronize(dev)
         optimizer._forget_keys(capture_stream)
+        #: this library's kernels in one replay of the graph
+        self.kernels_per_generation = L.launch_count() - n0
 
     def _set_base(self, generation: int) -> None:
-        self._base_host.copy_(self._opt.base_key(generation))
-        self._base_dev.copy_(self._base_host.view(1, 2), non_blocking=True)
+        # a fresh pinned buffer per call: the pinned allocator reuses it only
+        # after this copy has run, so queued generations never race on it
+        host = torch.empty((1, 2), dtype=torch.uint32, pin_memory=True)
+        host.copy_(self._opt.base_key(generation).view(1, 2))
+        self._base_dev.copy_(host, non_blocking=True)
 
-    def _generation(self, generation: int, opt_state):
+    def _generation(self, generation: int, opt_state, copy_back: bool):
         """The launch sequence of one generation, keys read from the device
         base-key buffer."""
         opt, dev, (start, count) = self._opt, self.device, self._range
@@ -125,6 +138,12 @@ class CapturedGeneration:
             losses = self._gather(losses.to(torch.float32))
         state = self._state_cls(generation, opt_state)
         new_params, new_opt_state, metrics = opt._complete(state, self._params, losses, cand_keys=cks_all)
+        if copy_back:
+            flag = metrics[3:4]  # non-finite loss count
+            for path, t in _leaves(self._params):
+                new = tree_get(new_params, path)
+                if new is not t:
+                    _ops.launch_copy_if_zero(t, new.contiguous(), flag)
         return new_params, new_opt_state, metrics
 
     @property
@@ -137,10 +156,7 @@ class CapturedGeneration:
         for path, t in _leaves(self._params):
             t.copy_(tree_get(params, path), non_blocking=True)
 
-    def step(self, state, batch: Any = None):
-        """One generation: copy `batch` (if given) into the captured batch,
-        replay the graph, check the losses, and update the parameters.
-        Returns (params, new state, metrics) like ``ZeroGrad.step``."""
+    def _queue(self, state, batch) -> None:
         if not isinstance(state, self._state_cls):
             raise TypeError("state must be a ZeroGradState")
         if batch is not None:
@@ -155,12 +171,42 @@ class CapturedGeneration:
                     d.copy_(s, non_blocking=True)
         self._set_base(state.generation)
         self._graph.replay()
-        new_params, new_opt_state, metrics = self._out
-        m = self._opt._metrics(state.generation, metrics)  # raises before the parameters change
-        for path, t in _leaves(self._params):
-            t.copy_(tree_get(new_params, path), non_blocking=True)
-        opt_state = _advance_state(state.opt_state, new_opt_state)
-        return self._params, self._state_cls(state.generation + 1, opt_state), m
+
+    def _next_state(self, state):
+        return self._state_cls(state.generation + 1, _advance_state(state.opt_state, self._out[1]))
+
+    def step(self, state, batch: Any = None):
+        """One generation: copy `batch` (if given) into the captured batch,
+        replay the graph and read its metrics.  Returns (params, new state,
+        metrics) like ``ZeroGrad.step``; raises ValueError, with the
+        parameters unchanged, when a loss is not finite."""
+        self._queue(state, batch)
+        m = self._opt._metrics(state.generation, self._out[2])
+        return self._params, self._next_state(state), m
+
+    def enqueue(self, state, batch: Any = None):
+        """Queue one generation without waiting for it.  Returns (params, new
+        state, pending); ``pending.result()`` waits and returns the metrics,
+        or raises ValueError if that generation's losses were not all finite
+        (its update was then not applied; generations queued after it start
+        from the unchanged parameters)."""
+        self._queue(state, batch)
+        host = torch.empty(4, dtype=torch.float32, pin_memory=True)
+        host.copy_(self._out[2], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.device))
+        return self._params, self._next_state(state), PendingGeneration(self._opt, state.generation, host, done)
+
+
+class PendingGeneration:
+    """Metrics of a queued generation, read when asked for."""
+
+    def __init__(self, optimizer, generation: int, host: torch.Tensor, done: torch.cuda.Event):
+        self._opt, self.generation, self._host, self._done = optimizer, generation, host, done
+
+    def result(self):
+        self._done.synchronize()
+        return self._opt._metrics(self.generation, self._host)
 
 
 def _advance_state(old, captured):
@@ -173,4 +219,4 @@ def _advance_state(old, captured):
     return captured
 
 
-__all__ = ["CapturedGeneration"]
+__all__ = ["CapturedGeneration", "PendingGeneration"]

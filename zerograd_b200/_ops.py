@@ -98,6 +98,16 @@ def launch_fold_in(keys: torch.Tensor, data: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def launch_copy_if_zero(dst: torch.Tensor, src: torch.Tensor, flag: torch.Tensor) -> None:
+    """dst <- src on the device when flag[0] == 0 (contiguous, same bytes)."""
+    dev = L.require_cuda(dst, src, flag)
+    if not (dst.is_contiguous() and src.is_contiguous()) or dst.nbytes != src.nbytes:
+        raise ValueError("copy_if_zero needs contiguous tensors of the same size")
+    if flag.dtype != torch.float32:
+        raise TypeError("the flag is a float32 count")
+    L.call("zg_copy_if_zero", L.ptr(dst), L.ptr(src), dst.nbytes, L.ptr(flag), L.stream_ptr(dev))
+
+
 def launch_normal(keys: torch.Tensor, n: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
     dev = L.require_cuda(keys)
     k = _keys2d(keys)

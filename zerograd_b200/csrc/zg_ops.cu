@@ -258,6 +258,23 @@ int ew_grid(int64_t n) {
     return (int)(g < 148 * 8 ? (g < 1 ? 1 : g) : 148 * 8);
 }
 
+// dst <- src when *flag == 0 (16-byte words when both are aligned, the tail
+// and unaligned buffers bytewise); a NaN or non-zero flag copies nothing.
+template <bool VEC>
+__global__ void copy_if_zero_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int64_t bytes,
+                                    const float* __restrict__ flag) {
+    if (!(*flag == 0.f)) return;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t done = 0;
+    if (VEC) {
+        const int64_t n16 = bytes / 16;
+        for (int64_t i = tid; i < n16; i += stride)
+            reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+        done = n16 * 16;
+    }
+    for (int64_t i = done + tid; i < bytes; i += stride) dst[i] = src[i];
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -491,6 +508,21 @@ extern "C" int zg_adamw_update(const void* param, void* param_out, int dtype, co
         adamw_kernel<float><<<ew_grid(n), 256, 0, st>>>((const float*)param, (float*)param_out, descent, mu, nu,
                                                         mu_out, nu_out, n, c);
     return zg::check_launch("zg_adamw_update");
+}
+
+extern "C" int zg_copy_if_zero(void* dst, const void* src, size_t bytes, const float* flag, void* stream) {
+    if (bytes == 0) return ZG_OK;
+    if (!dst || !src || !flag) return zg::fail(ZG_ERR_INVALID, "zg_copy_if_zero: null pointer");
+    if ((bytes > 0x7fffffffffffffffULL)) return zg::fail(ZG_ERR_INVALID, "zg_copy_if_zero: bad size");
+    cudaStream_t st = zg::as_stream(stream);
+    const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0;
+    const int64_t n = (int64_t)bytes;
+    zg::LaunchTimer zg_lt_("copy_if_zero", st);
+    if (vec)
+        copy_if_zero_kernel<true><<<ew_grid(n / 16 + 1), 256, 0, st>>>((uint8_t*)dst, (const uint8_t*)src, n, flag);
+    else
+        copy_if_zero_kernel<false><<<ew_grid(n), 256, 0, st>>>((uint8_t*)dst, (const uint8_t*)src, n, flag);
+    return zg::check_launch("zg_copy_if_zero");
 }
 
 extern "C" int zg_sgd_update(const void* param, void* param_out, int dtype, const float* descent, int64_t n,
