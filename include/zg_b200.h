@@ -183,20 +183,27 @@ ZG_API int zg_replay_operands(const float* shaped, const void* A, int a_transpos
  * on the pseudo-gradient -d, bit-identical to zg_replay_operands followed by
  * zg_sgd_update / zg_adamw_update.  param in `dtype` (float32 or bf16),
  * moments float32, all [rows, cols] row-major; descent_out (optional) also
- * receives d.  Workspace: zg_replay_operands_workspace_size.  Replaces
+ * receives d.  The outputs may alias the inputs (param_out == param, and
+ * the moments likewise): each element is read and written by one thread.
+ * guard (optional, device float): when *guard != 0 nothing is written, so an
+ * in-place update of a generation whose losses were rejected leaves the
+ * parameters as they were (zg_shape_fitness's non-finite count, metrics[3]);
+ * a guarded call takes no descent_out.
+ * Workspace: zg_replay_operands_workspace_size.  Replaces
  * replay_entry + transform.update + apply_updates
  * (src/zerograd/_replay.py:44-54, src/zerograd/_optimizer.py:229-234). */
 ZG_API int zg_replay_sgd(const float* shaped, const void* A, int a_transposed, const void* B,
                          int b_transposed, int P, int64_t rows, int64_t cols, int rank,
                          float inv_sqrt_rank, const void* param, void* param_out, int dtype,
-                         double lr, float* descent_out, void* workspace, size_t workspace_bytes,
-                         void* stream);
+                         double lr, float* descent_out, const float* guard, void* workspace,
+                         size_t workspace_bytes, void* stream);
 ZG_API int zg_replay_adamw(const float* shaped, const void* A, int a_transposed, const void* B,
                            int b_transposed, int P, int64_t rows, int64_t cols, int rank,
                            float inv_sqrt_rank, const void* param, void* param_out, int dtype,
                            const float* mu, const float* nu, float* mu_out, float* nu_out, int count,
                            double lr, double b1, double b2, double eps, double weight_decay,
-                           float* descent_out, void* workspace, size_t workspace_bytes, void* stream);
+                           float* descent_out, const float* guard, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Tied logits fused with softmax cross-entropy (bf16, tcgen05): for each
  * candidate p and row m

@@ -52,7 +52,7 @@ def test_fused_step_matches_replay_then_update(cuda, oracle, rows, cols, P, layo
     if opt == "sgd":
         want = _ops.launch_sgd(param, d, 0.05)
         L.call("zg_replay_sgd", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r, inv, L.ptr(param),
-               L.ptr(new), L.ZG_BF16, 0.05, L.ptr(d2), L.ptr(ws), ws.numel(), st)
+               L.ptr(new), L.ZG_BF16, 0.05, L.ptr(d2), None, L.ptr(ws), ws.numel(), st)
         assert torch.equal(new, want)
     else:
         mu = torch.randn(rows, cols, generator=g).to(cuda) * 1e-3
@@ -61,7 +61,7 @@ def test_fused_step_matches_replay_then_update(cuda, oracle, rows, cols, P, layo
         mo, vo = torch.empty_like(mu), torch.empty_like(nu)
         L.call("zg_replay_adamw", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r, inv, L.ptr(param),
                L.ptr(new), L.ZG_BF16, L.ptr(mu), L.ptr(nu), L.ptr(mo), L.ptr(vo), 3, 1e-3, 0.9, 0.999, 1e-8, 1e-4,
-               L.ptr(d2), L.ptr(ws), ws.numel(), st)
+               L.ptr(d2), None, L.ptr(ws), ws.numel(), st)
         assert torch.equal(new, want) and torch.equal(mo, wm) and torch.equal(vo, wv)
     assert torch.equal(d2, d)  # the optional descent output is the unfused replay's
     assert L.load().zg_device_error(1) == 0
@@ -113,4 +113,39 @@ def test_step_uses_fused_replay_and_matches_separate_update(cuda, transform):
     if isinstance(transform, zg.adamw):
         for k in params:
             assert torch.equal(sa.opt_state.mu[k], sb.mu[k]) and torch.equal(sa.opt_state.nu[k], sb.nu[k]), k
+    assert L.load().zg_device_error(1) == 0
+
+
+@pytest.mark.parametrize("rows,cols,P", [(520, 384, 48), (4096, 4096, 256)])
+@pytest.mark.parametrize("opt", ["sgd", "adamw"])
+def test_inplace_guarded_step(cuda, oracle, rows, cols, P, opt):
+    """In place with the guard at zero: the out-of-place step's bits; with the
+    guard set: nothing written (parameters and moments untouched)."""
+    r = 8
+    cks = _u32(oracle.candidate_keys(oracle.step_key(5, "guard", 0, 1), range(P)), cuda)
+    g = torch.Generator().manual_seed(rows * 3 + P)
+    w = torch.randn(P, generator=g).to(cuda)
+    param = (torch.randn(rows, cols, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
+    spec = {"kind": "sgd", "lr": 0.05}
+    if opt == "adamw":
+        spec = {"kind": "adamw", "lr": 1e-3, "b1": 0.9, "b2": 0.999, "eps": 1e-8, "weight_decay": 1e-4, "count": 2,
+                "mu": torch.randn(rows, cols, generator=g).to(cuda) * 1e-3,
+                "nu": torch.rand(rows, cols, generator=g).to(cuda) * 1e-4}
+    want = _ops.launch_replay_step(w, cks, 0, L.ZG_MATRIX, param, r, spec)
+    for flag, writes in ((0.0, True), (3.0, False)):
+        p2 = param.clone()
+        s2 = dict(spec)
+        if opt == "adamw":
+            s2["mu"], s2["nu"] = spec["mu"].clone(), spec["nu"].clone()
+        got = _ops.launch_replay_step(w, cks, 0, L.ZG_MATRIX, p2, r, s2,
+                                      inplace_guard=torch.tensor([flag], device=cuda))
+        assert got[0] is p2
+        if writes:
+            assert torch.equal(p2, want[0])
+            if opt == "adamw":
+                assert torch.equal(s2["mu"], want[1]) and torch.equal(s2["nu"], want[2])
+        else:
+            assert torch.equal(p2, param)
+            if opt == "adamw":
+                assert torch.equal(s2["mu"], spec["mu"]) and torch.equal(s2["nu"], spec["nu"])
     assert L.load().zg_device_error(1) == 0

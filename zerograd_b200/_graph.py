@@ -14,11 +14,12 @@ not launches:
   replay kernel reads keys from device memory);
 * the batch is copied into the captured batch buffers (from pinned host
   memory, or from the device);
-* the parameters live in captured buffers; the graph writes the updated
-  parameters to its own output buffers and copies them back at its end,
-  on the device, only when the shaping kernel counted no non-finite loss:
-  a rejected generation leaves the parameters as they were, and ``step``
-  raises as ``step_from_losses`` does.
+* the parameters live in captured buffers, updated on the device only when
+  the shaping kernel counted no non-finite loss: the entries whose step is
+  fused into the replay GEMM are updated in place with that count as the
+  epilogue's guard, the other leaves are written to the graph's own buffers
+  and copied back under the same guard.  A rejected generation leaves the
+  parameters as they were, and ``step`` raises as ``step_from_losses`` does.
 
 ``step`` reads the metrics back every generation (a synchronisation, as the
 reference's ``float(jnp.mean(losses))``); ``enqueue`` queues a generation
@@ -137,7 +138,10 @@ class CapturedGeneration:
         if self._gather is not None:
             losses = self._gather(losses.to(torch.float32))
         state = self._state_cls(generation, opt_state)
-        new_params, new_opt_state, metrics = opt._complete(state, self._params, losses, cand_keys=cks_all)
+        # in the graph, fused steps update the captured parameters in place,
+        # guarded by the non-finite count; the other leaves are copied back
+        new_params, new_opt_state, metrics = opt._complete(state, self._params, losses, cand_keys=cks_all,
+                                                           inplace=copy_back)
         if copy_back:
             flag = metrics[3:4]  # non-finite loss count
             for path, t in _leaves(self._params):

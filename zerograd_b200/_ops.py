@@ -590,13 +590,16 @@ def _replay_operands_for(cand_keys, group, layout, rows, cols, rank, gen, cache)
 
 
 def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, layout: int, param: torch.Tensor,
-                       rank: int, step: dict, gen: _Generation | None = None, cache: FactorCache = CACHE):
+                       rank: int, step: dict, gen: _Generation | None = None, cache: FactorCache = CACHE,
+                       inplace_guard: torch.Tensor | None = None):
     """Replay of one MATRIX/TABLE entry with the optimizer step fused into the
     replay GEMM's epilogue (bf16 parameters on the tensor cores).  `step`:
     {"kind": "sgd", "lr"} or {"kind": "adamw", "lr", "b1", "b2", "eps",
     "weight_decay", "count", "mu", "nu"}.  Returns (new param, new mu, new nu)
     -- the moments None for SGD -- or None when the fused path does not apply
-    (the caller then replays and updates separately, with identical results)."""
+    (the caller then replays and updates separately, with identical results).
+    With `inplace_guard` (a device float32 scalar) the step updates param and
+    the moments in place and writes nothing when the guard is non-zero."""
     dev = L.require_cuda(shaped, cand_keys, param)
     k = _keys2d(cand_keys)
     P = k.shape[0]
@@ -612,18 +615,25 @@ def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int
         return None
     inv = scaled_factor_value(rank, 1.0, param.dtype)
     ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, rank), dev)
-    out = torch.empty_like(param)
+    inplace = inplace_guard is not None
+    if inplace and (inplace_guard.dtype != torch.float32 or inplace_guard.device != dev):
+        raise TypeError("the guard is a float32 scalar on the parameter's device")
+    guard = L.ptr(inplace_guard) if inplace else None
+    out = param if inplace else torch.empty_like(param)
     st = L.stream_ptr(dev)
     if step["kind"] == "sgd":
         L.call("zg_replay_sgd", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, rank, inv, L.ptr(param),
-               L.ptr(out), L.ZG_BF16, float(step["lr"]), None, L.ptr(ws), ws.numel(), st)
+               L.ptr(out), L.ZG_BF16, float(step["lr"]), None, guard, L.ptr(ws), ws.numel(), st)
         return out, None, None
-    mu_out = torch.empty_like(step["mu"])
-    nu_out = torch.empty_like(step["nu"])
+    mu, nu = step["mu"].contiguous(), step["nu"].contiguous()
+    if inplace and (mu is not step["mu"] or nu is not step["nu"]):
+        raise ValueError("an in-place step needs contiguous moments")
+    mu_out = mu if inplace else torch.empty_like(mu)
+    nu_out = nu if inplace else torch.empty_like(nu)
     L.call("zg_replay_adamw", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, rank, inv, L.ptr(param),
-           L.ptr(out), L.ZG_BF16, L.ptr(step["mu"].contiguous()), L.ptr(step["nu"].contiguous()), L.ptr(mu_out),
-           L.ptr(nu_out), int(step["count"]), float(step["lr"]), float(step["b1"]), float(step["b2"]),
-           float(step["eps"]), float(step["weight_decay"]), None, L.ptr(ws), ws.numel(), st)
+           L.ptr(out), L.ZG_BF16, L.ptr(mu), L.ptr(nu), L.ptr(mu_out), L.ptr(nu_out), int(step["count"]),
+           float(step["lr"]), float(step["b1"]), float(step["b2"]), float(step["eps"]), float(step["weight_decay"]),
+           None, guard, L.ptr(ws), ws.numel(), st)
     return out, mu_out, nu_out
 
 

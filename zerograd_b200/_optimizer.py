@@ -263,11 +263,14 @@ class ZeroGrad:
         return StepMetrics(generation=generation, mean_loss=float(m[0]), min_loss=float(m[1]),
                            max_loss=float(m[2]), population_size=self._population_size)
 
-    def _complete(self, state, params, losses, cand_keys: torch.Tensor | None = None):
+    def _complete(self, state, params, losses, cand_keys: torch.Tensor | None = None, inplace: bool = False):
         """Device part of a generation's completion, all queued on the
         current stream with no host synchronisation: shaping, replay and the
         optimizer step.  Returns (new params, new optimizer state, device
-        metrics [mean, min, max, non-finite count])."""
+        metrics [mean, min, max, non-finite count]).  `inplace`: entries whose
+        step is fused into the replay are updated in place, and not at all
+        when a loss is not finite (the metrics' non-finite count guards the
+        writes); the other leaves still come back as new tensors."""
         self._check_losses(losses)
         device = _device_of(params)
         losses = losses.to(device)
@@ -285,7 +288,8 @@ class ZeroGrad:
             if fused:
                 # the optimizer step in the replay GEMM's epilogue (bf16 MATRIX/TABLE)
                 res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank,
-                                        self._transform.step_spec(state.opt_state, entry.path), gen)
+                                        self._transform.step_spec(state.opt_state, entry.path), gen,
+                                        inplace_guard=metrics[3:4] if inplace else None)
                 if res is not None:
                     done[tuple(entry.path)] = res
                     continue

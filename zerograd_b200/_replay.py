@@ -36,16 +36,20 @@ def replay_entry_keys(params: ParameterTree, manifest: Manifest, path: Parameter
 
 
 def replay_entry_step(params: ParameterTree, manifest: Manifest, path: ParameterPath, cand_keys: torch.Tensor,
-                      shaped_weights: torch.Tensor, rank: int, step: dict, gen=None):
+                      shaped_weights: torch.Tensor, rank: int, step: dict, gen=None,
+                      inplace_guard: torch.Tensor | None = None):
     """Replay of one entry with the optimizer step fused in: (param, mu, nu)
     or None where the fused form does not apply (VECTOR entries, float32
-    leaves), in which case the caller replays and steps separately."""
+    leaves), in which case the caller replays and steps separately.  With
+    `inplace_guard` the step updates the entry in place unless the guard
+    (a device float) is non-zero."""
     entry = manifest.entry(path)
     if entry.layout is ParameterLayout.VECTOR:
         return None
     parameter = manifest.resolve(params, path)
     return _ops.launch_replay_step(shaped_weights, cand_keys, manifest.group_index(entry.group),
-                                   LAYOUT_CODE[entry.layout], parameter, rank, step, gen=gen)
+                                   LAYOUT_CODE[entry.layout], parameter, rank, step, gen=gen,
+                                   inplace_guard=inplace_guard)
 
 
 def replay_entry(params: ParameterTree, manifest: Manifest, path: ParameterPath, base_key: torch.Tensor,

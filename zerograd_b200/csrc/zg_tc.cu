@@ -203,6 +203,9 @@ __device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0
 template <int W>
 __device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int col_base, uint32_t tacc) {
     const zg::FusedStep& st = args.step;
+    // a guarded step writes nothing at all when its guard is set (the same
+    // value in every lane, so the warp stays on one path)
+    if (st.guard != nullptr && !(*st.guard == 0.f)) return;
     const int64_t base = (int64_t)row * st.ldp + col_base;
     const bool lane_fast = st.kind == zg::ZG_STEP_SGD && st.param_bf16 && row < args.M && col_base + W <= args.N &&
                            ((reinterpret_cast<uintptr_t>(st.param) + base * 2) & 15) == 0 &&

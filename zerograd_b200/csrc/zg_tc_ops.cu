@@ -989,6 +989,8 @@ extern "C" int zg_replay_operands(const float* shaped, const void* A, int a_tran
 static int replay_step(const char* who, const float* shaped, const void* A, int a_t, const void* B, int b_t, int P,
                        int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const zg::FusedStep& step,
                        float* descent_out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (step.guard && descent_out)
+        return zg::fail(ZG_ERR_INVALID, "%s: a guarded step writes no descent", who);
     if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1) return zg::fail(ZG_ERR_INVALID, "%s: bad sizes", who);
     if (!shaped || !A || !B || !step.param || !step.param_out) return zg::fail(ZG_ERR_INVALID, "%s: null pointer", who);
     if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
@@ -1003,11 +1005,12 @@ static int replay_step(const char* who, const float* shaped, const void* A, int 
 
 extern "C" int zg_replay_sgd(const float* shaped, const void* A, int a_transposed, const void* B, int b_transposed,
                              int P, int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const void* param,
-                             void* param_out, int dtype, double lr, float* descent_out, void* workspace,
-                             size_t workspace_bytes, void* stream) {
+                             void* param_out, int dtype, double lr, float* descent_out, const float* guard,
+                             void* workspace, size_t workspace_bytes, void* stream) {
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay_sgd: bad dtype");
     zg::FusedStep st{};
     st.kind = zg::ZG_STEP_SGD;
+    st.guard = guard;
     st.param_bf16 = dtype == ZG_BF16;
     st.ldp = cols;
     st.param = param;
@@ -1021,12 +1024,13 @@ extern "C" int zg_replay_adamw(const float* shaped, const void* A, int a_transpo
                                int P, int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const void* param,
                                void* param_out, int dtype, const float* mu, const float* nu, float* mu_out,
                                float* nu_out, int count, double lr, double b1, double b2, double eps,
-                               double weight_decay, float* descent_out, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+                               double weight_decay, float* descent_out, const float* guard, void* workspace,
+                               size_t workspace_bytes, void* stream) {
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: bad dtype");
     if (count < 1) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: count must be >= 1");
     if (!mu || !nu || !mu_out || !nu_out) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: null moment");
     zg::FusedStep st{};
+    st.guard = guard;
     st.kind = zg::ZG_STEP_ADAMW;
     st.param_bf16 = dtype == ZG_BF16;
     st.ldp = cols;

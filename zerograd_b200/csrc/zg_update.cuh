@@ -60,7 +60,8 @@ struct FusedStep {
     const float* nu;
     float* mu_out;
     float* nu_out;
-    AdamConsts c;  // neg_lr is the SGD rate as well
+    AdamConsts c;        // neg_lr is the SGD rate as well
+    const float* guard;  // optional: when *guard != 0 the step writes nothing (in-place updates stay intact)
 };
 
 }  // namespace zg
