@@ -398,10 +398,11 @@ def run_ours(args):
     replay_entries = [(0, L.ZG_MATRIX, K, N, r)]
 
     def prefetch(gen):
-        # a shard's process replays the whole population: its replay factors
-        # are drawn on a second stream while the shard's forward runs
-        if world > 1:
-            _ops.prefetch_replay_factors(_ops._Generation(bases[gen], 0, P, keys[gen][0]), replay_entries)
+        # A shard's replay draws the whole population's factors after the
+        # forward (on the same stream): drawing them concurrently on a second
+        # stream contends with the forward's GEMMs for the SMs and measured
+        # slower.  Kept as a no-op hook for that alternative.
+        return None
 
     def device_step(W, gen):
         # the same sequence ZeroGrad.step runs: forward (factors kept for the
@@ -516,7 +517,7 @@ def run_ours(args):
         nonlocal state
         xb = x_host.to(dev, non_blocking=True)
         fl = fit_host[a:b].to(dev, non_blocking=True)
-        y = opt.evaluate_shard({"w": Wcur}, gen, fwd, xb, ids_local, prefetch_replay=world > 1)
+        y = opt.evaluate_shard({"w": Wcur}, gen, fwd, xb, ids_local)
         losses = gather(fl)
         newp, state, m = opt.step_from_losses(zg.ZeroGradState(gen, state.opt_state), {"w": Wcur}, losses)
         del y

@@ -102,9 +102,12 @@ class DeviceShard:
         self._loss_fn = loss_fn
         self.name = name or f"shard-{self.device.type}"
         self._candidate_ids: torch.Tensor | None = None
-        # True when this process also replays the whole population (one
-        # process per GPU): the shard then prefetches the replay's factors
-        self.replays = False
+        # Draw the whole population's replay factors on a second stream while
+        # this shard's forward runs (for a process that also replays).  Off by
+        # default: on B200 the integer-bound draws and the forward's GEMMs
+        # contend for the same SMs, and drawing after the forward measured
+        # faster at 2, 4 and 8 shards.
+        self.prefetch_replay = False
 
     def evaluate(self, params: ParameterTree, batch: Any, candidate_ids: torch.Tensor, generation: int,
                  rng: torch.Tensor | None = None) -> ShardResult:
@@ -119,7 +122,7 @@ class DeviceShard:
         with torch.cuda.device(self.device) if self.device.type == "cuda" else _null():
             self._optimizer.manifest.validate(params_d)
             losses = self._optimizer._evaluate_shard(params_d, generation, self._loss_fn, batch_d, ids,
-                                                     rng=rng.to(self.device), prefetch_replay=self.replays)
+                                                     rng=rng.to(self.device), prefetch_replay=self.prefetch_replay)
         return ShardResult(candidate_ids=candidate_ids, losses=losses)
 
     @property
@@ -176,7 +179,6 @@ class DistributedZeroGrad:
         self._weights = list(weights) if weights else [1.0] * n
         if self._pg_mode:
             self._shards = [DeviceShard(self._devices[0], optimizer, loss_fn, name=f"rank-{self._rank}")]
-            self._shards[0].replays = True
         else:
             self._shards = [DeviceShard(d, optimizer, loss_fn, name=f"worker-{i}-{d.type}")
                             for i, d in enumerate(self._devices)]

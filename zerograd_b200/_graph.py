@@ -85,9 +85,10 @@ class CapturedGeneration:
         self._params = _clone_tree(_materialize_tree(params))
         self._batch = _clone_tree(batch)
         self._loss_fn = loss_fn
-        # a shard replays the whole population: its replay factors are drawn
-        # on a second stream (a parallel branch of the graph) during the forward
-        self._prefetch = prefetch_replay or self._range != (0, P)
+        # prefetch_replay: a shard's replay factors drawn on a second stream
+        # (a parallel branch of the graph) during its forward; off by default,
+        # since the draws and the forward's GEMMs contend for the same SMs
+        self._prefetch = prefetch_replay
         self._base_dev = torch.empty((1, 2), dtype=torch.uint32, device=dev)
         self._ids = torch.arange(P, dtype=torch.int32, device=dev)
         g0 = state.generation if state is not None else 0
