@@ -361,6 +361,37 @@ ZG_API int zg_sgd_update(const void* param, void* param_out, int dtype, const fl
  * (_fitness.py:37-48 rejects them before any state changes). */
 ZG_API int zg_copy_if_zero(void* dst, const void* src, size_t bytes, const float* flag, void* stream);
 
+/* --------------------------------------------- transformer-block ops -- */
+
+/* Population-batched LayerNorm with per-candidate scale and bias (the
+ * vectors CandidateContext.vector returns for each candidate):
+ *   y[p, m] = (x[m] - mean) / sqrt(var + eps) * scale + bias
+ * mean and biased variance in float32 over the last axis (C), y rounded to
+ * dtype (ZG_F32 or ZG_BF16).  x [P, M, C] when x_batched, else [M, C] shared
+ * by the candidates; scale, bias [P, C] when p_batched, else [C]; bias may be
+ * NULL; y [P, M, C].  Replaces layer_norm of the reference's ViT example
+ * (examples/train_vit_cifar10.py:76-79) under jax.vmap. */
+ZG_API int zg_layer_norm(const void* x, int x_batched, const void* scale, const void* bias, int p_batched,
+                         int P, int64_t M, int C, float eps, int dtype, void* y, void* stream);
+
+/* Population-batched RMSNorm (the decoder LM's norm, scale a VECTOR entry):
+ *   y[p, m] = x[m] / sqrt(mean(x[m]^2) + eps) * scale
+ * layouts and precision as zg_layer_norm. */
+ZG_API int zg_rms_norm(const void* x, int x_batched, const void* scale, int p_batched, int P, int64_t M,
+                       int C, float eps, int dtype, void* y, void* stream);
+
+/* Softmax attention of every candidate's block, population-batched:
+ *   o[z, i, h] = sum_j softmax_j(q[z, i, h] . k[z, j, h] / sqrt(D)) v[z, j, h]
+ * q, k, v, o [Z, S, H, D] contiguous (Z = candidates x batch rows; the
+ * q/k/v projections' head-interleaved layout); causal != 0 masks keys j > i.
+ * bf16 with D = 64 and S <= 256 runs on the tensor cores (scores and P V
+ * accumulated in float32, P rounded to bf16, normalised by the sum of the
+ * rounded P); other shapes and float32 run a warp-per-row kernel in float32.
+ * D <= 256.  Replaces softmax(einsum(q, k) / sqrt(D)) @ v of the reference's
+ * ViT block (examples/train_vit_cifar10.py:166-172) under jax.vmap. */
+ZG_API int zg_attention(const void* q, const void* k, const void* v, int Z, int S, int H, int D, int causal,
+                        int dtype, void* o, void* stream);
+
 /* ------------------------------------------------- integer QAT linear -- */
 
 /* Integer linear with LUT activation for P candidates (no reference

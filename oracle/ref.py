@@ -248,6 +248,39 @@ def tied_logits_cross_entropy(x, T, gk, rank, sigma, labels, dtype="bfloat16"):
     return lse - picked
 
 
+def layer_norm(x, scale, bias=None, eps=1e-5):
+    """``(x - mean) / sqrt(var + eps) * scale + bias`` over the last axis,
+    biased variance, in float64 (``examples/train_vit_cifar10.py:76-79``)."""
+    x = np.asarray(x, np.float64)
+    mean = x.mean(axis=-1, keepdims=True)
+    var = ((x - mean) ** 2).mean(axis=-1, keepdims=True)
+    y = (x - mean) / np.sqrt(var + eps) * np.asarray(scale, np.float64)
+    return y if bias is None else y + np.asarray(bias, np.float64)
+
+
+def rms_norm(x, scale, eps=1e-6):
+    """``x / sqrt(mean(x^2) + eps) * scale`` over the last axis, in float64."""
+    x = np.asarray(x, np.float64)
+    return x / np.sqrt((x * x).mean(axis=-1, keepdims=True) + eps) * np.asarray(scale, np.float64)
+
+
+def attention(q, k, v, causal=False):
+    """softmax(q kᵀ / sqrt(d)) v per head, in float64, as the reference's ViT
+    block computes it (``examples/train_vit_cifar10.py:166-172``); q, k, v
+    [..., S, H, D] (the projections' head-interleaved layout), output the same.
+    `causal`: key j > query i masked (the decoder LM)."""
+    q, k, v = (np.asarray(t, np.float64) for t in (q, k, v))
+    qh, kh, vh = (np.swapaxes(t, -3, -2) for t in (q, k, v))      # [..., H, S, D]
+    s = qh @ np.swapaxes(kh, -1, -2) / math.sqrt(q.shape[-1])
+    if causal:
+        S = s.shape[-1]
+        s = np.where(np.triu(np.ones((S, S), bool), 1), -np.inf, s)
+    s = s - s.max(axis=-1, keepdims=True)
+    w = np.exp(s)
+    w /= w.sum(axis=-1, keepdims=True)
+    return np.swapaxes(w @ vh, -3, -2)
+
+
 def perturbed_vector(v, gk, sigma, dtype="float32"):
     s = scaled_factor(1, sigma, dtype)
     return np.asarray(v, np.float64) + s * vector_noise(gk, v.shape, dtype)

@@ -13,6 +13,7 @@ from ._factors import matrix_factors, scaled_factor, table_factors, vector_noise
 from ._fitness import shape_centered_loss, validate_losses
 from ._keys import candidate_key, group_key, step_key
 from ._manifest import Manifest, ManifestEntry, ParameterLayout, ParameterPath, ParameterTree
+from ._block import attention, layer_norm, rms_norm
 from ._graph import CapturedGeneration
 from ._optimizer import StepMetrics, ZeroGrad, ZeroGradState
 from ._replay import replay, replay_entry
@@ -21,11 +22,11 @@ from . import checkpoint, random
 from .checkpoint import EarlyStopping, load_checkpoint, save_checkpoint
 
 __all__ = [
-    "EarlyStopping", "load_checkpoint", "save_checkpoint", "checkpoint",
+    "attention", "EarlyStopping", "load_checkpoint", "save_checkpoint", "checkpoint",
     "CandidateContext", "CalibrationResult", "CapturedGeneration", "DeviceShard", "DistributedZeroGrad", "Manifest", "ManifestEntry",
     "ParameterLayout", "ParameterPath", "ParameterTree", "ShardResult", "StepMetrics", "ZeroGrad",
     "ZeroGradState", "adamw", "allgather_losses", "apply_updates", "candidate_key", "compute_partition_sizes",
-    "group_key", "matrix_factors", "perturbed_linear", "perturbed_table_lookup", "perturbed_tied_logits",
-    "perturbed_vector", "random", "replay", "replay_entry", "scaled_factor", "sgd", "shape_centered_loss",
+    "group_key", "layer_norm", "matrix_factors", "perturbed_linear", "perturbed_table_lookup", "perturbed_tied_logits",
+    "perturbed_vector", "random", "replay", "replay_entry", "rms_norm", "scaled_factor", "sgd", "shape_centered_loss",
     "step_key", "table_factors", "validate_losses", "vector_noise",
 ]

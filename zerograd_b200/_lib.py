@@ -76,6 +76,9 @@ SIGNATURES = {
                                _f64, _vp]),
     "zg_sgd_update": (_i32, [_vp, _vp, _i32, _vp, _i64, _f64, _vp]),
     "zg_copy_if_zero": (_i32, [_vp, _vp, _sz, _vp, _vp]),
+    "zg_layer_norm": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i64, _i32, _f32, _i32, _vp, _vp]),
+    "zg_rms_norm": (_i32, [_vp, _i32, _vp, _i32, _i32, _i64, _i32, _f32, _i32, _vp, _vp]),
+    "zg_attention": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "zg_int8_lut_linear_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "zg_int8_lut_linear": (_i32, [_vp, _i32, _vp, _vp, _f32, _f32, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                                   _i32, _f32, _vp, _vp, _vp, _sz, _vp]),

@@ -1,0 +1,229 @@
+// zg_norm.cu -- population-batched LayerNorm and RMSNorm with per-candidate
+// scale and bias: the normalisations of a candidate's transformer block, fed
+// by the vectors CandidateContext.vector returns for every candidate
+// (v + sigma * noise_p, src/zerograd/_candidate.py:41-45, 82-87).
+//
+//   layer_norm: y = (x - mean) / sqrt(var + eps) * scale + bias
+//               (biased variance; examples/train_vit_cifar10.py:76-79)
+//   rms_norm:   y = x / sqrt(mean(x^2) + eps) * scale
+//
+// Statistics in float32 over the last axis (C); output rounded to x's dtype.
+// x [P, M, C] (x_batched) or [M, C] shared by the candidates; scale, bias
+// [P, C] (p_batched) or [C]; y [P, M, C].  One warp per row; HBM-bound.
+#include <math.h>
+
+#include "zg_common.cuh"
+
+namespace {
+
+enum { NORM_LAYER = 0, NORM_RMS = 1 };
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+    if constexpr (sizeof(T) == 2) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    } else {
+        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
+    if constexpr (sizeof(T) == 2) {
+        uint4 o;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4*>(p) = o;
+    } else {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+struct NormArgs {
+    const void* x;
+    const void* scale;
+    const void* bias;
+    void* y;
+    int64_t M;
+    int P, C, x_batched, p_batched, kind;
+    float eps;
+};
+
+// Row held in registers: CH chunks of 8 values per lane (C <= 256 * CH, C a
+// multiple of 8, rows 16-byte aligned).
+template <typename T, int CH>
+__global__ void norm_reg_kernel(const NormArgs a) {
+    const int lane = threadIdx.x % 32;
+    const int64_t rows = (int64_t)a.P * a.M;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const int64_t nwarps = (int64_t)gridDim.x * blockDim.x / 32;
+    const int chunks = a.C / 8;
+    for (int64_t g = warp0; g < rows; g += nwarps) {
+        const int p = (int)(g / a.M);
+        const int64_t m = g % a.M;
+        const T* xr = static_cast<const T*>(a.x) + ((a.x_batched ? (int64_t)p : 0) * a.M + m) * a.C;
+        const T* sr = static_cast<const T*>(a.scale) + (a.p_batched ? (int64_t)p : 0) * a.C;
+        const T* br = a.bias ? static_cast<const T*>(a.bias) + (a.p_batched ? (int64_t)p : 0) * a.C : nullptr;
+        T* yr = static_cast<T*>(a.y) + g * a.C;
+        float v[CH][8];
+        float s1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const int c = lane + 32 * j;
+            if (c < chunks) {
+                load8(xr + 8 * c, v[j]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s1 += v[j][i];
+            }
+        }
+        float sd;
+        float mean = 0.f;
+        if (a.kind == NORM_LAYER) {
+            mean = __fdiv_rn(warp_sum(s1), (float)a.C);
+            float s2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+                if (lane + 32 * j < chunks)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float d = v[j][i] - mean;
+                        s2 = fmaf(d, d, s2);
+                    }
+            sd = __fsqrt_rn(__fdiv_rn(warp_sum(s2), (float)a.C) + a.eps);
+        } else {
+            float s2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+                if (lane + 32 * j < chunks)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) s2 = fmaf(v[j][i], v[j][i], s2);
+            sd = __fsqrt_rn(__fdiv_rn(warp_sum(s2), (float)a.C) + a.eps);
+        }
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const int c = lane + 32 * j;
+            if (c < chunks) {
+                float sc[8], bi[8], o[8];
+                load8(sr + 8 * c, sc);
+                if (br) load8(br + 8 * c, bi);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    o[i] = __fmul_rn(__fdiv_rn(v[j][i] - mean, sd), sc[i]);
+                    if (br) o[i] = __fadd_rn(o[i], bi[i]);
+                }
+                store8(yr + 8 * c, o);
+            }
+        }
+    }
+}
+
+// Any C and alignment: three passes over the row in global memory (the
+// second and third hit L1/L2).
+template <typename T>
+__global__ void norm_any_kernel(const NormArgs a) {
+    const int lane = threadIdx.x % 32;
+    const int64_t rows = (int64_t)a.P * a.M;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const int64_t nwarps = (int64_t)gridDim.x * blockDim.x / 32;
+    for (int64_t g = warp0; g < rows; g += nwarps) {
+        const int p = (int)(g / a.M);
+        const int64_t m = g % a.M;
+        const T* xr = static_cast<const T*>(a.x) + ((a.x_batched ? (int64_t)p : 0) * a.M + m) * a.C;
+        const T* sr = static_cast<const T*>(a.scale) + (a.p_batched ? (int64_t)p : 0) * a.C;
+        const T* br = a.bias ? static_cast<const T*>(a.bias) + (a.p_batched ? (int64_t)p : 0) * a.C : nullptr;
+        T* yr = static_cast<T*>(a.y) + g * a.C;
+        float mean = 0.f, s2 = 0.f;
+        if (a.kind == NORM_LAYER) {
+            float s1 = 0.f;
+            for (int c = lane; c < a.C; c += 32) s1 += zg_to_float(xr[c]);
+            mean = __fdiv_rn(warp_sum(s1), (float)a.C);
+            for (int c = lane; c < a.C; c += 32) {
+                const float d = zg_to_float(xr[c]) - mean;
+                s2 = fmaf(d, d, s2);
+            }
+        } else {
+            for (int c = lane; c < a.C; c += 32) {
+                const float xv = zg_to_float(xr[c]);
+                s2 = fmaf(xv, xv, s2);
+            }
+        }
+        const float sd = __fsqrt_rn(__fdiv_rn(warp_sum(s2), (float)a.C) + a.eps);
+        for (int c = lane; c < a.C; c += 32) {
+            float o = __fmul_rn(__fdiv_rn(zg_to_float(xr[c]) - mean, sd), zg_to_float(sr[c]));
+            if (br) o = __fadd_rn(o, zg_to_float(br[c]));
+            yr[c] = zg_from_float<T>(o);
+        }
+    }
+}
+
+int sm_count_norm() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+    }
+    return n;
+}
+
+template <typename T>
+int launch_norm(const NormArgs& a, cudaStream_t st, const char* name) {
+    const int64_t rows = (int64_t)a.P * a.M;
+    int64_t blocks = (rows + 7) / 8;  // 8 warps per block
+    if (blocks > (int64_t)sm_count_norm() * 16) blocks = (int64_t)sm_count_norm() * 16;
+    if (blocks < 1) blocks = 1;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool vec = a.C % 8 == 0 && al(a.x) && al(a.scale) && (!a.bias || al(a.bias)) && al(a.y);
+    zg::LaunchTimer zg_lt_(name, st);
+    if (vec && a.C <= 256)
+        norm_reg_kernel<T, 1><<<(unsigned)blocks, 256, 0, st>>>(a);
+    else if (vec && a.C <= 512)
+        norm_reg_kernel<T, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
+    else if (vec && a.C <= 1024)
+        norm_reg_kernel<T, 4><<<(unsigned)blocks, 256, 0, st>>>(a);
+    else if (vec && a.C <= 2048)
+        norm_reg_kernel<T, 8><<<(unsigned)blocks, 256, 0, st>>>(a);
+    else
+        norm_any_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(a);
+    return zg::check_launch(name);
+}
+
+int norm_entry(const char* who, int kind, const void* x, int x_batched, const void* scale, const void* bias,
+               int p_batched, int P, int64_t M, int C, float eps, int dtype, void* y, void* stream) {
+    if (P < 1 || M < 0 || C < 1) return zg::fail(ZG_ERR_INVALID, "%s: bad sizes", who);
+    if (!(eps >= 0.f)) return zg::fail(ZG_ERR_INVALID, "%s: eps must be >= 0", who);
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "%s: bad dtype", who);
+    if (M == 0) return ZG_OK;
+    if (!x || !scale || !y) return zg::fail(ZG_ERR_INVALID, "%s: null pointer", who);
+    NormArgs a{x, scale, bias, y, M, P, C, x_batched != 0, p_batched != 0, kind, eps};
+    cudaStream_t st = zg::as_stream(stream);
+    return dtype == ZG_BF16 ? launch_norm<__nv_bfloat16>(a, st, who) : launch_norm<float>(a, st, who);
+}
+
+}  // namespace
+
+extern "C" int zg_layer_norm(const void* x, int x_batched, const void* scale, const void* bias, int p_batched,
+                             int P, int64_t M, int C, float eps, int dtype, void* y, void* stream) {
+    return norm_entry("layer_norm", NORM_LAYER, x, x_batched, scale, bias, p_batched, P, M, C, eps, dtype, y,
+                      stream);
+}
+
+extern "C" int zg_rms_norm(const void* x, int x_batched, const void* scale, int p_batched, int P, int64_t M, int C,
+                           float eps, int dtype, void* y, void* stream) {
+    return norm_entry("rms_norm", NORM_RMS, x, x_batched, scale, nullptr, p_batched, P, M, C, eps, dtype, y, stream);
+}

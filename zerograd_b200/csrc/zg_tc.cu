@@ -988,8 +988,8 @@ extern "C" int zg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t l
 
 extern "C" int zg_device_error(int clear) {
     // one error word per translation unit with tensor-core kernels
-    const int w[4] = {ptx_error_word(clear), zg::batched_error_word(clear), zg::int8_error_word(clear),
-                      zg::ce_error_word(clear)};
+    const int w[5] = {ptx_error_word(clear), zg::batched_error_word(clear), zg::int8_error_word(clear),
+                      zg::ce_error_word(clear), zg::attn_error_word(clear)};
     for (int e : w)
         if (e < 0) return -1;
     for (int e : w)

@@ -20,6 +20,7 @@ bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t*
 int batched_error_word(int clear);
 int int8_error_word(int clear);
 int ce_error_word(int clear);
+int attn_error_word(int clear);
 
 // Factor fill transposed to [P r, rows]: out[p*r + j, row] =
 // round_dtype(normal(key_p, row*r + j)) (the [rows, r] row-major factor of
