@@ -272,6 +272,101 @@ def tied_ce_section(dev, args):
                          "traffic": traffic_for("tied_ce"), "launch_ms": ce}}
 
 
+def lm_block_section(dev, args):
+    """One decoder-LM block for 16 candidates through the public API
+    (evaluate_shard under vmap): embedding lookup of the tied TABLE (vocab
+    32000, width 768) with each candidate's perturbation, RMSNorm with the
+    perturbed VECTOR scale, perturbed q/k/v/o projections, causal softmax
+    attention (12 heads of 64), RMSNorm, perturbed MLP 768 -> 3072 -> 768
+    (GELU), residuals; 16 sequences x 256 tokens per candidate, rank 16.
+    Seeded synthetic tokens (uniform over the vocabulary) and weights
+    (N(0, 0.02)); loss = mean square of the block's output."""
+    import torch
+
+    import zerograd_b200 as zg
+    from zerograd_b200 import _lib as L
+
+    P, B, T, E, Hh, F, V, r = 16, 16, 256, 768, 12, 3072, 32000, 16
+    mats = {"q": (E, E), "k": (E, E), "v": (E, E), "o": (E, E), "mlp1": (E, F), "mlp2": (F, E)}
+    entries = [zg.ManifestEntry(("emb",), zg.ParameterLayout.TABLE, "emb"),
+               zg.ManifestEntry(("n1",), zg.ParameterLayout.VECTOR, "n1"),
+               zg.ManifestEntry(("n2",), zg.ParameterLayout.VECTOR, "n2")]
+    entries += [zg.ManifestEntry((n,), zg.ParameterLayout.MATRIX, n) for n in mats]
+    manifest = zg.Manifest(1, tuple(entries))
+    g = torch.Generator(device=dev).manual_seed(7)
+    params = {n: (torch.randn(*d, generator=g, device=dev) * 0.02).to(torch.bfloat16) for n, d in mats.items()}
+    params["emb"] = (torch.randn(V, E, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    params["n1"] = torch.ones(E, dtype=torch.bfloat16, device=dev)
+    params["n2"] = torch.ones(E, dtype=torch.bfloat16, device=dev)
+    tokens = torch.randint(0, V, (B, T), generator=g, device=dev)
+
+    def loss_fn(p, ctx, batch, rng):
+        x = ctx.table_lookup(p, ("emb",), batch)
+        h = zg.rms_norm(x, ctx.vector(p, ("n1",)))
+        q, k, v = (ctx.linear(p, (n,), h).reshape(B, T, Hh, E // Hh) for n in ("q", "k", "v"))
+        x = x + ctx.linear(p, ("o",), zg.attention(q, k, v, causal=True).reshape(B, T, E))
+        h = zg.rms_norm(x, ctx.vector(p, ("n2",)))
+        m = torch.nn.functional.gelu(ctx.linear(p, ("mlp1",), h))
+        x = x + ctx.linear(p, ("mlp2",), m)
+        return (x.float() ** 2).mean(), None
+
+    opt = zg.ZeroGrad(manifest, zg.sgd(1e-3), P, r, 0.01, 0, "lm-block")
+    # one generation (forward of every candidate, shaping, replay and SGD of
+    # all nine entries) as the public API's captured graph, queued back to back
+    cg = opt.capture(params, loss_fn, tokens)
+    state = opt.init(params)
+    pending = []
+
+    def run(gen):
+        nonlocal state
+        _, state, pend = cg.enqueue(zg.ZeroGradState(gen, state.opt_state))
+        pending.append(pend)
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record()
+        for i in range(steps):
+            run(10 + i)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    for pend in pending:
+        pend.result()
+    del cg
+    # per-kernel device times: the same generation launched eagerly under the profiler
+    eager_state = opt.init(params)
+    L.profile_begin()
+    for i in range(steps):
+        _, eager_state, _ = opt.step(zg.ZeroGradState(40 + i, eager_state.opt_state), params, tokens, loss_fn)
+    kern = L.profile_end()
+    pk = peaks()
+    per = {k: v[1] / steps for k, v in sorted(kern.items())}
+    tokens_all = P * B * T
+    # dense x W of q, k, v, o, mlp1, mlp2 plus their rank-r terms 2 tokens r (K + N)
+    lin_flops = 2.0 * tokens_all * (4 * E * E + 2 * E * F) + 2.0 * tokens_all * r * (10 * E + 2 * F)
+    attn_flops = 4.0 * P * B * Hh * T * T * (E // Hh)  # q k^T and p v, all T x T scores (causal half masked)
+    out = {"workload": "decoder-LM block (vocab 32000 tied table lookup, d 768, 12 heads, MLP 3072, RMSNorm, "
+                       "causal attention), 16 candidates x 16 sequences x 256 tokens, rank 16, bf16; one "
+                       "generation = forward + shaping + replay and SGD of all entries, captured",
+           "ms_per_generation": ms, "candidate_evals_per_sec": P / (ms / 1e3), "clocks": clk.summary(),
+           "kernels_ms_per_generation": per}
+    at = kern.get("attention")
+    if at:
+        a_ms = at[1] / at[0]
+        out["attention_roofline"] = {"kernel": "attention", "bound": "tensor",
+                                     "achieved": attn_flops / (a_ms / 1e3) / 1e12, "peak": pk["bf16_tflops"],
+                                     "unit": "TFLOP/s", "frac": attn_flops / (a_ms / 1e3) / 1e12 / pk["bf16_tflops"],
+                                     "launch_ms": a_ms, "peak_source": pk["source"]}
+    gemm_ms = sum(v for k, v in per.items() if k in ("batched_gemm", "batched_u_pass"))
+    if gemm_ms:
+        out["projection_tflops"] = lin_flops / (gemm_ms / 1e3) / 1e12
+    return out
+
+
 # ---------------------------------------------------------------------------
 # CPU arm: the oracle restatement of the reference on a bounded sample
 # ---------------------------------------------------------------------------
@@ -654,6 +749,7 @@ def run_ours(args):
         if world == 1:
             line["int8_qat_layer"] = int8_layer_section(dev, args)
             line["lm_tied_ce"] = tied_ce_section(dev, args)
+            line["lm_block"] = lm_block_section(dev, args)
         if world == 1:
             secs = cpu_generation_sample(8)
             n_cand = max(1, min(64, int(8 * 15.0 / max(secs, 1e-3))))

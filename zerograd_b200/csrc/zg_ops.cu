@@ -130,6 +130,48 @@ __global__ void table_lookup_kernel(const T* __restrict__ table, const int32_t* 
     }
 }
 
+// Rank 8 or 16: a block takes 32 gathered tokens of one candidate, draws
+// their A rows into shared memory once, and each thread keeps its column's
+// B row in registers across the 32 tokens (the same arithmetic, in the same
+// order, as table_lookup_kernel).
+template <typename T, int R>
+__global__ void table_lookup_tiled_kernel(const T* __restrict__ table, const int32_t* __restrict__ idx,
+                                          int idx_batched, int64_t n_idx, const uint32_t* __restrict__ keys,
+                                          int group, int64_t rows, int64_t cols, float s, const T* __restrict__ Bf,
+                                          T* __restrict__ out) {
+    constexpr int TB = 32;
+    __shared__ float a_s[TB][R];
+    __shared__ int64_t row_s[TB];
+    const int p = blockIdx.y;
+    const int64_t t0 = (int64_t)blockIdx.x * TB;
+    const int nt = n_idx - t0 < TB ? (int)(n_idx - t0) : TB;
+    if ((int)threadIdx.x < nt) {
+        int64_t row = idx[(idx_batched ? (int64_t)p * n_idx : 0) + t0 + threadIdx.x];
+        if (row < 0) row += rows;
+        row_s[threadIdx.x] = row < 0 ? 0 : (row >= rows ? rows - 1 : row);
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < nt * R) {
+        const ZgFactorKeys fk = zg_factor_keys(keys, p, group);
+        for (int i = threadIdx.x; i < nt * R; i += blockDim.x)
+            a_s[i / R][i % R] = zg_dtype_round<T>(zg_normal(fk.a, (uint64_t)row_s[i / R] * R + i % R));
+    }
+    __syncthreads();
+    const T* bp = Bf + (int64_t)p * cols * R;
+    T* ob = out + ((int64_t)p * n_idx + t0) * cols;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+        float b[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j) b[j] = zg_to_float(bp[c * R + j]);
+        for (int tt = 0; tt < nt; ++tt) {
+            float lr = 0.f;
+#pragma unroll
+            for (int j = 0; j < R; ++j) lr = fmaf(a_s[tt][j], b[j], lr);
+            ob[(int64_t)tt * cols + c] = zg_from_float<T>(fmaf(s, lr, zg_to_float(table[row_s[tt] * cols + c])));
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // vector: out[p,i] = v[i] + s * noise_p[i], with the reference's per-op
 // rounding to the leaf dtype (product, then sum).
@@ -391,6 +433,23 @@ extern "C" int zg_table_lookup(const void* T, const int32_t* idx, int idx_batche
     // rows inside the lookup kernel (rows = 0: no A elements are drawn).
     int rc = zg::launch_population_factors(keys, group, P, ZG_TABLE, 0, cols, rank, dtype, nullptr, fb, st);
     if (rc) return rc;
+    if (rank == 8 || rank == 16) {
+        dim3 grid((unsigned)((n_idx + 31) / 32), P);
+        const int threads = cols >= 256 ? 256 : (int)((cols + 31) / 32 * 32);
+        zg::LaunchTimer zg_lt_("table_lookup", st);
+#define ZG_LOOKUP(TT, R)                                                                                        \
+    table_lookup_tiled_kernel<TT, R><<<grid, threads, 0, st>>>((const TT*)T, idx, idx_batched, n_idx, keys, group, \
+                                                               rows, cols, s, (const TT*)fb, (TT*)out)
+        if (dtype == ZG_BF16) {
+            if (rank == 8) ZG_LOOKUP(__nv_bfloat16, 8);
+            else ZG_LOOKUP(__nv_bfloat16, 16);
+        } else {
+            if (rank == 8) ZG_LOOKUP(float, 8);
+            else ZG_LOOKUP(float, 16);
+        }
+#undef ZG_LOOKUP
+        return zg::check_launch("zg_table_lookup");
+    }
     dim3 grid((unsigned)n_idx, P);
     int threads = cols >= 256 ? 256 : (int)((cols + 31) / 32 * 32);
     if (threads < rank) threads = (rank + 31) / 32 * 32;

@@ -98,6 +98,50 @@ __global__ void fill_operand_r8_kernel(const uint32_t* __restrict__ keys, int gr
     }
 }
 
+// Small populations (P <= 64): threads are (candidate, row) pairs -- x over
+// the P candidates padded to 8/16/32/64, y over rows -- so a row's R-wide
+// candidate slices are written by adjacent threads and every lane works;
+// the values are fill_operand_r8_kernel's.
+template <typename T, int R>
+__global__ void fill_operand_small_kernel(const uint32_t* __restrict__ keys, int group, int P, int64_t rows,
+                                          int which, int col_major, const float* __restrict__ scale,
+                                          int rows_per_thread, T* __restrict__ out) {
+    const int p = threadIdx.x;
+    if (p >= P) return;
+    ZgFactorKeys fk = zg_factor_keys(keys, p, group);
+    const ZgKey k = which == 0 ? fk.a : fk.b;
+    const float sc = scale ? scale[p] : 1.f;
+    const int64_t ld = (int64_t)P * R;
+    const int64_t r0 = ((int64_t)blockIdx.x * blockDim.y + threadIdx.y) * rows_per_thread;
+    for (int64_t row = r0; row < r0 + rows_per_thread && row < rows; ++row) {
+        T* dst = out + row * ld + (int64_t)p * R;
+#pragma unroll
+        for (int j0 = 0; j0 < R; j0 += 8) {
+            uint64_t ctr[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                ctr[i] = col_major ? (uint64_t)(j0 + i) * rows + row : (uint64_t)row * R + j0 + i;
+            float v[8];
+            zg_normal_x8(k, ctr, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[i] = zg_dtype_round<T>(v[i]);
+                if (scale) v[i] = __fmul_rn(v[i], sc);
+            }
+            if constexpr (sizeof(T) == 2) {
+                uint4 pk;
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                *reinterpret_cast<uint4*>(dst + j0) = pk;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dst[j0 + i] = v[i];
+            }
+        }
+    }
+}
+
 // Transposed fill: out[(p*R + j) * rows + row] = bf16(normal(key_p, row*R + j)).
 // Thread = 8 consecutive rows of one candidate and all R ranks, so each of
 // its R stores is 16 bytes and a warp's stores for one j are 512 contiguous
@@ -410,6 +454,28 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
     dim3 grid(pblocks, (unsigned)yblocks);
     zg::LaunchTimer zg_lt_(name, st);
     const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && extra_scale == 1.f;
+    if (aligned && (rank == 8 || rank == 16) && P <= 64) {
+        const int px = P <= 8 ? 8 : P <= 16 ? 16 : P <= 32 ? 32 : 64;
+        const int ry = 128 / px;
+        int64_t want_threads = (int64_t)sm_count() * 8 * ry;  // ~8 blocks of 128 threads per SM
+        int rpt = (int)((rows + want_threads - 1) / want_threads);
+        if (rpt < 2) rpt = 2;  // amortise the per-thread key derivation
+        const int64_t gx = (rows + (int64_t)ry * rpt - 1) / ((int64_t)ry * rpt);
+        if (gx > 2147483647) return fail(ZG_ERR_INVALID, "fill_operand: too many rows");
+        dim3 g2((unsigned)gx), b2(px, ry);
+#define ZG_FILL_SMALL(TT, RR)                                                                                      \
+    fill_operand_small_kernel<TT, RR><<<g2, b2, 0, st>>>(keys, group, P, rows, which, col_major, scale, rpt, \
+                                                          static_cast<TT*>(out))
+        if (dtype == ZG_BF16) {
+            if (rank == 8) ZG_FILL_SMALL(__nv_bfloat16, 8);
+            else ZG_FILL_SMALL(__nv_bfloat16, 16);
+        } else {
+            if (rank == 8) ZG_FILL_SMALL(float, 8);
+            else ZG_FILL_SMALL(float, 16);
+        }
+#undef ZG_FILL_SMALL
+        return check_launch("fill_operand");
+    }
     if (aligned && (rank == 8 || rank == 16)) {
         if (dtype == ZG_BF16) {
             if (rank == 8)
