@@ -142,3 +142,28 @@ def test_vit_block_under_vmap(cuda):
     assert torch.isfinite(batched).all()
     np.testing.assert_allclose(batched.cpu().numpy(), single.cpu().numpy(), rtol=2e-2, atol=1e-3)
     assert L.load().zg_device_error(1) == 0
+
+
+def test_attention_lm_size(cuda, oracle):
+    """The decoder LM's attention for 16 candidates x 16 sequences (256
+    tokens, 12 heads of 64, causal); the first and last z against the oracle."""
+    Z, S, H, D = 256, 256, 12, 64
+    g = torch.Generator(device=cuda).manual_seed(11)
+    q, k, v = (torch.randn(Z, S, H, D, generator=g, device=cuda).to(torch.bfloat16) for _ in range(3))
+    o = _block.launch_attention(q, k, v, True)
+    assert L.load().zg_device_error(1) == 0
+    for z in (0, Z - 1):
+        want = oracle.attention(_np(q[z]), _np(k[z]), _np(v[z]), True)
+        np.testing.assert_allclose(_np(o[z]), want, rtol=2e-2, atol=2e-2)
+
+
+def test_rms_norm_lm_size(cuda, oracle):
+    """RMSNorm of 16 candidates' hidden states [16, 4096, 768] with their own
+    scales; rows of the first and last candidate against the oracle."""
+    P, M, C = 16, 4096, 768
+    g = torch.Generator(device=cuda).manual_seed(12)
+    x = torch.randn(P, M, C, generator=g, device=cuda).to(torch.bfloat16)
+    sc = (1 + 0.1 * torch.randn(P, C, generator=g, device=cuda)).to(torch.bfloat16)
+    y = _block.launch_norm("rms", x, sc, None, 1e-6, True, True, P)
+    for p in (0, P - 1):
+        np.testing.assert_allclose(_np(y[p, :64]), oracle.rms_norm(_np(x[p, :64]), _np(sc[p])), rtol=2e-2, atol=2e-2)

@@ -57,7 +57,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const int t = threadIdx.x, warp = t / 32;
     const int qt = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
     const int q0 = qt * 128;
-    const int kboxes = a.s_pad / 128;
+    // keys this query tile can see: causal tiles stop at their last query
+    const int n_keys = a.causal && q0 + 128 < a.s_pad ? q0 + 128 : a.s_pad;
+    const int kboxes = n_keys / 128;
 
     if (t == 0) {
         mbar_init(&load_bar, 1);
@@ -80,7 +82,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         }
         if (mbar_wait(&load_bar, 0, 81)) {
             tc_fence_after();
-            const uint32_t idesc = idesc_bf16(128, a.s_pad, 0);
+            const uint32_t idesc = idesc_bf16(128, n_keys, 0);
             const uint32_t qa = smem_u32(smem + AT_Q), ka = smem_u32(smem + AT_K);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
@@ -95,30 +97,35 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     // ---- softmax over this thread's query row ----
     const int qi = q0 + t;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    // columns [0, vis) are visible to this query: the keys, up to the query when causal
+    const int vis = a.causal ? (qi + 1 < a.S ? qi + 1 : a.S) : a.S;
     float mx = -INFINITY;
-    for (int c = 0; c < a.s_pad; c += 32) {
+    for (int c = 0; c < n_keys; c += 32) {
         float v[32];
         tmem_ld32(trow + c, v);
+        if (c + 32 <= vis) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int col = c + j;
-            const bool live = col < a.S && !(a.causal && col > qi);
-            mx = fmaxf(mx, live ? v[j] * a.scale_log2 : -INFINITY);
+            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, v[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (c + j < vis) mx = fmaxf(mx, v[j]);
         }
     }
+    mx *= a.scale_log2;  // scale_log2 > 0, so max(s) * scale = max(s * scale)
     float sum = 0.f;
-    for (int c = 0; c < a.s_pad; c += 32) {
+    for (int c = 0; c < n_keys; c += 32) {
         float v[32];
         tmem_ld32(trow + c, v);
         uint32_t pk[16];
+        const bool full = c + 32 <= vis;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             float pe[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int col = c + 2 * j + e;
-                const bool live = col < a.S && !(a.causal && col > qi);
-                pe[e] = live ? ex2_approx(fmaf(v[2 * j + e], a.scale_log2, -mx)) : 0.f;
+                pe[e] = full || col < vis ? ex2_approx(fmaf(v[2 * j + e], a.scale_log2, -mx)) : 0.f;
             }
             const __nv_bfloat162 b2 = __floats2bfloat162_rn(pe[0], pe[1]);
             sum += __low2float(b2) + __high2float(b2);  // the weights the PV product uses
@@ -142,7 +149,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (t == 0 && ok) {
         const uint32_t idesc = idesc_bf16(128, 64, 1);
         const uint32_t pa = smem_u32(smem + AT_P), va = smem_u32(smem + AT_V);
-        for (int kk = 0; kk < a.s_pad / 16; ++kk)
+        for (int kk = 0; kk < n_keys / 16; ++kk)
             umma_bf16(tmem, smem_desc(pa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
                       smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc, kk > 0 ? 1u : 0u);
         umma_commit(&mma_bar);
