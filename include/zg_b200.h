@@ -188,7 +188,10 @@ ZG_API int zg_replay_operands(const float* shaped, const void* A, int a_transpos
  * guard (optional, device float): when *guard != 0 nothing is written, so an
  * in-place update of a generation whose losses were rejected leaves the
  * parameters as they were (zg_shape_fitness's non-finite count, metrics[3]);
- * a guarded call takes no descent_out.
+ * a guarded call takes no descent_out.  bias_corrections (optional, device
+ * float[2]): AdamW's [1 - b1^count, 1 - b2^count] read at run time instead
+ * of derived from count (zg_adam_bias_corrections gives the same floats),
+ * so a captured generation can advance the step count.
  * Workspace: zg_replay_operands_workspace_size.  Replaces
  * replay_entry + transform.update + apply_updates
  * (src/zerograd/_replay.py:44-54, src/zerograd/_optimizer.py:229-234). */
@@ -202,8 +205,8 @@ ZG_API int zg_replay_adamw(const float* shaped, const void* A, int a_transposed,
                            float inv_sqrt_rank, const void* param, void* param_out, int dtype,
                            const float* mu, const float* nu, float* mu_out, float* nu_out, int count,
                            double lr, double b1, double b2, double eps, double weight_decay,
-                           float* descent_out, const float* guard, void* workspace,
-                           size_t workspace_bytes, void* stream);
+                           float* descent_out, const float* guard, const float* bias_corrections,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* Tied logits fused with softmax cross-entropy (bf16, tcgen05): for each
  * candidate p and row m
@@ -341,13 +344,19 @@ ZG_API int zg_replay_noalloc(const float* shaped, const uint32_t* keys, int grou
  * alias the inputs).  param is in `dtype`; the moments are float32.
  * `count` is the step count AFTER increment (1 on the first step).  The
  * hyper-parameters are the Python floats given to the transform.
+ * bias_corrections (optional, device float[2]) replaces the count's
+ * [1 - b1^count, 1 - b2^count] as in zg_replay_adamw.
  * Replaces transform.update + optax.apply_updates
  * (src/zerograd/_optimizer.py:233-234) and _build_pseudo_grad
  * (src/zerograd/_optimizer.py:299-326). */
 ZG_API int zg_adamw_update(const void* param, void* param_out, int dtype, const float* descent,
                            const float* mu, const float* nu, float* mu_out, float* nu_out,
                            int64_t n, int count, double lr, double b1, double b2, double eps,
-                           double weight_decay, void* stream);
+                           double weight_decay, const float* bias_corrections, void* stream);
+
+/* AdamW's bias corrections [1 - b1^count, 1 - b2^count] as the update
+ * kernels compute them (float32, on the host), into out[2]. */
+ZG_API int zg_adam_bias_corrections(int count, double b1, double b2, float* out);
 
 /* Fused SGD (optax.sgd without momentum): param_out = param + (-lr) * g with
  * g = -descent (zero when descent is NULL). */

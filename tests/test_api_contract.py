@@ -268,8 +268,9 @@ def test_cpu_tensors_fail_loudly():
 
 
 def test_capture_refusals():
-    """A captured generation needs sgd (adamw's bias correction is a
-    per-step host value) and CUDA parameters; shards need a gather."""
+    """A captured generation needs the library's sgd or adamw transform
+    (their kernels take the per-step values from device buffers) and CUDA
+    parameters; shards need a gather."""
     from zerograd_b200._graph import CapturedGeneration
     from zerograd_b200._lib import ZgLibraryError
 
@@ -277,7 +278,16 @@ def test_capture_refusals():
     params = {"linear": {"weight": torch.zeros(4, 3)}, "table": {"embed": torch.zeros(5, 3)},
               "vector": {"scale": torch.zeros(3)}}
     loss = lambda p, ctx, batch, rng: (torch.zeros(()), None)  # noqa: E731
+    class custom:  # an optax-style transform the graph cannot see into
+        def init(self, params):
+            return ()
+
+        def update(self, grads, state, params=None):
+            return grads, state
+
     with pytest.raises(NotImplementedError):
+        zg.ZeroGrad(m, custom(), 4, 2, 0.1, 0, "r").capture(params, loss, torch.zeros(2, 4))
+    with pytest.raises(ZgLibraryError):
         zg.ZeroGrad(m, zg.adamw(1e-3), 4, 2, 0.1, 0, "r").capture(params, loss, torch.zeros(2, 4))
     opt = zg.ZeroGrad(m, zg.sgd(0.1), 4, 2, 0.1, 0, "r")
     with pytest.raises(ZgLibraryError):

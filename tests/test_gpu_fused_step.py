@@ -61,7 +61,7 @@ def test_fused_step_matches_replay_then_update(cuda, oracle, rows, cols, P, layo
         mo, vo = torch.empty_like(mu), torch.empty_like(nu)
         L.call("zg_replay_adamw", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r, inv, L.ptr(param),
                L.ptr(new), L.ZG_BF16, L.ptr(mu), L.ptr(nu), L.ptr(mo), L.ptr(vo), 3, 1e-3, 0.9, 0.999, 1e-8, 1e-4,
-               L.ptr(d2), None, L.ptr(ws), ws.numel(), st)
+               L.ptr(d2), None, None, L.ptr(ws), ws.numel(), st)
         assert torch.equal(new, want) and torch.equal(mo, wm) and torch.equal(vo, wv)
     assert torch.equal(d2, d)  # the optional descent output is the unfused replay's
     assert L.load().zg_device_error(1) == 0

@@ -27,9 +27,11 @@ and returns a handle whose ``result()`` does that read later, so successive
 generations keep the GPU busy.
 
 Each replay gives the same bits as the eager ``evaluate_shard`` +
-``step_from_losses`` of the same generation.  Capturable optimizers are the
-ones whose kernels take no per-generation host value: ``sgd``.  (AdamW's bias
-correction 1 - b^t is a host value that changes every step.)
+``step_from_losses`` of the same generation, for ``sgd`` and ``adamw``.
+AdamW's bias corrections 1 - b^t change every step: the host computes them
+as the eager kernels do (``zg_adam_bias_corrections``) and copies them into
+a device buffer before each replay, and the moments live in captured
+buffers updated in place like the parameters.
 
 With a process group, ``gather`` (the fitness all-gather) is captured in the
 graph as well, and each process captures its own shard of candidates.
@@ -65,11 +67,10 @@ class CapturedGeneration:
                  gather: Callable[[torch.Tensor], torch.Tensor] | None = None,
                  rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2):
         from ._optimizer import ZeroGradState, _device_of, _materialize_tree
-        from ._transforms import sgd
+        from ._transforms import AdamWState, adamw, sgd
 
-        if not isinstance(optimizer.transform, sgd):
-            raise NotImplementedError("capture needs an optimizer whose kernels take no per-generation host "
-                                      "value: sgd (adamw's bias correction changes every step)")
+        if not isinstance(optimizer.transform, (sgd, adamw)):
+            raise NotImplementedError("capture supports the library's sgd and adamw transforms")
         optimizer.manifest.validate(params)
         self._opt = optimizer
         self._gather = gather
@@ -94,6 +95,15 @@ class CapturedGeneration:
         g0 = state.generation if state is not None else 0
         opt_state0 = state.opt_state if state is not None else optimizer.init(self._params).opt_state
         self._state_cls = ZeroGradState
+        self._adam = isinstance(optimizer.transform, adamw)
+        if self._adam:
+            # the moments in captured buffers; the bias corrections of each
+            # step in a device buffer filled before the replay
+            self._bc_dev = torch.zeros(2, dtype=torch.float32, device=dev)
+            self._adam_cls = AdamWState
+            opt_state0 = AdamWState(opt_state0.count, _clone_tree(opt_state0.mu), _clone_tree(opt_state0.nu),
+                                    bias_corrections=self._bc_dev)
+        self._opt_state = opt_state0
 
         # warm-up outside the graph: first-call setup (kernel attributes, the
         # factor-cache budget, the communicator) must not happen in a capture
@@ -102,6 +112,7 @@ class CapturedGeneration:
         with torch.cuda.stream(side):
             for i in range(max(1, warmup)):
                 self._set_base(g0 + i)
+                self._set_count(opt_state0)
                 self._generation(g0 + i, opt_state0, copy_back=False)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
@@ -116,6 +127,15 @@ class CapturedGeneration:
         optimizer._forget_keys(capture_stream)
         #: this library's kernels in one replay of the graph
         self.kernels_per_generation = L.launch_count() - n0
+
+    def _set_count(self, opt_state) -> None:
+        """AdamW: the bias corrections of step count + 1 into the device buffer."""
+        if not self._adam:
+            return
+        t = self._opt.transform
+        host = torch.empty(2, dtype=torch.float32, pin_memory=True)
+        L.call("zg_adam_bias_corrections", int(opt_state.count) + 1, float(t.b1), float(t.b2), L.ptr(host))
+        self._bc_dev.copy_(host, non_blocking=True)
 
     def _set_base(self, generation: int) -> None:
         # a fresh pinned buffer per call: the pinned allocator reuses it only
@@ -145,8 +165,12 @@ class CapturedGeneration:
                                                            inplace=copy_back)
         if copy_back:
             flag = metrics[3:4]  # non-finite loss count
-            for path, t in _leaves(self._params):
-                new = tree_get(new_params, path)
+            pairs = [(t, tree_get(new_params, path)) for path, t in _leaves(self._params)]
+            if self._adam:
+                for which in ("mu", "nu"):
+                    old, new = getattr(opt_state, which), getattr(new_opt_state, which)
+                    pairs += [(t, tree_get(new, path)) for path, t in _leaves(old)]
+            for t, new in pairs:
                 if new is not t:
                     _ops.launch_copy_if_zero(t, new.contiguous(), flag)
         return new_params, new_opt_state, metrics
@@ -175,10 +199,22 @@ class CapturedGeneration:
                         raise ValueError(f"batch leaf of shape {tuple(s.shape)}; captured {tuple(d.shape)}")
                     d.copy_(s, non_blocking=True)
         self._set_base(state.generation)
+        self._set_count(state.opt_state)
         self._graph.replay()
 
+    @property
+    def opt_state(self):
+        """The captured optimizer state (AdamW's moments live here)."""
+        return self._opt_state
+
     def _next_state(self, state):
-        return self._state_cls(state.generation + 1, _advance_state(state.opt_state, self._out[1]))
+        """The state after one replay: the generation and the step count
+        advance; AdamW's moments are the captured buffers."""
+        if self._adam:
+            nxt = self._adam_cls(int(state.opt_state.count) + 1, self._opt_state.mu, self._opt_state.nu)
+        else:
+            nxt = _advance_state(state.opt_state, self._out[1])
+        return self._state_cls(state.generation + 1, nxt)
 
     def step(self, state, batch: Any = None):
         """One generation: copy `batch` (if given) into the captured batch,

@@ -49,7 +49,7 @@ SIGNATURES = {
     "zg_replay_sgd": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _i32, _f64, _vp,
                              _vp, _vp, _sz, _vp]),
     "zg_replay_adamw": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _i32, _vp, _vp,
-                               _vp, _vp, _i32, _f64, _f64, _f64, _f64, _f64, _vp, _vp, _vp, _sz, _vp]),
+                               _vp, _vp, _i32, _f64, _f64, _f64, _f64, _f64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "zg_tied_logits_ce_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "zg_tied_logits_ce": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
                                  _vp]),
@@ -73,7 +73,8 @@ SIGNATURES = {
     "zg_replay": (_i32, [_vp, _vp, _i32, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp, _vp, _sz, _vp]),
     "zg_replay_noalloc": (_i32, [_vp, _vp, _i32, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp, _vp]),
     "zg_adamw_update": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _f64, _f64, _f64, _f64,
-                               _f64, _vp]),
+                               _f64, _vp, _vp]),
+    "zg_adam_bias_corrections": (_i32, [_i32, _f64, _f64, _vp]),
     "zg_sgd_update": (_i32, [_vp, _vp, _i32, _vp, _i64, _f64, _vp]),
     "zg_copy_if_zero": (_i32, [_vp, _vp, _sz, _vp, _vp]),
     "zg_layer_norm": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i64, _i32, _f32, _i32, _vp, _vp]),

@@ -633,12 +633,13 @@ def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int
     L.call("zg_replay_adamw", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, rank, inv, L.ptr(param),
            L.ptr(out), L.ZG_BF16, L.ptr(mu), L.ptr(nu), L.ptr(mu_out), L.ptr(nu_out), int(step["count"]),
            float(step["lr"]), float(step["b1"]), float(step["b2"]), float(step["eps"]), float(step["weight_decay"]),
-           None, guard, L.ptr(ws), ws.numel(), st)
+           None, guard, L.ptr(step.get("bc")), L.ptr(ws), ws.numel(), st)
     return out, mu_out, nu_out
 
 
 def launch_adamw(param: torch.Tensor, descent: torch.Tensor | None, mu: torch.Tensor, nu: torch.Tensor,
-                 count: int, lr: float, b1: float, b2: float, eps: float, weight_decay: float):
+                 count: int, lr: float, b1: float, b2: float, eps: float, weight_decay: float,
+                 bias_corrections: torch.Tensor | None = None):
     dev = L.require_cuda(param, descent, mu, nu)
     p_out = torch.empty_like(param)
     mu_out = torch.empty_like(mu)
@@ -646,7 +647,7 @@ def launch_adamw(param: torch.Tensor, descent: torch.Tensor | None, mu: torch.Te
     d = None if descent is None else descent.to(torch.float32).contiguous()
     L.call("zg_adamw_update", L.ptr(param.contiguous()), L.ptr(p_out), L.dtype_code(param.dtype), L.ptr(d),
            L.ptr(mu), L.ptr(nu), L.ptr(mu_out), L.ptr(nu_out), param.numel(), count, lr, b1, b2, eps,
-           weight_decay, L.stream_ptr(dev))
+           weight_decay, L.ptr(bias_corrections), L.stream_ptr(dev))
     return p_out, mu_out, nu_out
 
 

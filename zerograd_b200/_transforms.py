@@ -47,6 +47,10 @@ class AdamWState:
     count: int
     mu: dict
     nu: dict
+    # Optional device float32 [2]: the bias corrections of step count + 1,
+    # read by the kernels instead of deriving them from `count` (a captured
+    # generation fills it before each replay).  None: derived from `count`.
+    bias_corrections: torch.Tensor | None = None
 
 
 @dataclass(frozen=True)
@@ -71,7 +75,7 @@ class adamw:
         """The step of one leaf, for a replay that applies it in its epilogue."""
         return {"kind": "adamw", "lr": self.learning_rate, "b1": self.b1, "b2": self.b2, "eps": self.eps,
                 "weight_decay": self.weight_decay, "count": state.count + 1, "mu": tree_get(state.mu, path),
-                "nu": tree_get(state.nu, path)}
+                "nu": tree_get(state.nu, path), "bc": state.bias_corrections}
 
     def apply(self, params: dict, descent: dict, state: AdamWState, done: dict | None = None):
         """New params and state from the descent tree (missing leaf: zero
@@ -91,11 +95,12 @@ class adamw:
                 continue
             d = tree_get(descent, path)
             pn, m, v = _ops.launch_adamw(p, d, tree_get(state.mu, path), tree_get(state.nu, path), count,
-                                         self.learning_rate, self.b1, self.b2, self.eps, self.weight_decay)
+                                         self.learning_rate, self.b1, self.b2, self.eps, self.weight_decay,
+                                         state.bias_corrections)
             tree_set(new_p, path, pn)
             tree_set(mu, path, m)
             tree_set(nu, path, v)
-        return new_p, AdamWState(count=count, mu=mu, nu=nu)
+        return new_p, AdamWState(count=count, mu=mu, nu=nu, bias_corrections=state.bias_corrections)
 
 
 @dataclass(frozen=True)

@@ -273,7 +273,9 @@ template <typename T>
 __global__ void adamw_kernel(const T* __restrict__ param, T* __restrict__ param_out,
                              const float* __restrict__ descent, const float* __restrict__ mu,
                              const float* __restrict__ nu, float* __restrict__ mu_out,
-                             float* __restrict__ nu_out, int64_t n, zg::AdamConsts c) {
+                             float* __restrict__ nu_out, int64_t n, zg::AdamConsts c0,
+                             const float* __restrict__ bc) {
+    const zg::AdamConsts c = zg::adam_consts_dev(c0, bc);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float g = descent ? -descent[i] : 0.f;  // pseudo_grad = -descent
@@ -551,7 +553,7 @@ extern "C" int zg_replay(const float* shaped, const uint32_t* keys, int group, i
 extern "C" int zg_adamw_update(const void* param, void* param_out, int dtype, const float* descent,
                                const float* mu, const float* nu, float* mu_out, float* nu_out, int64_t n,
                                int count, double lr, double b1, double b2, double eps, double weight_decay,
-                               void* stream) {
+                               const float* bias_corrections, void* stream) {
     if (n < 0 || count < 1) return zg::fail(ZG_ERR_INVALID, "zg_adamw_update: bad sizes");
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_adamw_update: bad dtype");
     if (n == 0) return ZG_OK;
@@ -562,11 +564,20 @@ extern "C" int zg_adamw_update(const void* param, void* param_out, int dtype, co
     zg::LaunchTimer zg_lt_("adamw_update", st);
     if (dtype == ZG_BF16)
         adamw_kernel<__nv_bfloat16><<<ew_grid(n), 256, 0, st>>>((const __nv_bfloat16*)param, (__nv_bfloat16*)param_out,
-                                                                descent, mu, nu, mu_out, nu_out, n, c);
+                                                                descent, mu, nu, mu_out, nu_out, n, c,
+                                                                bias_corrections);
     else
         adamw_kernel<float><<<ew_grid(n), 256, 0, st>>>((const float*)param, (float*)param_out, descent, mu, nu,
-                                                        mu_out, nu_out, n, c);
+                                                        mu_out, nu_out, n, c, bias_corrections);
     return zg::check_launch("zg_adamw_update");
+}
+
+extern "C" int zg_adam_bias_corrections(int count, double b1, double b2, float* out) {
+    if (count < 1 || !out) return zg::fail(ZG_ERR_INVALID, "zg_adam_bias_corrections: count >= 1 and an output");
+    const zg::AdamConsts c = zg::adam_consts(count, 0.0, b1, b2, 0.0, 0.0);
+    out[0] = c.bc1;
+    out[1] = c.bc2;
+    return ZG_OK;
 }
 
 extern "C" int zg_copy_if_zero(void* dst, const void* src, size_t bytes, const float* flag, void* stream) {

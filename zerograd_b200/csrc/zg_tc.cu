@@ -89,13 +89,14 @@ __device__ __forceinline__ void tc_step8(const zg::FusedStep& st, int64_t e0, co
         }
     }
     float pn[8], m[8], vv[8];
+    const zg::AdamConsts ac = st.kind == zg::ZG_STEP_ADAMW ? zg::adam_consts_dev(st.c, st.bc) : st.c;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float g = -d[i];  // pseudo-gradient
         if (st.kind == zg::ZG_STEP_SGD) {
             pn[i] = zg::sgd_step(p[i], g, st.c.neg_lr);
         } else {
-            pn[i] = zg::adamw_step(p[i], g, mu[i], nu[i], st.c, m[i], vv[i]);
+            pn[i] = zg::adamw_step(p[i], g, mu[i], nu[i], ac, m[i], vv[i]);
         }
     }
     if (vec) {

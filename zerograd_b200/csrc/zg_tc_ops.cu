@@ -1090,13 +1090,15 @@ extern "C" int zg_replay_adamw(const float* shaped, const void* A, int a_transpo
                                int P, int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, const void* param,
                                void* param_out, int dtype, const float* mu, const float* nu, float* mu_out,
                                float* nu_out, int count, double lr, double b1, double b2, double eps,
-                               double weight_decay, float* descent_out, const float* guard, void* workspace,
-                               size_t workspace_bytes, void* stream) {
+                               double weight_decay, float* descent_out, const float* guard,
+                               const float* bias_corrections, void* workspace, size_t workspace_bytes,
+                               void* stream) {
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: bad dtype");
     if (count < 1) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: count must be >= 1");
     if (!mu || !nu || !mu_out || !nu_out) return zg::fail(ZG_ERR_INVALID, "zg_replay_adamw: null moment");
     zg::FusedStep st{};
     st.guard = guard;
+    st.bc = bias_corrections;
     st.kind = zg::ZG_STEP_ADAMW;
     st.param_bf16 = dtype == ZG_BF16;
     st.ldp = cols;

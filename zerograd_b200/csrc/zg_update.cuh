@@ -30,6 +30,17 @@ inline AdamConsts adam_consts(int count, double lr, double b1, double b2, double
     return c;
 }
 
+// The constants with the bias corrections [1 - b1^count, 1 - b2^count] read
+// from device memory when `bc` is given (a captured generation writes them
+// for each step; adam_consts computes the same floats on the host).
+__device__ __forceinline__ AdamConsts adam_consts_dev(AdamConsts c, const float* bc) {
+    if (bc) {
+        c.bc1 = bc[0];
+        c.bc2 = bc[1];
+    }
+    return c;
+}
+
 // optax.adamw on one element: new moments (m, v) and the new parameter.
 __device__ __forceinline__ float adamw_step(float p, float g, float mu, float nu, const AdamConsts& c, float& m,
                                            float& v) {
@@ -62,6 +73,7 @@ struct FusedStep {
     float* nu_out;
     AdamConsts c;        // neg_lr is the SGD rate as well
     const float* guard;  // optional: when *guard != 0 the step writes nothing (in-place updates stay intact)
+    const float* bc;     // optional: AdamW bias corrections in device memory (replace c.bc1, c.bc2)
 };
 
 }  // namespace zg
