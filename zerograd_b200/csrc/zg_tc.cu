@@ -556,7 +556,7 @@ constexpr uint32_t EX_OP = 128 * 16;                       // one operand tile: 
 constexpr uint32_t EX_A = 0, EX_AZ = EX_STAGES * EX_OP;    // A data, A zero half
 constexpr uint32_t EX_B = 2 * EX_STAGES * EX_OP, EX_BZ = 3 * EX_STAGES * EX_OP;
 constexpr uint32_t EX_LBO = EX_STAGES * EX_OP;             // data -> zero half, same for every stage
-constexpr uint32_t EX_STG = 32768;                         // staging buffers, each 2 x 16 KiB sub-tiles
+constexpr uint32_t EX_STG = 4 * EX_STAGES * EX_OP;        // staging buffers, each 2 x 16 KiB sub-tiles
 constexpr uint32_t EX_STG_BYTES = 128 * 128 * 2;
 constexpr int EX_NSTG = 4;                                 // staging buffers in flight
 constexpr int EX_NACC = 4;                                 // TMEM accumulators of 128 columns (all 512)
@@ -569,7 +569,8 @@ struct ExpandArgs {
     int tiles_m, tiles_n, chunk, chunks;
 };
 
-constexpr int EX_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue (2 per TMEM lane quadrant)
+constexpr int EX_THREADS = 352;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue (2 per TMEM lane quadrant),
+                                 // warp 10 TMA stores
 __device__ __forceinline__ void ex_item_range(int items, int& t0, int& t1) {
     const int per = items / (int)gridDim.x, rem = items % (int)gridDim.x, b = blockIdx.x;
     t0 = b * per + min(b, rem);
@@ -666,12 +667,34 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
         umma_commit(&mma_done);
         for (uint32_t i = 0; i < kSpinLimit; ++i)
             if (mbar_try_wait(&mma_done, 0)) break;
+    } else if (warp == 10) {
+        // ---------------- TMA stores: a full staging buffer -> y[p] tile ----------------
+        if (lane == 0) {
+            int c = 0;
+            bool ok = true;
+            for (int t = t_begin; ok && t < t_end; ++t) {
+                const int chunk = t % a.chunks, tile = t / a.chunks;
+                const int m0 = (tile / a.tiles_n) * 128, n0 = (tile % a.tiles_n) * 128;
+                const int p1 = min(a.P, (chunk + 1) * a.chunk);
+                for (int p = chunk * a.chunk; p < p1; ++p, ++c) {
+                    const int sb = c % EX_NSTG;
+                    if (!mbar_wait(&stg_full[sb], (uint32_t)(c / EX_NSTG) & 1, 16)) { ok = false; break; }
+                    uint8_t* stg = smem + EX_STG + sb * EX_STG_BYTES;
+                    tma_store_3d(&tmY, stg, n0, m0, p);
+                    tma_store_3d(&tmY, stg + 128 * 128, n0 + 64, m0, p);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    // all but the two newest stores have finished reading their buffers
+                    asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
+                    if (c >= 2) mbar_arrive(&stg_free[(c - 2) % EX_NSTG]);
+                }
+            }
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        }
     } else if (warp >= 2) {
-        // ---------------- epilogue: TMEM -> bf16 -> swizzled smem -> TMA store ----------------
+        // ---------------- epilogue: TMEM -> bf16 -> swizzled smem (warp 10 stores it) ----------------
         const int quad = warp % 4;             // TMEM lanes 32*quad..32*quad+31
         const int half = (warp - 2) / 4;       // columns 64*half..64*half+63
         const int row = quad * 32 + lane;      // TMEM lane == tile row
-        const bool issuer = (warp == 2 && lane == 0);
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const float2 s2 = make_float2(a.s, a.s);
         float2 xw[32];  // this thread's row of the XW tile, its 64 columns (constant within a tile)
@@ -725,19 +748,8 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
                 if (++acc == EX_NACC) { acc = 0; acc_phase ^= 1; }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive(&stg_full[sb]);
-                if (issuer) {
-                    if (!mbar_wait(&stg_full[sb], use & 1, 16)) { ok = false; break; }
-                    uint8_t* stg = smem + EX_STG + sb * EX_STG_BYTES;
-                    tma_store_3d(&tmY, stg, n0, m0, p);
-                    tma_store_3d(&tmY, stg + 128 * 128, n0 + 64, m0, p);
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                    // all but the two newest stores have finished reading their buffers
-                    asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
-                    if (c >= 2) mbar_arrive(&stg_free[(c - 2) % EX_NSTG]);
-                }
             }
         }
-        if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
