@@ -626,9 +626,9 @@ def run_ours(args):
     eager_ms = max_over_ranks(eager_ms)
     barrier()
 
-    # Captured form, the headline: CapturedGeneration.step with the batch
+    # Captured form, synchronous: CapturedGeneration.step with the batch
     # copied in from pinned host memory and the metrics read back (a host
-    # synchronisation) every generation.
+    # synchronisation) before the next generation is queued.
     def captured_step(Wcur, gen):
         nonlocal cstate
         _, cstate, _ = cg.step(zg.ZeroGradState(gen, cstate.opt_state), x_host)
@@ -637,8 +637,44 @@ def run_ours(args):
     for i in range(min(args.warmup, 3)):
         captured_step(None, i)
     barrier()
-    e2e_ms, _ = timed(captured_step, args.steps, None)
-    e2e_ms = max_over_ranks(e2e_ms)
+    sync_ms, _ = timed(captured_step, args.steps, None)
+    sync_ms = max_over_ranks(sync_ms)
+    barrier()
+
+    # Captured form, pipelined, the headline: CapturedGeneration.enqueue with
+    # the batch copied from pinned host memory every generation (on the copy
+    # stream, into the batch slot the previous-but-one generation used, while
+    # the previous generation computes) and generation g-1's metrics read
+    # back on the host before generation g+1 is queued.  Timed as one
+    # interval on the device from before the first copy to after the last
+    # metrics read, less the L2 flushes queued between generations (each
+    # bracketed by its own events on the compute stream).  The copy of
+    # generation g+1 is issued when generation g-1 ends, so it runs during
+    # generation g, not during a flush.
+    def pipelined(steps, first):
+        nonlocal cstate
+        pend, flushes = [], []
+        ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+        start, end = ev(), ev()
+        start.record()
+        for i in range(steps):
+            f0, f1 = ev(), ev()
+            f0.record()
+            flush.zero_()
+            f1.record()
+            flushes.append((f0, f1))
+            _, cstate, p = cg.enqueue(zg.ZeroGradState(first + i, cstate.opt_state), x_host)
+            pend.append(p)
+            if i >= 1:
+                pend[i - 1].result()
+        pend[-1].result()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) - sum(a.elapsed_time(b) for a, b in flushes)
+
+    pipelined(max(3, args.warmup), 0)
+    barrier()
+    e2e_ms = max_over_ranks(pipelined(args.steps, args.warmup))
     barrier()
     del cg  # holds NCCL work with more than one rank: released before the process group
     torch.cuda.synchronize()
@@ -682,6 +718,7 @@ def run_ours(args):
 
     value = P * args.steps / (ms / 1e3)
     e2e_value = P * args.steps / (e2e_ms / 1e3)
+    sync_value = P * args.steps / (sync_ms / 1e3)
     eager_value = P * args.steps / (eager_ms / 1e3)
     eager_dev_value = P * args.steps / (eager_dev_ms / 1e3)
     if rank == 0:
@@ -719,7 +756,13 @@ def run_ours(args):
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 8,
                     "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms / args.steps,
-                    "api": "ZeroGrad.capture -> CapturedGeneration.step (the generation as one CUDA graph)"},
+                    "api": "ZeroGrad.capture -> CapturedGeneration.enqueue, pinned host batch every generation "
+                           "(copied during the previous generation), metrics read back one generation behind",
+                    "l2": "flushed before every generation (256 MiB write on the compute stream); "
+                          "the flushes' own event time subtracted from the loop's interval"},
+            "e2e_sync": {"value": sync_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 8,
+                         "d2h_bytes_per_step": 16, "ms_per_step": sync_ms / args.steps,
+                         "api": "CapturedGeneration.step: copy, replay, metrics read before the next generation"},
             "e2e_eager": {"value": eager_value, "unit": UNIT, "h2d_bytes_per_step": M * K * 2 + 4 * P_local,
                           "d2h_bytes_per_step": 16, "ms_per_step": eager_ms / args.steps,
                           "api": "evaluate_shard + step_from_losses (fitness from the host)"},

@@ -155,3 +155,33 @@ def test_captured_adamw_matches_eager(cuda):
     for k in before[0]:
         assert torch.equal(cg.params[k], before[0][k]) and torch.equal(cg.opt_state.mu[k], before[1][k])
     assert L.load().zg_device_error(1) == 0
+
+
+@pytest.mark.parametrize("slots,transform", [(2, "sgd"), (1, "sgd"), (2, "adamw")])
+def test_enqueued_host_batches_match_eager(cuda, slots, transform):
+    """Batches from pinned host memory, queued back to back: with two slots
+    the copies of generation g+1 run on the copy stream while generation g
+    computes; every generation's parameters and metrics are those of the
+    eager steps on the same batches."""
+    manifest, params, _, loss_fn = _small(cuda)
+    g = torch.Generator().manual_seed(17)
+    host = [torch.randn(64, 256, generator=g).to(torch.bfloat16).pin_memory() for _ in range(7)]
+    tf = zg.sgd(0.05) if transform == "sgd" else zg.adamw(3e-3)
+    opt = zg.ZeroGrad(manifest, tf, 48, 8, 0.02, 5, "graph-host")
+    cg = opt.capture(params, loss_fn, host[0].to(cuda), slots=slots)
+    state = opt.init(params)
+    pending, snaps = [], []
+    for i, b in enumerate(host):
+        _, state, p = cg.enqueue(state, b)
+        pending.append(p)
+        if i >= 1:
+            pending[i - 1].result()  # the previous generation's metrics, read while this one runs
+        snaps.append({k: v.clone() for k, v in cg.params.items()})  # ordered after this replay
+    pe, se = params, opt.init(params)
+    for i, b in enumerate(host):
+        pe, se, me = opt.step(se, pe, b.to(cuda), loss_fn)
+        assert pending[i].result().mean_loss == me.mean_loss, i
+        for k in pe:
+            assert torch.equal(snaps[i][k], pe[k]), (i, k)
+    assert state.generation == len(host)
+    assert L.load().zg_device_error(1) == 0

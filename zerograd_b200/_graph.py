@@ -13,7 +13,12 @@ not launches:
   are derived from that buffer in the graph (every factor draw, forward and
   replay kernel reads keys from device memory);
 * the batch is copied into the captured batch buffers (from pinned host
-  memory, or from the device);
+  memory, or from the device).  With ``slots=2`` (the default) the
+  generation is captured twice, over two batch buffers that share one graph
+  memory pool, and successive generations alternate between them: the
+  host-to-device copies of generation g+1 (batch, base key, AdamW bias
+  corrections) run on a copy stream while generation g computes, ordered
+  by events after the last replay that read the same slot;
 * the parameters live in captured buffers, updated on the device only when
   the shaping kernel counted no non-finite loss: the entries whose step is
   fused into the replay GEMM are updated in place with that count as the
@@ -65,7 +70,8 @@ class CapturedGeneration:
     def __init__(self, optimizer, params: ParameterTree, loss_fn: Callable, batch: Any, *, state=None,
                  candidate_range: tuple[int, int] | None = None,
                  gather: Callable[[torch.Tensor], torch.Tensor] | None = None,
-                 rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2):
+                 rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2,
+                 slots: int = 2):
         from ._optimizer import ZeroGradState, _device_of, _materialize_tree
         from ._transforms import AdamWState, adamw, sgd
 
@@ -83,14 +89,17 @@ class CapturedGeneration:
         dev = self.device
         if dev.type != "cuda":
             raise L.ZgLibraryError("capture runs on CUDA devices only; there is no CPU fallback")
+        if slots not in (1, 2):
+            raise ValueError("slots must be 1 or 2")
+        self._slots = slots
         self._params = _clone_tree(_materialize_tree(params))
-        self._batch = _clone_tree(batch)
+        self._batches = [_clone_tree(batch) for _ in range(slots)]
         self._loss_fn = loss_fn
         # prefetch_replay: a shard's replay factors drawn on a second stream
         # (a parallel branch of the graph) during its forward; off by default,
         # since the draws and the forward's GEMMs contend for the same SMs
         self._prefetch = prefetch_replay
-        self._base_dev = torch.empty((1, 2), dtype=torch.uint32, device=dev)
+        self._base_dev = torch.empty((slots, 1, 2), dtype=torch.uint32, device=dev)
         self._ids = torch.arange(P, dtype=torch.int32, device=dev)
         g0 = state.generation if state is not None else 0
         opt_state0 = state.opt_state if state is not None else optimizer.init(self._params).opt_state
@@ -99,10 +108,9 @@ class CapturedGeneration:
         if self._adam:
             # the moments in captured buffers; the bias corrections of each
             # step in a device buffer filled before the replay
-            self._bc_dev = torch.zeros(2, dtype=torch.float32, device=dev)
+            self._bc_dev = torch.zeros((slots, 2), dtype=torch.float32, device=dev)
             self._adam_cls = AdamWState
-            opt_state0 = AdamWState(opt_state0.count, _clone_tree(opt_state0.mu), _clone_tree(opt_state0.nu),
-                                    bias_corrections=self._bc_dev)
+            opt_state0 = AdamWState(opt_state0.count, _clone_tree(opt_state0.mu), _clone_tree(opt_state0.nu))
         self._opt_state = opt_state0
 
         # warm-up outside the graph: first-call setup (kernel attributes, the
@@ -111,49 +119,67 @@ class CapturedGeneration:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for i in range(max(1, warmup)):
-                self._set_base(g0 + i)
-                self._set_count(opt_state0)
-                self._generation(g0 + i, opt_state0, copy_back=False)
+                self._set_base(g0 + i, 0)
+                self._set_count(opt_state0, 0)
+                self._generation(g0 + i, self._slot_state(opt_state0, 0), 0, copy_back=False)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
 
-        self._graph = torch.cuda.CUDAGraph()
-        self._set_base(g0)
-        n0 = L.launch_count()
-        with torch.cuda.graph(self._graph):
-            capture_stream = L.stream_ptr(dev).value
-            self._out = self._generation(g0, opt_state0, copy_back=True)
-        torch.cuda.synchronize(dev)
-        optimizer._forget_keys(capture_stream)
+        # one graph per batch slot, all in one memory pool: replays never
+        # overlap (one stream), so their intermediates may share memory
+        pool = torch.cuda.graph_pool_handle()
+        self._graphs, self._outs = [], []
+        for slot in range(slots):
+            graph = torch.cuda.CUDAGraph()
+            self._set_base(g0, slot)
+            n0 = L.launch_count()
+            with torch.cuda.graph(graph, pool=pool):
+                capture_stream = L.stream_ptr(dev).value
+                out = self._generation(g0, self._slot_state(opt_state0, slot), slot, copy_back=True)
+            torch.cuda.synchronize(dev)
+            optimizer._forget_keys(capture_stream)
+            self._graphs.append(graph)
+            self._outs.append(out)
         #: this library's kernels in one replay of the graph
         self.kernels_per_generation = L.launch_count() - n0
+        self._copy_stream = torch.cuda.Stream(dev)
+        self._ready = [torch.cuda.Event() for _ in range(slots)]  # slot's inputs copied
+        self._free = [torch.cuda.Event() for _ in range(slots)]  # slot's last replay done
+        self._next = 0
 
-    def _set_count(self, opt_state) -> None:
-        """AdamW: the bias corrections of step count + 1 into the device buffer."""
+    def _slot_state(self, opt_state, slot: int):
+        """The optimizer state a slot's graph reads: AdamW's bias corrections
+        from that slot's device buffer."""
+        if not self._adam:
+            return opt_state
+        return self._adam_cls(opt_state.count, opt_state.mu, opt_state.nu, bias_corrections=self._bc_dev[slot])
+
+    def _set_count(self, opt_state, slot: int) -> None:
+        """AdamW: the bias corrections of step count + 1 into the slot's device buffer."""
         if not self._adam:
             return
         t = self._opt.transform
         host = torch.empty(2, dtype=torch.float32, pin_memory=True)
         L.call("zg_adam_bias_corrections", int(opt_state.count) + 1, float(t.b1), float(t.b2), L.ptr(host))
-        self._bc_dev.copy_(host, non_blocking=True)
+        self._bc_dev[slot].copy_(host, non_blocking=True)
 
-    def _set_base(self, generation: int) -> None:
+    def _set_base(self, generation: int, slot: int) -> None:
         # a fresh pinned buffer per call: the pinned allocator reuses it only
         # after this copy has run, so queued generations never race on it
         host = torch.empty((1, 2), dtype=torch.uint32, pin_memory=True)
         host.copy_(self._opt.base_key(generation).view(1, 2))
-        self._base_dev.copy_(host, non_blocking=True)
+        self._base_dev[slot].copy_(host, non_blocking=True)
 
-    def _generation(self, generation: int, opt_state, copy_back: bool):
-        """The launch sequence of one generation, keys read from the device
-        base-key buffer."""
+    def _generation(self, generation: int, opt_state, slot: int, copy_back: bool):
+        """The launch sequence of one generation over batch slot `slot`, keys
+        read from the slot's device base-key buffer."""
         opt, dev, (start, count) = self._opt, self.device, self._range
         P = opt.population_size
-        cks_all = _ops.launch_fold_in(self._base_dev, self._ids)
+        cks_all = _ops.launch_fold_in(self._base_dev[slot], self._ids)
         opt._seed_keys(generation, 0, P, dev, cks_all)
         if (start, count) != (0, P):
             opt._seed_keys(generation, start, count, dev, cks_all[start:start + count])
-        losses = opt._evaluate_shard(self._params, generation, self._loss_fn, self._batch,
+        losses = opt._evaluate_shard(self._params, generation, self._loss_fn, self._batches[slot],
                                      range(start, start + count), rng=self._rng,
                                      prefetch_replay=self._prefetch)
         if self._gather is not None:
@@ -185,11 +211,15 @@ class CapturedGeneration:
         for path, t in _leaves(self._params):
             t.copy_(tree_get(params, path), non_blocking=True)
 
-    def _queue(self, state, batch) -> None:
+    def _queue(self, state, batch) -> int:
+        """Copy one generation's inputs into the next slot and replay that
+        slot's graph; returns the slot."""
         if not isinstance(state, self._state_cls):
             raise TypeError("state must be a ZeroGradState")
+        slot = self._next
+        pairs = []
         if batch is not None:
-            dst = pytree.tree_leaves(self._batch)
+            dst = pytree.tree_leaves(self._batches[slot])
             src = pytree.tree_leaves(batch)
             if len(dst) != len(src):
                 raise ValueError("batch does not match the captured batch's structure")
@@ -197,23 +227,40 @@ class CapturedGeneration:
                 if isinstance(d, torch.Tensor):
                     if tuple(s.shape) != tuple(d.shape):
                         raise ValueError(f"batch leaf of shape {tuple(s.shape)}; captured {tuple(d.shape)}")
+                    pairs.append((d, s))
+        self._next = (slot + 1) % self._slots
+        cur = torch.cuda.current_stream(self.device)
+        cs = self._copy_stream
+        # host-side inputs on the copy stream, once the slot's last replay is
+        # done; it overlaps the generation queued before this one
+        with torch.cuda.stream(cs):
+            cs.wait_event(self._free[slot])
+            for d, s in pairs:
+                if not s.is_cuda:
                     d.copy_(s, non_blocking=True)
-        self._set_base(state.generation)
-        self._set_count(state.opt_state)
-        self._graph.replay()
+            self._set_base(state.generation, slot)
+            self._set_count(state.opt_state, slot)
+            self._ready[slot].record(cs)
+        cur.wait_event(self._ready[slot])
+        for d, s in pairs:
+            if s.is_cuda:  # produced on the current stream: copied there
+                d.copy_(s, non_blocking=True)
+        self._graphs[slot].replay()
+        self._free[slot].record(cur)
+        return slot
 
     @property
     def opt_state(self):
         """The captured optimizer state (AdamW's moments live here)."""
         return self._opt_state
 
-    def _next_state(self, state):
+    def _next_state(self, state, slot: int):
         """The state after one replay: the generation and the step count
         advance; AdamW's moments are the captured buffers."""
         if self._adam:
             nxt = self._adam_cls(int(state.opt_state.count) + 1, self._opt_state.mu, self._opt_state.nu)
         else:
-            nxt = _advance_state(state.opt_state, self._out[1])
+            nxt = _advance_state(state.opt_state, self._outs[slot][1])
         return self._state_cls(state.generation + 1, nxt)
 
     def step(self, state, batch: Any = None):
@@ -221,9 +268,9 @@ class CapturedGeneration:
         replay the graph and read its metrics.  Returns (params, new state,
         metrics) like ``ZeroGrad.step``; raises ValueError, with the
         parameters unchanged, when a loss is not finite."""
-        self._queue(state, batch)
-        m = self._opt._metrics(state.generation, self._out[2])
-        return self._params, self._next_state(state), m
+        slot = self._queue(state, batch)
+        m = self._opt._metrics(state.generation, self._outs[slot][2])
+        return self._params, self._next_state(state, slot), m
 
     def enqueue(self, state, batch: Any = None):
         """Queue one generation without waiting for it.  Returns (params, new
@@ -231,12 +278,13 @@ class CapturedGeneration:
         or raises ValueError if that generation's losses were not all finite
         (its update was then not applied; generations queued after it start
         from the unchanged parameters)."""
-        self._queue(state, batch)
+        slot = self._queue(state, batch)
         host = torch.empty(4, dtype=torch.float32, pin_memory=True)
-        host.copy_(self._out[2], non_blocking=True)
+        host.copy_(self._outs[slot][2], non_blocking=True)
         done = torch.cuda.Event()
         done.record(torch.cuda.current_stream(self.device))
-        return self._params, self._next_state(state), PendingGeneration(self._opt, state.generation, host, done)
+        return self._params, self._next_state(state, slot), PendingGeneration(self._opt, state.generation, host,
+                                                                               done)
 
 
 class PendingGeneration:

@@ -319,14 +319,16 @@ class ZeroGrad:
         return params, state, metrics
 
     def capture(self, params: ParameterTree, loss_fn: LossFn, batch: Any, *, state: ZeroGradState | None = None,
-                rng: torch.Tensor | None = None, warmup: int = 2):
+                rng: torch.Tensor | None = None, warmup: int = 2, slots: int = 2):
         """The generation ``step`` runs, captured as a CUDA graph
         (:class:`CapturedGeneration`): replaying it costs one graph launch
         instead of the per-op host work.  `params` and `batch` give the
-        shapes and the initial values; the graph keeps its own copies."""
+        shapes and the initial values; the graph keeps its own copies.
+        `slots` = 2 captures it over two batch buffers, so the next
+        generation's host-to-device copies overlap the current one."""
         from ._graph import CapturedGeneration
 
-        return CapturedGeneration(self, params, loss_fn, batch, state=state, rng=rng, warmup=warmup)
+        return CapturedGeneration(self, params, loss_fn, batch, state=state, rng=rng, warmup=warmup, slots=slots)
 
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, loss_fn: LossFn, *,
              rng: torch.Tensor | None = None):
