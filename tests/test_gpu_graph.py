@@ -185,3 +185,54 @@ def test_enqueued_host_batches_match_eager(cuda, slots, transform):
             assert torch.equal(snaps[i][k], pe[k]), (i, k)
     assert state.generation == len(host)
     assert L.load().zg_device_error(1) == 0
+
+
+def test_draw_ahead_out_of_sequence_generations(cuda):
+    """Factors drawn one generation ahead are used only for the generation
+    they were drawn for: generations called out of sequence (a restart, a
+    jump back) draw their own first; every step matches the eager one."""
+    manifest, params, batches, loss_fn = _small(cuda)
+    opt = zg.ZeroGrad(manifest, zg.sgd(0.05), 48, 8, 0.02, 6, "graph-ahead")
+    cg = opt.capture(params, loss_fn, batches[0])
+    assert cg._entries, "the bf16 MATRIX leaf is drawn ahead"
+    pe = params
+    sc = opt.init(params)
+    for gen in (0, 1, 2, 7, 8, 3, 3, 9):
+        b = batches[gen % 4]
+        pe, se, me = opt.step(zg.ZeroGradState(gen, sc.opt_state), pe, b, loss_fn)
+        pc, sc, mc = cg.step(zg.ZeroGradState(gen, sc.opt_state), b)
+        assert mc.mean_loss == me.mean_loss, gen
+        for k in pe:
+            assert torch.equal(pc[k], pe[k]), (gen, k)
+    assert L.load().zg_device_error(1) == 0
+
+
+def test_draw_ahead_tied_table(cuda):
+    """A tied embedding TABLE (lookup + tied logits) and a MATRIX leaf, both
+    drawn ahead, against the eager steps."""
+    V, C, B, T = 512, 128, 2, 16
+    manifest = zg.Manifest(1, (zg.ManifestEntry(("emb",), zg.ParameterLayout.TABLE, "emb"),
+                               zg.ManifestEntry(("w",), zg.ParameterLayout.MATRIX, "w")))
+    g = torch.Generator().manual_seed(9)
+    params = {"emb": (torch.randn(V, C, generator=g) * 0.05).to(torch.bfloat16).to(cuda),
+              "w": (torch.randn(C, C, generator=g) * 0.05).to(torch.bfloat16).to(cuda)}
+    toks = [torch.randint(0, V, (B, T), generator=g).to(cuda) for _ in range(3)]
+
+    def loss_fn(p, ctx, batch, rng):
+        h = ctx.table_lookup(p, ("emb",), batch)
+        h = ctx.linear(p, ("w",), h)
+        logits = ctx.tied_logits(p, ("emb",), h)
+        return (logits.float() ** 2).mean(), None
+
+    opt = zg.ZeroGrad(manifest, zg.sgd(0.02), 32, 8, 0.02, 8, "graph-table")
+    cg = opt.capture(params, loss_fn, toks[0])
+    assert len(cg._entries) == 2
+    pe, se = params, opt.init(params)
+    sc = opt.init(params)
+    for i in range(3):
+        pe, se, me = opt.step(se, pe, toks[i], loss_fn)
+        pc, sc, mc = cg.step(sc, toks[i])
+        assert mc.mean_loss == me.mean_loss, i
+        for k in pe:
+            assert torch.equal(pc[k], pe[k]), (i, k)
+    assert L.load().zg_device_error(1) == 0

@@ -222,7 +222,8 @@ class DistributedZeroGrad:
 
     # -- one generation -----------------------------------------------------
     def capture(self, params: ParameterTree, batch: Any, *, state: ZeroGradState | None = None,
-                rng: torch.Tensor | None = None, warmup: int = 2, slots: int = 2):
+                rng: torch.Tensor | None = None, warmup: int = 2, slots: int = 2,
+                draw_ahead: bool = True):
         """The generation ``step`` runs in process-group mode, captured as a
         CUDA graph: this process's shard of the forward, the fitness
         all-gather (NCCL, in the graph) and the replicated completion.  Every
@@ -239,7 +240,7 @@ class DistributedZeroGrad:
         return CapturedGeneration(self._optimizer, _to_device(_materialize_tree(params), self._devices[0]),
                                   self._loss_fn, batch, state=state, candidate_range=(a, b - a),
                                   gather=lambda local: allgather_losses(local, sizes, group), rng=rng,
-                                  warmup=warmup, slots=slots)
+                                  warmup=warmup, slots=slots, draw_ahead=draw_ahead)
 
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, *, rng: torch.Tensor | None = None):
         if rng is None:

@@ -19,6 +19,17 @@ not launches:
   host-to-device copies of generation g+1 (batch, base key, AdamW bias
   corrections) run on a copy stream while generation g computes, ordered
   by events after the last replay that read the same slot;
+* with two slots, generation g+1's operand factors (every bf16
+  MATRIX/TABLE leaf, the whole population) are drawn on a second stream
+  into the other slot's factor buffers while generation g's graph runs:
+  those integer-bound draws then share the SMs with g's tensor-core and
+  HBM-bound kernels instead of running ahead of g+1's forward.  They are
+  launched just before g's graph and joined into the caller's stream just
+  after it, so a generation's work includes its draws of the next one.
+  Generation g+1's forward and replay read them (they are a function of
+  g+1's keys alone).  When a call's generation is not the one drawn ahead
+  (the first call, or generations out of sequence), its factors are drawn
+  before its replay;
 * the parameters live in captured buffers, updated on the device only when
   the shaping kernel counted no non-finite loss: the entries whose step is
   fused into the replay GEMM are updated in place with that count as the
@@ -71,7 +82,7 @@ class CapturedGeneration:
                  candidate_range: tuple[int, int] | None = None,
                  gather: Callable[[torch.Tensor], torch.Tensor] | None = None,
                  rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2,
-                 slots: int = 2):
+                 slots: int = 2, draw_ahead: bool = True):
         from ._optimizer import ZeroGradState, _device_of, _materialize_tree
         from ._transforms import AdamWState, adamw, sgd
 
@@ -99,7 +110,10 @@ class CapturedGeneration:
         # (a parallel branch of the graph) during its forward; off by default,
         # since the draws and the forward's GEMMs contend for the same SMs
         self._prefetch = prefetch_replay
-        self._base_dev = torch.empty((slots, 1, 2), dtype=torch.uint32, device=dev)
+        # a slot's per-generation inputs, one row of 8 words copied in by one
+        # host-to-device copy: the base key (words 0-1), the next
+        # generation's base key (2-3), AdamW's bias corrections (float32, 4-5)
+        self._inputs = torch.zeros((slots, 8), dtype=torch.uint32, device=dev)
         self._ids = torch.arange(P, dtype=torch.int32, device=dev)
         g0 = state.generation if state is not None else 0
         opt_state0 = state.opt_state if state is not None else optimizer.init(self._params).opt_state
@@ -107,8 +121,7 @@ class CapturedGeneration:
         self._adam = isinstance(optimizer.transform, adamw)
         if self._adam:
             # the moments in captured buffers; the bias corrections of each
-            # step in a device buffer filled before the replay
-            self._bc_dev = torch.zeros((slots, 2), dtype=torch.float32, device=dev)
+            # step in the slot's inputs, filled before the replay
             self._adam_cls = AdamWState
             opt_state0 = AdamWState(opt_state0.count, _clone_tree(opt_state0.mu), _clone_tree(opt_state0.nu))
         self._opt_state = opt_state0
@@ -119,63 +132,111 @@ class CapturedGeneration:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for i in range(max(1, warmup)):
-                self._set_base(g0 + i, 0)
-                self._set_count(opt_state0, 0)
+                self._set_inputs(g0 + i, opt_state0, 0, False)
                 self._generation(g0 + i, self._slot_state(opt_state0, 0), 0, copy_back=False)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
+
+        # factors drawn one generation ahead (two slots): per slot, one
+        # (A_op, B_op) buffer pair per bf16 MATRIX/TABLE leaf
+        self._entries = []
+        if slots == 2 and draw_ahead and torch.cuda.get_device_capability(dev) == (10, 0):
+            self._entries = optimizer._factor_entries(self._params)
+            need = sum((rows + cols) * P * rank * 2 for _, _, rows, cols, rank in self._entries)
+            if need > _ops.CACHE._budget(dev):
+                self._entries = []  # over the factor-cache budget: drawn in the generation, as eagerly
+        self._fbuf = [[(torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev),
+                        torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev))
+                       for _, _, rows, cols, rank in self._entries] for _ in range(slots)]
+        self._draw_stream = torch.cuda.Stream(dev)
+        self._drawn: list = [None] * slots  # generation whose factors each slot's buffers hold
+        self._draw_done = [torch.cuda.Event() for _ in range(slots)]  # draws into the slot's buffers done
 
         # one graph per batch slot, all in one memory pool: replays never
         # overlap (one stream), so their intermediates may share memory
         pool = torch.cuda.graph_pool_handle()
         self._graphs, self._outs = [], []
+        base0 = tuple(int(v) for v in optimizer.base_key(g0))
         for slot in range(slots):
             graph = torch.cuda.CUDAGraph()
-            self._set_base(g0, slot)
+            self._set_inputs(g0, opt_state0, slot, False)
+            for e, bufs in zip(self._entries, self._fbuf[slot]):
+                # the forward and the replay read the slot's factor buffers
+                _ops.CACHE.put((base0, 0, P) + e, bufs, dev)
             n0 = L.launch_count()
             with torch.cuda.graph(graph, pool=pool):
                 capture_stream = L.stream_ptr(dev).value
                 out = self._generation(g0, self._slot_state(opt_state0, slot), slot, copy_back=True)
             torch.cuda.synchronize(dev)
             optimizer._forget_keys(capture_stream)
+            _ops.CACHE.drop_generation(base0)
             self._graphs.append(graph)
             self._outs.append(out)
-        #: this library's kernels in one replay of the graph
+        #: this library's kernels in one generation: the graph's, and the draws
+        #: of the next generation's factors
         self.kernels_per_generation = L.launch_count() - n0
+        self._draw_graphs = []
+        if self._entries:
+            # g0's factors into slot 0 (the first call's), eagerly; then per
+            # slot a graph of the draws from the slot's next base key into the
+            # other slot's buffers (each in its own memory pool: it runs beside
+            # the generation's graph)
+            self._draw(self._opt.base_key(g0), self._fbuf[0])
+            self._drawn[0] = g0
+            torch.cuda.synchronize(dev)
+            for slot in range(slots):
+                dg = torch.cuda.CUDAGraph()
+                n0 = L.launch_count()
+                with torch.cuda.graph(dg):
+                    self._draw(self._inputs[slot, 2:4], self._fbuf[1 - slot])
+                self._draw_graphs.append(dg)
+            self.kernels_per_generation += L.launch_count() - n0
+            torch.cuda.synchronize(dev)
         self._copy_stream = torch.cuda.Stream(dev)
         self._ready = [torch.cuda.Event() for _ in range(slots)]  # slot's inputs copied
         self._free = [torch.cuda.Event() for _ in range(slots)]  # slot's last replay done
         self._next = 0
 
+    def _draw(self, base: torch.Tensor, bufs) -> None:
+        """Every entry's operand factors, for the whole population of the
+        generation with base key `base`, into `bufs` (current stream)."""
+        cks = _ops.launch_fold_in(base, self._ids)
+        P = self._opt.population_size
+        for (group, layout, rows, cols, rank), (A, B) in zip(self._entries, bufs):
+            L.call("zg_factor_operands", L.ptr(cks), group, P, layout, rows, cols, rank, L.ZG_BF16, L.ptr(A),
+                   L.ptr(B), L.stream_ptr(self.device))
+
     def _slot_state(self, opt_state, slot: int):
         """The optimizer state a slot's graph reads: AdamW's bias corrections
-        from that slot's device buffer."""
+        from that slot's inputs."""
         if not self._adam:
             return opt_state
-        return self._adam_cls(opt_state.count, opt_state.mu, opt_state.nu, bias_corrections=self._bc_dev[slot])
+        bc = self._inputs[slot, 4:6].view(torch.float32)
+        return self._adam_cls(opt_state.count, opt_state.mu, opt_state.nu, bias_corrections=bc)
 
-    def _set_count(self, opt_state, slot: int) -> None:
-        """AdamW: the bias corrections of step count + 1 into the slot's device buffer."""
-        if not self._adam:
-            return
-        t = self._opt.transform
-        host = torch.empty(2, dtype=torch.float32, pin_memory=True)
-        L.call("zg_adam_bias_corrections", int(opt_state.count) + 1, float(t.b1), float(t.b2), L.ptr(host))
-        self._bc_dev[slot].copy_(host, non_blocking=True)
-
-    def _set_base(self, generation: int, slot: int) -> None:
+    def _set_inputs(self, generation: int, opt_state, slot: int, ahead: bool) -> None:
+        """The slot's inputs for `generation` (current stream): its base key,
+        the next generation's when drawing ahead, AdamW's bias corrections of
+        step count + 1."""
         # a fresh pinned buffer per call: the pinned allocator reuses it only
         # after this copy has run, so queued generations never race on it
-        host = torch.empty((1, 2), dtype=torch.uint32, pin_memory=True)
-        host.copy_(self._opt.base_key(generation).view(1, 2))
-        self._base_dev[slot].copy_(host, non_blocking=True)
+        host = torch.zeros(8, dtype=torch.uint32, pin_memory=True)
+        h = host.numpy()
+        h[0:2] = self._opt.base_key(generation).numpy()
+        if ahead:
+            h[2:4] = self._opt.base_key(generation + 1).numpy()
+        if self._adam:
+            t = self._opt.transform
+            L.call("zg_adam_bias_corrections", int(opt_state.count) + 1, float(t.b1), float(t.b2),
+                   host.data_ptr() + 16)
+        self._inputs[slot].copy_(host, non_blocking=True)
 
     def _generation(self, generation: int, opt_state, slot: int, copy_back: bool):
         """The launch sequence of one generation over batch slot `slot`, keys
         read from the slot's device base-key buffer."""
         opt, dev, (start, count) = self._opt, self.device, self._range
         P = opt.population_size
-        cks_all = _ops.launch_fold_in(self._base_dev[slot], self._ids)
+        cks_all = _ops.launch_fold_in(self._inputs[slot, 0:2], self._ids)
         opt._seed_keys(generation, 0, P, dev, cks_all)
         if (start, count) != (0, P):
             opt._seed_keys(generation, start, count, dev, cks_all[start:start + count])
@@ -238,15 +299,30 @@ class CapturedGeneration:
             for d, s in pairs:
                 if not s.is_cuda:
                     d.copy_(s, non_blocking=True)
-            self._set_base(state.generation, slot)
-            self._set_count(state.opt_state, slot)
+            self._set_inputs(state.generation, state.opt_state, slot, bool(self._entries))
             self._ready[slot].record(cs)
         cur.wait_event(self._ready[slot])
         for d, s in pairs:
             if s.is_cuda:  # produced on the current stream: copied there
                 d.copy_(s, non_blocking=True)
+        if self._entries and self._drawn[slot] != state.generation:
+            # not drawn ahead with the previous generation: draw this one's now
+            self._draw(self._opt.base_key(state.generation), self._fbuf[slot])
+        if self._entries:
+            # the next generation's factors, beside this one: the other slot's
+            # buffers were last read by the replay before this one (done on
+            # this stream), and its base key is in with this slot's inputs
+            ds = self._draw_stream
+            ds.wait_stream(cur)
+            with torch.cuda.stream(ds):
+                self._draw_graphs[slot].replay()
+                self._draw_done[1 - slot].record(ds)
         self._graphs[slot].replay()
-        self._free[slot].record(cur)
+        if self._entries:
+            cur.wait_event(self._draw_done[1 - slot])
+            self._drawn[slot] = state.generation
+            self._drawn[1 - slot] = state.generation + 1
+        self._free[slot].record(cur)  # the slot's inputs (batch, keys) are read by now
         return slot
 
     @property

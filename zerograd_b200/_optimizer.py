@@ -217,15 +217,23 @@ class ZeroGrad:
         with _ops.generation_scope(base_words, id_range[0], id_range[1], cks):
             return torch.func.vmap(evaluate_candidate)(cks, rngs)
 
-    def _prefetch_replay(self, params, generation, base_words, device) -> None:
+    def _factor_entries(self, params) -> list:
+        """(group, layout, rows, cols, rank) of every bf16 MATRIX/TABLE leaf:
+        the operand factors the replay reads, in the factor cache's key terms."""
         entries = []
         for entry in self._manifest.entries:
             if entry.layout is ParameterLayout.VECTOR:
                 continue
             p = self._manifest.resolve(params, entry.path)
             if isinstance(p, torch.Tensor) and p.dtype == torch.bfloat16 and p.ndim == 2:
-                entries.append((self._manifest.group_index(entry.group), LAYOUT_CODE[entry.layout],
-                                int(p.shape[0]), int(p.shape[1]), self._rank))
+                e = (self._manifest.group_index(entry.group), LAYOUT_CODE[entry.layout], int(p.shape[0]),
+                     int(p.shape[1]), self._rank)
+                if e not in entries:
+                    entries.append(e)
+        return entries
+
+    def _prefetch_replay(self, params, generation, base_words, device) -> None:
+        entries = self._factor_entries(params)
         if not entries or torch.cuda.get_device_capability(device) != (10, 0):
             return
         cks = self._candidate_keys_range(generation, 0, self._population_size, device)
@@ -319,16 +327,19 @@ class ZeroGrad:
         return params, state, metrics
 
     def capture(self, params: ParameterTree, loss_fn: LossFn, batch: Any, *, state: ZeroGradState | None = None,
-                rng: torch.Tensor | None = None, warmup: int = 2, slots: int = 2):
+                rng: torch.Tensor | None = None, warmup: int = 2, slots: int = 2,
+                draw_ahead: bool = True):
         """The generation ``step`` runs, captured as a CUDA graph
         (:class:`CapturedGeneration`): replaying it costs one graph launch
         instead of the per-op host work.  `params` and `batch` give the
         shapes and the initial values; the graph keeps its own copies.
         `slots` = 2 captures it over two batch buffers, so the next
-        generation's host-to-device copies overlap the current one."""
+        generation's host-to-device copies overlap the current one; with
+        `draw_ahead` each generation also draws the next one's factors."""
         from ._graph import CapturedGeneration
 
-        return CapturedGeneration(self, params, loss_fn, batch, state=state, rng=rng, warmup=warmup, slots=slots)
+        return CapturedGeneration(self, params, loss_fn, batch, state=state, rng=rng, warmup=warmup, slots=slots,
+                                  draw_ahead=draw_ahead)
 
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, loss_fn: LossFn, *,
              rng: torch.Tensor | None = None):
