@@ -172,15 +172,17 @@ def test_replay_factors_entry_matches_replay(cuda, oracle):
     assert torch.equal(direct, cached)
 
 
-@pytest.mark.parametrize("rows,cols,P", [(1024, 1024, 64),     # 32 tiles: fewer than one wave
-                                         (6400, 1024, 32),     # 200 tiles: one wave and a partial one
-                                         (4096, 4096, 256),    # 512 tiles: the bench replay
-                                         (5504, 1792, 64),     # 301 tiles, ragged rows
-                                         (1280, 768, 40)])     # 30 tiles, 320-deep contraction
-def test_replay_factors_matches_fp32(cuda, rows, cols, P):
+@pytest.mark.parametrize("rows,cols,P,r", [(1024, 1024, 64, 8),     # 32 tiles: fewer than one wave
+                                           (6400, 1024, 32, 8),     # 200 tiles: one wave and a partial one
+                                           (4096, 4096, 256, 8),    # 512 tiles: the bench replay
+                                           (5504, 1792, 64, 8),     # 301 tiles, ragged rows
+                                           (1280, 768, 40, 8),      # 30 tiles, 320-deep contraction
+                                           (4096, 2048, 128, 4),    # rank 4: two weights per 8 columns
+                                           (4352, 2048, 100, 16)])  # rank 16, 1600-deep contraction
+def test_replay_factors_matches_fp32(cuda, rows, cols, P, r):
     """The replay GEMM over P*r matches a float32 matmul of the same weighted
-    bf16 operands, and is identical from call to call."""
-    r = 8
+    bf16 operands, is identical from call to call, and is bit for bit the
+    plain GEMM of the operand weighted and rounded to bf16 on the host."""
     q = P * r
     g = torch.Generator().manual_seed(rows + cols + P)
     A = torch.randn(rows, q, generator=g).to(torch.bfloat16).to(cuda)
@@ -198,7 +200,9 @@ def test_replay_factors_matches_fp32(cuda, rows, cols, P):
     b = run()
     assert L.load().zg_device_error(1) == 0
     assert torch.equal(a, b)
-    Aw = (A.float() * w.repeat_interleave(r)[None, :]).to(torch.bfloat16).float()
-    ref = 0.5 * (Aw @ B.float().t())
+    Aw16 = (A.float() * w.repeat_interleave(r)[None, :]).to(torch.bfloat16)
+    plain = _gemm(Aw16, B, False, rows, cols, q, alpha=0.5)
+    assert torch.equal(a, plain)
+    ref = 0.5 * (Aw16.float() @ B.float().t())
     err = (a - ref).abs().max().item()
     assert err <= 1e-3 * ref.abs().max().item(), err

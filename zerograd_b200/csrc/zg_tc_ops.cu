@@ -221,7 +221,7 @@ __global__ void fill_operand_kernel(const uint32_t* __restrict__ keys, int group
 // Block tile 64 m x 128 n, 256 threads, each 4 m x 8 n; candidates split
 // over gridDim.z; q-chunks of QC columns staged in shared memory.
 // ---------------------------------------------------------------------------
-constexpr int EX_BM = 64, EX_BN = 128, EX_QC = 64;
+constexpr int EX_BM = 64, EX_BN = 128;
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
