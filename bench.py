@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    # with more than one GPU: every rank replays the whole update (the
+    # reference's protocol) or its block of W's rows, then W is all-gathered
+    ap.add_argument("--replay", choices=["replicated", "sharded"], default="replicated")
     return ap.parse_args()
 
 
@@ -132,7 +135,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # algorithmic work per launch of each kernel (this workload)
 # ---------------------------------------------------------------------------
-def kernel_work(name: str, P_local: int, world: int = 1):
+def kernel_work(name: str, P_local: int, world: int = 1, row_blocks: int = 1):
     P, r, M, K, N = WL["P"], WL["rank"], WL["M"], WL["K"], WL["N"]
     if name == "factor_fill":
         # bf16 operand bytes written per launch: the forward draws A_op and B_op
@@ -144,8 +147,8 @@ def kernel_work(name: str, P_local: int, world: int = 1):
         return "hbm", sum(fills) / len(fills)
     if name == "lowrank_expand":      # y = xW + s (xA) B : write y bf16, read xW f32, U f32, B bf16
         return "hbm", P_local * M * N * 2 + M * N * 4 + P_local * M * r * 4 + P_local * r * N * 2
-    if name == "replay_gemm":         # [K, P r] x [P r, N]
-        return "tensor", 2.0 * K * N * P * r
+    if name == "replay_gemm":         # [K, P r] x [P r, N] (this rank's block of the K rows)
+        return "tensor", 2.0 * (K // row_blocks) * N * P * r
     if name in ("forward_xw_gemm", "shared_xw"):
         return "tensor", 2.0 * M * K * N
     if name in ("forward_u_gemm", "lowrank_u"):
@@ -499,6 +502,24 @@ def run_ours(args):
         # slower.  Kept as a no-op hook for that alternative.
         return None
 
+    row_shard = zg.RowShard(rank, world) if (world > 1 and args.replay == "sharded") else None
+    row_blocks = world if row_shard is not None else 1
+
+    def replay_update(shaped, cks, W, gen):
+        # replay with the SGD step in the replay GEMM's epilogue (what
+        # ZeroGrad.step runs): the whole of W, or this rank's block of rows
+        # followed by the all-gather of W
+        g = _ops._Generation(bases[gen], 0, P, cks)
+        spec = {"kind": "sgd", "lr": WL["lr"]}
+        if row_shard is not None:
+            blk = K // world
+            W, _, _ = _ops.launch_replay_step(shaped, cks, 0, L.ZG_MATRIX, W, r, spec, gen=g,
+                                              row_range=(rank * blk, (rank + 1) * blk))
+            row_shard.gather(W, rank * blk, (rank + 1) * blk)
+            return W
+        W, _, _ = _ops.launch_replay_step(shaped, cks, 0, L.ZG_MATRIX, W, r, spec, gen=g)
+        return W
+
     def device_step(W, gen):
         # the same sequence ZeroGrad.step runs: forward (factors kept for the
         # generation), fitness exchange, shaping, replay (cached factors when
@@ -509,9 +530,7 @@ def run_ours(args):
             y = _ops.launch_linear(x, W, cks_local, 0, r, sigma, False)
         losses = gather(fitness[a:b])
         shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
-        # replay with the SGD step in the replay GEMM's epilogue (what ZeroGrad.step runs)
-        W, _, _ = _ops.launch_replay_step(shaped, cks, 0, L.ZG_MATRIX, W, r, {"kind": "sgd", "lr": WL["lr"]},
-                                          gen=_ops._Generation(bases[gen], 0, P, cks))
+        W = replay_update(shaped, cks, W, gen)
         _ops.CACHE.drop_generation(bases[gen])
         del y
         return W
@@ -554,7 +573,8 @@ def run_ours(args):
 
     cg = zg.CapturedGeneration(opt, {"w": W0}, fwd_loss, x, state=opt.init({"w": W0}),
                                candidate_range=(a, P_local) if world > 1 else None,
-                               gather=(lambda l: zg.allgather_losses(l, sizes)) if world > 1 else None)
+                               gather=(lambda l: zg.allgather_losses(l, sizes)) if world > 1 else None,
+                               row_shard=row_shard)
     cstate = opt.init({"w": W0})
     pending = []
 
@@ -692,9 +712,7 @@ def run_ours(args):
             y = _ops.launch_linear(xb_all, W, cks_local, 0, r, sigma, True)
         losses = gather(fitness[a:b])
         shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
-        # replay with the SGD step in the replay GEMM's epilogue (what ZeroGrad.step runs)
-        W, _, _ = _ops.launch_replay_step(shaped, cks, 0, L.ZG_MATRIX, W, r, {"kind": "sgd", "lr": WL["lr"]},
-                                          gen=_ops._Generation(bases[gen], 0, P, cks))
+        W = replay_update(shaped, cks, W, gen)
         _ops.CACHE.drop_generation(bases[gen])
         del y
         return W
@@ -723,12 +741,12 @@ def run_ours(args):
     eager_dev_value = P * args.steps / (eager_dev_ms / 1e3)
     if rank == 0:
         pk = peaks()
-        known = {k: v for k, v in kernels.items() if kernel_work(k, P_local, world)[0] is not None}
+        known = {k: v for k, v in kernels.items() if kernel_work(k, P_local, world, row_blocks)[0] is not None}
         top = max(known.items(), key=lambda kv: kv[1][1]) if known else None
         roof = None
         if top:
             name, (n, tot) = top
-            bound, work = kernel_work(name, P_local, world)
+            bound, work = kernel_work(name, P_local, world, row_blocks)
             per = tot / n / 1e3
             if bound == "hbm":
                 ach, peak, unit = work / per / 1e9, pk["hbm_gbs"], "GB/s"
@@ -747,8 +765,11 @@ def run_ours(args):
             "eager_launch_value": {"value": eager_dev_value, "ms_per_step": eager_dev_ms / args.steps,
                                    "what": "the same kernels issued one by one from Python, fitness N(0,1)"},
             "config": {"workload": WORKLOAD_NAME, "population": P, "rank": r, "batch": M, "d_in": K, "d_out": N,
-                       "parallelism": f"population shards x{world}, fitness allgather" if world > 1 else "1 GPU",
-                       "l2": "flushed between steps (256 MiB write outside the timed events)"},
+                       "parallelism": (f"population shards x{world}, fitness allgather, "
+                                       + ("row-sharded update + W allgather" if row_shard is not None
+                                          else "replicated update")) if world > 1 else "1 GPU",
+                       "l2": "flushed between steps (256 MiB write outside the timed events)",
+                       "update": ("row-sharded" if row_shard is not None else "replicated") if world > 1 else "whole"},
             "roofline": roof,
             "kernels_ms_per_step": {k: v[1] / args.steps for k, v in sorted(kernels.items())},
             "profiled_ms_per_step": prof_ms / args.steps,

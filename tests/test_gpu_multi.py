@@ -142,3 +142,65 @@ def test_captured_process_group_generation():
     assert same0 and same1
     for k in p0:
         assert torch.equal(p0[k], p1[k]), k
+
+
+def _worker_row_sharded(rank, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import zerograd_b200 as zg
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        opt0, params0, x, loss_fn = _problem(dev)
+        opt = zg.ZeroGrad(opt0.manifest, zg.sgd(0.05), 48, 8, 0.02, 0, "multi-rows")
+        rep = zg.DistributedZeroGrad(opt, None, loss_fn)
+        sh = zg.DistributedZeroGrad(opt, None, loss_fn, replay="sharded")
+        cg = sh.capture(params0, x)
+        pr, sr = params0, opt.init(params0)
+        ps, ss = params0, opt.init(params0)
+        sc = opt.init(params0)
+        same_graph = True
+        for g in range(3):
+            xg = x * (1.0 + 0.25 * g)
+            pr, sr, mr = rep.step(sr, pr, xg)
+            ps, ss, ms = sh.step(ss, ps, xg)
+            pc, sc, mc = cg.step(sc, xg)
+            same_graph = same_graph and all(torch.equal(pc[k], ps[k]) for k in ps) and mc.mean_loss == ms.mean_loss
+        q.put((rank, same_graph, {k: v.float().cpu() for k, v in ps.items()},
+               {k: v.float().cpu() for k, v in pr.items()}))
+        del cg  # the graph holds NCCL work: released before the process group
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_row_sharded_update_matches_replicated():
+    """Row-sharded update (each rank replays and updates its half of W's
+    rows, then the halves are all-gathered): every rank ends with the same
+    bits, the captured generation gives the eager step's bits, and the
+    result equals the replicated update within float tolerance (the GEMM
+    tiles of a half differ from the whole one's, so the sums round
+    differently)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_row_sharded, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=300) for _ in procs], key=lambda t: t[0])
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    (_, g0, s0, r0), (_, g1, s1, r1) = out
+    assert g0 and g1
+    for k in s0:
+        assert torch.equal(s0[k], s1[k]), k
+        torch.testing.assert_close(s0[k], r0[k], rtol=1e-2, atol=1e-2)

@@ -93,6 +93,31 @@ def allgather_losses(local: torch.Tensor, sizes: list[int], group=None) -> torch
     return torch.cat([gathered[r, : sizes[r]] for r in range(world)])
 
 
+@dataclass(frozen=True)
+class RowShard:
+    """The row-sharded update (an option beside the reference's replicated
+    replay): after the fitness all-gather, rank ``rank`` of ``world``
+    replays and updates rows [rank*R/world, (rank+1)*R/world) of each SGD
+    leaf, and ``gather`` all-gathers the row blocks in place, so every
+    rank holds the same parameters.  Each rank does 1/world of the replay
+    GEMM, its weighting pass and its update; the parameters cross NVLink
+    once per generation.  The blocks are computed by the same kernels as the
+    whole replay, on fewer rows; the GEMM's tile schedule differs, so
+    results agree with the replicated update to float32 rounding, not bit
+    for bit, while every rank ends bit-identical to every other."""
+
+    rank: int
+    world: int
+    group: Any = None
+
+    def gather(self, t: torch.Tensor, r0: int, r1: int) -> None:
+        """All-gather the row blocks of `t` ([rows, ...], contiguous; this
+        rank's block is rows r0..r1) in place."""
+        flat = t.view(-1)
+        per_row = flat.numel() // t.shape[0]
+        dist.all_gather_into_tensor(flat, flat[r0 * per_row:r1 * per_row], group=self.group)
+
+
 class DeviceShard:
     """Evaluates a population shard on one device (``_distributed.py:88-139``)."""
 
@@ -153,11 +178,16 @@ class DistributedZeroGrad:
     """Multi-device coordinator with weighted partitioning (``_distributed.py:142-366``)."""
 
     def __init__(self, optimizer: ZeroGrad, devices: list | None, loss_fn: LossFn, weights: list[float] | None = None,
-                 coordinator_device=None, process_group=None) -> None:
+                 coordinator_device=None, process_group=None, replay: str = "replicated") -> None:
         self._optimizer = optimizer
         self._loss_fn = loss_fn
         self._group = process_group
         self._pg_mode = devices is None
+        if replay not in ("replicated", "sharded"):
+            raise ValueError("replay must be 'replicated' or 'sharded'")
+        if replay == "sharded" and not self._pg_mode:
+            raise ValueError("the row-sharded update is for process-group mode (one process per GPU)")
+        self._replay = replay
         if self._pg_mode:
             if not dist.is_initialized():
                 raise ValueError("devices=None requires an initialised torch.distributed process group")
@@ -184,6 +214,7 @@ class DistributedZeroGrad:
                             for i, d in enumerate(self._devices)]
         self._partition_sizes = compute_partition_sizes(optimizer.population_size, self._weights)
         self._apply_partition()
+        self._row_shard = RowShard(self._rank, n, process_group) if replay == "sharded" else None
         self._executor = None if self._pg_mode else ThreadPoolExecutor(max_workers=n)
         self._closed = False
 
@@ -226,7 +257,8 @@ class DistributedZeroGrad:
                 draw_ahead: bool = True):
         """The generation ``step`` runs in process-group mode, captured as a
         CUDA graph: this process's shard of the forward, the fitness
-        all-gather (NCCL, in the graph) and the replicated completion.  Every
+        all-gather (NCCL, in the graph) and the completion (replicated, or
+        row-sharded with the parameters' all-gather in the graph).  Every
         rank must capture together.  Release the returned object before the
         process group is destroyed."""
         from ._graph import CapturedGeneration
@@ -240,7 +272,7 @@ class DistributedZeroGrad:
         return CapturedGeneration(self._optimizer, _to_device(_materialize_tree(params), self._devices[0]),
                                   self._loss_fn, batch, state=state, candidate_range=(a, b - a),
                                   gather=lambda local: allgather_losses(local, sizes, group), rng=rng,
-                                  warmup=warmup, slots=slots, draw_ahead=draw_ahead)
+                                  warmup=warmup, slots=slots, draw_ahead=draw_ahead, row_shard=self._row_shard)
 
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, *, rng: torch.Tensor | None = None):
         if rng is None:
@@ -257,6 +289,10 @@ class DistributedZeroGrad:
                 local = torch.empty(0, dtype=torch.float32, device=shard.device)
             losses = allgather_losses(local.to(torch.float32), self._partition_sizes, self._group)
             params_c = _to_device(_materialize_tree(params), shard.device)
+            if self._row_shard is not None:
+                opt = self._optimizer
+                opt._manifest.validate(params_c)
+                return opt._step_from_losses(state, params_c, losses, row_shard=self._row_shard)
             return self._optimizer.step_from_losses(state, params_c, losses)
         futures = []
         for shard in self._shards:

@@ -82,7 +82,7 @@ class CapturedGeneration:
                  candidate_range: tuple[int, int] | None = None,
                  gather: Callable[[torch.Tensor], torch.Tensor] | None = None,
                  rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2,
-                 slots: int = 2, draw_ahead: bool = True):
+                 slots: int = 2, draw_ahead: bool = True, row_shard=None):
         from ._optimizer import ZeroGradState, _device_of, _materialize_tree
         from ._transforms import AdamWState, adamw, sgd
 
@@ -110,6 +110,7 @@ class CapturedGeneration:
         # (a parallel branch of the graph) during its forward; off by default,
         # since the draws and the forward's GEMMs contend for the same SMs
         self._prefetch = prefetch_replay
+        self._row_shard = row_shard  # the row-sharded update (RowShard), or None: replicated
         # a slot's per-generation inputs, one row of 8 words copied in by one
         # host-to-device copy: the base key (words 0-1), the next
         # generation's base key (2-3), AdamW's bias corrections (float32, 4-5)
@@ -249,7 +250,7 @@ class CapturedGeneration:
         # in the graph, fused steps update the captured parameters in place,
         # guarded by the non-finite count; the other leaves are copied back
         new_params, new_opt_state, metrics = opt._complete(state, self._params, losses, cand_keys=cks_all,
-                                                           inplace=copy_back)
+                                                           inplace=copy_back, row_shard=self._row_shard)
         if copy_back:
             flag = metrics[3:4]  # non-finite loss count
             pairs = [(t, tree_get(new_params, path)) for path, t in _leaves(self._params)]

@@ -27,7 +27,7 @@ from ._keys import key as make_key
 from ._keys import step_key
 from ._manifest import LAYOUT_CODE, Manifest, ParameterLayout, ParameterTree
 from ._replay import candidate_keys, replay_entry_keys, replay_entry_step
-from ._transforms import _leaves, apply_updates, is_fused, tree_get, tree_set
+from ._transforms import _leaves, apply_updates, is_fused, sgd, tree_get, tree_set
 
 LossFn = Callable[[ParameterTree, CandidateContext, Any, torch.Tensor], tuple[torch.Tensor, Any]]
 
@@ -254,8 +254,8 @@ class ZeroGrad:
         if losses.shape[0] != self._population_size:
             raise ValueError(f"losses must have {self._population_size} entries, got {losses.shape[0]}")
 
-    def _step_from_losses(self, state, params, losses, cand_keys: torch.Tensor | None = None):
-        new_params, new_opt_state, metrics = self._complete(state, params, losses, cand_keys)
+    def _step_from_losses(self, state, params, losses, cand_keys: torch.Tensor | None = None, row_shard=None):
+        new_params, new_opt_state, metrics = self._complete(state, params, losses, cand_keys, row_shard=row_shard)
         # The one host sync of a generation, after all its work is queued.  The
         # update wrote new tensors only, so rejecting non-finite losses here
         # leaves params and state exactly as they were.
@@ -271,14 +271,19 @@ class ZeroGrad:
         return StepMetrics(generation=generation, mean_loss=float(m[0]), min_loss=float(m[1]),
                            max_loss=float(m[2]), population_size=self._population_size)
 
-    def _complete(self, state, params, losses, cand_keys: torch.Tensor | None = None, inplace: bool = False):
+    def _complete(self, state, params, losses, cand_keys: torch.Tensor | None = None, inplace: bool = False,
+                  row_shard=None):
         """Device part of a generation's completion, all queued on the
         current stream with no host synchronisation: shaping, replay and the
         optimizer step.  Returns (new params, new optimizer state, device
         metrics [mean, min, max, non-finite count]).  `inplace`: entries whose
         step is fused into the replay are updated in place, and not at all
         when a loss is not finite (the metrics' non-finite count guards the
-        writes); the other leaves still come back as new tensors."""
+        writes); the other leaves still come back as new tensors.
+        `row_shard` (one process per GPU, SGD): each rank replays and updates
+        its block of rows of every bf16 MATRIX/TABLE leaf whose row count the
+        ranks divide, then the blocks are all-gathered (``row_shard.gather``),
+        so every rank ends with the same parameters."""
         self._check_losses(losses)
         device = _device_of(params)
         losses = losses.to(device)
@@ -292,12 +297,25 @@ class ZeroGrad:
         descent: dict = {}
         fused = is_fused(self._transform)
         done: dict = {}
+        shard_rows = row_shard is not None and isinstance(self._transform, sgd)
         for entry in self._manifest.entries:
             if fused:
                 # the optimizer step in the replay GEMM's epilogue (bf16 MATRIX/TABLE)
-                res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank,
-                                        self._transform.step_spec(state.opt_state, entry.path), gen,
-                                        inplace_guard=metrics[3:4] if inplace else None)
+                spec = self._transform.step_spec(state.opt_state, entry.path)
+                guard = metrics[3:4] if inplace else None
+                res = None
+                leaf = self._manifest.resolve(params, entry.path) if shard_rows else None
+                if shard_rows and isinstance(leaf, torch.Tensor) and leaf.ndim == 2 and \
+                        leaf.shape[0] % row_shard.world == 0:
+                    block = leaf.shape[0] // row_shard.world
+                    r0 = row_shard.rank * block
+                    res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank, spec,
+                                            gen, inplace_guard=guard, row_range=(r0, r0 + block))
+                    if res is not None:
+                        row_shard.gather(res[0], r0, r0 + block)
+                if res is None:
+                    res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank, spec,
+                                            gen, inplace_guard=guard)
                 if res is not None:
                     done[tuple(entry.path)] = res
                     continue
