@@ -53,6 +53,10 @@ def parse():
     # with more than one GPU: every rank replays the whole update (the
     # reference's protocol) or its block of W's rows, then W is all-gathered
     ap.add_argument("--replay", choices=["replicated", "sharded"], default="replicated")
+    # "headline": the shared-input generation alone (value, e2e, the eager
+    # launch sequence and its per-kernel times), for profiler runs; the
+    # default also runs the secondary workloads and the CPU baseline
+    ap.add_argument("--sections", choices=["all", "headline"], default="all")
     return ap.parse_args()
 
 
@@ -699,40 +703,44 @@ def run_ours(args):
     del cg  # holds NCCL work with more than one rank: released before the process group
     torch.cuda.synchronize()
 
-    # the hidden-layer form of the same generation: every candidate has its own
-    # input x_p [256, 4096] (seeded N(0, 0.02)), so x_p W is a batched GEMM on
-    # the tensor cores; replay reuses the forward's factors; SGD update
-    gx = torch.Generator(device=dev).manual_seed(WL["seed"] + a)
-    xb_all = (torch.randn(P_local, M, K, generator=gx, device=dev) * 0.02).to(torch.bfloat16)
+    # "--sections headline" stops here: no secondary workloads
+    secondary = args.sections == "all"
+    h_kernels, h_ms, h_steps, h_clocks = {}, None, 0, None
+    if secondary:
+        # the hidden-layer form of the same generation: every candidate has its own
+        # input x_p [256, 4096] (seeded N(0, 0.02)), so x_p W is a batched GEMM on
+        # the tensor cores; replay reuses the forward's factors; SGD update
+        gx = torch.Generator(device=dev).manual_seed(WL["seed"] + a)
+        xb_all = (torch.randn(P_local, M, K, generator=gx, device=dev) * 0.02).to(torch.bfloat16)
 
-    def hidden_step(W, gen):
-        cks, cks_local = keys[gen]
-        prefetch(gen)
-        with _ops.generation_scope(bases[gen], a, P_local, cks_local):
-            y = _ops.launch_linear(xb_all, W, cks_local, 0, r, sigma, True)
-        losses = gather(fitness[a:b])
-        shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
-        W = replay_update(shaped, cks, W, gen)
-        _ops.CACHE.drop_generation(bases[gen])
-        del y
-        return W
+        def hidden_step(W, gen):
+            cks, cks_local = keys[gen]
+            prefetch(gen)
+            with _ops.generation_scope(bases[gen], a, P_local, cks_local):
+                y = _ops.launch_linear(xb_all, W, cks_local, 0, r, sigma, True)
+            losses = gather(fitness[a:b])
+            shaped, metrics = _ops.launch_shape_fitness(losses, sigma)
+            W = replay_update(shaped, cks, W, gen)
+            _ops.CACHE.drop_generation(bases[gen])
+            del y
+            return W
 
-    h_steps = max(1, min(args.steps, 50))
-    Wh = W0
-    for i in range(args.warmup):
-        Wh = hidden_step(Wh, i)
-    barrier()
-    with ClockSampler(dev) as h_clk:
+        h_steps = max(1, min(args.steps, 50))
+        Wh = W0
+        for i in range(args.warmup):
+            Wh = hidden_step(Wh, i)
         barrier()
-        h_ms, _ = timed(hidden_step, h_steps, W0)
+        with ClockSampler(dev) as h_clk:
+            barrier()
+            h_ms, _ = timed(hidden_step, h_steps, W0)
+            barrier()
+        h_ms = max_over_ranks(h_ms)
+        h_clocks = h_clk.summary()
+        L.profile_begin(1 << 14)
+        timed(hidden_step, h_steps, W0)
+        h_kernels = L.profile_end()
         barrier()
-    h_ms = max_over_ranks(h_ms)
-    h_clocks = h_clk.summary()
-    L.profile_begin(1 << 14)
-    timed(hidden_step, h_steps, W0)
-    h_kernels = L.profile_end()
-    barrier()
-    del xb_all
+        del xb_all
 
     value = P * args.steps / (ms / 1e3)
     e2e_value = P * args.steps / (e2e_ms / 1e3)
@@ -789,12 +797,12 @@ def run_ours(args):
                           "api": "evaluate_shard + step_from_losses (fitness from the host)"},
         }
         hg = h_kernels.get("batched_gemm")
-        hidden = {"workload": "same generation with a per-candidate input x_p[256,4096] (seeded N(0,0.02)): "
+        hidden = None if not secondary else {"workload": "same generation with a per-candidate input x_p[256,4096] (seeded N(0,0.02)): "
                               "batched perturbed GEMM on the tensor cores, replay from the forward's factors, SGD",
                   "value": P * h_steps / (h_ms / 1e3), "unit": UNIT, "steps": h_steps,
                   "ms_per_step": h_ms / h_steps, "clocks": h_clocks,
                   "kernels_ms_per_step": {k: v[1] / h_steps for k, v in sorted(h_kernels.items())}}
-        if hg:
+        if hidden is not None and hg:
             per = hg[1] / hg[0] / 1e3
             ach = kernel_work("batched_gemm", P_local, world)[1] / per / 1e12
             # the loop keeps the tensor cores busy for ~0.1 s, so the sustained
@@ -809,12 +817,13 @@ def run_ours(args):
             fwd_ms = sum(h_kernels[k][1] for k in ("batched_gemm", "batched_u_pass") if k in h_kernels) / h_steps
             flops = 2.0 * P_local * M * K * N + 2.0 * P_local * M * r * (K + N)
             hidden["forward_tflops"] = flops / (fwd_ms / 1e3) / 1e12
-        line["hidden_layer"] = hidden
-        if world == 1:
+        if hidden is not None:
+            line["hidden_layer"] = hidden
+        if world == 1 and secondary:
             line["int8_qat_layer"] = int8_layer_section(dev, args)
             line["lm_tied_ce"] = tied_ce_section(dev, args)
             line["lm_block"] = lm_block_section(dev, args)
-        if world == 1:
+        if world == 1 and secondary:
             secs = cpu_generation_sample(8)
             n_cand = max(1, min(64, int(8 * 15.0 / max(secs, 1e-3))))
             secs = cpu_generation_sample(n_cand)
