@@ -142,6 +142,20 @@ ZG_API int zg_forward_factors(const void* x, const void* W, int w_is_kn, const v
                               const void* F2, int P, int M, int K, int N, int rank, float s,
                               void* y, void* workspace, size_t workspace_bytes, void* stream);
 
+/* zg_forward_factors with F1's and F2's rows ld1 and ld2 elements apart
+ * (multiples of 8, at least P*rank): F1 and F2 may be a column block of a
+ * larger population's operand factors, such as one process's candidates
+ * inside the whole population's factors drawn for the replay, so a
+ * population shard's forward reads them instead of drawing its own
+ * (src/zerograd/_distributed.py:88-139 evaluates a shard; its factors are
+ * those of _factors.py:30-74 for the shard's candidate ids).  A leading
+ * dimension above P*rank needs the rank-8 tensor-core expansion (rank 8,
+ * N a multiple of 8, 16-byte aligned F2); otherwise ZG_ERR_UNSUPPORTED.
+ * Workspace: zg_forward_factors_workspace_size. */
+ZG_API int zg_forward_factors_ld(const void* x, const void* W, int w_is_kn, const void* F1, int64_t ld1,
+                                 const void* F2, int64_t ld2, int P, int M, int K, int N, int rank, float s,
+                                 void* y, void* workspace, size_t workspace_bytes, void* stream);
+
 /* The same forward that also draws its operand factors into F1 / F2
  * (bf16 [K, P*rank] / [N, P*rank], kept by the caller for the replay of the
  * generation): linear (w_is_kn = 1) F1 = A_op, F2 = B_op of the MATRIX

@@ -60,3 +60,47 @@ def test_shard_prefetch_feeds_the_replay_bit_identically(cuda):
         assert torch.equal(a[k], b[k]), k
         assert torch.equal(sa.opt_state.mu[k], sb.opt_state.mu[k]), k
     assert ma == mb
+
+
+def test_shard_forward_reads_the_whole_population_factors(cuda):
+    """With the whole population's factors of a generation already drawn
+    (drawn ahead, or prefetched for the replay), a shard's forward reads its
+    candidates' columns of them (zg_forward_factors_ld) and draws nothing;
+    its outputs are bit for bit those of the shard drawing its own."""
+    from zerograd_b200 import _lib as L
+
+    opt, params, x, loss_fn, P = _problem(cuda)
+    _ops.CACHE.clear()
+    L.profile_begin()
+    ref = opt.evaluate_shard(params, 0, loss_fn, x, range(16, 48))  # draws its own factors
+    prof_ref = L.profile_end()
+    _ops.CACHE.clear()
+    opt._prefetch_replay(params, 0, tuple(int(v) for v in opt.base_key(0)), cuda)  # the whole population's
+    torch.cuda.synchronize()
+    L.profile_begin()
+    got = opt.evaluate_shard(params, 0, loss_fn, x, range(16, 48))
+    prof = L.profile_end()
+    # the linear layer's two operand draws are gone (the tied logits here,
+    # V=300, take the path that regenerates its factors in-kernel)
+    fills = lambda p: p.get("factor_fill", (0, 0.0))[0]  # noqa: E731
+    assert fills(prof) == fills(prof_ref) - 2, (prof_ref, prof)
+    assert torch.equal(got, ref)
+    _ops.CACHE.clear()
+    assert L.load().zg_device_error(1) == 0
+
+
+def test_strided_factors_rejected_without_the_tensor_core_expansion(cuda):
+    """A leading dimension above P*rank needs the rank-8 tensor-core
+    expansion: rank 16 is refused with a clear error."""
+    from zerograd_b200 import _lib as L
+
+    P, r, M, K, N = 8, 16, 32, 64, 64
+    x = torch.zeros(M, K, dtype=torch.bfloat16, device=cuda)
+    W = torch.zeros(K, N, dtype=torch.bfloat16, device=cuda)
+    F1 = torch.zeros(K, 2 * P * r, dtype=torch.bfloat16, device=cuda)
+    F2 = torch.zeros(N, 2 * P * r, dtype=torch.bfloat16, device=cuda)
+    y = torch.empty(P, M, N, dtype=torch.bfloat16, device=cuda)
+    ws = L.workspace(L.query("zg_forward_factors_workspace_size", P, M, N, r), cuda)
+    with pytest.raises(L.ZgLibraryError, match="strided factors"):
+        L.call("zg_forward_factors_ld", L.ptr(x), L.ptr(W), 1, L.ptr(F1), 2 * P * r, L.ptr(F2), 2 * P * r, P, M, K, N,
+               r, 0.1, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(cuda))

@@ -38,6 +38,8 @@ SIGNATURES = {
     "zg_population_factors": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "zg_factor_operands": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "zg_forward_factors_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
+    "zg_forward_factors_ld": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _vp,
+                                     _vp, _sz, _vp]),
     "zg_forward_factors": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
                                   _vp]),
     "zg_forward_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp,

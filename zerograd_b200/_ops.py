@@ -209,6 +209,17 @@ class FactorCache:
         self.misses += 1
         return None, None
 
+    def covering(self, base: tuple, start: int, count: int, tail: tuple):
+        """(count of its population, value) of an entry drawn for candidates
+        0..n of the generation `base` that covers candidates start..start+count
+        (same group, layout, shape and rank: `tail`), or None.  A shard's
+        forward reads its candidates' columns from it."""
+        for key in list(self._entries):
+            if (len(key) == 3 + len(tail) and key[0] == base and key[1] == 0 and key[2] >= start + count
+                    and key[3:] == tail):
+                return key[2], self.get(key)
+        return None
+
     def __contains__(self, key) -> bool:
         return key in self._entries
 
@@ -344,6 +355,19 @@ def _forward_cached(x, W, w_is_kn: bool, keys, group, layout, rows, cols, P, M, 
         A_op, B_op = hit
         F1, F2 = (A_op, B_op) if w_is_kn else (B_op, A_op)
         _forward_factors(x, W, w_is_kn, F1, F2, P, M, K, N, rank, s, y)
+        return
+    cover = cache.covering(gen.base, gen.start, gen.count, ckey[3:]) if (rank == 8 and gen.count == P) else None
+    if cover is not None:
+        # a shard of a population whose factors are drawn already (for the
+        # replay): its candidates' columns, rows P_all*rank apart
+        _, (A_all, B_all) = cover
+        c0 = gen.start * rank
+        A_v, B_v = A_all[:, c0:c0 + P * rank], B_all[:, c0:c0 + P * rank]
+        F1, F2 = (A_v, B_v) if w_is_kn else (B_v, A_v)
+        ld = int(A_all.shape[1])
+        ws = L.workspace(L.query("zg_forward_factors_workspace_size", P, M, N, rank), dev)
+        L.call("zg_forward_factors_ld", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(F1), ld, L.ptr(F2), ld, P, M, K, N,
+               rank, s, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
         return
     A_op = torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev)
     B_op = torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev)

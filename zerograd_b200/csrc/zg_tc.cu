@@ -961,12 +961,12 @@ bool tc_expand_ok(int P, int M, int N, int rank, const void* XW, const void* U, 
            al(y, 16);
 }
 
-int tc_expand_r8(const float* XW, const void* U, const void* Bq, int P, int M, int N, float s, void* y,
+int tc_expand_r8(const float* XW, const void* U, const void* Bq, int64_t ldb, int P, int M, int N, float s, void* y,
                  cudaStream_t st) {
     CUtensorMap tu, tb, ty;
     const uint64_t q = (uint64_t)P * 8;
     if (!make_map_2d(&tu, U, q, M, q, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&tb, Bq, q, N, q, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) || !make_map_y(&ty, y, N, M, P))
+        !make_map_2d(&tb, Bq, q, N, (uint64_t)ldb, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) || !make_map_y(&ty, y, N, M, P))
         return fail(ZG_ERR_CUDA, "tc_expand: tensor maps");
     ExpandArgs a{XW, M, N, P, s, (M + 127) / 128, (N + 127) / 128, 0, 0};
     const int tiles = a.tiles_m * a.tiles_n;

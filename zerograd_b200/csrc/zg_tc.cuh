@@ -60,10 +60,11 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
                  const float* scale, float extra_scale, int dtype, void* out, cudaStream_t st,
                  const char* name = "factor_fill");
 
-// Rank-8 expansion on the tensor cores: U bf16 [M, P*8], Bq bf16 [N, P*8],
-// XW float32 [M, N], y bf16 [P, M, N] written with TMA bulk stores.
+// Rank-8 expansion on the tensor cores: U bf16 [M, P*8], Bq bf16 [N, P*8]
+// with rows ldb apart, XW float32 [M, N], y bf16 [P, M, N] written with TMA
+// bulk stores.
 bool tc_expand_ok(int P, int M, int N, int rank, const void* XW, const void* U, const void* Bq, const void* y);
-int tc_expand_r8(const float* XW, const void* U, const void* Bq, int P, int M, int N, float s, void* y,
+int tc_expand_r8(const float* XW, const void* U, const void* Bq, int64_t ldb, int P, int M, int N, float s, void* y,
                  cudaStream_t st);
 
 // y[p, m, n] = XW[m, n] + s * sum_j U[m, p*r + j] * Bq[n, p*r + j].

@@ -615,15 +615,20 @@ SideStream* side_stream() {
 //   side stream:          XW = x W -> [fill F2] ------------'
 // The fills are integer-ALU bound and the GEMMs tensor/L2 bound, so the two
 // streams overlap on the same SMs.
+// F1's and F2's rows have leading dimensions ld1 and ld2 (P r for buffers of
+// this population alone; larger for a column block of a larger population's
+// factors, which only the tensor-core expansion reads).
 int tc_forward_schedule(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const uint32_t* keys, int group,
                         int f1_which, int f1_col_major, int f2_which, int f2_col_major, bool draw, const void* F1,
-                        const void* F2, int P, int M, int K, int N, int rank, float s, void* y, Carver& cv,
-                        cudaStream_t st) {
+                        int64_t ld1, const void* F2, int64_t ld2, int P, int M, int K, int N, int rank, float s,
+                        void* y, Carver& cv, cudaStream_t st) {
     const int64_t q = (int64_t)P * rank;
     float* U = cv.take<float>((size_t)M * q);
     float* XW = cv.take<float>((size_t)M * N);
     if (!U || !XW) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
     const bool tc_exp = tc_expand_ok(P, M, N, rank, XW, U, F2, y);
+    if ((draw && (ld1 != q || ld2 != q)) || (!tc_exp && ld2 != q))
+        return fail(ZG_ERR_UNSUPPORTED, "tc forward: strided factors need the rank-8 tensor-core expansion");
     SideStream* ss = side_stream();
     if (!ss) return fail(ZG_ERR_CUDA, "tc forward: side stream");
     int rc = ZG_OK, rc_side = ZG_OK;
@@ -640,21 +645,23 @@ int tc_forward_schedule(const void* x, const void* Wop, bool w_mn_major, int64_t
                               const_cast<void*>(F1), st, "factor_fill");
         // U = x F1 (F1 is MN-major for this product); bf16 for the tensor-core
         // expansion (x @ A rounded to the leaf dtype, as the reference's bf16 x @ a is)
-        if (!rc) rc = tc_gemm_bf16(x, K, F1, q, true, U, q, tc_exp, M, (int)q, K, 1.f, st, "forward_u_gemm");
+        if (!rc) rc = tc_gemm_bf16(x, K, F1, ld1, true, U, q, tc_exp, M, (int)q, K, 1.f, st, "forward_u_gemm");
         // join unconditionally so the side stream never outlives the call
         if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
             return fail(ZG_ERR_CUDA, "tc forward: join");
     }
     if (rc) return rc;
     if (rc_side) return rc_side;
-    if (tc_exp) return tc_expand_r8(XW, U, F2, P, M, N, s, y, st);
+    if (tc_exp) return tc_expand_r8(XW, U, F2, ld2, P, M, N, s, y, st);
     return lowrank_expand(XW, U, F2, P, M, N, rank, s, ZG_BF16, y, st);
 }
 
 int tc_forward_factors(const void* x, const void* Wop, bool w_mn_major, int64_t ldw, const void* F1, const void* F2,
-                       int P, int M, int K, int N, int rank, float s, void* y, Carver& cv, cudaStream_t st) {
-    return tc_forward_schedule(x, Wop, w_mn_major, ldw, nullptr, 0, 0, 0, 0, 0, false, F1, F2, P, M, K, N, rank, s,
-                               y, cv, st);
+                       int P, int M, int K, int N, int rank, float s, void* y, Carver& cv, cudaStream_t st,
+                       int64_t ld1 = 0, int64_t ld2 = 0) {
+    const int64_t q = (int64_t)P * rank;
+    return tc_forward_schedule(x, Wop, w_mn_major, ldw, nullptr, 0, 0, 0, 0, 0, false, F1, ld1 ? ld1 : q, F2,
+                               ld2 ? ld2 : q, P, M, K, N, rank, s, y, cv, st);
 }
 
 size_t tc_shared_forward_workspace(int P, int M, int K, int N, int rank) {
@@ -670,7 +677,7 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
     __nv_bfloat16* F2 = cv.take<__nv_bfloat16>((size_t)N * q);
     if (!F1 || !F2) return fail(ZG_ERR_WORKSPACE, "tc forward: workspace too small");
     return tc_forward_schedule(x, Wop, w_mn_major, ldw, keys, group, f1_which, f1_col_major, f2_which, f2_col_major,
-                               true, F1, F2, P, M, K, N, rank, s, y, cv, st);
+                               true, F1, q, F2, q, P, M, K, N, rank, s, y, cv, st);
 }
 
 bool batched_forward_ok(int P, int M, int K, int N, int rank) {
@@ -937,6 +944,26 @@ extern "C" int zg_forward_factors(const void* x, const void* W, int w_is_kn, con
                                   zg::as_stream(stream));
 }
 
+extern "C" int zg_forward_factors_ld(const void* x, const void* W, int w_is_kn, const void* F1, int64_t ld1,
+                                     const void* F2, int64_t ld2, int P, int M, int K, int N, int rank, float s,
+                                     void* y, void* workspace, size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || M < 1 || K < 1 || N < 1 || rank < 1)
+        return zg::fail(ZG_ERR_INVALID, "zg_forward_factors_ld: bad sizes");
+    if (!x || !W || !F1 || !F2 || !y) return zg::fail(ZG_ERR_INVALID, "zg_forward_factors_ld: null pointer");
+    const int64_t q = (int64_t)P * rank;
+    if (ld1 < q || ld2 < q || ld1 % 8 || ld2 % 8)
+        return zg::fail(ZG_ERR_INVALID, "zg_forward_factors_ld: leading dimensions must be multiples of 8, >= P*rank");
+    if (!zg::tc_shared_forward_ok(P, M, K, N, rank))
+        return zg::fail(ZG_ERR_UNSUPPORTED,
+                        "zg_forward_factors_ld: needs sm_100, P*rank, K, N multiples of 8, rank<=32");
+    size_t need = zg::tc_forward_factors_workspace(P, M, N, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_forward_factors_ld: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::tc_forward_factors(x, W, w_is_kn != 0, w_is_kn ? N : K, F1, F2, P, M, K, N, rank, s, y, cv,
+                                  zg::as_stream(stream), ld1, ld2);
+}
+
 extern "C" int zg_forward_operands(const void* x, const void* W, int w_is_kn, const uint32_t* keys, int group, int P,
                                    int M, int K, int N, int rank, float s, void* F1, void* F2, void* y,
                                    void* workspace, size_t workspace_bytes, void* stream) {
@@ -952,8 +979,9 @@ extern "C" int zg_forward_operands(const void* x, const void* W, int w_is_kn, co
     // linear: F1 = A_op (A, counter k*r + j), F2 = B_op (B, counter j*N + n);
     // tied table: F1 = table B_op (counter c*r + j), F2 = table A_op (counter v*r + j)
     const bool kn = w_is_kn != 0;
+    const int64_t q = (int64_t)P * rank;
     return zg::tc_forward_schedule(x, W, kn, kn ? N : K, keys, group, kn ? 0 : 1, 0, kn ? 1 : 0, kn ? 1 : 0, true, F1,
-                                   F2, P, M, K, N, rank, s, y, cv, zg::as_stream(stream));
+                                   q, F2, q, P, M, K, N, rank, s, y, cv, zg::as_stream(stream));
 }
 
 extern "C" size_t zg_replay_factors_workspace_size(int P, int64_t rows, int rank) {
