@@ -217,6 +217,12 @@ class FactorCache:
         for key in list(self._entries):
             if (len(key) == 3 + len(tail) and key[0] == base and key[1] == 0 and key[2] >= start + count
                     and key[3:] == tail):
+                ev = self._ready.get(key)
+                if ev is not None and not torch.cuda.is_current_stream_capturing() and not ev.query():
+                    # still being drawn on another stream (a replay prefetch
+                    # that overlaps this forward): the shard draws its own
+                    # rather than wait for the whole population's
+                    return None
                 return key[2], self.get(key)
         return None
 
