@@ -43,6 +43,8 @@ enum {
 };
 enum { ZG_F32 = 0, ZG_BF16 = 1 };
 enum { ZG_MATRIX = 0, ZG_TABLE = 1, ZG_VECTOR = 2 };
+/* Element-wise activation applied in a forward GEMM's epilogue. */
+enum { ZG_ACT_NONE = 0, ZG_ACT_GELU = 1 };
 
 /* Message of the last failing call on this host thread ("" if none). */
 ZG_API const char* zg_last_error(void);
@@ -128,6 +130,18 @@ ZG_API int zg_population_factors(const uint32_t* keys, int group, int P, int lay
 ZG_API int zg_factor_operands(const uint32_t* keys, int group, int P, int layout, int64_t rows,
                               int64_t cols, int rank, int dtype, void* A_op, void* B_op,
                               void* stream);
+
+/* The same factors in the per-candidate-input forward's layout (bf16, rank
+ * 8 or 16): MATRIX [rows = K, cols = N]: F1T = A^T [P*rank, rows] (row
+ * p*rank + j = A_p[:, j]) and F2 = B_op [cols, P*rank]; tied TABLE
+ * [rows = V, cols = C]: F1T = B^T [P*rank, cols] and F2 = A_op [rows,
+ * P*rank].  F2's rows are ld2 elements apart (0: P*rank).  What
+ * zg_batched_forward_ex and zg_tied_logits_ce_ex draw, for drawing a
+ * generation's factors ahead of its forward (the matrix_factors /
+ * table_factors draws under jax.vmap, src/zerograd/_factors.py:43-67). */
+ZG_API int zg_factor_operands_t(const uint32_t* keys, int group, int P, int layout, int64_t rows,
+                                int64_t cols, int rank, void* F1T, void* F2, int64_t ld2,
+                                void* stream);
 
 /* Shared-input population forward from operand factors (bf16, tcgen05):
  *   y[p] = x @ Wop + s * (x @ F1_p) @ F2_p^T, x [M,K], F1 [K, P*rank],
@@ -239,6 +253,17 @@ ZG_API int zg_tied_logits_ce(const void* x, int x_batched, const void* T, const 
                              int group, const int32_t* labels, int P, int M, int V, int C,
                              int rank, float s, float* loss, void* workspace,
                              size_t workspace_bytes, void* stream);
+/* The same with the table factors in caller buffers, F1T = B^T [P*rank, C]
+ * and F2 = A_op [V, P*rank] with rows ld2 apart (0: P*rank; larger: these
+ * candidates' column block of a population's buffer), drawn first when
+ * draw != 0 (keys may be NULL otherwise).  The workspace then holds only the
+ * low-rank activations (zg_tied_logits_ce_ex_workspace_size). */
+ZG_API size_t zg_tied_logits_ce_ex_workspace_size(int P, int M, int V, int C, int rank);
+ZG_API int zg_tied_logits_ce_ex(const void* x, int x_batched, const void* T, const uint32_t* keys,
+                                int group, const int32_t* labels, int P, int M, int V, int C,
+                                int rank, float s, void* F1T, void* F2, int64_t ld2, int draw,
+                                float* loss, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /* Per-candidate-input population forward (bf16, tcgen05), the hidden-layer
  * case: x [P, M, K] (one input per candidate), y [P, M, N],
@@ -262,6 +287,29 @@ ZG_API int zg_batched_forward_operands(const void* x, const void* W, int w_is_kn
                                        const uint32_t* keys, int group, int P, int M, int K, int N,
                                        int rank, float s, void* F1T, void* F2, void* y,
                                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* The per-candidate-input forward with the options a chunked population
+ * evaluation and a transformer block need (same workspace size query):
+ *   - F2's rows are ld2 elements apart (0: P*rank).  With ld2 > P*rank, F1T
+ *     and F2 are these P candidates' block of a larger population's
+ *     factors (F1T + c0*rank*K rows, F2 + c0*rank columns), so the
+ *     population's factors are drawn once per generation, chunk by chunk,
+ *     and the replay reads the whole buffers;
+ *   - draw != 0: F1T and F2 are drawn from `keys` first (as
+ *     zg_batched_forward_operands), else read as given;
+ *   - epilogue: y = bf16(acc); activation ZG_ACT_GELU then gives
+ *     y = bf16(gelu(y)) (tanh form, 0.5 y (1 + tanh(sqrt(2/pi)(y + 0.044715 y^3))));
+ *     a non-null `residual` [P, M, N] then gives y = bf16(residual + y) --
+ *     the roundings of the unfused linear, activation and residual add.
+ * A candidate's output does not depend on its position among the P.
+ * Replaces perturbed_linear (src/zerograd/_candidate.py:17-22) under
+ * jax.vmap followed by the user's element-wise activation and residual add
+ * (the transformer block of examples/train_vit_cifar10.py:137-191). */
+ZG_API int zg_batched_forward_ex(const void* x, const void* W, int w_is_kn, const uint32_t* keys,
+                                 int group, int P, int M, int K, int N, int rank, float s, void* F1T,
+                                 void* F2, int64_t ld2, int draw, int activation,
+                                 const void* residual, void* y, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------- forward ops -- */
 
@@ -305,6 +353,13 @@ ZG_API int zg_perturbed_vector(const void* v, int v_batched, const uint32_t* key
                         int64_t n, float s, int dtype, void* out, void* stream);
 
 /* --------------------------------------------- fitness / replay / update -- */
+
+/* out[r] = mean(x[r, 0:n]) for r in [0, rows) (float32 in, float64
+ * accumulation in a fixed order, float32 out): a candidate's mean loss over
+ * its rows, independent of how many candidates one launch holds.  Replaces
+ * the loss function's jnp.mean over the per-row cross-entropies
+ * (examples/train_cifar10.py:77-78) under jax.vmap. */
+ZG_API int zg_row_mean(const float* x, int64_t rows, int64_t n, float* out, void* stream);
 
 /* Validates and shapes the gathered losses [P] (float32):
  *   shaped[p] = -(l[p] - mean(l)) / (P * sigma)
@@ -414,6 +469,17 @@ ZG_API int zg_rms_norm(const void* x, int x_batched, const void* scale, int p_ba
  * ViT block (examples/train_vit_cifar10.py:166-172) under jax.vmap. */
 ZG_API int zg_attention(const void* q, const void* k, const void* v, int Z, int S, int H, int D, int causal,
                         int dtype, void* o, void* stream);
+/* The same with q, k and v rows (sequence positions) `ld` elements apart
+ * (>= H*D; consecutive z blocks S*ld apart), e.g. three views into one
+ * fused [Z, S, 3, H, D] q/k/v projection; o stays [Z, S, H, D] contiguous. */
+ZG_API int zg_attention_ex(const void* q, const void* k, const void* v, int64_t ld, int Z, int S, int H,
+                           int D, int causal, int dtype, void* o, void* stream);
+
+/* Element-wise GELU (tanh form, as the ZG_ACT_GELU epilogue):
+ *   y[i] = round_dtype(gelu(x[i])), x, y [n] of `dtype`.
+ * Replaces the activation of the reference examples' MLP blocks
+ * (examples/train_vit_cifar10.py:183) applied to a candidate's output. */
+ZG_API int zg_gelu(const void* x, void* y, int64_t n, int dtype, void* stream);
 
 /* ------------------------------------------------- integer QAT linear -- */
 

@@ -16,6 +16,7 @@ from ._build import LIB_PATH
 ZG_OK, ZG_ERR_INVALID, ZG_ERR_CUDA, ZG_ERR_WORKSPACE, ZG_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
 ZG_F32, ZG_BF16 = 0, 1
 ZG_MATRIX, ZG_TABLE, ZG_VECTOR = 0, 1, 2
+ZG_ACT_NONE, ZG_ACT_GELU = 0, 1
 
 _c = ctypes
 _vp, _i32, _i64, _f32, _f64, _sz = _c.c_void_p, _c.c_int, _c.c_int64, _c.c_float, _c.c_double, _c.c_size_t
@@ -37,6 +38,7 @@ SIGNATURES = {
     "zg_normal": (_i32, [_vp, _i64, _i64, _i32, _vp, _vp]),
     "zg_population_factors": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "zg_factor_operands": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "zg_factor_operands_t": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _i32, _vp, _vp, _i64, _vp]),
     "zg_forward_factors_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "zg_forward_factors_ld": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _vp,
                                      _vp, _sz, _vp]),
@@ -60,6 +62,13 @@ SIGNATURES = {
                                           _sz, _vp]),
     "zg_batched_forward_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp,
                                            _vp, _vp, _sz, _vp]),
+    "zg_batched_forward_ex": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _i64,
+                                     _i32, _i32, _vp, _vp, _vp, _sz, _vp]),
+    "zg_tied_logits_ce_ex_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "zg_tied_logits_ce_ex": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp,
+                                    _i64, _i32, _vp, _vp, _sz, _vp]),
+    "zg_attention_ex": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "zg_gelu": (_i32, [_vp, _vp, _i64, _i32, _vp]),
     "zg_perturbed_linear_workspace_size":(_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "zg_perturbed_linear": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32,
                                    _vp, _vp, _sz, _vp]),
@@ -71,6 +80,7 @@ SIGNATURES = {
                               _vp, _sz, _vp]),
     "zg_perturbed_vector": (_i32, [_vp, _i32, _vp, _i32, _i32, _i64, _f32, _i32, _vp, _vp]),
     "zg_shape_fitness": (_i32, [_vp, _i32, _f64, _vp, _vp, _vp]),
+    "zg_row_mean": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "zg_replay_workspace_size": (_sz, [_i32, _i32, _i64, _i64, _i32, _i32]),
     "zg_replay": (_i32, [_vp, _vp, _i32, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp, _vp, _sz, _vp]),
     "zg_replay_noalloc": (_i32, [_vp, _vp, _i32, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp, _vp]),

@@ -183,7 +183,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // dimension, online softmax over the keys, float32 arithmetic.
 template <typename T>
 __global__ void attn_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                                 T* __restrict__ o, int Z, int S, int H, int D, int causal, float scale) {
+                                 T* __restrict__ o, int Z, int S, int H, int D, int causal, float scale, int64_t ld) {
     const int lane = threadIdx.x % 32;
     const int64_t rows = (int64_t)Z * S * H;
     const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
@@ -192,7 +192,7 @@ __global__ void attn_simt_kernel(const T* __restrict__ q, const T* __restrict__ 
         const int h = (int)(r % H);
         const int qi = (int)((r / H) % S);
         const int64_t z = r / ((int64_t)H * S);
-        const T* qr = q + ((z * S + qi) * H + h) * D;
+        const T* qr = q + (z * S + qi) * ld + (int64_t)h * D;
         float qv[8], acc[8];
         for (int i = 0; i < 8; ++i) {
             const int d = lane + 32 * i;
@@ -202,7 +202,7 @@ __global__ void attn_simt_kernel(const T* __restrict__ q, const T* __restrict__ 
         float mx = -INFINITY, den = 0.f;
         const int jend = causal ? qi + 1 : S;
         for (int j = 0; j < jend; ++j) {
-            const T* kr = k + ((z * S + j) * H + h) * D;
+            const T* kr = k + (z * S + j) * ld + (int64_t)h * D;
             float s = 0.f;
             for (int i = 0; i < 8; ++i) {
                 const int d = lane + 32 * i;
@@ -214,7 +214,7 @@ __global__ void attn_simt_kernel(const T* __restrict__ q, const T* __restrict__ 
             const float m2 = fmaxf(mx, s);
             const float corr = expf(mx - m2), p = expf(s - m2);
             den = den * corr + p;
-            const T* vr = v + ((z * S + j) * H + h) * D;
+            const T* vr = v + (z * S + j) * ld + (int64_t)h * D;
             for (int i = 0; i < 8; ++i) {
                 const int d = lane + 32 * i;
                 if (d < D) acc[i] = fmaf(p, zg_to_float(vr[d]), acc[i] * corr);
@@ -250,7 +250,13 @@ int attn_error_word(int clear) { return ptx_error_word(clear); }
 
 extern "C" int zg_attention(const void* q, const void* k, const void* v, int Z, int S, int H, int D, int causal,
                             int dtype, void* o, void* stream) {
+    return zg_attention_ex(q, k, v, (int64_t)H * D, Z, S, H, D, causal, dtype, o, stream);
+}
+
+extern "C" int zg_attention_ex(const void* q, const void* k, const void* v, int64_t ld, int Z, int S, int H, int D,
+                               int causal, int dtype, void* o, void* stream) {
     if (Z < 0 || S < 0 || H < 1 || D < 1) return zg::fail(ZG_ERR_INVALID, "zg_attention: bad sizes");
+    if (ld < (int64_t)H * D) return zg::fail(ZG_ERR_INVALID, "zg_attention: row pitch below H*D");
     if (D > 256) return zg::fail(ZG_ERR_UNSUPPORTED, "zg_attention: head dim above 256");
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_attention: bad dtype");
     if (Z == 0 || S == 0) return ZG_OK;
@@ -259,7 +265,7 @@ extern "C" int zg_attention(const void* q, const void* k, const void* v, int Z, 
     cudaStream_t st = zg::as_stream(stream);
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     const bool tc = dtype == ZG_BF16 && D == 64 && S <= 256 && Z <= 65535 && H <= 65535 && zg::tc_available() &&
-                    al(q) && al(k) && al(v) && al(o);
+                    al(q) && al(k) && al(v) && al(o) && (ld * 2) % 16 == 0;
     if (tc) {
         static bool attr = false;
         const size_t smem = AT_SMEM + 1024;
@@ -271,7 +277,7 @@ extern "C" int zg_attention(const void* q, const void* k, const void* v, int Z, 
         }
         CUtensorMap tq, tk, tv;
         const uint64_t dims[4] = {64, (uint64_t)H, (uint64_t)S, (uint64_t)Z};
-        const uint64_t strides[3] = {64 * 2, (uint64_t)H * 64 * 2, (uint64_t)S * H * 64 * 2};
+        const uint64_t strides[3] = {64 * 2, (uint64_t)ld * 2, (uint64_t)S * ld * 2};
         const uint32_t box[4] = {64, 1, 128, 1};
         if (!zg::tensor_map_bf16(&tq, q, 4, dims, strides, box, true) ||
             !zg::tensor_map_bf16(&tk, k, 4, dims, strides, box, true) ||
@@ -292,10 +298,10 @@ extern "C" int zg_attention(const void* q, const void* k, const void* v, int Z, 
     if (dtype == ZG_BF16)
         attn_simt_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
             static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-            static_cast<const __nv_bfloat16*>(v), static_cast<__nv_bfloat16*>(o), Z, S, H, D, causal != 0, scale);
+            static_cast<const __nv_bfloat16*>(v), static_cast<__nv_bfloat16*>(o), Z, S, H, D, causal != 0, scale, ld);
     else
         attn_simt_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(
             static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
-            static_cast<float*>(o), Z, S, H, D, causal != 0, scale);
+            static_cast<float*>(o), Z, S, H, D, causal != 0, scale, ld);
     return zg::check_launch("zg_attention");
 }

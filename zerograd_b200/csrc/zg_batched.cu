@@ -185,6 +185,8 @@ constexpr uint32_t BG_SMEM = BG_STAGES * BG_STAGE + 2 * BG_CORR;  // 216 KiB
 struct GemmArgs {
     __nv_bfloat16* y;
     int M, N, K, P, rank, tiles_m, tiles_n;
+    const __nv_bfloat16* res;  // residual [P, M, N] added after the activation, or null
+    int act;                   // ZG_ACT_NONE / ZG_ACT_GELU
 };
 
 template <bool B_MN>
@@ -245,7 +247,11 @@ batched_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             if (++acc == 2) { acc = 0; acc_phase ^= 1; }
             // main loop operands; tiles start their K sweep at different blocks
             // so CTAs sharing an operand tile do not request the same lines at once
-            const int k_start = t % k_blocks;
+            // K sweeps start at different blocks for neighbouring tiles (so CTAs
+            // sharing an operand tile do not request the same lines at once),
+            // by the tile's place in its candidate's output only: a
+            // candidate's result does not depend on its position in the batch
+            const int k_start = (tm * a.tiles_n + tn) % k_blocks;
             for (int kb = 0; kb < k_blocks; ++kb) {
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 42)) { ok = false; break; }
                 const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
@@ -325,25 +331,14 @@ batched_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             const int tn = t % a.tiles_n, rest = t / a.tiles_n;
             const int tm = rest % a.tiles_m, p = rest / a.tiles_m;
             const int row = tm * BM + quad * 32 + lane;
-            __nv_bfloat16* yrow = a.y + ((int64_t)p * a.M + row) * a.N;
+            const int64_t row_off = ((int64_t)p * a.M + row) * a.N;
 #pragma unroll 1
             for (int c0 = 0; c0 < BG_BN; c0 += 32) {
                 float v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BG_BN + c0, v);
                 const int col0 = tn * BG_BN + c0;
                 if (row >= a.M || col0 >= a.N) continue;
-                __nv_bfloat16* d = yrow + col0;
-                if (col0 + 32 <= a.N) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        __nv_bfloat162 h[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[i + 2 * j], v[i + 2 * j + 1]);
-                        *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
-                    }
-                } else {
-                    for (int i = 0; i < 32 && col0 + i < a.N; ++i) d[i] = __float2bfloat16_rn(v[i]);
-                }
+                zg_store_row32(v, a.y + row_off + col0, a.res ? a.res + row_off + col0 : nullptr, a.act, a.N - col0);
             }
             tc_fence_before();
             __syncwarp();
@@ -360,27 +355,46 @@ batched_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
 // ---------------------------------------------------------------------------
 // The same GEMM on CTA pairs: 256 x 256 tiles, CTA r of the pair stages rows
 // [128 r, 128 r + 128) of the x tile and columns [128 r, 128 r + 128) of the
-// Wop tile (32 KiB per K block, 6 stages), plus its halves of the correction
+// Wop tile (32 KiB per K block, 5 stages), plus its halves of the correction
 // operands (U rows, F2 rows: 8 KiB per accumulator); the leader issues the
 // M=256 N=256 MMAs, the correction included, into both CTAs' TMEM.
+//
+// Epilogue: eight warps per CTA, two per TMEM lane quadrant, each owning 32
+// rows and 128 of the tile's 256 columns, in boxes of 32 x 32.  A box goes
+// TMEM -> registers -> (activation, residual) -> bf16 -> a 64-byte-swizzled
+// staging buffer -> one TMA bulk store issued by the warp's lane 0, so every
+// HBM write is a full box of lines (a lane storing its own row straight to
+// global memory touches 32 lines per store instruction, and the load/store
+// unit then takes a cycle per line).  A residual box is brought into the
+// same staging buffer by a TMA load first.  Two staging buffers per warp; a
+// buffer is rewritten once the bulk store issued from it two boxes earlier
+// has read it.
 // ---------------------------------------------------------------------------
-constexpr int BP_STAGES = 6;
+constexpr int BP_THREADS = 320;                                    // warp 0 TMA, 1 MMA, 2..9 epilogue
+constexpr int BP_STAGES = 5;
 constexpr uint32_t BP_A = BM * BK * 2;                             // 16 KiB: 128 rows of x
 constexpr uint32_t BP_B = 128 * BK * 2;                            // 16 KiB: 128 columns of Wop
 constexpr uint32_t BP_STAGE = BP_A + BP_B;                         // 32 KiB
 constexpr uint32_t BP_CU = 128 * 16;                               // 8 K columns of 128 U rows
 constexpr uint32_t BP_CF = 128 * 16;                               // 8 K columns of 128 F2 rows
 constexpr uint32_t BP_CORR = 2 * BP_CU + 2 * BP_CF;                // 8 KiB per accumulator
-constexpr uint32_t BP_SMEM = BP_STAGES * BP_STAGE + 2 * BP_CORR;   // 208 KiB
+constexpr uint32_t BP_BOX = 32 * 32 * 2;                           // 2 KiB: 32 rows x 32 bf16 columns
+constexpr uint32_t BP_STG = BP_STAGES * BP_STAGE + 2 * BP_CORR;    // staging buffers' offset (1 KiB aligned)
+constexpr uint32_t BP_SMEM = BP_STG + 8 * 2 * BP_BOX;              // 208 KiB
+
+// Byte offset of the 16-byte chunk `c` (0..3) of row `r` (0..31) in a
+// 32 x 32 bf16 box with 64-byte swizzle: chunk bits [4,6) ^= address bits [7,9).
+__device__ __forceinline__ uint32_t box64_off(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
 template <bool B_MN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BP_THREADS, 1)
 batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                          const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmF,
+                         const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                          const GemmArgs a) {
     extern __shared__ uint8_t dyn_smem[];
     __shared__ __align__(8) uint64_t full_bar[BP_STAGES], empty_bar[BP_STAGES], tmem_full[2], tmem_empty[2],
-        corr_full[2], corr_empty[2], mma_done;
+        corr_full[2], corr_empty[2], mma_done, res_bar[16];
     __shared__ uint32_t tmem_base_sh;
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
@@ -398,10 +412,11 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 8);  // 4 epilogue warps in each CTA
+            mbar_init(&tmem_empty[b], 16);  // 8 epilogue warps in each CTA
             mbar_init(&corr_full[b], 1);
             mbar_init(&corr_empty[b], 1);
         }
+        for (int b = 0; b < 16; ++b) mbar_init(&res_bar[b], 1);
         mbar_init(&mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -432,7 +447,10 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
             c_issued |= 1u << acc;
             c_parity = (c_parity & ~(1u << acc)) | (acc_phase << acc);
             if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-            const int k_start = t % k_blocks;
+            // K sweeps start at different blocks for neighbouring tiles, by the
+            // tile's place in its candidate's output only (a candidate's result
+            // does not depend on its position in the batch)
+            const int k_start = (tm * a.tiles_n + tn) % k_blocks;
             for (int kb = 0; kb < k_blocks; ++kb) {
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 52)) { ok = false; break; }
                 const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
@@ -511,41 +529,81 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
             if (mbar_try_wait(&mma_done, 0)) break;
     } else if (warp >= 2) {
         // ---------------- epilogue (both CTAs, own TMEM rows) ----------------
-        const int quad = warp % 4;
+        const int ew = warp - 2;               // epilogue warp 0..7
+        const int quad = warp % 4;             // TMEM lanes 32*quad .. 32*quad + 31
+        const int half = ew / 4;               // tile columns 128*half .. 128*half + 127
         const uint32_t empty_leader = cluster_addr(&tmem_empty[0], 0);
+        uint8_t* stg = smem + BP_STG + ew * 2 * BP_BOX;
+        uint64_t* rbar = &res_bar[ew * 2];
+        const bool has_res = a.res != nullptr;
         int acc = 0;
-        uint32_t acc_phase = 0;
-        for (int t = pair; t < num_tiles; t += pairs) {
+        uint32_t acc_phase = 0, box = 0, rphase = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < num_tiles; t += pairs) {
             if (!mbar_wait(&tmem_full[acc], acc_phase, 56)) break;
             tc_fence_after();
             const int tn = t % a.tiles_n, rest = t / a.tiles_n;
             const int tm = rest % a.tiles_m, p = rest / a.tiles_m;
-            const int row = tm * 256 + (int)rank * 128 + quad * 32 + lane;
-            __nv_bfloat16* yrow = a.y + ((int64_t)p * a.M + row) * a.N;
+            const int row0 = tm * 256 + (int)rank * 128 + quad * 32;  // the box's first row
+            const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + half * 128;
 #pragma unroll 1
-            for (int c0 = 0; c0 < 256; c0 += 32) {
-                float v[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + c0, v);
-                const int col0 = tn * 256 + c0;
-                if (row >= a.M || col0 >= a.N) continue;
-                __nv_bfloat16* d = yrow + col0;
-                if (col0 + 32 <= a.N) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        __nv_bfloat162 h[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[i + 2 * j], v[i + 2 * j + 1]);
-                        *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
+            for (int ch = 0; ch < 4; ++ch, ++box) {
+                const int b = (int)(box & 1);
+                uint8_t* buf = stg + b * BP_BOX;
+                const int col0 = tn * 256 + half * 128 + ch * 32;
+                const bool active = row0 < a.M && col0 < a.N;  // warp-uniform; TMA clips partial boxes
+                if (lane == 0) {
+                    // the store issued from this buffer two boxes ago has read it
+                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    if (has_res && active) {
+                        mbar_expect_tx(&rbar[b], BP_BOX);
+                        tma_load_3d(buf, &tmR, &rbar[b], col0, row0, p);
                     }
-                } else {
-                    for (int i = 0; i < 32 && col0 + i < a.N; ++i) d[i] = __float2bfloat16_rn(v[i]);
+                }
+                __syncwarp();
+                float v[32];
+                tmem_ld32(t_addr + ch * 32, v);
+                if (ch == 3) {
+                    // the accumulator is read: release it to the MMA issuer
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
+                }
+                if (!active) continue;
+                uint4 rv[4];
+                if (has_res) {
+                    if (!mbar_wait(&rbar[b], (rphase >> b) & 1, 57)) { ok = false; break; }
+                    rphase ^= 1u << b;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) rv[c] = *reinterpret_cast<const uint4*>(buf + box64_off(lane, c));
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    __nv_bfloat162 h[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float r0 = 0.f, r1 = 0.f;
+                        if (has_res) {
+                            const __nv_bfloat162 rr = reinterpret_cast<const __nv_bfloat162*>(&rv[c])[j];
+                            r0 = __bfloat162float(rr.x);
+                            r1 = __bfloat162float(rr.y);
+                        }
+                        h[j] = __floats2bfloat162_rn(zg_epilogue_value(v[8 * c + 2 * j], a.act, has_res, r0),
+                                                     zg_epilogue_value(v[8 * c + 2 * j + 1], a.act, has_res, r1));
+                    }
+                    *reinterpret_cast<uint4*>(buf + box64_off(lane, c)) = *reinterpret_cast<uint4*>(h);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the bulk store
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&tmY, buf, col0, row0, p);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
             if (++acc == 2) { acc = 0; acc_phase ^= 1; }
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
     tc_fence_before();
     cluster_sync();
@@ -564,7 +622,7 @@ int batched_pair_slots() {
                                  (int)smem) == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(2 * 74, 1, 1);
-            cfg.blockDim = dim3(THREADS, 1, 1);
+            cfg.blockDim = dim3(BP_THREADS, 1, 1);
             cfg.dynamicSmemBytes = smem;
             int clusters = 0;
             if (cudaOccupancyMaxActiveClusters(&clusters, batched_gemm_pair_kernel<B_MN>, &cfg) == cudaSuccess)
@@ -607,10 +665,16 @@ int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank
 }
 
 int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U, const void* F2, int P, int M, int K,
-                 int N, int rank, void* y, cudaStream_t st) {
+                 int N, int rank, void* y, cudaStream_t st, int64_t ld2, int act, const void* res) {
     if ((rank != 8 && rank != 16) || K % 8 || N % 8 || P < 1 || M < 1)
         return fail(ZG_ERR_INVALID, "batched_gemm: rank 8 or 16, K and N multiples of 8");
+    if (act != ZG_ACT_NONE && act != ZG_ACT_GELU) return fail(ZG_ERR_INVALID, "batched_gemm: unknown activation");
+    if (res && (reinterpret_cast<uintptr_t>(res) & 15)) return fail(ZG_ERR_INVALID, "batched_gemm: residual alignment");
     const uint64_t q = (uint64_t)P * rank;
+    // F2's rows are ld2 elements apart (a column block of a larger population's buffer when ld2 > q)
+    const uint64_t ldf = ld2 ? (uint64_t)ld2 : q;
+    if (ldf < q || ldf % 8) return fail(ZG_ERR_INVALID, "batched_gemm: F2 row pitch");
+    const __nv_bfloat16* resb = static_cast<const __nv_bfloat16*>(res);
     CUtensorMap tx, tw, tu, tf;
     const uint64_t dx[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)P};
     const uint64_t sx[2] = {(uint64_t)K * 2, (uint64_t)M * K * 2};
@@ -631,7 +695,7 @@ int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U,
     const uint64_t su[2] = {32, (uint64_t)M * 32};
     const uint32_t bu[3] = {8, BM, 1};
     const uint64_t df[2] = {q, (uint64_t)N};
-    const uint64_t sf[1] = {q * 2};
+    const uint64_t sf[1] = {ldf * 2};
     const uint32_t bf[2] = {8, BG_BN};
     ok = ok && tensor_map_bf16(&tu, U, 3, du, su, bu, false) && tensor_map_bf16(&tf, F2, 2, df, sf, bf, false);
     if (!ok) return fail(ZG_ERR_CUDA, "batched_gemm: tensor maps");
@@ -656,18 +720,25 @@ int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U,
         const uint32_t bu2[3] = {8, 128, 1};
         const uint32_t bf2[2] = {8, 128};
         ok2 = ok2 && tensor_map_bf16(&tu2, U, 3, du, su, bu2, false) && tensor_map_bf16(&tf2, F2, 2, df, sf, bf2, false);
+        // output and residual [P, M, N] in 32 x 32 boxes, 64-byte swizzle (the epilogue's staging layout)
+        CUtensorMap ty, tr;
+        const uint64_t dy[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)P};
+        const uint64_t sy[2] = {(uint64_t)N * 2, (uint64_t)M * N * 2};
+        const uint32_t by[3] = {32, 32, 1};
+        ok2 = ok2 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 && tensor_map_bf16_swz(&ty, y, 3, dy, sy, by, 64);
+        ok2 = ok2 && tensor_map_bf16_swz(&tr, res ? res : y, 3, dy, sy, by, 64);
         if (!ok2) return fail(ZG_ERR_CUDA, "batched_gemm: tensor maps");
-        GemmArgs a2{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + 255) / 256, (N + 255) / 256};
+        GemmArgs a2{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + 255) / 256, (N + 255) / 256, resb, act};
         const int pairs = pair_tiles < slots ? (int)pair_tiles : slots;
         const size_t smem2 = BP_SMEM + 1024;
         zg::LaunchTimer zg_lt_("batched_gemm", st);
         if (w_mn_major)
-            batched_gemm_pair_kernel<true><<<2 * pairs, THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, a2);
+            batched_gemm_pair_kernel<true><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
         else
-            batched_gemm_pair_kernel<false><<<2 * pairs, THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, a2);
+            batched_gemm_pair_kernel<false><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
         return check_launch("batched_gemm");
     }
-    GemmArgs a{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + BM - 1) / BM, (N + BG_BN - 1) / BG_BN};
+    GemmArgs a{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + BM - 1) / BM, (N + BG_BN - 1) / BG_BN, resb, act};
     const int64_t tiles = (int64_t)P * a.tiles_m * a.tiles_n;
     if (tiles > INT_MAX) return fail(ZG_ERR_INVALID, "batched_gemm: too many tiles");
     const int grid = tiles < sm_count_b() ? (int)tiles : sm_count_b();

@@ -35,50 +35,27 @@ constexpr uint32_t CE_SMEM = CE_STAGES * CE_STAGE + 2 * CE_CORR;   // 208 KiB
 struct CeArgs {
     float* loss;            // [P, M]
     const int32_t* labels;  // [M]
-    float4* partial;        // [pairs, 2, 256]: (max, sum of exp, label logit, flags) of units cut by a pair's range
     int M, V, C, P, rank, tiles_m, tiles_n, x_batched;
 };
 
-// Schedule of the (unit, 256-column block) tiles over G CTA pairs.  Whole
-// units go out in rounds, unit k G + g to pair g, so that all pairs sweep the
-// vocabulary together and each table tile is fetched from DRAM about once per
-// round; the tiles of the remaining units, r = (unit - rounds G) tiles_n + tn,
-// are split into contiguous balanced ranges, pair g owning [RT g / G, RT (g+1) / G).
-__host__ __device__ __forceinline__ int64_t range_begin(int64_t T, int g, int G) { return T * g / G; }
-__host__ __device__ __forceinline__ int pair_of_tile(int64_t t, int64_t T, int G) {
-    return (int)(((int64_t)G * (t + 1) - 1) / T);
-}
-
+// Schedule of the (unit, 256-column block) tiles over G CTA pairs: whole
+// units in rounds, unit k G + g to pair g, so all pairs sweep the vocabulary
+// together and each table tile is fetched from DRAM about once per round.
+// A unit's columns are always swept in order by one pair, so a candidate's
+// loss does not depend on the population size or its place in it.
 struct CeSched {
-    int g, G, tiles_n, rounds;
-    int64_t round_tiles, rb, re;  // rounds * tiles_n; this pair's remainder range [rb, re)
+    int g, G, tiles_n, n_units;
     __device__ CeSched(int g_, int G_, int units, int tiles_n_) : g(g_), G(G_), tiles_n(tiles_n_) {
-        rounds = units / G;
-        round_tiles = (int64_t)rounds * tiles_n;
-        const int64_t rt = (int64_t)(units - rounds * G) * tiles_n;
-        rb = range_begin(rt, g, G);
-        re = range_begin(rt, g + 1, G);
+        n_units = units > g ? (units - g + G - 1) / G : 0;
     }
-    __device__ int64_t count() const { return round_tiles + (re - rb); }
+    __device__ int64_t count() const { return (int64_t)n_units * tiles_n; }
     __device__ void at(int64_t j, int& u, int& tn) const {
-        if (j < round_tiles) {
-            u = (int)(j / tiles_n) * G + g;
-            tn = (int)(j % tiles_n);
-        } else {
-            const int64_t t = rb + (j - round_tiles);
-            u = rounds * G + (int)(t / tiles_n);
-            tn = (int)(t % tiles_n);
-        }
-    }
-    // whole in this pair: a round unit, or a remainder unit inside [rb, re)
-    __device__ bool whole(int u) const {
-        if (u < rounds * G) return true;
-        const int64_t t0 = (int64_t)(u - rounds * G) * tiles_n;
-        return t0 >= rb && t0 + tiles_n <= re;
+        u = (int)(j / tiles_n) * G + g;
+        tn = (int)(j % tiles_n);
     }
 };
 
-// Flags of a partial record.
+// Flags of a row half's record (merged with the other half at a unit's end).
 constexpr int kFound = 1, kOk = 2;
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -208,7 +185,7 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
                 c_issued |= 1u << acc;
                 c_parity = (c_parity & ~(1u << acc)) | (acc_phase << acc);
                 if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-                const int k_start = (int)(((int64_t)u * a.tiles_n + tn) % k_blocks);
+                const int k_start = (int)(((int64_t)tm * a.tiles_n + tn) % k_blocks);
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!mbar_wait(&empty_bar[stage], phase ^ 1, 72)) { ok = false; break; }
                     const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
@@ -283,13 +260,11 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         // Thread = one row of this CTA's 128 and one half (128 columns) of
         // every 256-column block; per 64-column chunk: the chunk's max and sum
         // of exponentials, merged into the running pair of the row half.  At
-        // the last tile of a unit in this pair's range the halves merge; a
-        // unit the range holds whole gets its loss, a cut one a partial record.
+        // the last tile of a unit the halves merge and the row's loss is written.
         __shared__ float s_half[2][4][128];  // second halves' (max, sum, label logit, flags), by parity
         const int quad = warp % 4, half = (warp - 2) / 4, r = quad * 32 + lane;
         const uint32_t empty_leader = cluster_addr(&tmem_empty[0], 0);
         const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + half * 128;
-        const int first_cut = sch.rounds * pairs + (int)(sch.rb / a.tiles_n);  // first remainder unit
         int acc = 0, parity = 0, label = -1, row = 0;
         uint32_t acc_phase = 0;
         bool ok = true, found = false;
@@ -297,7 +272,7 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         for (int64_t j = 0; j < n_mine; ++j) {
             int u, tn;
             sch.at(j, u, tn);
-            if (tn == 0 || j == sch.round_tiles) {
+            if (tn == 0) {
                 row = (u % a.tiles_m) * 256 + (int)rank * 128 + r;
                 // a label outside [0, V) never matches a column: its loss is NaN
                 label = row < a.M ? a.labels[row] : -1;
@@ -344,7 +319,7 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             __syncwarp();
             if (lane == 0 && ok) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
             if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-            if (tn == a.tiles_n - 1 || j == n_mine - 1) {
+            if (tn == a.tiles_n - 1) {
                 if (half == 1) {
                     s_half[parity][0][r] = run_max;
                     s_half[parity][1][r] = run_sum;
@@ -360,15 +335,9 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
                     const float sum =
                         run_sum * ex2_approx((run_max - m) * kLog2e) + s1 * ex2_approx((m1 - m) * kLog2e);
                     const float lab = found ? label_logit : s_half[parity][2][r];
-                    if (sch.whole(u)) {
-                        if ((flags & kOk) && row < a.M)
-                            a.loss[(int64_t)(u / a.tiles_m) * a.M + row] =
-                                (flags & kFound) ? m + logf(sum) - lab : __int_as_float(0x7fc00000);
-                    } else {
-                        const int slot = u == first_cut ? 0 : 1;
-                        a.partial[((int64_t)pair * 2 + slot) * 256 + (int)rank * 128 + r] =
-                            make_float4(m, sum, lab, (float)flags);
-                    }
+                    if ((flags & kOk) && row < a.M)
+                        a.loss[(int64_t)(u / a.tiles_m) * a.M + row] =
+                            (flags & kFound) ? m + logf(sum) - lab : __int_as_float(0x7fc00000);
                 }
                 parity ^= 1;
             }
@@ -380,44 +349,7 @@ tied_ce_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
-// Loss of every unit that the pair ranges cut, from the records of the pairs
-// that share it, merged the way the epilogue merges the two halves of a row.
-__global__ void tied_ce_merge_kernel(const float4* __restrict__ partial, float* __restrict__ loss, int M, int tiles_m,
-                                     int tiles_n, int units, int pairs) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (int64_t)units * 256) return;
-    const int u = (int)(idx / 256), lr = (int)(idx % 256);
-    const int row = (u % tiles_m) * 256 + lr;
-    if (row >= M) return;
-    const int rounds = units / pairs, ur = u - rounds * pairs;
-    if (ur < 0) return;  // a round unit: written whole by its pair
-    const int64_t rt = (int64_t)(units - rounds * pairs) * tiles_n;
-    const int g_lo = pair_of_tile((int64_t)ur * tiles_n, rt, pairs);
-    const int g_hi = pair_of_tile((int64_t)(ur + 1) * tiles_n - 1, rt, pairs);
-    if (g_lo == g_hi) return;  // held whole by one range: written by the main kernel
-    const int slot_lo = range_begin(rt, g_lo, pairs) / tiles_n == ur ? 0 : 1;
-    float m = -INFINITY;
-    for (int g = g_lo; g <= g_hi; ++g)
-        if (range_begin(rt, g + 1, pairs) > range_begin(rt, g, pairs))
-            m = fmaxf(m, partial[((int64_t)g * 2 + (g == g_lo ? slot_lo : 0)) * 256 + lr].x);
-    float sum = 0.f, lab = 0.f;
-    int flags = kOk;
-    for (int g = g_lo; g <= g_hi; ++g) {
-        if (range_begin(rt, g + 1, pairs) == range_begin(rt, g, pairs)) continue;  // an empty range
-        const float4 rec = partial[((int64_t)g * 2 + (g == g_lo ? slot_lo : 0)) * 256 + lr];
-        const int f = (int)rec.w;
-        sum += rec.y * ex2_approx((rec.x - m) * kLog2e);
-        if (f & kFound) {
-            lab = rec.z;
-            flags |= kFound;
-        }
-        if (!(f & kOk)) flags &= ~kOk;
-    }
-    if (flags & kOk)
-        loss[(int64_t)(u / tiles_m) * M + row] = (flags & kFound) ? m + logf(sum) - lab : __int_as_float(0x7fc00000);
-}
-
-constexpr int kMaxPairs = 256;  // bound on the pairs of one launch (sizes the partial records)
+constexpr int kMaxPairs = 256;  // bound on the pairs of one launch
 
 }  // namespace
 
@@ -428,10 +360,10 @@ bool tied_ce_ok(int P, int M, int V, int C, int rank) {
            (int64_t)P * ((M + 255) / 256) <= INT_MAX;
 }
 
-size_t tied_ce_workspace(int P, int M, int V, int C, int rank) {
+size_t tied_ce_workspace(int P, int M, int V, int C, int rank, bool factors) {
     const size_t q = (size_t)P * rank;
-    return Carver::need({(size_t)P * M * 16 * 2, q * C * 2, (size_t)V * q * 2, (size_t)kMaxPairs * 2 * 256 * 16}) +
-           256;
+    if (!factors) return Carver::need({(size_t)P * M * 16 * 2}) + 256;
+    return Carver::need({(size_t)P * M * 16 * 2, q * C * 2, (size_t)V * q * 2}) + 256;
 }
 
 // CTA pairs that can be resident at once (0 if unknown).
@@ -454,19 +386,33 @@ static int tied_ce_slots() {
     return n;
 }
 
+// F1T / F2: the caller's table factors (B^T [P r, C], A_op [V, rows ld2
+// apart]) drawn first when `draw`; null: drawn into the workspace.
 int tied_ce(const void* x, int x_batched, const void* T, const uint32_t* keys, int group, const int32_t* labels,
-            int P, int M, int V, int C, int rank, float s, float* loss, Carver& cv, cudaStream_t st) {
+            int P, int M, int V, int C, int rank, float s, float* loss, Carver& cv, cudaStream_t st, void* F1T_in,
+            void* F2_in, int64_t ld2, bool draw) {
     const int64_t q = (int64_t)P * rank;
     __nv_bfloat16* U = cv.take<__nv_bfloat16>((size_t)P * M * 16);
-    __nv_bfloat16* F1T = cv.take<__nv_bfloat16>((size_t)q * C);
-    __nv_bfloat16* F2 = cv.take<__nv_bfloat16>((size_t)V * q);
-    float4* partial = cv.take<float4>((size_t)kMaxPairs * 2 * 256);
-    if (!U || !F1T || !F2 || !partial) return fail(ZG_ERR_WORKSPACE, "tied_ce: workspace too small");
+    __nv_bfloat16* F1T = static_cast<__nv_bfloat16*>(F1T_in);
+    __nv_bfloat16* F2 = static_cast<__nv_bfloat16*>(F2_in);
+    if (!F1T || !F2) {
+        F1T = cv.take<__nv_bfloat16>((size_t)q * C);
+        F2 = cv.take<__nv_bfloat16>((size_t)V * q);
+        ld2 = 0;
+        draw = true;
+    }
+    const uint64_t ldf = ld2 ? (uint64_t)ld2 : (uint64_t)q;
+    if (!U || !F1T || !F2) return fail(ZG_ERR_WORKSPACE, "tied_ce: workspace too small");
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    if (!al(x) || !al(T)) return fail(ZG_ERR_INVALID, "tied_ce: x and T must be 16-byte aligned");
+    if (!al(x) || !al(T) || !al(F1T) || !al(F2))
+        return fail(ZG_ERR_INVALID, "tied_ce: x, T and the factors must be 16-byte aligned");
+    if (ldf < (uint64_t)q || ldf % 8) return fail(ZG_ERR_INVALID, "tied_ce: factor row pitch");
     // table factors: F2 = A_op [V, q] (counter v*r + j), F1T = B^T [q, C] (counter c*r + j)
-    int rc = fill_operand(keys, group, P, rank, V, 0, 0, nullptr, 1.f, ZG_BF16, F2, st, "factor_fill");
-    if (!rc) rc = fill_operand_t(keys, group, P, rank, C, 1, F1T, st, "factor_fill");
+    int rc = ZG_OK;
+    if (draw) {
+        rc = fill_operand(keys, group, P, rank, V, 0, 0, nullptr, 1.f, ZG_BF16, F2, st, "factor_fill", (int64_t)ldf);
+        if (!rc) rc = fill_operand_t(keys, group, P, rank, C, 1, F1T, st, "factor_fill");
+    }
     if (!rc) rc = batched_u_pass(x, F1T, P, M, C, rank, s, U, st, x_batched != 0);
     if (rc) return rc;
     const int slots = tied_ce_slots();
@@ -482,28 +428,19 @@ int tied_ce(const void* x, int x_batched, const void* T, const uint32_t* keys, i
     const uint64_t su[2] = {32, (uint64_t)M * 32};
     const uint32_t bu[3] = {8, 128, 1};
     const uint64_t df[2] = {(uint64_t)q, (uint64_t)V};
-    const uint64_t sf[1] = {(uint64_t)q * 2};
+    const uint64_t sf[1] = {ldf * 2};
     const uint32_t bf[2] = {8, 128};
     if (!tensor_map_bf16(&tx, x, 3, dx, sx, bx, true) || !tensor_map_bf16(&tt, T, 2, dt, stt, bt, true) ||
         !tensor_map_bf16(&tu, U, 3, du, su, bu, false) || !tensor_map_bf16(&tf, F2, 2, df, sf, bf, false))
         return fail(ZG_ERR_CUDA, "tied_ce: tensor maps");
-    CeArgs a{loss, labels, partial, M, V, C, P, rank, (M + 255) / 256, (V + 255) / 256, x_batched != 0};
+    CeArgs a{loss, labels, M, V, C, P, rank, (M + 255) / 256, (V + 255) / 256, x_batched != 0};
     const int units = P * a.tiles_m;
-    const int64_t n_tiles = (int64_t)units * a.tiles_n;
     int pairs = slots < kMaxPairs ? slots : kMaxPairs;
-    if (n_tiles < pairs) pairs = (int)n_tiles;
+    if (units < pairs) pairs = units;
     const size_t smem = (size_t)CE_SMEM + 1024;
-    {
-        zg::LaunchTimer zg_lt_("tied_ce", st);
-        tied_ce_pair_kernel<<<2 * pairs, THREADS, smem, st>>>(tx, tt, tu, tf, a);
-        if (int e = check_launch("tied_ce")) return e;
-    }
-    if (units % pairs == 0) return 0;  // every unit went out whole in a round
-    zg::LaunchTimer zg_lt_("tied_ce_merge", st);
-    const int64_t n = (int64_t)units * 256;
-    tied_ce_merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partial, loss, M, a.tiles_m, a.tiles_n, units,
-                                                                     pairs);
-    return check_launch("tied_ce_merge");
+    zg::LaunchTimer zg_lt_("tied_ce", st);
+    tied_ce_pair_kernel<<<2 * pairs, THREADS, smem, st>>>(tx, tt, tu, tf, a);
+    return check_launch("tied_ce");
 }
 
 int ce_error_word(int clear) { return ptx_error_word(clear); }
@@ -512,7 +449,33 @@ int ce_error_word(int clear) { return ptx_error_word(clear); }
 
 extern "C" size_t zg_tied_logits_ce_workspace_size(int P, int M, int V, int C, int rank) {
     if (P < 1 || M < 1 || V < 1 || C < 1 || rank < 1) return 0;
-    return zg::tied_ce_workspace(P, M, V, C, rank);
+    return zg::tied_ce_workspace(P, M, V, C, rank, true);
+}
+
+extern "C" size_t zg_tied_logits_ce_ex_workspace_size(int P, int M, int V, int C, int rank) {
+    if (P < 1 || M < 1 || V < 1 || C < 1 || rank < 1) return 0;
+    return zg::tied_ce_workspace(P, M, V, C, rank, false);
+}
+
+extern "C" int zg_tied_logits_ce_ex(const void* x, int x_batched, const void* T, const uint32_t* keys, int group,
+                                    const int32_t* labels, int P, int M, int V, int C, int rank, float s, void* F1T,
+                                    void* F2, int64_t ld2, int draw, float* loss, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || M < 1 || V < 1 || C < 1 || rank < 1)
+        return zg::fail(ZG_ERR_INVALID, "zg_tied_logits_ce_ex: bad sizes");
+    if (!x || !T || !labels || !loss || !F1T || !F2 || (draw && !keys))
+        return zg::fail(ZG_ERR_INVALID, "zg_tied_logits_ce_ex: null pointer");
+    if (!zg::tied_ce_ok(P, M, V, C, rank))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "zg_tied_logits_ce_ex: needs sm_100, rank 8 or 16, C a multiple of 8");
+    const int64_t q = (int64_t)P * rank;
+    if (ld2 != 0 && (ld2 < q || ld2 % 8))
+        return zg::fail(ZG_ERR_INVALID, "zg_tied_logits_ce_ex: ld2 must be 0 or a multiple of 8 >= P*rank");
+    const size_t need = zg::tied_ce_workspace(P, M, V, C, rank, false);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_tied_logits_ce_ex: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::tied_ce(x, x_batched, T, keys, group, labels, P, M, V, C, rank, s, loss, cv, zg::as_stream(stream), F1T,
+                       F2, ld2, draw != 0);
 }
 
 extern "C" int zg_tied_logits_ce(const void* x, int x_batched, const void* T, const uint32_t* keys, int group,
@@ -523,9 +486,10 @@ extern "C" int zg_tied_logits_ce(const void* x, int x_batched, const void* T, co
     if (!x || !T || !keys || !labels || !loss) return zg::fail(ZG_ERR_INVALID, "zg_tied_logits_ce: null pointer");
     if (!zg::tied_ce_ok(P, M, V, C, rank))
         return zg::fail(ZG_ERR_UNSUPPORTED, "zg_tied_logits_ce: needs sm_100, rank 8 or 16, C a multiple of 8");
-    const size_t need = zg::tied_ce_workspace(P, M, V, C, rank);
+    const size_t need = zg::tied_ce_workspace(P, M, V, C, rank, true);
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "zg_tied_logits_ce: workspace %zu < %zu bytes", workspace_bytes, need);
     zg::Carver cv(workspace, workspace_bytes);
-    return zg::tied_ce(x, x_batched, T, keys, group, labels, P, M, V, C, rank, s, loss, cv, zg::as_stream(stream));
+    return zg::tied_ce(x, x_batched, T, keys, group, labels, P, M, V, C, rank, s, loss, cv, zg::as_stream(stream),
+                       nullptr, nullptr, 0, true);
 }

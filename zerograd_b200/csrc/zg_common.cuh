@@ -189,3 +189,66 @@ __device__ __forceinline__ ZgKey zg_group_key(const uint32_t* cand_keys, int p, 
     ZgKey ck = zg_make_key(cand_keys[2 * p], cand_keys[2 * p + 1]);
     return group >= 0 ? zg_fold(ck, (uint32_t)group) : ck;
 }
+
+// ---------------------------------------------------------------------------
+// Activation and residual epilogue of the population forward.
+// ---------------------------------------------------------------------------
+// GELU in the tanh form of Hendrycks & Gimpel (arXiv:1606.08415, the form
+// GPT-2 uses): 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3),
+// evaluated as x * sigmoid(2u) = x / (1 + 2^(-2u log2 e)), which keeps its
+// relative accuracy on the negative tail where 1 + tanh(u) cancels.
+__device__ __forceinline__ float zg_gelu_tanh(float x) {
+    const float u = x * fmaf(0.044715f * 0.7978845608028654f, x * x, 0.7978845608028654f);
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * (-2.f * 1.4426950408889634f)));
+    return __fdividef(x, 1.f + e);
+}
+
+// One output element: y = bf16(v); with `act` (ZG_ACT_GELU) y = bf16(gelu(y));
+// with a residual r, y = bf16(r + y): the roundings of the unfused ops (the
+// linear's bf16 output, an element-wise activation of it, a bf16 residual add).
+__device__ __forceinline__ float zg_epilogue_value(float v, int act, bool has_res, float r) {
+    if (act || has_res) v = __bfloat162float(__float2bfloat16_rn(v));
+    if (act == ZG_ACT_GELU) {
+        v = zg_gelu_tanh(v);
+        if (has_res) v = __bfloat162float(__float2bfloat16_rn(v));
+    }
+    return has_res ? r + v : v;
+}
+
+// One thread's 32 consecutive outputs of a row, written straight to global
+// memory (zg_epilogue_value per element).  d and r 16-byte aligned; `n`
+// valid columns (32 or more take the vector path).
+__device__ __forceinline__ void zg_store_row32(const float (&v)[32], __nv_bfloat16* d, const __nv_bfloat16* r,
+                                               int act, int n) {
+    if (n >= 32) {
+        uint4 rv[4];
+        if (r) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) rv[i] = reinterpret_cast<const uint4*>(r)[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float r0 = 0.f, r1 = 0.f;
+                if (r) {
+                    const __nv_bfloat162 rr = reinterpret_cast<const __nv_bfloat162*>(&rv[i / 8])[j];
+                    r0 = __bfloat162float(rr.x);
+                    r1 = __bfloat162float(rr.y);
+                }
+                h[j] = __floats2bfloat162_rn(zg_epilogue_value(v[i + 2 * j], act, r != nullptr, r0),
+                                             zg_epilogue_value(v[i + 2 * j + 1], act, r != nullptr, r1));
+            }
+            *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
+        }
+        return;
+    }
+    // ragged end of a row: unrolled with a guard, so v stays in registers
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        if (i >= n) break;
+        d[i] = __float2bfloat16_rn(zg_epilogue_value(v[i], act, r != nullptr, r ? __bfloat162float(r[i]) : 0.f));
+    }
+}

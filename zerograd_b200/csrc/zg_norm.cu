@@ -230,3 +230,56 @@ extern "C" int zg_rms_norm(const void* x, int x_batched, const void* scale, int 
                            float eps, int dtype, void* y, void* stream) {
     return norm_entry("rms_norm", NORM_RMS, x, x_batched, scale, nullptr, p_batched, P, M, C, eps, dtype, y, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Element-wise GELU (tanh form), the unfused twin of the forward GEMM's
+// ZG_ACT_GELU epilogue: y = round_dtype(gelu(float(x))), same device function.
+// ---------------------------------------------------------------------------
+namespace {
+
+__global__ void gelu_bf16x8_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, int64_t n8) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+        uint4 v = x[i];
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            h[j] = __floats2bfloat162_rn(zg_gelu_tanh(__bfloat162float(h[j].x)), zg_gelu_tanh(__bfloat162float(h[j].y)));
+        y[i] = v;
+    }
+}
+
+template <typename T>
+__global__ void gelu_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = zg_from_float<T>(zg_gelu_tanh(zg_to_float(x[i])));
+}
+
+}  // namespace
+
+extern "C" int zg_gelu(const void* x, void* y, int64_t n, int dtype, void* stream) {
+    if (n < 0) return zg::fail(ZG_ERR_INVALID, "zg_gelu: bad size");
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_gelu: bad dtype");
+    if (n == 0) return ZG_OK;
+    if (!x || !y) return zg::fail(ZG_ERR_INVALID, "zg_gelu: null pointer");
+    cudaStream_t st = zg::as_stream(stream);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    zg::LaunchTimer zg_lt_("gelu", st);
+    if (dtype == ZG_BF16 && n % 8 == 0 && al(x) && al(y)) {
+        const int64_t n8 = n / 8;
+        int64_t blocks = (n8 + 255) / 256;
+        if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+        gelu_bf16x8_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(y), n8);
+        return zg::check_launch("zg_gelu");
+    }
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+    if (dtype == ZG_BF16)
+        gelu_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                      static_cast<__nv_bfloat16*>(y), n);
+    else
+        gelu_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const float*>(x), static_cast<float*>(y), n);
+    return zg::check_launch("zg_gelu");
+}

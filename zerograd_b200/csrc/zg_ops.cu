@@ -499,6 +499,32 @@ extern "C" int zg_shape_fitness(const float* losses, int P, double sigma, float*
     return zg::check_launch("zg_shape_fitness");
 }
 
+// out[r] = mean of x[r, 0:n], float64 accumulation in a fixed order (each of
+// 256 threads sums a fixed stride of the row, then a fixed tree), so a row's
+// mean does not depend on how many rows the launch has.
+__global__ void row_mean_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
+    __shared__ double part[256];
+    const float* row = x + (int64_t)blockIdx.x * n;
+    double acc = 0.0;
+    for (int64_t i = threadIdx.x; i < n; i += 256) acc += (double)row[i];
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = (float)(part[0] / (double)n);
+}
+
+extern "C" int zg_row_mean(const float* x, int64_t rows, int64_t n, float* out, void* stream) {
+    if (rows < 0 || n < 1 || rows > 2147483647LL) return zg::fail(ZG_ERR_INVALID, "zg_row_mean: bad sizes");
+    if (rows == 0) return ZG_OK;
+    if (!x || !out) return zg::fail(ZG_ERR_INVALID, "zg_row_mean: null pointer");
+    zg::LaunchTimer zg_lt_("row_mean", zg::as_stream(stream));
+    row_mean_kernel<<<(unsigned)rows, 256, 0, zg::as_stream(stream)>>>(x, n, out);
+    return zg::check_launch("zg_row_mean");
+}
+
 extern "C" size_t zg_replay_workspace_size(int P, int layout, int64_t rows, int64_t cols, int rank, int dtype) {
     if (P < 1 || rows < 1 || !zg::dtype_ok(dtype)) return 0;
     if (layout == ZG_VECTOR) return 256;

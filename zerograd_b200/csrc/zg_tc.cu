@@ -890,7 +890,15 @@ bool tc_available() {
 
 bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                      const uint32_t* box, bool swizzle128) {
+    return tensor_map_bf16_swz(m, base, rank, dims, strides_bytes, box, swizzle128 ? 128 : 0);
+}
+
+bool tensor_map_bf16_swz(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
     auto fn = encode_fn();
+    const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                         : CU_TENSOR_MAP_SWIZZLE_NONE;
     if (!fn || rank < 1 || rank > 5) return false;
     cuuint64_t d[5], s[4];
     cuuint32_t b[5], e[5];
@@ -901,8 +909,8 @@ bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t*
         if (i + 1 < rank) s[i] = strides_bytes[i];
     }
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,

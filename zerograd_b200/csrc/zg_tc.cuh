@@ -15,6 +15,9 @@ bool tc_available();
 // elements read as zero.
 bool tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                      const uint32_t* box, bool swizzle128);
+// The same with the swizzle span in bytes: 0 (none), 64 or 128.
+bool tensor_map_bf16_swz(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes);
 
 // Kernel error words of the per-candidate-input and int8 kernels (0 = none).
 int batched_error_word(int clear);
@@ -36,13 +39,17 @@ int fill_operand_t(const uint32_t* keys, int group, int P, int rank, int64_t row
 //   y[p] = bf16(x_p . Wop + U_p . F2_p^T)
 int batched_u_pass(const void* x, const void* F1T, int P, int M, int K, int rank, float s, void* U, cudaStream_t st,
                    bool x_batched = true);
+// F2's rows are ld2 elements apart (0: P*rank).  The epilogue rounds to bf16,
+// then applies `act` (ZG_ACT_*) and adds the bf16 residual `res` [P, M, N]
+// (or null), rounding after each step as the unfused ops do.
 int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U, const void* F2, int P, int M, int K,
-                 int N, int rank, void* y, cudaStream_t st);
+                 int N, int rank, void* y, cudaStream_t st, int64_t ld2 = 0, int act = 0, const void* res = nullptr);
 bool batched_forward_ok(int P, int M, int K, int N, int rank);
 size_t batched_forward_workspace(int P, int M, int K, int N, int rank, bool draw);
 int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint32_t* keys, int group, int f1_which,
                     int f2_which, int f2_col_major, bool draw, const void* F1T, const void* F2, int P, int M, int K,
-                    int N, int rank, float s, void* y, Carver& cv, cudaStream_t st);
+                    int N, int rank, float s, void* y, Carver& cv, cudaStream_t st, int64_t ld2 = 0, int act = 0,
+                    const void* res = nullptr);
 
 // D[M,N] = alpha * A[M,K] . B^T; A K-major row-major (lda), B K-major
 // [N,K] (ldb) or MN-major [K,N] (ldb); D row-major float32 or bf16 (ldd).
@@ -53,12 +60,14 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
                  bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name = "gemm",
                  const FusedStep* step = nullptr);
 
-// Factor fill in GEMM-operand layout: out[row, p*r + j] =
+// Factor fill in GEMM-operand layout: out[row * ld + p*r + j] =
 // scale_p * round_dtype(normal(key_p, ctr)), ctr = row*r + j (row-major) or
-// j*rows + row (col_major); which = 0 for the A factor key, 1 for B.
+// j*rows + row (col_major); which = 0 for the A factor key, 1 for B.  ld is
+// the row pitch in elements (0: P*r, a buffer of these P candidates alone;
+// larger: their column block of a larger population's buffer).
 int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows, int which, int col_major,
                  const float* scale, float extra_scale, int dtype, void* out, cudaStream_t st,
-                 const char* name = "factor_fill");
+                 const char* name = "factor_fill", int64_t ld = 0);
 
 // Rank-8 expansion on the tensor cores: U bf16 [M, P*8], Bq bf16 [N, P*8]
 // with rows ldb apart, XW float32 [M, N], y bf16 [P, M, N] written with TMA

@@ -60,13 +60,12 @@ __device__ __forceinline__ void zg_normal_x8(const ZgKey& k, const uint64_t (&ct
 template <typename T, int R>
 __global__ void fill_operand_r8_kernel(const uint32_t* __restrict__ keys, int group, int P, int64_t rows, int which,
                                        int col_major, const float* __restrict__ scale, int rows_per_block,
-                                       T* __restrict__ out) {
+                                       int64_t ld, T* __restrict__ out) {
     const int p = blockIdx.x * blockDim.x + threadIdx.x;
     if (p >= P) return;
     ZgFactorKeys fk = zg_factor_keys(keys, p, group);
     const ZgKey k = which == 0 ? fk.a : fk.b;
     const float sc = scale ? scale[p] : 1.f;
-    const int64_t ld = (int64_t)P * R;
     const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
     const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
     for (int64_t row = r0; row < r1; ++row) {
@@ -105,13 +104,12 @@ __global__ void fill_operand_r8_kernel(const uint32_t* __restrict__ keys, int gr
 template <typename T, int R>
 __global__ void fill_operand_small_kernel(const uint32_t* __restrict__ keys, int group, int P, int64_t rows,
                                           int which, int col_major, const float* __restrict__ scale,
-                                          int rows_per_thread, T* __restrict__ out) {
+                                          int rows_per_thread, int64_t ld, T* __restrict__ out) {
     const int p = threadIdx.x;
     if (p >= P) return;
     ZgFactorKeys fk = zg_factor_keys(keys, p, group);
     const ZgKey k = which == 0 ? fk.a : fk.b;
     const float sc = scale ? scale[p] : 1.f;
-    const int64_t ld = (int64_t)P * R;
     const int64_t r0 = ((int64_t)blockIdx.x * blockDim.y + threadIdx.y) * rows_per_thread;
     for (int64_t row = r0; row < r0 + rows_per_thread && row < rows; ++row) {
         T* dst = out + row * ld + (int64_t)p * R;
@@ -178,13 +176,12 @@ __global__ void fill_operand_t_kernel(const uint32_t* __restrict__ keys, int gro
 template <typename T>
 __global__ void fill_operand_kernel(const uint32_t* __restrict__ keys, int group, int P, int rank, int64_t rows,
                                     int which, int col_major, const float* __restrict__ scale, float extra_scale,
-                                    int rows_per_block, T* __restrict__ out) {
+                                    int rows_per_block, int64_t ld, T* __restrict__ out) {
     const int p = blockIdx.x * blockDim.x + threadIdx.x;
     if (p >= P) return;
     ZgFactorKeys fk = zg_factor_keys(keys, p, group);
     const ZgKey k = which == 0 ? fk.a : fk.b;
     const float sc = scale ? scale[p] * extra_scale : extra_scale;
-    const int64_t ld = (int64_t)P * rank;
     const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
     const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
     // 16-byte stores of 8 bf16 when the rank and the row pitch allow it.
@@ -441,7 +438,10 @@ int sm_count() {
 namespace zg {
 
 int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows, int which, int col_major,
-                 const float* scale, float extra_scale, int dtype, void* out, cudaStream_t st, const char* name) {
+                 const float* scale, float extra_scale, int dtype, void* out, cudaStream_t st, const char* name,
+                 int64_t ld) {
+    if (ld == 0) ld = (int64_t)P * rank;
+    if (ld < (int64_t)P * rank) return fail(ZG_ERR_INVALID, "fill_operand: row pitch below P*rank");
     const int threads = P >= 128 ? 128 : ((P + 31) / 32) * 32;
     const int pblocks = (P + threads - 1) / threads;
     // enough blocks for ~8 waves of rows, each block >= 4 rows
@@ -453,7 +453,8 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
     if (yblocks > 65535) return fail(ZG_ERR_INVALID, "fill_operand: too many rows");
     dim3 grid(pblocks, (unsigned)yblocks);
     zg::LaunchTimer zg_lt_(name, st);
-    const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && extra_scale == 1.f;
+    const size_t esz = dtype == ZG_BF16 ? 2 : 4;
+    const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && extra_scale == 1.f && (ld * esz) % 16 == 0;
     if (aligned && (rank == 8 || rank == 16) && P <= 64) {
         const int px = P <= 8 ? 8 : P <= 16 ? 16 : P <= 32 ? 32 : 64;
         const int ry = 128 / px;
@@ -465,7 +466,7 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
         dim3 g2((unsigned)gx), b2(px, ry);
 #define ZG_FILL_SMALL(TT, RR)                                                                                      \
     fill_operand_small_kernel<TT, RR><<<g2, b2, 0, st>>>(keys, group, P, rows, which, col_major, scale, rpt, \
-                                                          static_cast<TT*>(out))
+                                                          ld, static_cast<TT*>(out))
         if (dtype == ZG_BF16) {
             if (rank == 8) ZG_FILL_SMALL(__nv_bfloat16, 8);
             else ZG_FILL_SMALL(__nv_bfloat16, 16);
@@ -480,29 +481,29 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
         if (dtype == ZG_BF16) {
             if (rank == 8)
                 fill_operand_r8_kernel<__nv_bfloat16, 8><<<grid, threads, 0, st>>>(
-                    keys, group, P, rows, which, col_major, scale, rows_per_block, static_cast<__nv_bfloat16*>(out));
+                    keys, group, P, rows, which, col_major, scale, rows_per_block, ld, static_cast<__nv_bfloat16*>(out));
             else
                 fill_operand_r8_kernel<__nv_bfloat16, 16><<<grid, threads, 0, st>>>(
-                    keys, group, P, rows, which, col_major, scale, rows_per_block, static_cast<__nv_bfloat16*>(out));
+                    keys, group, P, rows, which, col_major, scale, rows_per_block, ld, static_cast<__nv_bfloat16*>(out));
         } else {
             if (rank == 8)
                 fill_operand_r8_kernel<float, 8><<<grid, threads, 0, st>>>(keys, group, P, rows, which, col_major,
-                                                                           scale, rows_per_block,
+                                                                           scale, rows_per_block, ld,
                                                                            static_cast<float*>(out));
             else
                 fill_operand_r8_kernel<float, 16><<<grid, threads, 0, st>>>(keys, group, P, rows, which, col_major,
-                                                                            scale, rows_per_block,
+                                                                            scale, rows_per_block, ld,
                                                                             static_cast<float*>(out));
         }
         return check_launch("fill_operand");
     }
     if (dtype == ZG_BF16)
         fill_operand_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(keys, group, P, rank, rows, which, col_major,
-                                                                     scale, extra_scale, rows_per_block,
+                                                                     scale, extra_scale, rows_per_block, ld,
                                                                      static_cast<__nv_bfloat16*>(out));
     else
         fill_operand_kernel<float><<<grid, threads, 0, st>>>(keys, group, P, rank, rows, which, col_major, scale,
-                                                             extra_scale, rows_per_block, static_cast<float*>(out));
+                                                             extra_scale, rows_per_block, ld, static_cast<float*>(out));
     return check_launch("fill_operand");
 }
 
@@ -698,11 +699,15 @@ size_t batched_forward_workspace(int P, int M, int K, int N, int rank, bool draw
 //   side stream:   [fill F2] -------------------'
 int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint32_t* keys, int group, int f1_which,
                     int f2_which, int f2_col_major, bool draw, const void* F1T, const void* F2, int P, int M, int K,
-                    int N, int rank, float s, void* y, Carver& cv, cudaStream_t st) {
+                    int N, int rank, float s, void* y, Carver& cv, cudaStream_t st, int64_t ld2, int act,
+                    const void* res) {
     const int64_t q = (int64_t)P * rank;
     __nv_bfloat16* U = cv.take<__nv_bfloat16>((size_t)P * M * 16);
     if (draw && !F1T) F1T = cv.take<__nv_bfloat16>((size_t)q * K);
-    if (draw && !F2) F2 = cv.take<__nv_bfloat16>((size_t)N * q);
+    if (draw && !F2) {
+        F2 = cv.take<__nv_bfloat16>((size_t)N * q);
+        ld2 = 0;
+    }
     if (!U || !F1T || !F2) return fail(ZG_ERR_WORKSPACE, "batched forward: workspace too small");
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!al(x) || !al(Wop) || !al(F1T) || !al(F2) || !al(y))
@@ -715,7 +720,7 @@ int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint3
         if (cudaEventRecord(ss->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess)
             return fail(ZG_ERR_CUDA, "batched forward: fork");
         rc_side = fill_operand(keys, group, P, rank, N, f2_which, f2_col_major, nullptr, 1.f, ZG_BF16,
-                               const_cast<void*>(F2), ss->s, "factor_fill");
+                               const_cast<void*>(F2), ss->s, "factor_fill", ld2);
         rc = fill_operand_t(keys, group, P, rank, K, f1_which, const_cast<void*>(F1T), st, "factor_fill");
         if (!rc) rc = batched_u_pass(x, F1T, P, M, K, rank, s, U, st);
         if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
@@ -725,7 +730,7 @@ int batched_forward(const void* x, const void* Wop, bool w_mn_major, const uint3
     }
     if (rc) return rc;
     if (rc_side) return rc_side;
-    return batched_gemm(x, Wop, w_mn_major, U, F2, P, M, K, N, rank, y, st);
+    return batched_gemm(x, Wop, w_mn_major, U, F2, P, M, K, N, rank, y, st, ld2, act, res);
 }
 
 // Aw[row, q] = bf16(float(A[row, q]) * w[q / rank]): the reference's
@@ -1053,6 +1058,49 @@ extern "C" int zg_batched_forward_operands(const void* x, const void* W, int w_i
     const bool kn = w_is_kn != 0;
     return zg::batched_forward(x, W, kn, keys, group, kn ? 0 : 1, kn ? 1 : 0, kn ? 1 : 0, true, F1T, F2, P, M, K, N,
                                rank, s, y, cv, zg::as_stream(stream));
+}
+
+extern "C" int zg_factor_operands_t(const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols,
+                                    int rank, void* F1T, void* F2, int64_t ld2, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || (rank != 8 && rank != 16))
+        return zg::fail(ZG_ERR_INVALID, "zg_factor_operands_t: bad sizes (rank 8 or 16)");
+    if (!keys || !F1T || !F2) return zg::fail(ZG_ERR_INVALID, "zg_factor_operands_t: null pointer");
+    if (layout != ZG_MATRIX && layout != ZG_TABLE) return zg::fail(ZG_ERR_INVALID, "zg_factor_operands_t: layout");
+    const int64_t q = (int64_t)P * rank;
+    if (ld2 != 0 && (ld2 < q || ld2 % 8))
+        return zg::fail(ZG_ERR_INVALID, "zg_factor_operands_t: ld2 must be 0 or a multiple of 8 >= P*rank");
+    cudaStream_t st = zg::as_stream(stream);
+    // MATRIX [K=rows, N=cols]: F1T = A^T [q, rows], F2 = B_op [cols, q] (counter j*cols + n);
+    // tied TABLE [V=rows, C=cols]: F1T = B^T [q, cols], F2 = A_op [rows, q] (counter v*r + j)
+    const bool mat = layout == ZG_MATRIX;
+    int rc = zg::fill_operand_t(keys, group, P, rank, mat ? rows : cols, mat ? 0 : 1, F1T, st, "factor_fill");
+    if (!rc)
+        rc = zg::fill_operand(keys, group, P, rank, mat ? cols : rows, mat ? 1 : 0, mat ? 1 : 0, nullptr, 1.f, ZG_BF16,
+                              F2, st, "factor_fill", ld2);
+    return rc;
+}
+
+extern "C" int zg_batched_forward_ex(const void* x, const void* W, int w_is_kn, const uint32_t* keys, int group,
+                                     int P, int M, int K, int N, int rank, float s, void* F1T, void* F2, int64_t ld2,
+                                     int draw, int activation, const void* residual, void* y, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    int rc = batched_args_ok("zg_batched_forward_ex", x, W, F1T, F2, y, P, M, K, N, rank);
+    if (rc) return rc;
+    if (draw && !keys) return zg::fail(ZG_ERR_INVALID, "zg_batched_forward_ex: null keys");
+    if (activation != ZG_ACT_NONE && activation != ZG_ACT_GELU)
+        return zg::fail(ZG_ERR_INVALID, "zg_batched_forward_ex: unknown activation %d", activation);
+    const int64_t q = (int64_t)P * rank;
+    if (ld2 != 0 && (ld2 < q || ld2 % 8))
+        return zg::fail(ZG_ERR_INVALID, "zg_batched_forward_ex: ld2 must be 0 or a multiple of 8 >= P*rank");
+    if ((reinterpret_cast<uintptr_t>(F2) & 15) || (residual && (reinterpret_cast<uintptr_t>(residual) & 15)))
+        return zg::fail(ZG_ERR_INVALID, "zg_batched_forward_ex: F2 and the residual must be 16-byte aligned");
+    const size_t need = zg::batched_forward_workspace(P, M, K, N, rank, false);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_batched_forward_ex: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    const bool kn = w_is_kn != 0;
+    return zg::batched_forward(x, W, kn, keys, group, kn ? 0 : 1, kn ? 1 : 0, kn ? 1 : 0, draw != 0, F1T, F2, P, M, K,
+                               N, rank, s, y, cv, zg::as_stream(stream), ld2, activation, residual);
 }
 
 extern "C" size_t zg_replay_operands_workspace_size(int P, int64_t rows, int rank) {
