@@ -108,9 +108,31 @@ def rms_norm(x: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6) -> torch.T
     return _rms_norm_op(x, scale, float(eps))
 
 
+def _row_pitch(t: torch.Tensor) -> int | None:
+    """Elements between consecutive sequence positions of a [..., S, H, D]
+    tensor whose heads are contiguous and whose leading axes collapse into
+    one axis of S-position blocks (a view into a fused q/k/v projection
+    [..., S, 3, H, D] qualifies); None otherwise."""
+    S, H, D = (int(d) for d in t.shape[-3:])
+    st = t.stride()
+    if st[-1] != 1 or (H > 1 and st[-2] != D):
+        return None
+    ld = st[-3] if S > 1 else H * D
+    if ld < H * D:
+        return None
+    block = S * ld
+    for d in range(t.ndim - 4, -1, -1):
+        if t.shape[d] > 1 and st[d] != block:
+            return None
+        block *= t.shape[d]
+    return ld
+
+
 def launch_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool) -> torch.Tensor:
     """softmax(q kᵀ / √D) v over [..., S, H, D] tensors (leading axes: the
-    candidates and batch rows), one launch."""
+    candidates and batch rows), one launch.  q, k and v may be views with a
+    common row pitch (three slices of a fused q/k/v projection); the output
+    is contiguous."""
     dev = L.require_cuda(q, k, v)
     if q.ndim < 3 or tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
         raise ValueError("q, k and v must share one [..., S, H, D] shape")
@@ -118,10 +140,16 @@ def launch_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: 
     L.dtype_code(dt)
     S, H, D = (int(d) for d in q.shape[-3:])
     Z = math.prod(q.shape[:-3])
-    q, k, v = q.contiguous(), _as(k, dt).contiguous(), _as(v, dt).contiguous()
-    o = torch.empty_like(q)
-    L.call("zg_attention", L.ptr(q), L.ptr(k), L.ptr(v), Z, S, H, D, int(bool(causal)), L.dtype_code(dt), L.ptr(o),
-           L.stream_ptr(dev))
+    k, v = _as(k, dt), _as(v, dt)
+    pitches = {_row_pitch(t) for t in (q, k, v)}
+    if len(pitches) != 1 or None in pitches:
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        ld = H * D
+    else:
+        ld = pitches.pop()
+    o = torch.empty(q.shape, dtype=dt, device=dev)
+    L.call("zg_attention_ex", L.ptr(q), L.ptr(k), L.ptr(v), ld, Z, S, H, D, int(bool(causal)), L.dtype_code(dt),
+           L.ptr(o), L.stream_ptr(dev))
     return o
 
 

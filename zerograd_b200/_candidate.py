@@ -70,14 +70,24 @@ class CandidateContext:
     def _group(self, path: ParameterPath) -> int:
         return self.manifest.group_index(self.manifest.entry(path).group)
 
-    def linear(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor) -> torch.Tensor:
+    def linear(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor, *, activation: str | None = None,
+               residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``x @ W + s (x @ A) @ B`` of the candidate (``_candidate.py:61-66``).
+
+        Keyword additions to the reference's signature: ``activation="gelu"``
+        returns ``zerograd_b200.gelu(y)`` and ``residual=r`` returns
+        ``r + y`` (after the activation), with the roundings of those
+        separate ops; on the tensor-core path for a per-candidate bf16
+        input they run in the GEMM's epilogue, so the pre-activation output
+        is never written."""
         entry = self.manifest.entry(path)
         if entry.layout is not ParameterLayout.MATRIX:
             raise ValueError(f"{'.'.join(path)} is not a matrix entry")
         weight = self.manifest.resolve(params, path)
         if weight.ndim != 2 or x.shape[-1] != weight.shape[0]:
             raise ValueError("linear input and [in, out] weight shapes are incompatible")
-        return _ops.linear(x, weight, self.candidate_key, self._group(path), self.rank, self.sigma)
+        return _ops.linear(x, weight, self.candidate_key, self._group(path), self.rank, self.sigma,
+                           activation=activation, residual=residual)
 
     def table_lookup(self, params: ParameterTree, path: ParameterPath, indices: torch.Tensor) -> torch.Tensor:
         entry = self.manifest.entry(path)
@@ -98,20 +108,24 @@ class CandidateContext:
         return _ops.tied_logits(x, table, self.candidate_key, self._group(path), self.rank, self.sigma)
 
     def tied_logits_cross_entropy(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor,
-                                  labels: torch.Tensor) -> torch.Tensor:
+                                  labels: torch.Tensor, *, reduction: str = "none") -> torch.Tensor:
         """Per-row softmax cross-entropy of ``tied_logits(params, path, x)``
         against integer ``labels`` (float32, shape of x without its last axis),
         computed without materialising the [rows, vocabulary] logits: the
         logits are the bf16 values tied_logits returns, the log-sum-exp runs
-        in float32.  An addition to the reference's context (which leaves the
-        cross-entropy to the loss function); bf16 tables, rank 8 or 16."""
+        in float32.  ``reduction="mean"`` returns the mean over the rows
+        (float64 accumulation in a fixed order, so a candidate's loss does not
+        depend on how many candidates are evaluated with it).  An addition to
+        the reference's context (which leaves the cross-entropy to the loss
+        function); bf16 tables, rank 8 or 16."""
         entry = self.manifest.entry(path)
         if entry.layout is not ParameterLayout.TABLE:
             raise ValueError(f"{'.'.join(path)} is not a table entry")
         table = self.manifest.resolve(params, path)
         if table.ndim != 2 or x.shape[-1] != table.shape[1]:
             raise ValueError("logit input and [rows, cols] table shapes are incompatible")
-        return _ops.tied_logits_ce(x, table, labels, self.candidate_key, self._group(path), self.rank, self.sigma)
+        return _ops.tied_logits_ce(x, table, labels, self.candidate_key, self._group(path), self.rank, self.sigma,
+                                   reduction)
 
     def vector(self, params: ParameterTree, path: ParameterPath) -> torch.Tensor:
         entry = self.manifest.entry(path)

@@ -128,27 +128,36 @@ class CapturedGeneration:
         self._opt_state = opt_state0
 
         # warm-up outside the graph: first-call setup (kernel attributes, the
-        # factor-cache budget, the communicator) must not happen in a capture
+        # factor-cache budget, the communicator) must not happen in a capture.
+        # The warm-up also shows which factor layout the forward draws for
+        # each entry (a shared-input op's operand layout, or a per-candidate
+        # input's, "t"): the layout drawn ahead below.
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for i in range(max(1, warmup)):
-                self._set_inputs(g0 + i, opt_state0, 0, False)
-                self._generation(g0 + i, self._slot_state(opt_state0, 0), 0, copy_back=False)
+        _ops.CACHE.log = []
+        try:
+            with torch.cuda.stream(side):
+                for i in range(max(1, warmup)):
+                    self._set_inputs(g0 + i, opt_state0, 0, False)
+                    self._generation(g0 + i, self._slot_state(opt_state0, 0), 0, copy_back=False)
+            forward_keys = list(_ops.CACHE.log)
+        finally:
+            _ops.CACHE.log = None
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
+        t_entries = {k[3:8] for k in forward_keys if len(k) == 9 and k[8] == _ops._T_TAG}
 
         # factors drawn one generation ahead (two slots): per slot, one
-        # (A_op, B_op) buffer pair per bf16 MATRIX/TABLE leaf
+        # buffer pair per bf16 MATRIX/TABLE leaf, in the layout its forward
+        # reads ((A_op, B_op), or the per-candidate-input (F1T, F2) pair)
         self._entries = []
         if slots == 2 and draw_ahead and torch.cuda.get_device_capability(dev) == (10, 0):
-            self._entries = optimizer._factor_entries(self._params)
-            need = sum((rows + cols) * P * rank * 2 for _, _, rows, cols, rank in self._entries)
+            self._entries = [e + ((_ops._T_TAG,) if e in t_entries and e[4] in (8, 16) else ())
+                             for e in optimizer._factor_entries(self._params)]
+            need = sum((e[2] + e[3]) * P * e[4] * 2 for e in self._entries)
             if need > _ops.CACHE._budget(dev):
                 self._entries = []  # over the factor-cache budget: drawn in the generation, as eagerly
-        self._fbuf = [[(torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev),
-                        torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev))
-                       for _, _, rows, cols, rank in self._entries] for _ in range(slots)]
+        self._fbuf = [[self._factor_buffers(e) for e in self._entries] for _ in range(slots)]
         self._draw_stream = torch.cuda.Stream(dev)
         self._drawn: list = [None] * slots  # generation whose factors each slot's buffers hold
         self._draw_done = [torch.cuda.Event() for _ in range(slots)]  # draws into the slot's buffers done
@@ -164,6 +173,7 @@ class CapturedGeneration:
             for e, bufs in zip(self._entries, self._fbuf[slot]):
                 # the forward and the replay read the slot's factor buffers
                 _ops.CACHE.put((base0, 0, P) + e, bufs, dev)
+                _ops.CACHE.mark_drawn((base0, 0, P) + e)
             n0 = L.launch_count()
             with torch.cuda.graph(graph, pool=pool):
                 capture_stream = L.stream_ptr(dev).value
@@ -198,14 +208,33 @@ class CapturedGeneration:
         self._free = [torch.cuda.Event() for _ in range(slots)]  # slot's last replay done
         self._next = 0
 
+    def _factor_buffers(self, e):
+        """A buffer pair for entry `e` = (group, layout, rows, cols, rank[,
+        "t"]) of the whole population, in the factor cache's (A, B) order."""
+        P, dev = self._opt.population_size, self.device
+        _, layout, rows, cols, rank = e[:5]
+        if len(e) == 6:  # per-candidate-input layout
+            k_rows, n_rows = (rows, cols) if layout == L.ZG_MATRIX else (cols, rows)
+            F1T = torch.empty((P * rank, k_rows), dtype=torch.bfloat16, device=dev)
+            F2 = torch.empty((n_rows, P * rank), dtype=torch.bfloat16, device=dev)
+            return (F1T, F2) if layout == L.ZG_MATRIX else (F2, F1T)
+        return (torch.empty((rows, P * rank), dtype=torch.bfloat16, device=dev),
+                torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev))
+
     def _draw(self, base: torch.Tensor, bufs) -> None:
-        """Every entry's operand factors, for the whole population of the
-        generation with base key `base`, into `bufs` (current stream)."""
+        """Every entry's factors, for the whole population of the generation
+        with base key `base`, into `bufs` (current stream)."""
         cks = _ops.launch_fold_in(base, self._ids)
         P = self._opt.population_size
-        for (group, layout, rows, cols, rank), (A, B) in zip(self._entries, bufs):
-            L.call("zg_factor_operands", L.ptr(cks), group, P, layout, rows, cols, rank, L.ZG_BF16, L.ptr(A),
-                   L.ptr(B), L.stream_ptr(self.device))
+        for e, (A, B) in zip(self._entries, bufs):
+            group, layout, rows, cols, rank = e[:5]
+            if len(e) == 6:
+                F1T, F2 = (A, B) if layout == L.ZG_MATRIX else (B, A)
+                L.call("zg_factor_operands_t", L.ptr(cks), group, P, layout, rows, cols, rank, L.ptr(F1T), L.ptr(F2),
+                       0, L.stream_ptr(self.device))
+            else:
+                L.call("zg_factor_operands", L.ptr(cks), group, P, layout, rows, cols, rank, L.ZG_BF16, L.ptr(A),
+                       L.ptr(B), L.stream_ptr(self.device))
 
     def _slot_state(self, opt_state, slot: int):
         """The optimizer state a slot's graph reads: AdamW's bias corrections

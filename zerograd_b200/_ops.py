@@ -150,10 +150,31 @@ def launch_factors(keys: torch.Tensor, group: int, layout: int, shape, rank: int
 
 
 class _Generation:
-    """The candidate keys of one generation being evaluated by ZeroGrad."""
+    """The candidate keys of one generation being evaluated by ZeroGrad.
 
-    def __init__(self, base: tuple, start: int, count: int, cks: torch.Tensor):
+    `pop` = (start, count) of the id range whose factors are kept for the
+    replay; a chunk of that range (ids start..start+count) draws its block
+    of the range's factor buffers and reads it from there.  By default the
+    range is the chunk itself."""
+
+    def __init__(self, base: tuple, start: int, count: int, cks: torch.Tensor, pop: tuple | None = None):
         self.base, self.start, self.count, self.cks = base, start, count, cks
+        self.pop_start, self.pop_count = pop if pop is not None else (start, count)
+
+
+def _capturing() -> bool:
+    """True while the current CUDA stream is being captured into a graph."""
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
+class _AllChunks(set):
+    """The drawn-chunk record of buffers drawn whole (every chunk is in)."""
+
+    def __contains__(self, item) -> bool:
+        return True
+
+
+ALL_DRAWN = _AllChunks()
 
 
 class FactorCache:
@@ -167,7 +188,9 @@ class FactorCache:
         self.budget_bytes = budget_bytes
         self._entries: dict = {}
         self._ready: dict = {}  # key -> event: entry drawn on another stream, not yet waited for
+        self._drawn: dict = {}  # key -> set of (start, count) chunks of an id range's buffers drawn so far
         self._bytes = 0
+        self.log: list | None = None  # when a list: every key put is appended (a capture learns the layouts)
         self.hits = 0
         self.misses = 0
         self._active: _Generation | None = None
@@ -218,40 +241,76 @@ class FactorCache:
             if (len(key) == 3 + len(tail) and key[0] == base and key[1] == 0 and key[2] >= start + count
                     and key[3:] == tail):
                 ev = self._ready.get(key)
-                if ev is not None and not torch.cuda.is_current_stream_capturing() and not ev.query():
+                if ev is not None and not _capturing() and not ev.query():
                     # still being drawn on another stream (a replay prefetch
-                    # that overlaps this forward): the shard draws its own
-                    # rather than wait for the whole population's
-                    return None
+                    # that overlaps this forward): look for one that is
+                    # ready; without one the shard draws its own rather
+                    # than wait for the whole population's
+                    continue
                 return key[2], self.get(key)
         return None
 
     def __contains__(self, key) -> bool:
         return key in self._entries
 
-    def put(self, key, value, device, ready=None) -> None:
+    def put(self, key, value, device, ready=None) -> bool:
+        """Keep `value` under `key` within the budget (oldest entries go
+        first); False when it alone exceeds the budget and is not kept."""
         nbytes = sum(t.numel() * t.element_size() for t in value)
         budget = self._budget(device)
         while self._entries and self._bytes + nbytes > budget:
-            old_key = next(iter(self._entries))
-            old = self._entries.pop(old_key)
-            self._ready.pop(old_key, None)
-            self._bytes -= sum(t.numel() * t.element_size() for t in old)
+            self._pop(next(iter(self._entries)))
+        if self.log is not None:
+            self.log.append(key)
         if nbytes <= budget:
             self._entries[key] = value
             self._bytes += nbytes
             if ready is not None:
                 self._ready[key] = ready
+            return True
+        return False
+
+    def _pop(self, key):
+        old = self._entries.pop(key)
+        self._ready.pop(key, None)
+        self._drawn.pop(key, None)
+        self._bytes -= sum(t.numel() * t.element_size() for t in old)
+        return old
+
+    def range_buffers(self, key, make, device):
+        """(value, drawn chunks) of the factor buffers of an id range, made
+        by `make()` and kept on first use; the caller records the chunks it
+        draws into them in the returned set."""
+        hit = self.get(key)
+        if hit is None:
+            hit = make()
+            if not self.put(key, hit, device):
+                return hit, set()
+        return hit, self._drawn.setdefault(key, set())
+
+    def mark_drawn(self, key) -> None:
+        """Record that the buffers under `key` hold every candidate's factors."""
+        if key in self._entries:
+            self._drawn[key] = ALL_DRAWN
+
+    def covering_drawn(self, base: tuple, start: int, count: int, tail: tuple):
+        """(n, value) of buffers of candidates 0..n of the generation `base`,
+        drawn whole, that cover candidates start..start+count (same `tail`),
+        or None.  A shard's (or chunk's) forward reads its block of them."""
+        for key in list(self._entries):
+            if (len(key) == 3 + len(tail) and key[0] == base and key[1] == 0 and key[2] >= start + count
+                    and key[3:] == tail and self._drawn.get(key) is ALL_DRAWN):
+                return key[2], self.get(key)
+        return None
 
     def drop_generation(self, base: tuple) -> None:
         for key in [k for k in self._entries if k[0] == base]:
-            old = self._entries.pop(key)
-            self._ready.pop(key, None)
-            self._bytes -= sum(t.numel() * t.element_size() for t in old)
+            self._pop(key)
 
     def clear(self) -> None:
         self._entries.clear()
         self._ready.clear()
+        self._drawn.clear()
         self._bytes = 0
 
 
@@ -262,8 +321,9 @@ class generation_scope:
     """Context manager marking `cks` as the keys of candidates start..start+count
     of the generation with base key words `base` (used by ZeroGrad)."""
 
-    def __init__(self, base: tuple, start: int, count: int, cks: torch.Tensor, cache: FactorCache = CACHE):
-        self.gen = _Generation(base, start, count, cks)
+    def __init__(self, base: tuple, start: int, count: int, cks: torch.Tensor, cache: FactorCache = CACHE,
+                 pop: tuple | None = None):
+        self.gen = _Generation(base, start, count, cks, pop)
         self.cache = cache
 
     def __enter__(self):
@@ -393,32 +453,87 @@ def _batched_ok(dev: torch.device, P: int, K: int, N: int, rank: int) -> bool:
     return torch.cuda.get_device_capability(dev) == (10, 0) and rank in (8, 16) and K % 8 == 0 and N % 8 == 0
 
 
+def _range_factors(gen: _Generation, key_tail: tuple, q_rows: int, n_rows: int, rank: int, dev,
+                   cache: FactorCache = CACHE):
+    """(F1T, F2, ld2, draw) for the candidates of `gen` in the per-candidate-
+    input layout: F1T [count r, q_rows] rows and F2 [n_rows, count r] columns
+    of the factor buffers of gen's id range (F1T [Pp r, q_rows], F2 [n_rows,
+    Pp r], kept in the cache in the replay's (A, B) order: MATRIX (F1T, F2),
+    tied TABLE (F2, F1T)), and whether this chunk still has to draw them."""
+    Pp = gen.pop_count
+    key = (gen.base, gen.pop_start, gen.pop_count) + key_tail
+    if key not in cache:
+        # the whole population's buffers, drawn already (a generation drawn
+        # ahead): read this chunk's block of them
+        cover = cache.covering_drawn(gen.base, gen.start, gen.count, key_tail)
+        if cover is not None:
+            n, val = cover
+            F1T_all, F2_all = val if key_tail[1] == L.ZG_MATRIX else (val[1], val[0])
+            return (F1T_all[gen.start * rank:(gen.start + gen.count) * rank], F2_all[:, gen.start * rank:],
+                    n * rank, False)
+
+    def make():
+        F1T = torch.empty((Pp * rank, q_rows), dtype=torch.bfloat16, device=dev)
+        F2 = torch.empty((n_rows, Pp * rank), dtype=torch.bfloat16, device=dev)
+        return (F1T, F2) if key_tail[1] == L.ZG_MATRIX else (F2, F1T)
+
+    val, drawn = cache.range_buffers(key, make, dev)
+    F1T_all, F2_all = val if key_tail[1] == L.ZG_MATRIX else (val[1], val[0])
+    off = gen.start - gen.pop_start
+    F1T = F1T_all[off * rank:(off + gen.count) * rank]
+    F2 = F2_all[:, off * rank:]
+    chunk = (gen.start, gen.count)
+    draw = chunk not in drawn
+    drawn.add(chunk)
+    return F1T, F2, Pp * rank, draw
+
+
 def _forward_batched(x, W, w_is_kn: bool, keys, group, layout, rows, cols, P, M, K, N, rank, s, y, gen,
-                     cache: FactorCache = CACHE):
-    """Per-candidate-input forward (x [P, M, K]) on the tensor cores whose
-    factors (F1T [P r, K] K-major, F2 [N, P r]) are kept in the cache for the
-    generation's replay, stored in the replay's (A, B) order."""
+                     cache: FactorCache = CACHE, act: int = 0, res: torch.Tensor | None = None):
+    """Per-candidate-input forward (x [P, M, K]) on the tensor cores.  Its
+    factors (F1T [P r, K] K-major, F2 [N, P r]) are the candidates' block of
+    the buffers of gen's id range, drawn by the first op of each chunk that
+    uses them and kept in the cache for the generation's replay, in the
+    replay's (A, B) order.  `act` / `res`: the epilogue's activation and
+    residual (zg_batched_forward_ex)."""
     dev = x.device
     ws = L.workspace(L.query("zg_batched_forward_workspace_size", P, M, K, N, rank), dev)
-    ckey = (gen.base, gen.start, gen.count, group, layout, rows, cols, rank, _T_TAG)
-    hit = cache.get(ckey)
-    if hit is not None:
-        F1T, F2 = hit if w_is_kn else (hit[1], hit[0])
-        L.call("zg_batched_forward_factors", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(F1T), L.ptr(F2), P, M, K, N,
-               rank, s, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
-        return
-    F1T = torch.empty((P * rank, K), dtype=torch.bfloat16, device=dev)
-    F2 = torch.empty((N, P * rank), dtype=torch.bfloat16, device=dev)
-    L.call("zg_batched_forward_operands", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(_keys2d(keys)), group, P, M, K,
-           N, rank, s, L.ptr(F1T), L.ptr(F2), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
-    # MATRIX: A^T = F1T, B_op = F2;  tied TABLE: A_op = F2, B^T = F1T
-    cache.put(ckey, (F1T, F2) if w_is_kn else (F2, F1T), dev)
+    F1T, F2, ld2, draw = _range_factors(gen, (group, layout, rows, cols, rank, _T_TAG), K, N, rank, dev, cache)
+    L.call("zg_batched_forward_ex", L.ptr(x), L.ptr(W), int(w_is_kn), L.ptr(_keys2d(keys)), group, P, M, K, N, rank,
+           s, L.ptr(F1T), L.ptr(F2), ld2, int(draw), int(act), L.ptr(res), L.ptr(y), L.ptr(ws), ws.numel(),
+           L.stream_ptr(dev))
+
+
+ACTIVATIONS = {None: L.ZG_ACT_NONE, "none": L.ZG_ACT_NONE, "gelu": L.ZG_ACT_GELU}
+
+
+def launch_gelu(x: torch.Tensor) -> torch.Tensor:
+    """Element-wise GELU (tanh form) of a float32 or bf16 tensor."""
+    dev = L.require_cuda(x)
+    xc = x.contiguous()
+    y = torch.empty_like(xc)
+    L.call("zg_gelu", L.ptr(xc), L.ptr(y), xc.numel(), L.dtype_code(xc.dtype), L.stream_ptr(dev))
+    return y
+
+
+def _epilogue_unfused(y: torch.Tensor, act: int, res: torch.Tensor | None) -> torch.Tensor:
+    """The activation and residual of a linear whose kernel has no fused
+    epilogue: the same roundings as the fused one (bf16 / float32 result,
+    element-wise GELU, then the residual add in the result's dtype)."""
+    if act == L.ZG_ACT_GELU:
+        y = launch_gelu(y)
+    if res is not None:
+        y = res.to(y.dtype) + y
+    return y
 
 
 def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
-                  sigma: float, x_batched: bool) -> torch.Tensor:
-    """y[p] = x_p @ W + s (x_p @ A_p) @ B_p; x [*M, K] shared or [P, *M, K]."""
-    dev = L.require_cuda(x, weight, keys)
+                  sigma: float, x_batched: bool, act: int = 0, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """y[p] = x_p @ W + s (x_p @ A_p) @ B_p; x [*M, K] shared or [P, *M, K].
+    `act` (ZG_ACT_*) and `residual` ([P, *M, N]): y = act(y) + residual with
+    the unfused ops' roundings, fused into the GEMM's epilogue on the
+    per-candidate-input tensor-core path."""
+    dev = L.require_cuda(x, weight, keys, residual)
     k = _keys2d(keys)
     P = k.shape[0]
     if weight.ndim != 2 or x.ndim < 1 or x.shape[-1] != weight.shape[0]:
@@ -432,21 +547,31 @@ def launch_linear(x: torch.Tensor, weight: torch.Tensor, keys: torch.Tensor, gro
     mshape = tuple(x.shape[1:-1] if x_batched else x.shape[:-1])
     M = math.prod(mshape)
     y = torch.empty((P, *mshape, N), dtype=dt, device=dev)
+    if residual is not None and tuple(residual.shape) != tuple(y.shape):
+        raise ValueError(f"residual of shape {tuple(residual.shape)} does not match the output {tuple(y.shape)}")
     if M == 0:
         return y
     s = scaled_factor_value(rank, sigma, weight.dtype)
     code = L.dtype_code(dt)
     gen = CACHE.active_for(keys)
+    if x_batched and dt == torch.bfloat16 and _batched_ok(dev, P, K, N, rank):
+        res = None if residual is None else residual.to(dt).contiguous()
+        if gen is None:
+            # outside a generation (a direct call): a one-off range of these candidates
+            _forward_batched(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y,
+                             _Generation((-1, -1, id(k)), 0, P, k), cache=FactorCache(budget_bytes=0), act=act,
+                             res=res)
+        else:
+            _forward_batched(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y, gen, act=act,
+                             res=res)
+        return y
     if gen is not None and dt == torch.bfloat16 and not x_batched and _tc_ok(dev, P, K, N, rank):
         _forward_cached(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y, gen)
-        return y
-    if gen is not None and dt == torch.bfloat16 and x_batched and _batched_ok(dev, P, K, N, rank):
-        _forward_batched(x, W, True, k, group, L.ZG_MATRIX, K, N, P, M, K, N, rank, s, y, gen)
-        return y
+        return _epilogue_unfused(y, act, residual)
     ws = L.workspace(L.query("zg_perturbed_linear_workspace_size", P, M, K, N, rank, code, int(x_batched)), dev)
     L.call("zg_perturbed_linear", L.ptr(x), int(x_batched), L.ptr(W), L.ptr(k), group, P, M, K, N, rank, s,
            code, L.ptr(y), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
-    return y
+    return _epilogue_unfused(y, act, residual)
 
 
 def launch_tied_logits(x: torch.Tensor, table: torch.Tensor, keys: torch.Tensor, group: int, rank: int,
@@ -508,6 +633,16 @@ def launch_tied_logits_ce(x: torch.Tensor, table: torch.Tensor, labels: torch.Te
         return loss
     s = scaled_factor_value(rank, sigma, table.dtype)
     lab = labels.to(torch.int32).contiguous()
+    gen = CACHE.active_for(keys)
+    if gen is not None and group >= 0:
+        # the table's factors in the per-candidate-input layout (F2 = A_op,
+        # F1T = B^T): this chunk's block of its id range's buffers, kept for
+        # the replay like a batched tied_logits'
+        F1T, F2, ld2, draw = _range_factors(gen, (group, L.ZG_TABLE, V, C, rank, _T_TAG), C, V, rank, dev)
+        ws = L.workspace(L.query("zg_tied_logits_ce_ex_workspace_size", P, M, V, C, rank), dev)
+        L.call("zg_tied_logits_ce_ex", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, L.ptr(lab), P, M, V, C,
+               rank, s, L.ptr(F1T), L.ptr(F2), ld2, int(draw), L.ptr(loss), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
+        return loss
     ws = L.workspace(L.query("zg_tied_logits_ce_workspace_size", P, M, V, C, rank), dev)
     L.call("zg_tied_logits_ce", L.ptr(x), int(x_batched), L.ptr(T), L.ptr(k), group, L.ptr(lab), P, M, V, C, rank,
            s, L.ptr(loss), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
@@ -762,19 +897,30 @@ def fold_in(key: torch.Tensor, data) -> torch.Tensor:
 
 @torch.library.custom_op(f"{_NS}::linear", mutates_args=())
 def _linear_op(x: torch.Tensor, weight: torch.Tensor, key: torch.Tensor, group: int, rank: int,
-               sigma: float) -> torch.Tensor:
-    return launch_linear(x, weight, key.reshape(1, 2), group, rank, sigma, False)[0]
+               sigma: float, act: int, residual: torch.Tensor | None) -> torch.Tensor:
+    res = None if residual is None else residual.unsqueeze(0)
+    return launch_linear(x, weight, key.reshape(1, 2), group, rank, sigma, False, act, res)[0]
 
 
 @torch.library.register_vmap(f"{_NS}::linear")
-def _linear_vmap(info, in_dims, x, weight, key, group, rank, sigma):
+def _linear_vmap(info, in_dims, x, weight, key, group, rank, sigma, act, residual):
     xd, wd, kd = in_dims[:3]
+    rd = in_dims[7]
     if wd is not None:
         raise NotImplementedError("weights batched over candidates are not supported")
     x = _movedim0(x, xd)
     if kd is None:
-        return launch_linear(x, weight, key.reshape(1, 2), group, rank, sigma, False)[0], 0
-    return launch_linear(x, weight, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
+        # one key for every batch row: a single candidate's op over the rows
+        y = _epilogue_unfused(launch_linear(x, weight, key.reshape(1, 2), group, rank, sigma, False)[0], act, None)
+        if residual is not None:
+            y = _movedim0(residual, rd).to(y.dtype) + y if rd is not None else residual.to(y.dtype) + y
+        return y, 0
+    keys = _movedim0(key, kd)
+    P = keys.shape[0]
+    res = None
+    if residual is not None:
+        res = _movedim0(residual, rd) if rd is not None else residual.unsqueeze(0).expand(P, *residual.shape)
+    return launch_linear(x, weight, keys, group, rank, sigma, xd is not None, act, res), 0
 
 
 @torch.library.custom_op(f"{_NS}::tied_logits", mutates_args=())
@@ -794,21 +940,37 @@ def _tied_vmap(info, in_dims, x, table, key, group, rank, sigma):
     return launch_tied_logits(x, table, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
 
 
+def launch_row_mean(x: torch.Tensor) -> torch.Tensor:
+    """[P, ...] float32 -> [P]: each leading row's mean, float64 accumulation
+    in a fixed order (independent of P)."""
+    dev = L.require_cuda(x)
+    x2 = x.to(torch.float32).reshape(x.shape[0], -1).contiguous()
+    out = torch.empty(x.shape[0], dtype=torch.float32, device=dev)
+    L.call("zg_row_mean", L.ptr(x2), x2.shape[0], x2.shape[1], L.ptr(out), L.stream_ptr(dev))
+    return out
+
+
+def _ce_reduce(loss: torch.Tensor, mean: bool) -> torch.Tensor:
+    return launch_row_mean(loss) if mean else loss
+
+
 @torch.library.custom_op(f"{_NS}::tied_logits_ce", mutates_args=())
 def _tied_ce_op(x: torch.Tensor, table: torch.Tensor, labels: torch.Tensor, key: torch.Tensor, group: int,
-                rank: int, sigma: float) -> torch.Tensor:
-    return launch_tied_logits_ce(x, table, labels, key.reshape(1, 2), group, rank, sigma, False)[0]
+                rank: int, sigma: float, mean: bool) -> torch.Tensor:
+    return _ce_reduce(launch_tied_logits_ce(x, table, labels, key.reshape(1, 2), group, rank, sigma, False), mean)[0]
 
 
 @torch.library.register_vmap(f"{_NS}::tied_logits_ce")
-def _tied_ce_vmap(info, in_dims, x, table, labels, key, group, rank, sigma):
+def _tied_ce_vmap(info, in_dims, x, table, labels, key, group, rank, sigma, mean):
     xd, td, ld, kd = in_dims[:4]
     if td is not None or ld is not None:
         raise NotImplementedError("tables and labels batched over candidates are not supported")
     x = _movedim0(x, xd)
     if kd is None:
-        return launch_tied_logits_ce(x, table, labels, key.reshape(1, 2), group, rank, sigma, False)[0], 0
-    return launch_tied_logits_ce(x, table, labels, _movedim0(key, kd), group, rank, sigma, xd is not None), 0
+        out = _ce_reduce(launch_tied_logits_ce(x, table, labels, key.reshape(1, 2), group, rank, sigma, False), mean)
+        return out[0], None
+    return _ce_reduce(launch_tied_logits_ce(x, table, labels, _movedim0(key, kd), group, rank, sigma, xd is not None),
+                      mean), 0
 
 
 @torch.library.custom_op(f"{_NS}::table_lookup", mutates_args=())
@@ -865,16 +1027,38 @@ def _bits_vmap(info, in_dims, key, n):
     return launch_bits(_movedim0(key, in_dims[0]), n), 0
 
 
-def linear(x, weight, key, group, rank, sigma):
-    return _linear_op(x, weight, key, int(group), int(rank), float(sigma))
+def linear(x, weight, key, group, rank, sigma, activation=None, residual=None):
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"unknown activation {activation!r}: expected one of None, 'gelu'")
+    return _linear_op(x, weight, key, int(group), int(rank), float(sigma), ACTIVATIONS[activation], residual)
+
+
+@torch.library.custom_op(f"{_NS}::gelu", mutates_args=())
+def _gelu_op(x: torch.Tensor) -> torch.Tensor:
+    return launch_gelu(x)
+
+
+@torch.library.register_vmap(f"{_NS}::gelu")
+def _gelu_vmap(info, in_dims, x):
+    return launch_gelu(x), in_dims[0]
+
+
+def gelu(x: torch.Tensor) -> torch.Tensor:
+    """GELU in its tanh form, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+    (the form GPT-2 uses), element-wise in float32, rounded to x's dtype;
+    the same values as ``CandidateContext.linear(..., activation="gelu")``
+    produces in its epilogue."""
+    return _gelu_op(x)
 
 
 def tied_logits(x, table, key, group, rank, sigma):
     return _tied_op(x, table, key, int(group), int(rank), float(sigma))
 
 
-def tied_logits_ce(x, table, labels, key, group, rank, sigma):
-    return _tied_ce_op(x, table, labels, key, int(group), int(rank), float(sigma))
+def tied_logits_ce(x, table, labels, key, group, rank, sigma, reduction="none"):
+    if reduction not in ("none", "mean"):
+        raise ValueError(f"reduction must be 'none' or 'mean', got {reduction!r}")
+    return _tied_ce_op(x, table, labels, key, int(group), int(rank), float(sigma), reduction == "mean")
 
 
 def table_lookup(table, indices, key, group, rank, sigma):

@@ -62,7 +62,14 @@ class ZeroGrad:
     """Factor-only ES optimizer (``_optimizer.py:44-277``)."""
 
     def __init__(self, manifest: Manifest, transform, population_size: int, rank: int, sigma: float, seed: int,
-                 run_id: str) -> None:
+                 run_id: str, *, chunk_size: int | None = None) -> None:
+        """``chunk_size`` (an addition to the reference's signature): the
+        candidates of one evaluation run through ``loss_fn`` in chunks of at
+        most this many, so a large population's activations need not fit at
+        once.  Each candidate's factors are still drawn once per generation,
+        chunk by chunk, into buffers of the whole evaluated id range that the
+        replay reads.  None: all candidates at once (the reference's single
+        vmap)."""
         if not isinstance(manifest, Manifest):
             raise TypeError("manifest must be a Manifest")
         if not isinstance(population_size, int) or isinstance(population_size, bool) or population_size < 2:
@@ -75,6 +82,10 @@ class ZeroGrad:
             raise TypeError("seed must be an integer")
         if not isinstance(run_id, str) or not run_id:
             raise ValueError("run_id must be a non-empty string")
+        if chunk_size is not None and (not isinstance(chunk_size, int) or isinstance(chunk_size, bool)
+                                       or chunk_size < 1):
+            raise ValueError("chunk_size must be a positive integer or None")
+        self._chunk_size = chunk_size
         self._manifest = manifest
         self._transform = transform
         self._population_size = population_size
@@ -149,6 +160,10 @@ class ZeroGrad:
     def transform(self):
         return self._transform
 
+    @property
+    def chunk_size(self) -> int | None:
+        return self._chunk_size
+
     # -- evaluation ---------------------------------------------------------
 
     def base_key(self, generation: int) -> torch.Tensor:
@@ -214,8 +229,19 @@ class ZeroGrad:
             self._prefetch_replay(params, generation, base_words, device)
         # A contiguous id range known on the host: the factors drawn by the
         # forward ops are kept for this generation's replay.
-        with _ops.generation_scope(base_words, id_range[0], id_range[1], cks):
-            return torch.func.vmap(evaluate_candidate)(cks, rngs)
+        start, count = id_range
+        chunk = self._chunk_size
+        if chunk is None or count <= chunk:
+            with _ops.generation_scope(base_words, start, count, cks):
+                return torch.func.vmap(evaluate_candidate)(cks, rngs)
+        # In chunks: each chunk's ops draw their block of the range's factor
+        # buffers (kept for the replay) and read it from there.
+        out = []
+        for c0 in range(0, count, chunk):
+            n = min(chunk, count - c0)
+            with _ops.generation_scope(base_words, start + c0, n, cks[c0:c0 + n], pop=(start, count)):
+                out.append(torch.func.vmap(evaluate_candidate)(cks[c0:c0 + n], rngs[c0:c0 + n]))
+        return torch.cat(out)
 
     def _factor_entries(self, params) -> list:
         """(group, layout, rows, cols, rank) of every bf16 MATRIX/TABLE leaf:
