@@ -162,8 +162,15 @@ def test_reduced_lm_generation_matches_oracle(cuda, oracle):
         r = cfg["rank"] if layouts[name] != 2 else 1
         descent = oracle.replay_entry(hp[name].shape, layouts[name], base, range(cfg["P"]), shaped, r, g,
                                       "bfloat16")
-        want_p = hp[name].astype(np.float64) + cfg["lr"] * descent
-        assert_bf16_close(_np(new[name]), want_p, what=name)
+        # the update is a sum over P*r rank-one terms whose weighted factors
+        # are rounded to bf16, so an element's error scales with the terms
+        # (about the update's RMS), not with its possibly cancelling sum:
+        # element-wise rel 2e-2 with the RMS as floor, and 5e-3 in Frobenius norm
+        want_d = cfg["lr"] * descent
+        got_d = _np(new[name]) - hp[name].astype(np.float64)
+        rms = float(np.sqrt(np.mean(want_d ** 2)))
+        assert_bf16_close(got_d, want_d, floor=rms, what=name)
+        assert np.linalg.norm(got_d - want_d) <= 5e-3 * np.linalg.norm(want_d), name
     assert st2.generation == gen + 1 and metrics.population_size == cfg["P"]
 
 
