@@ -16,8 +16,10 @@ cross-entropy (the examples' loss over logits, ``examples/train_cifar10.py:77-78
 Every op restates ``oracle/ref.py``'s (factors from the C threefry
 restatement) and is rounded to bf16 wherever the CUDA path stores a bf16
 tensor, so a comparison measures the kernels' accumulation order, not a
-different model.  `dtype` is the arithmetic: float64 for parity checks,
-float32 for the timed CPU baseline.
+different model.  `dtype` is the arithmetic: float64 for parity checks
+(bf16 storage roundings emulated), float32 for the timed CPU baseline (a
+plain float32 forward, as a CPU implementation computes it: no emulated
+bf16 rounding).
 """
 from __future__ import annotations
 
@@ -29,12 +31,37 @@ from . import ref
 
 
 def gelu_tanh(x):
-    """0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) (Hendrycks & Gimpel)."""
-    return 0.5 * x * (1.0 + np.tanh(math.sqrt(2.0 / math.pi) * (x + 0.044715 * x ** 3)))
+    """0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) (Hendrycks & Gimpel), in x's dtype."""
+    c = x.dtype.type(math.sqrt(2.0 / math.pi))
+    t = x * x
+    t *= x.dtype.type(0.044715)
+    t += 1
+    t *= x
+    t *= c
+    np.tanh(t, out=t)
+    t += 1
+    t *= x
+    t *= x.dtype.type(0.5)
+    return t
 
 
 def _bf16(a, dtype):
+    if dtype == np.float32:
+        return np.asarray(a, np.float32)
     return ref.round_bf16(np.asarray(a, np.float32)).astype(dtype, copy=False)
+
+
+def _attention(q, k, v, dtype):
+    """Causal softmax attention in `dtype` (ref.attention's float64 for parity)."""
+    if dtype != np.float32:
+        return ref.attention(q, k, v, causal=True)
+    qh, kh, vh = (np.swapaxes(t, -3, -2) for t in (q, k, v))
+    s = qh @ np.swapaxes(kh, -1, -2) * np.float32(1.0 / math.sqrt(q.shape[-1]))
+    S = s.shape[-1]
+    s = np.where(np.triu(np.ones((S, S), bool), 1), np.float32(-np.inf), s)
+    s = np.exp(s - s.max(axis=-1, keepdims=True))
+    s /= s.sum(axis=-1, keepdims=True)
+    return np.swapaxes(s @ vh, -3, -2)
 
 
 def candidate_loss(params: dict, entries: list, ck: np.ndarray, cfg: dict, tokens: np.ndarray,
@@ -77,7 +104,7 @@ def candidate_loss(params: dict, entries: list, ck: np.ndarray, cfg: dict, token
         p = f"l{layer}."
         h = rms(x, vec(p + "n1"))
         qkv = linear(p + "qkv", h).reshape(B, T, 3, H, D)
-        a = _bf16(ref.attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], causal=True), dtype)
+        a = _bf16(_attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], dtype), dtype)
         x = linear(p + "o", a.reshape(B, T, E), residual=x)
         h = rms(x, vec(p + "n2"))
         m = linear(p + "fc", h, act="gelu")

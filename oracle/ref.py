@@ -150,13 +150,18 @@ def bits_to_normal(bits: np.ndarray) -> np.ndarray:
 # --------------------------------------------------------------------------
 
 def round_bf16(a: np.ndarray) -> np.ndarray:
-    """float32 -> bfloat16 -> float32 with round-to-nearest-even."""
+    """float32 -> bfloat16 -> float32 with round-to-nearest-even (uint32
+    arithmetic: a finite value's carry runs into the exponent, up to inf)."""
     a = np.ascontiguousarray(a, np.float32)
-    u = a.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    u = a.view(np.uint32)
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    out = r.view(np.float32)
     nan = np.isnan(a)
-    out = r.view(np.float32).copy()
-    out[nan] = np.nan
+    if nan.any():
+        out[nan] = np.nan
     return out
 
 
