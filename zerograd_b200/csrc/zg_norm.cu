@@ -66,70 +66,86 @@ struct NormArgs {
     float eps;
 };
 
-// Row held in registers: CH chunks of 8 values per lane (C <= 256 * CH, C a
-// multiple of 8, rows 16-byte aligned).
-template <typename T, int CH>
-__global__ void norm_reg_kernel(const NormArgs a) {
+// Rows held in registers: CH chunks of 8 values per lane (C <= 256 * CH, C a
+// multiple of 8, rows 16-byte aligned), R rows per warp per pass with every
+// row's loads issued before the first reduction, so a warp keeps R rows of
+// HBM reads in flight (a norm is HBM-bound: its rate is the bytes in flight
+// per SM over the memory latency).
+template <typename T, int CH, int R>
+__global__ void __launch_bounds__(256) norm_reg_kernel(const NormArgs a) {
     const int lane = threadIdx.x % 32;
     const int64_t rows = (int64_t)a.P * a.M;
     const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
     const int64_t nwarps = (int64_t)gridDim.x * blockDim.x / 32;
     const int chunks = a.C / 8;
-    for (int64_t g = warp0; g < rows; g += nwarps) {
-        const int p = (int)(g / a.M);
-        const int64_t m = g % a.M;
-        const T* xr = static_cast<const T*>(a.x) + ((a.x_batched ? (int64_t)p : 0) * a.M + m) * a.C;
-        const T* sr = static_cast<const T*>(a.scale) + (a.p_batched ? (int64_t)p : 0) * a.C;
-        const T* br = a.bias ? static_cast<const T*>(a.bias) + (a.p_batched ? (int64_t)p : 0) * a.C : nullptr;
-        T* yr = static_cast<T*>(a.y) + g * a.C;
-        float v[CH][8];
-        float s1 = 0.f;
+    for (int64_t g0 = warp0 * R; g0 < rows; g0 += nwarps * R) {
+        float v[R][CH][8];
+        float s1[R], s2[R], mean[R], rinv[R];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-            const int c = lane + 32 * j;
-            if (c < chunks) {
-                load8(xr + 8 * c, v[j]);
+        for (int q = 0; q < R; ++q) {
+            const int64_t g = g0 + q;
+            s1[q] = 0.f;
+            if (g >= rows) continue;
+            const int p = (int)(g / a.M);
+            const int64_t m = g % a.M;
+            const T* xr = static_cast<const T*>(a.x) + ((a.x_batched ? (int64_t)p : 0) * a.M + m) * a.C;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) s1 += v[j][i];
+            for (int j = 0; j < CH; ++j) {
+                const int c = lane + 32 * j;
+                if (c < chunks) load8(xr + 8 * c, v[q][j]);
             }
         }
-        float sd;
-        float mean = 0.f;
-        if (a.kind == NORM_LAYER) {
-            mean = __fdiv_rn(warp_sum(s1), (float)a.C);
-            float s2 = 0.f;
 #pragma unroll
-            for (int j = 0; j < CH; ++j)
-                if (lane + 32 * j < chunks)
+        for (int q = 0; q < R; ++q) {
+            mean[q] = 0.f;
+            s2[q] = 0.f;
+            if (a.kind == NORM_LAYER) {
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                    if (lane + 32 * j < chunks)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) s1[q] += v[q][j][i];
+                mean[q] = __fdiv_rn(warp_sum(s1[q]), (float)a.C);
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                    if (lane + 32 * j < chunks)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float d = v[q][j][i] - mean[q];
+                            s2[q] = fmaf(d, d, s2[q]);
+                        }
+            } else {
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                    if (lane + 32 * j < chunks)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) s2[q] = fmaf(v[q][j][i], v[q][j][i], s2[q]);
+            }
+            // one division per row
+            rinv[q] = __fdiv_rn(1.f, __fsqrt_rn(__fdiv_rn(warp_sum(s2[q]), (float)a.C) + a.eps));
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t g = g0 + q;
+            if (g >= rows) continue;
+            const int p = (int)(g / a.M);
+            const T* sr = static_cast<const T*>(a.scale) + (a.p_batched ? (int64_t)p : 0) * a.C;
+            const T* br = a.bias ? static_cast<const T*>(a.bias) + (a.p_batched ? (int64_t)p : 0) * a.C : nullptr;
+            T* yr = static_cast<T*>(a.y) + g * a.C;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+                const int c = lane + 32 * j;
+                if (c < chunks) {
+                    float sc[8], bi[8], o[8];
+                    load8(sr + 8 * c, sc);
+                    if (br) load8(br + 8 * c, bi);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float d = v[j][i] - mean;
-                        s2 = fmaf(d, d, s2);
+                        o[i] = __fmul_rn(__fmul_rn(v[q][j][i] - mean[q], rinv[q]), sc[i]);
+                        if (br) o[i] = __fadd_rn(o[i], bi[i]);
                     }
-            sd = __fsqrt_rn(__fdiv_rn(warp_sum(s2), (float)a.C) + a.eps);
-        } else {
-            float s2 = 0.f;
-#pragma unroll
-            for (int j = 0; j < CH; ++j)
-                if (lane + 32 * j < chunks)
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) s2 = fmaf(v[j][i], v[j][i], s2);
-            sd = __fsqrt_rn(__fdiv_rn(warp_sum(s2), (float)a.C) + a.eps);
-        }
-        const float rinv = __fdiv_rn(1.f, sd);  // one division per row
-#pragma unroll
-        for (int j = 0; j < CH; ++j) {
-            const int c = lane + 32 * j;
-            if (c < chunks) {
-                float sc[8], bi[8], o[8];
-                load8(sr + 8 * c, sc);
-                if (br) load8(br + 8 * c, bi);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    o[i] = __fmul_rn(__fmul_rn(v[j][i] - mean, rinv), sc[i]);
-                    if (br) o[i] = __fadd_rn(o[i], bi[i]);
+                    store8(yr + 8 * c, o);
                 }
-                store8(yr + 8 * c, o);
             }
         }
     }
@@ -187,20 +203,24 @@ int sm_count_norm() {
 template <typename T>
 int launch_norm(const NormArgs& a, cudaStream_t st, const char* name) {
     const int64_t rows = (int64_t)a.P * a.M;
-    int64_t blocks = (rows + 7) / 8;  // 8 warps per block
-    if (blocks > (int64_t)sm_count_norm() * 16) blocks = (int64_t)sm_count_norm() * 16;
-    if (blocks < 1) blocks = 1;
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     const bool vec = a.C % 8 == 0 && al(a.x) && al(a.scale) && (!a.bias || al(a.bias)) && al(a.y);
+    // rows per warp pass: two for the register-resident widths up to 1024
+    const int R = vec && a.C <= 1024 ? 2 : 1;
+    int64_t blocks = (rows + 8 * R - 1) / (8 * R);  // 8 warps per block
+    if (blocks > (int64_t)sm_count_norm() * 16) blocks = (int64_t)sm_count_norm() * 16;
+    if (blocks < 1) blocks = 1;
     zg::LaunchTimer zg_lt_(name, st);
     if (vec && a.C <= 256)
-        norm_reg_kernel<T, 1><<<(unsigned)blocks, 256, 0, st>>>(a);
+        norm_reg_kernel<T, 1, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
     else if (vec && a.C <= 512)
-        norm_reg_kernel<T, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
+        norm_reg_kernel<T, 2, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
+    else if (vec && a.C <= 768)
+        norm_reg_kernel<T, 3, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
     else if (vec && a.C <= 1024)
-        norm_reg_kernel<T, 4><<<(unsigned)blocks, 256, 0, st>>>(a);
+        norm_reg_kernel<T, 4, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
     else if (vec && a.C <= 2048)
-        norm_reg_kernel<T, 8><<<(unsigned)blocks, 256, 0, st>>>(a);
+        norm_reg_kernel<T, 8, 1><<<(unsigned)blocks, 256, 0, st>>>(a);
     else
         norm_any_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(a);
     return zg::check_launch(name);
