@@ -237,33 +237,45 @@ __global__ void shape_fitness_kernel(const float* __restrict__ losses, int P, fl
 
 // ---------------------------------------------------------------------------
 // VECTOR replay: out[i] = sum_p w_p * noise_p[i] (noise regenerated).
+// Candidates are split into slices of VR_SLICE; block (column tile, slice)
+// writes the slice's partial sums, and a second pass adds the slices in
+// order.  The split depends only on (P, n), so the result does too.
 // ---------------------------------------------------------------------------
+constexpr int VR_SLICE = 32, VR_COLS = 128;
+
+inline int vector_replay_slices(int P) { return (P + VR_SLICE - 1) / VR_SLICE; }
+
 template <typename T>
-__global__ void vector_replay_kernel(const float* __restrict__ w, const uint32_t* __restrict__ keys,
-                                     int group, int P, int64_t n, float* __restrict__ out) {
-    constexpr int CH = 1024;
-    __shared__ uint32_t sk[CH][2];
-    __shared__ float sw[CH];
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    float acc = 0.f;
-    for (int p0 = 0; p0 < P; p0 += CH) {
-        const int cnt = min(CH, P - p0);
-        for (int q = threadIdx.x; q < cnt; q += blockDim.x) {
-            ZgKey gk = zg_group_key(keys, p0 + q, group);
-            sk[q][0] = gk.k0; sk[q][1] = gk.k1;
-            sw[q] = w[p0 + q];
-        }
-        __syncthreads();
-        if (i < n) {
-            for (int q = 0; q < cnt; ++q) {
-                ZgKey gk = zg_make_key(sk[q][0], sk[q][1]);
-                float noise = zg_dtype_round<T>(zg_normal(gk, (uint64_t)i));
-                acc = fmaf(noise, sw[q], acc);
-            }
-        }
-        __syncthreads();
+__global__ void vector_replay_partial_kernel(const float* __restrict__ w, const uint32_t* __restrict__ keys, int group,
+                                             int P, int64_t n, float* __restrict__ partial) {
+    __shared__ uint32_t sk[VR_SLICE][2];
+    __shared__ float sw[VR_SLICE];
+    const int64_t i = blockIdx.x * (int64_t)VR_COLS + threadIdx.x;
+    const int p0 = blockIdx.y * VR_SLICE;
+    const int cnt = min(VR_SLICE, P - p0);
+    if ((int)threadIdx.x < cnt) {
+        const ZgKey gk = zg_group_key(keys, p0 + threadIdx.x, group);
+        sk[threadIdx.x][0] = gk.k0;
+        sk[threadIdx.x][1] = gk.k1;
+        sw[threadIdx.x] = w[p0 + threadIdx.x];
     }
-    if (i < n) out[i] = acc;
+    __syncthreads();
+    if (i >= n) return;
+    float acc = 0.f;
+    for (int q = 0; q < cnt; ++q) {
+        const ZgKey gk = zg_make_key(sk[q][0], sk[q][1]);
+        acc = fmaf(zg_dtype_round<T>(zg_normal(gk, (uint64_t)i)), sw[q], acc);
+    }
+    partial[(int64_t)blockIdx.y * n + i] = acc;
+}
+
+__global__ void vector_replay_sum_kernel(const float* __restrict__ partial, int slices, int64_t n,
+                                         float* __restrict__ out) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float acc = 0.f;
+    for (int s = 0; s < slices; ++s) acc += partial[(int64_t)s * n + i];
+    out[i] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -527,7 +539,7 @@ extern "C" int zg_row_mean(const float* x, int64_t rows, int64_t n, float* out, 
 
 extern "C" size_t zg_replay_workspace_size(int P, int layout, int64_t rows, int64_t cols, int rank, int dtype) {
     if (P < 1 || rows < 1 || !zg::dtype_ok(dtype)) return 0;
-    if (layout == ZG_VECTOR) return 256;
+    if (layout == ZG_VECTOR) return Carver::need({(size_t)vector_replay_slices(P) * rows * 4}) + 256;
     if (cols < 1 || rank < 1) return 0;
     size_t es = zg::dtype_size(dtype);
     size_t simt_need = Carver::need({(size_t)P * rows * rank * es, (size_t)P * cols * rank * es});
@@ -544,19 +556,30 @@ extern "C" int zg_replay(const float* shaped, const uint32_t* keys, int group, i
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay: bad dtype");
     if (!shaped || !keys || !out) return zg::fail(ZG_ERR_INVALID, "zg_replay: null pointer");
     cudaStream_t st = zg::as_stream(stream);
-    if (layout == ZG_VECTOR) {
-        int blocks = (int)((rows + 255) / 256);
-        zg::LaunchTimer zg_lt_("replay_vector", st);
-        if (dtype == ZG_BF16)
-            vector_replay_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(shaped, keys, group, P, rows, out);
-        else
-            vector_replay_kernel<float><<<blocks, 256, 0, st>>>(shaped, keys, group, P, rows, out);
-        return zg::check_launch("zg_replay(vector)");
-    }
     size_t need = zg_replay_workspace_size(P, layout, rows, cols, rank, dtype);
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "zg_replay: workspace %zu < %zu bytes", workspace_bytes, need);
     Carver cv(workspace, workspace_bytes);
+    if (layout == ZG_VECTOR) {
+        const int slices = vector_replay_slices(P);
+        float* partial = cv.take<float>((size_t)slices * rows);
+        if (!partial) return zg::fail(ZG_ERR_WORKSPACE, "zg_replay: workspace too small");
+        const int64_t tiles = (rows + VR_COLS - 1) / VR_COLS;
+        if (tiles > 2147483647LL || slices > 65535) return zg::fail(ZG_ERR_INVALID, "zg_replay: vector too long");
+        {
+            zg::LaunchTimer zg_lt_("replay_vector", st);
+            dim3 grid((unsigned)tiles, (unsigned)slices);
+            if (dtype == ZG_BF16)
+                vector_replay_partial_kernel<__nv_bfloat16><<<grid, VR_COLS, 0, st>>>(shaped, keys, group, P, rows,
+                                                                                        partial);
+            else
+                vector_replay_partial_kernel<float><<<grid, VR_COLS, 0, st>>>(shaped, keys, group, P, rows, partial);
+            if (int e = zg::check_launch("zg_replay(vector)")) return e;
+        }
+        zg::LaunchTimer zg_lt2_("replay_vector_sum", st);
+        vector_replay_sum_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(partial, slices, rows, out);
+        return zg::check_launch("zg_replay(vector sum)");
+    }
     if (zg::tc_replay_ok(P, rows, cols, rank, dtype))
         return zg::tc_replay_run(shaped, keys, group, P, layout, rows, cols, rank, inv_sqrt_rank, out, cv, st);
     size_t es = zg::dtype_size(dtype);
