@@ -396,7 +396,12 @@ ZG_API int zg_replay(const float* shaped, const uint32_t* keys, int group, int P
  * zg_replay_workspace_size() exceeds 16 MiB is rejected with
  * ZG_ERR_WORKSPACE.  The first call on a device looks up the buffer's
  * device address (cudaGetSymbolAddress) with that device current; make that
- * first call before any stream capture.  All calls on a device share the one
+ * first call before any stream capture.  Under lazy module loading (the
+ * CUDA default, CUDA_MODULE_LOADING=LAZY) that first call is also when the
+ * 16 MiB are taken on the device, so a host that fixes its memory at
+ * start-up should make it there.  The looked-up address is kept for the
+ * process: cudaDeviceReset (or unloading the library's modules) is not
+ * supported between calls.  All calls on a device share the one
  * buffer, so calls that overlap on the GPU (different streams, or host
  * threads racing on one device) corrupt each other's results; serialise
  * them.  The buffer keeps the last call's contents; the replay writes every

@@ -1,7 +1,6 @@
 """Checkpoint helpers (host side, CPU tensors)."""
 import os
 
-import pytest
 import torch
 
 import zerograd_b200 as zg
@@ -19,14 +18,3 @@ def test_checkpoint_round_trip_and_atomic_replace(tmp_path):
     assert ck["state"].generation == 7
     assert torch.equal(ck["params"]["w"], params["w"])
     assert ck["params"]["sub"]["b"].dtype == torch.bfloat16
-
-
-def test_early_stopping_modes():
-    es = zg.EarlyStopping(patience=2, mode="min", min_delta=0.1)
-    assert [es(v) for v in (1.0, 0.95, 0.97, 0.5, 0.6, 0.7)] == [False, False, True, False, False, True]
-    es = zg.EarlyStopping(patience=1, mode="max")
-    assert [es(v) for v in (0.1, 0.2, 0.2)] == [False, False, True]
-    with pytest.raises(ValueError):
-        zg.EarlyStopping(patience=0)
-    with pytest.raises(ValueError):
-        zg.EarlyStopping(mode="median")

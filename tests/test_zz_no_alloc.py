@@ -17,6 +17,9 @@ pytestmark = pytest.mark.gpu
 
 # the tolerance of the float32 parity tests (the reference's rtol/atol 1e-5)
 RTOL, ATOL = 1e-5, 1e-5
+# the scratch the library holds on a device, and the page rounding of free-memory reports
+SCRATCH, SLACK = 16 << 20, 4 << 20
+_first_call_done = []
 
 
 def _keys(oracle, P, dev):
@@ -53,6 +56,11 @@ def test_noalloc_replay_matches_workspace_replay(cuda, oracle, dtype, layout, sh
         torch.cuda.synchronize()
         if call == 1:
             assert torch.cuda.mem_get_info(cuda)[0] == free_before
+        elif not _first_call_done:
+            # the process's first call may load the buffer's module (lazy
+            # loading) and so take the built-in scratch, and no more
+            assert free_before - torch.cuda.mem_get_info(cuda)[0] <= SCRATCH + SLACK
+            _first_call_done.append(True)
         np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=RTOL, atol=ATOL)
     assert L.load().zg_device_error(1) == 0
 

@@ -20,10 +20,10 @@ from ._optimizer import StepMetrics, ZeroGrad, ZeroGradState
 from ._replay import replay, replay_entry
 from ._transforms import adamw, apply_updates, sgd
 from . import checkpoint, random
-from .checkpoint import EarlyStopping, load_checkpoint, save_checkpoint
+from .checkpoint import load_checkpoint, save_checkpoint
 
 __all__ = [
-    "attention", "EarlyStopping", "load_checkpoint", "save_checkpoint", "checkpoint",
+    "attention", "load_checkpoint", "save_checkpoint", "checkpoint",
     "CandidateContext", "CalibrationResult", "CapturedGeneration", "DeviceShard", "DistributedZeroGrad", "Manifest", "ManifestEntry",
     "ParameterLayout", "ParameterPath", "ParameterTree", "RowShard", "ShardResult", "StepMetrics", "ZeroGrad",
     "ZeroGradState", "adamw", "allgather_losses", "apply_updates", "candidate_key", "compute_partition_sizes",

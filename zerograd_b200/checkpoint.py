@@ -1,4 +1,4 @@
-"""Checkpoint, resume and early stopping for long ZeroGrad runs.
+"""Checkpoint and resume for long ZeroGrad runs.
 
 A checkpoint holds the step, the parameter tree, the ``ZeroGradState``
 (generation and optimizer state) and any extra data (for example the loss
@@ -30,36 +30,3 @@ def load_checkpoint(path: str, map_location=None) -> dict:
     """Load a checkpoint written by :func:`save_checkpoint`.  It is unpickled,
     so load only checkpoints from sources you trust."""
     return torch.load(path, map_location=map_location, weights_only=False)
-
-
-class EarlyStopping:
-    """Stop once a monitored metric stops improving for ``patience`` calls.
-
-    ``mode='min'`` tracks the lowest value (a loss), ``mode='max'`` the highest
-    (an accuracy); an improvement must exceed ``min_delta``.  Calling the
-    object with the latest value returns True once patience is exhausted."""
-
-    def __init__(self, patience: int = 50, mode: str = "min", min_delta: float = 0.0) -> None:
-        if not isinstance(patience, int) or isinstance(patience, bool) or patience < 1:
-            raise ValueError("patience must be a positive integer")
-        if mode not in ("min", "max"):
-            raise ValueError("mode must be 'min' or 'max'")
-        self.patience = patience
-        self.mode = mode
-        self.min_delta = min_delta
-        self.best: float | None = None
-        self.wait = 0
-
-    def __call__(self, metric: float) -> bool:
-        if self.best is None:
-            improved = True
-        elif self.mode == "min":
-            improved = metric < self.best - self.min_delta
-        else:
-            improved = metric > self.best + self.min_delta
-        if improved:
-            self.best = metric
-            self.wait = 0
-            return False
-        self.wait += 1
-        return self.wait >= self.patience

@@ -15,7 +15,10 @@
 // process exits.  In host code the array's name is only a host-side handle,
 // not a device address, so the device address is looked up with
 // cudaGetSymbolAddress once per device (on the first call made with that
-// device current) and cached.
+// device current) and cached for the process (a cudaDeviceReset between calls
+// would leave the cached address stale: not supported).  This file is its own
+// module; under lazy module loading the lookup loads it, so the first call on
+// a device is the one that takes the 16 MiB.
 #include <mutex>
 
 #include "zg_common.cuh"
