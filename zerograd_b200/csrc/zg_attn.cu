@@ -27,11 +27,12 @@
 
 namespace {
 
-constexpr int AT_THREADS = 128;
+constexpr int AT_THREADS = 256;  // two threads per query row, each half of the key columns
 constexpr uint32_t AT_Q = 0;                // 16 KiB: 128 query rows x 128 B
 constexpr uint32_t AT_K = 16384;            // 32 KiB: up to 256 key rows
 constexpr uint32_t AT_V = 65536;            // 32 KiB: up to 256 value rows
 constexpr uint32_t AT_P = 0;                // 64 KiB over Q, K and the gap: P [128, 256] bf16, 4 K-blocks
+constexpr uint32_t AT_O = 0;                // 16 KiB over P once P V is done: the output tile [128, 64] bf16
 constexpr uint32_t AT_SMEM = 65536 + 32768; // 96 KiB
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -48,13 +49,16 @@ struct AttnArgs {
 
 __global__ void __launch_bounds__(AT_THREADS, 2)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-               const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
     extern __shared__ uint8_t dyn_smem[];
     __shared__ __align__(8) uint64_t load_bar, mma_bar;
     __shared__ uint32_t tmem_base_sh;
+    __shared__ float s_red[2][128];  // the two column halves' row max, then row sum
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
-    const int t = threadIdx.x, warp = t / 32;
+    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+    const int quad = warp % 4, half = warp / 4;  // TMEM lane quadrant; key-column half
+    const int r = quad * 32 + lane;              // this thread's query row in the tile
     const int qt = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
     const int q0 = qt * 128;
     // keys this query tile can see: causal tiles stop at their last query
@@ -94,13 +98,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     ok = mbar_wait(&mma_bar, 0, 82);
     tc_fence_after();
 
-    // ---- softmax over this thread's query row ----
-    const int qi = q0 + t;
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    // ---- softmax: this thread's row, its half of the key columns ----
+    const int qi = q0 + r;
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     // columns [0, vis) are visible to this query: the keys, up to the query when causal
     const int vis = a.causal ? (qi + 1 < a.S ? qi + 1 : a.S) : a.S;
+    // the warp's last visible column (its last row sees the most): chunks past it hold no weight
+    const int wvis = __reduce_max_sync(0xffffffffu, vis);
+    const int hw = n_keys / 2, c_lo = half * hw, c_hi = c_lo + hw;
+    const int c_end = wvis < c_hi ? ((wvis - c_lo + 31) / 32) * 32 + c_lo : c_hi;  // chunks to evaluate
     float mx = -INFINITY;
-    for (int c = 0; c < n_keys; c += 32) {
+    for (int c = c_lo; c < c_end; c += 32) {
         float v[32];
         tmem_ld32(trow + c, v);
         if (c + 32 <= vis) {
@@ -112,39 +120,47 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (c + j < vis) mx = fmaxf(mx, v[j]);
         }
     }
-    mx *= a.scale_log2;  // scale_log2 > 0, so max(s) * scale = max(s * scale)
+    s_red[half][r] = mx;
+    __syncthreads();
+    mx = fmaxf(s_red[0][r], s_red[1][r]) * a.scale_log2;  // scale_log2 > 0: max(s) * scale = max(s * scale)
     float sum = 0.f;
-    for (int c = 0; c < n_keys; c += 32) {
-        float v[32];
-        tmem_ld32(trow + c, v);
+    for (int c = c_lo; c < c_hi; c += 32) {
         uint32_t pk[16];
-        const bool full = c + 32 <= vis;
+        if (c < c_end) {
+            float v[32];
+            tmem_ld32(trow + c, v);
+            const bool full = c + 32 <= vis;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            float pe[2];
+            for (int j = 0; j < 16; ++j) {
+                float pe[2];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int col = c + 2 * j + e;
-                pe[e] = full || col < vis ? ex2_approx(fmaf(v[2 * j + e], a.scale_log2, -mx)) : 0.f;
+                for (int e = 0; e < 2; ++e) {
+                    const int col = c + 2 * j + e;
+                    pe[e] = full || col < vis ? ex2_approx(fmaf(v[2 * j + e], a.scale_log2, -mx)) : 0.f;
+                }
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(pe[0], pe[1]);
+                sum += __low2float(b2) + __high2float(b2);  // the weights the PV product uses
+                pk[j] = *reinterpret_cast<const uint32_t*>(&b2);
             }
-            const __nv_bfloat162 b2 = __floats2bfloat162_rn(pe[0], pe[1]);
-            sum += __low2float(b2) + __high2float(b2);  // the weights the PV product uses
-            pk[j] = *reinterpret_cast<const uint32_t*>(&b2);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pk[j] = 0u;  // masked keys: zero weight
         }
         // P is the K-major, 128-byte swizzled A operand: 64-column blocks of
         // [128 rows x 128 B], 16-byte chunk ch of row r at (ch ^ (r & 7)) * 16
-        uint8_t* blk = smem + AT_P + (c / 64) * 16384 + t * 128;
+        uint8_t* blk = smem + AT_P + (c / 64) * 16384 + r * 128;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int ch = (c % 64) / 8 + i;
-            *reinterpret_cast<uint4*>(blk + ((ch ^ (t & 7)) * 16)) =
+            *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) * 16)) =
                 make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();  // every thread's max is read (s_red reusable), P complete
     tc_fence_after();
+    s_red[half][r] = sum;
 
     if (t == 0 && ok) {
         const uint32_t idesc = idesc_bf16(128, 64, 1);
@@ -156,25 +172,34 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     ok = ok && mbar_wait(&mma_bar, 1, 83);
     tc_fence_after();
+    __syncthreads();  // both halves' sums are in s_red; P is consumed by the MMA
     {
-        float o0[32], o1[32];
-        tmem_ld32(trow, o0);
-        tmem_ld32(trow + 32, o1);
-        if (ok && qi < a.S) {
-            const float inv = 1.f / sum;
-            __nv_bfloat16* dst = a.o + (((int64_t)z * a.S + qi) * a.H + h) * 64;
+        // O / sum -> bf16 into the staging tile (over P; 128-byte swizzle,
+        // the layout of the output box), then one TMA store
+        float o[32];
+        tmem_ld32(trow + half * 32, o);
+        const float inv = 1.f / (s_red[0][r] + s_red[1][r]);
+        uint8_t* row = smem + AT_O + r * 128;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float* src = i < 4 ? o0 + 8 * i : o1 + 8 * (i - 4);
-                uint4 pk;
-                __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
+        for (int i = 0; i < 4; ++i) {
+            uint4 pk;
+            __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) hp[e] = __floats2bfloat162_rn(src[2 * e] * inv, src[2 * e + 1] * inv);
-                reinterpret_cast<uint4*>(dst)[i] = pk;
-            }
+            for (int e = 0; e < 4; ++e) hp[e] = __floats2bfloat162_rn(o[8 * i + 2 * e] * inv, o[8 * i + 2 * e + 1] * inv);
+            const int ch = half * 4 + i;
+            *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) * 16)) = pk;
         }
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the bulk store
     tc_fence_before();
+    __syncthreads();
+    if (t == 0) {
+        if (ok) {
+            tma_store_4d(&tmO, smem + AT_O, 0, h, q0, z);  // rows past S are clipped
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 256);
 }
@@ -275,19 +300,21 @@ extern "C" int zg_attention_ex(const void* q, const void* k, const void* v, int6
                 return zg::fail(ZG_ERR_CUDA, "zg_attention: shared memory attribute");
             attr = true;
         }
-        CUtensorMap tq, tk, tv;
+        CUtensorMap tq, tk, tv, to;
         const uint64_t dims[4] = {64, (uint64_t)H, (uint64_t)S, (uint64_t)Z};
         const uint64_t strides[3] = {64 * 2, (uint64_t)ld * 2, (uint64_t)S * ld * 2};
+        const uint64_t ostrides[3] = {64 * 2, (uint64_t)H * 64 * 2, (uint64_t)S * H * 64 * 2};
         const uint32_t box[4] = {64, 1, 128, 1};
         if (!zg::tensor_map_bf16(&tq, q, 4, dims, strides, box, true) ||
             !zg::tensor_map_bf16(&tk, k, 4, dims, strides, box, true) ||
-            !zg::tensor_map_bf16(&tv, v, 4, dims, strides, box, true))
+            !zg::tensor_map_bf16(&tv, v, 4, dims, strides, box, true) ||
+            !zg::tensor_map_bf16(&to, o, 4, dims, ostrides, box, true))
             return zg::fail(ZG_ERR_CUDA, "zg_attention: tensor maps");
         AttnArgs a{static_cast<__nv_bfloat16*>(o), Z, S, H, S <= 128 ? 128 : 256, causal != 0,
                    (float)(1.4426950408889634 / sqrt(64.0))};
         dim3 grid((unsigned)((S + 127) / 128), (unsigned)H, (unsigned)Z);
         zg::LaunchTimer zg_lt_("attention", st);
-        attn_tc_kernel<<<grid, AT_THREADS, smem, st>>>(tq, tk, tv, a);
+        attn_tc_kernel<<<grid, AT_THREADS, smem, st>>>(tq, tk, tv, to, a);
         return zg::check_launch("zg_attention");
     }
     const int64_t rows = (int64_t)Z * S * H;
