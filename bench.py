@@ -567,6 +567,7 @@ def run_ours(args):
     if R.world == 1 and args.sections == "all":
         secondary["perturbed_gemm"] = perturbed_gemm_section(R.dev, args)
         secondary["mlp_f32"] = mlp_section(R.dev, args)
+        secondary["vit_small"] = vit_section(R.dev, args)
         secondary["int8_qat_layer"] = int8_layer_section(R.dev, args)
     if R.rank == 0:
         kern = lm["kernels"]
@@ -601,6 +602,180 @@ def run_ours(args):
         R.dist.barrier(device_ids=[R.local])
         R.dist.destroy_process_group()
     torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# the ViT-small workload (the reference example's model at the configuration's size)
+# ---------------------------------------------------------------------------
+VIT = dict(embed=384, layers=6, heads=6, mlp=1536, classes=10, patch=4, img=32, batch=128, P=1024, rank=8,
+           sigma=0.01, seed=0, run_id="vit", lr=1e-3, chunk=128)
+
+
+def vit_tokens(cfg=VIT) -> int:
+    return (cfg["img"] // cfg["patch"]) ** 2 + 1
+
+
+def vit_manifest(cfg=VIT):
+    """The reference example's manifest (``examples/train_vit_cifar10.py:109-133``): one group per entry."""
+    import zerograd_b200 as zg
+
+    M, T, V = zg.ParameterLayout.MATRIX, zg.ParameterLayout.TABLE, zg.ParameterLayout.VECTOR
+    e = [(("patch_embed", "weight"), M, "patch_embed"), (("cls_token",), V, "cls_token"),
+         (("pos_embed",), T, "pos_embed"), (("ln_f", "scale"), V, "ln_f_scale"), (("ln_f", "bias"), V, "ln_f_bias"),
+         (("head", "weight"), M, "head_w"), (("head", "bias"), V, "head_b")]
+    for i in range(cfg["layers"]):
+        p = f"layer{i}"
+        e += [((p, n, "weight"), M, f"{p}_{n}") for n in ("q", "k", "v", "o", "mlp1", "mlp2")]
+        e += [((p, ln, w), V, f"{p}_{ln}_{w[0]}") for ln in ("ln1", "ln2") for w in ("scale", "bias")]
+    return zg.Manifest(1, tuple(zg.ManifestEntry(path, lay, g) for path, lay, g in e))
+
+
+def vit_params_host(cfg=VIT, seed=0) -> dict:
+    """Seeded synthetic weights in the example's tree: N(0, 0.02) matrices,
+    CLS token and positional table; unit LayerNorm scales, zero biases (bf16)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    E, F, C = cfg["embed"], cfg["mlp"], cfg["classes"]
+    pd = cfg["patch"] ** 2 * 3
+
+    def n(*shape):
+        return (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16)
+
+    def ln():
+        return {"scale": torch.ones(E, dtype=torch.bfloat16), "bias": torch.zeros(E, dtype=torch.bfloat16)}
+
+    p = {"patch_embed": {"weight": n(pd, E)}, "cls_token": n(E), "pos_embed": n(vit_tokens(cfg), E),
+         "ln_f": ln(), "head": {"weight": n(E, C), "bias": torch.zeros(C, dtype=torch.bfloat16)}}
+    for i in range(cfg["layers"]):
+        p[f"layer{i}"] = {"q": {"weight": n(E, E)}, "k": {"weight": n(E, E)}, "v": {"weight": n(E, E)},
+                          "o": {"weight": n(E, E)}, "mlp1": {"weight": n(E, F)}, "mlp2": {"weight": n(F, E)},
+                          "ln1": ln(), "ln2": ln()}
+    return p
+
+
+def vit_batch_host(cfg=VIT, seed=0):
+    """Images U[0, 1] [B, 32, 32, 3] cut into patches [B, 64, 48] (bf16, the
+    example's extract_patches order) and labels uniform over the classes."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed + 1)
+    B, I, ps = cfg["batch"], cfg["img"], cfg["patch"]
+    img = torch.rand(B, I, I, 3, generator=g)
+    patches = img.reshape(B, I // ps, ps, I // ps, ps, 3).permute(0, 1, 3, 2, 4, 5).reshape(B, (I // ps) ** 2, -1)
+    labels = torch.randint(0, cfg["classes"], (B,), generator=g)
+    return patches.to(torch.bfloat16).contiguous(), labels
+
+
+def make_vit_loss(cfg=VIT):
+    """The reference example's candidate forward (``examples/train_vit_cifar10.py:137-191``)
+    with its residual adds and GELU in the projections' epilogues, and the
+    mean softmax cross-entropy over the CLS logits."""
+    import torch.nn.functional as F_
+
+    import zerograd_b200 as zg
+
+    E, H, T, B = cfg["embed"], cfg["heads"], vit_tokens(cfg), cfg["batch"]
+    D = E // H
+
+    def loss_fn(p, ctx, batch, rng):
+        patches, labels = batch
+        x = ctx.linear(p, ("patch_embed", "weight"), patches)                       # [B, 64, E]
+        cls = ctx.vector(p, ("cls_token",)).reshape(1, 1, E).expand(B, 1, E)
+        x = torch_cat((cls, x), 1)
+        x = x + ctx.table_lookup(p, ("pos_embed",), pos_ids(x.device))              # [T, E] broadcast
+        for i in range(cfg["layers"]):
+            n = f"layer{i}"
+            h = zg.layer_norm(x, ctx.vector(p, (n, "ln1", "scale")), ctx.vector(p, (n, "ln1", "bias")))
+            q, k, v = (ctx.linear(p, (n, w, "weight"), h).reshape(B, T, H, D) for w in ("q", "k", "v"))
+            a = zg.attention(q, k, v).reshape(B, T, E)
+            x = ctx.linear(p, (n, "o", "weight"), a, residual=x)
+            h = zg.layer_norm(x, ctx.vector(p, (n, "ln2", "scale")), ctx.vector(p, (n, "ln2", "bias")))
+            h = ctx.linear(p, (n, "mlp1", "weight"), h, activation="gelu")
+            x = ctx.linear(p, (n, "mlp2", "weight"), h, residual=x)
+        x = zg.layer_norm(x, ctx.vector(p, ("ln_f", "scale")), ctx.vector(p, ("ln_f", "bias")))
+        logits = ctx.linear(p, ("head", "weight"), x[:, 0, :]) + ctx.vector(p, ("head", "bias"))
+        return F_.cross_entropy(logits.float(), labels), None
+
+    _ids = {}
+
+    def pos_ids(dev):
+        if dev not in _ids:
+            import torch
+
+            _ids[dev] = torch.arange(T, dtype=torch.int32, device=dev)
+        return _ids[dev]
+
+    def torch_cat(ts, dim):
+        import torch
+
+        return torch.cat(ts, dim)
+
+    return loss_fn
+
+
+def tree_to(tree, dev):
+    """A nested dict of tensors moved to `dev`."""
+    return {k: tree_to(v, dev) if isinstance(v, dict) else v.to(dev) for k, v in tree.items()}
+
+
+def vit_flops(cfg=VIT) -> float:
+    """Forward FLOPs of one candidate: projections (dense + rank-r) and attention."""
+    E, F, L, r, T, B = cfg["embed"], cfg["mlp"], cfg["layers"], cfg["rank"], vit_tokens(cfg), cfg["batch"]
+    tok = B * T
+    per_layer = 2.0 * tok * (4 * E * E + 2 * E * F) + 2.0 * tok * r * (4 * E + F + E)
+    attn = 4.0 * B * cfg["heads"] * T * T * (E // cfg["heads"])
+    patch = 2.0 * B * (T - 1) * (cfg["patch"] ** 2 * 3) * E
+    return L * (per_layer + attn) + patch
+
+
+def vit_section(dev, args):
+    """The ViT-small configuration's whole generation (P=1024, rank 8, batch
+    128, 6 layers, width 384, 65 tokens) through ZeroGrad.capture, chunks of 128."""
+    import torch
+
+    import zerograd_b200 as zg
+    from zerograd_b200 import _lib as L
+
+    cfg = VIT
+    params = tree_to(vit_params_host(cfg), dev)
+    batch = tuple(t.to(dev) for t in vit_batch_host(cfg))
+    opt = zg.ZeroGrad(vit_manifest(cfg), zg.sgd(cfg["lr"]), cfg["P"], cfg["rank"], cfg["sigma"], cfg["seed"],
+                      cfg["run_id"], chunk_size=cfg["chunk"])
+    loss = make_vit_loss(cfg)
+    cg = opt.capture(params, loss, batch)
+    st = opt.init(params)
+    pend = []
+
+    def step(i):
+        nonlocal st
+        _, st, pe = cg.enqueue(zg.ZeroGradState(i, st.opt_state))
+        pend.append(pe)
+
+    for i in range(3):
+        step(i)
+    steps = max(1, min(args.steps, 10))
+    with ClockSampler(dev) as clk:
+        ms = _timed_events(lambda i: step(10 + i), steps)
+    m = [pe.result() for pe in pend][-1]
+    del cg
+    L.profile_begin(1 << 15)
+    losses = opt.evaluate_shard(params, 100, loss, batch, range(cfg["P"]))
+    opt.step_from_losses(zg.ZeroGradState(100, st.opt_state), params, losses)
+    kern = L.profile_end()
+    pk = peaks()
+    gemm = kern.get("batched_gemm", (1, 0.0))[1]
+    proj = vit_flops(cfg) - cfg["layers"] * 4.0 * cfg["batch"] * cfg["heads"] * vit_tokens(cfg) ** 2 * 64 - \
+        2.0 * cfg["batch"] * (vit_tokens(cfg) - 1) * 48 * cfg["embed"]
+    return {"workload": "ViT-small generation: 32x32x3 images U[0,1], patch 4 (64 tokens + CLS), d 384, 6 layers, 6 "
+                        "heads, MLP 1536, 10 classes, bf16; P=1024, rank 8, batch 128, CE; chunks of 128, captured",
+            "ms_per_generation": ms / steps, "generations_per_sec": steps / (ms / 1e3),
+            "candidate_evals_per_sec": cfg["P"] * steps / (ms / 1e3), "steps": steps, "clocks": clk.summary(),
+            "forward_tflops_per_generation": cfg["P"] * vit_flops(cfg) / 1e12, "last_mean_loss": m.mean_loss,
+            "kernels_ms_per_generation": {k: v[1] for k, v in sorted(kern.items())},
+            "batched_gemm_rate": {"TFLOP/s": cfg["P"] * proj / (gemm / 1e3) / 1e12 if gemm else None,
+                                  "frac_sustained": (cfg["P"] * proj / (gemm / 1e3) / 1e12 /
+                                                     pk["bf16_tflops_sustained"]) if gemm else None}}
 
 
 # ---------------------------------------------------------------------------
