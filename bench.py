@@ -62,9 +62,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    # "headline": the decoder-LM generation alone (for profiler runs); "all"
-    # adds the secondary workloads and the CPU baseline on one GPU
-    ap.add_argument("--sections", choices=["all", "headline"], default="all")
+    # "headline": the decoder-LM generation alone; "all" adds the secondary
+    # workloads and the CPU baseline on one GPU; "profile": a small case for
+    # ncu captures (two evaluations of a 2-layer decoder-LM chunk of 16
+    # candidates at the LM's shapes), no JSON line
+    ap.add_argument("--sections", choices=["all", "headline", "profile"], default="all")
     return ap.parse_args()
 
 
@@ -552,6 +554,26 @@ def family_rates(kern: dict, P_local: int) -> dict:
     return out
 
 
+def profile_case(dev):
+    """Two evaluations of a 2-layer decoder-LM chunk (16 candidates, the LM's
+    shapes): every forward kernel of the headline at a size ncu captures
+    in seconds."""
+    import torch
+
+    import zerograd_b200 as zg
+
+    cfg = dict(LM, layers=2, P=16, chunk=16)
+    params = {k: v.to(dev) for k, v in lm_params_host(cfg, 0).items()}
+    batch = tuple(t.to(dev) for t in lm_batch_host(cfg, 0))
+    opt = zg.ZeroGrad(lm_manifest(cfg), zg.sgd(1e-3), cfg["P"], cfg["rank"], cfg["sigma"], 0, "profile",
+                      chunk_size=cfg["chunk"])
+    loss = make_lm_loss(cfg)
+    for gen in range(2):
+        losses = opt.evaluate_shard(params, gen, loss, batch, range(cfg["P"]))
+        torch.cuda.synchronize()
+    print("profile case done, mean loss", float(losses.mean()))
+
+
 def run_ours(args):
     import torch
 
@@ -559,6 +581,9 @@ def run_ours(args):
 
     R = Ranks(args)
     L.load()
+    if args.sections == "profile":
+        profile_case(R.dev)
+        return
     lm = lm_section(args, R)
     P = LM["P"]
     value = P * args.steps / (lm["ms"] / 1e3)
@@ -568,6 +593,7 @@ def run_ours(args):
         secondary["perturbed_gemm"] = perturbed_gemm_section(R.dev, args)
         secondary["mlp_f32"] = mlp_section(R.dev, args)
         secondary["vit_small"] = vit_section(R.dev, args)
+        secondary["int8_qat_mlp"] = qat_section(R.dev, args)
         secondary["int8_qat_layer"] = int8_layer_section(R.dev, args)
     if R.rank == 0:
         kern = lm["kernels"]
@@ -776,6 +802,123 @@ def vit_section(dev, args):
             "batched_gemm_rate": {"TFLOP/s": cfg["P"] * proj / (gemm / 1e3) / 1e12 if gemm else None,
                                   "frac_sustained": (cfg["P"] * proj / (gemm / 1e3) / 1e12 /
                                                      pk["bf16_tflops_sustained"]) if gemm else None}}
+
+
+# ---------------------------------------------------------------------------
+# the integer QAT MLP workload
+# ---------------------------------------------------------------------------
+QAT = dict(dims=(1024, 4096, 4096, 1024), batch=512, P=512, rank=4, sigma=2.5e-5, seed=0, run_id="qat", lr=1e-2,
+           chunk=128)
+# Activations are int8 with scale 1/127 (inputs uniform in [-127, 127]; the
+# tanh LUT's outputs 127 tanh(q / 32)); every layer quantises its output
+# at 1/32.  The low-rank term acts on the integer activations, so sigma is
+# the weights' relative perturbation times the activations' scale 1/127.
+QAT_X_SCALE, QAT_Y_SCALE = 1.0 / 127.0, 1.0 / 32.0
+
+
+def qat_luts():
+    """The hidden layers' tanh LUT (lut[q + 128] = round(127 tanh(q / 32)))
+    and the last layer's identity LUT, int8 [256] each."""
+    import torch
+
+    q = torch.arange(-128, 128, dtype=torch.float64)
+    return torch.round(127 * torch.tanh(q / 32)).to(torch.int8), q.to(torch.int8)
+
+
+def qat_manifest(cfg=QAT):
+    import zerograd_b200 as zg
+
+    n = len(cfg["dims"]) - 1
+    return zg.Manifest(1, tuple(zg.ManifestEntry((f"w{i}",), zg.ParameterLayout.MATRIX, f"w{i}") for i in range(n)))
+
+
+def qat_params_host(cfg=QAT, seed=0) -> dict:
+    """float32 master weights N(0, 1/fan_in), quantised per output channel by the forward."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    d = cfg["dims"]
+    return {f"w{i}": torch.randn(d[i], d[i + 1], generator=g) / d[i] ** 0.5 for i in range(len(d) - 1)}
+
+
+def qat_batch_host(cfg=QAT, seed=0):
+    """int8 inputs uniform in [-127, 127] [B, d0] and N(0, 1) targets [B, d_last]."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed + 1)
+    x = torch.randint(-127, 128, (cfg["batch"], cfg["dims"][0]), generator=g, dtype=torch.int8)
+    t = torch.randn(cfg["batch"], cfg["dims"][-1], generator=g)
+    return x, t
+
+
+def make_qat_loss(cfg=QAT, luts=None):
+    """Quantise the master weights (once per launch: they are shared by the
+    candidates), three integer LUT layers, the last with the identity LUT,
+    dequantised output, mean-square error against the targets."""
+    import zerograd_b200 as zg
+
+    n = len(cfg["dims"]) - 1
+    tanh_lut, ident_lut = luts
+
+    def loss_fn(p, ctx, batch, rng):
+        x, target = batch
+        for i in range(n):
+            wq, ws = zg.quantize_int8_columns(p[f"w{i}"])
+            x = ctx.int8_lut_linear(p, (f"w{i}",), x, wq, ws, QAT_X_SCALE, QAT_Y_SCALE,
+                                    ident_lut if i == n - 1 else tanh_lut)
+        y = x.float() * QAT_Y_SCALE
+        return ((y - target) ** 2).mean(), None
+
+    return loss_fn
+
+
+def qat_section(dev, args):
+    """The integer QAT MLP's whole generation (1024 -> 4096 -> 4096 -> 1024,
+    P=512, rank 4, batch 512, MSE) through ZeroGrad.capture, chunks of 128."""
+    import zerograd_b200 as zg
+    from zerograd_b200 import _lib as L
+
+    cfg = QAT
+    params = tree_to(qat_params_host(cfg), dev)
+    batch = tuple(t.to(dev) for t in qat_batch_host(cfg))
+    luts = tuple(t.to(dev) for t in qat_luts())
+    opt = zg.ZeroGrad(qat_manifest(cfg), zg.sgd(cfg["lr"]), cfg["P"], cfg["rank"], cfg["sigma"], cfg["seed"],
+                      cfg["run_id"], chunk_size=cfg["chunk"])
+    loss = make_qat_loss(cfg, luts)
+    cg = opt.capture(params, loss, batch)
+    st = opt.init(params)
+    pend = []
+
+    def step(i):
+        nonlocal st
+        _, st, pe = cg.enqueue(zg.ZeroGradState(i, st.opt_state))
+        pend.append(pe)
+
+    for i in range(2):
+        step(i)
+    steps = max(1, min(args.steps, 3))
+    with ClockSampler(dev) as clk:
+        ms = _timed_events(lambda i: step(10 + i), steps)
+    m = [pe.result() for pe in pend][-1]
+    del cg
+    L.profile_begin(1 << 14)
+    losses = opt.evaluate_shard(params, 100, loss, batch, range(cfg["P"]))
+    opt.step_from_losses(zg.ZeroGradState(100, st.opt_state), params, losses)
+    kern = L.profile_end()
+    d, B, P = cfg["dims"], cfg["batch"], cfg["P"]
+    ops = 2.0 * B * d[0] * d[1] + P * 2.0 * B * sum(d[i] * d[i + 1] for i in range(1, len(d) - 1))
+    gm = kern.get("int8_lut_gemm", (1, 0.0))[1]
+    pk = peaks()
+    return {"workload": "integer QAT MLP generation 1024->4096->4096->1024: int8 weights quantised per output "
+                        "channel from float32 masters, int8 activations through a 256-entry tanh LUT, identity LUT "
+                        "on the last layer, MSE vs N(0,1) targets; P=512, rank 4, batch 512; chunks of 128, captured",
+            "ms_per_generation": ms / steps, "generations_per_sec": steps / (ms / 1e3),
+            "candidate_evals_per_sec": P * steps / (ms / 1e3), "steps": steps, "clocks": clk.summary(),
+            "int8_tera_ops_per_generation": ops / 1e12, "last_mean_loss": m.mean_loss,
+            "kernels_ms_per_generation": {k: v[1] for k, v in sorted(kern.items())},
+            "int8_gemm_rate": {"TOP/s": ops / (gm / 1e3) / 1e12 if gm else None,
+                               "frac_of_2x_bf16_burst": ops / (gm / 1e3) / 1e12 / (2 * pk["bf16_tflops"])
+                               if gm else None}}
 
 
 # ---------------------------------------------------------------------------

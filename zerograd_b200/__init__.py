@@ -14,7 +14,7 @@ from ._fitness import shape_centered_loss, validate_losses
 from ._keys import candidate_key, group_key, step_key
 from ._manifest import Manifest, ManifestEntry, ParameterLayout, ParameterPath, ParameterTree
 from ._block import attention, layer_norm, rms_norm
-from ._ops import gelu
+from ._ops import gelu, quantize_int8_columns
 from ._graph import CapturedGeneration
 from ._optimizer import StepMetrics, ZeroGrad, ZeroGradState
 from ._replay import replay, replay_entry
@@ -27,7 +27,7 @@ __all__ = [
     "CandidateContext", "CalibrationResult", "CapturedGeneration", "DeviceShard", "DistributedZeroGrad", "Manifest", "ManifestEntry",
     "ParameterLayout", "ParameterPath", "ParameterTree", "RowShard", "ShardResult", "StepMetrics", "ZeroGrad",
     "ZeroGradState", "adamw", "allgather_losses", "apply_updates", "candidate_key", "compute_partition_sizes",
-    "gelu", "group_key", "layer_norm", "matrix_factors", "perturbed_linear", "perturbed_table_lookup", "perturbed_tied_logits",
+    "gelu", "quantize_int8_columns", "group_key", "layer_norm", "matrix_factors", "perturbed_linear", "perturbed_table_lookup", "perturbed_tied_logits",
     "perturbed_vector", "random", "replay", "replay_entry", "rms_norm", "scaled_factor", "sgd", "shape_centered_loss",
     "step_key", "table_factors", "validate_losses", "vector_noise",
 ]

@@ -127,6 +127,35 @@ class CandidateContext:
         return _ops.tied_logits_ce(x, table, labels, self.candidate_key, self._group(path), self.rank, self.sigma,
                                    reduction)
 
+    def int8_lut_linear(self, params: ParameterTree, path: ParameterPath, x: torch.Tensor, w_q: torch.Tensor,
+                        w_scale: torch.Tensor, x_scale: float, y_scale: float, lut: torch.Tensor) -> torch.Tensor:
+        """The candidate's integer linear with a 256-entry LUT activation (an
+        addition to the reference's context; the reference only has float
+        fake quantisation, ``examples/train_qat_xor.py:41-50``):
+
+            acc = x @ w_q                          (int8 x int8 -> int32, exact)
+            y   = acc * x_scale * w_scale[n] + s * (x @ A) @ B   (float32; x as integers)
+            out = lut[clamp(rint(y / y_scale), -128, 127) + 128]          (int8)
+
+        The low-rank term acts on the integer activations, so a
+        perturbation of relative size ``sigma`` in the weights' units needs
+        ``sigma`` scaled by ``x_scale``.
+
+        ``path`` names the MATRIX entry whose factors (float32 draws) perturb
+        the layer, and whose leaf (a float32 master weight, quantised per
+        output channel into ``w_q``/``w_scale``, e.g. by
+        :func:`zerograd_b200.quantize_int8_columns`) the replay updates.
+        Under ``vmap`` over candidates it is one launch of the tcgen05
+        ``kind::i8`` kernel for the population."""
+        entry = self.manifest.entry(path)
+        if entry.layout is not ParameterLayout.MATRIX:
+            raise ValueError(f"{'.'.join(path)} is not a matrix entry")
+        weight = self.manifest.resolve(params, path)
+        if tuple(weight.shape) != tuple(w_q.shape) or x.shape[-1] != w_q.shape[0]:
+            raise ValueError("int8 linear input, quantised weight and [in, out] leaf shapes are incompatible")
+        return _ops.int8_lut_linear(x, w_q, w_scale, lut, self.candidate_key, self._group(path), self.rank, self.sigma,
+                                    x_scale, y_scale)
+
     def vector(self, params: ParameterTree, path: ParameterPath) -> torch.Tensor:
         entry = self.manifest.entry(path)
         if entry.layout is not ParameterLayout.VECTOR:

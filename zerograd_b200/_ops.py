@@ -1027,6 +1027,40 @@ def _bits_vmap(info, in_dims, key, n):
     return launch_bits(_movedim0(key, in_dims[0]), n), 0
 
 
+@torch.library.custom_op(f"{_NS}::int8_lut_linear", mutates_args=())
+def _int8_op(x: torch.Tensor, w_q: torch.Tensor, w_scale: torch.Tensor, lut: torch.Tensor, key: torch.Tensor,
+             group: int, rank: int, sigma: float, x_scale: float, y_scale: float) -> torch.Tensor:
+    return launch_int8_lut_linear(x, w_q, w_scale, x_scale, y_scale, lut, key.reshape(1, 2), group, rank, sigma,
+                                  False)[0]
+
+
+@torch.library.register_vmap(f"{_NS}::int8_lut_linear")
+def _int8_vmap(info, in_dims, x, w_q, w_scale, lut, key, group, rank, sigma, x_scale, y_scale):
+    xd, wd, sd, ld, kd = in_dims[:5]
+    if wd is not None or sd is not None or ld is not None:
+        raise NotImplementedError("int8 weights, scales and LUTs batched over candidates are not supported")
+    x = _movedim0(x, xd)
+    if kd is None:
+        return launch_int8_lut_linear(x, w_q, w_scale, x_scale, y_scale, lut, key.reshape(1, 2), group, rank, sigma,
+                                      False)[0], 0
+    return launch_int8_lut_linear(x, w_q, w_scale, x_scale, y_scale, lut, _movedim0(key, kd), group, rank, sigma,
+                                  xd is not None), 0
+
+
+def int8_lut_linear(x, w_q, w_scale, lut, key, group, rank, sigma, x_scale, y_scale):
+    return _int8_op(x, w_q, w_scale, lut, key, int(group), int(rank), float(sigma), float(x_scale), float(y_scale))
+
+
+def quantize_int8_columns(weight: torch.Tensor):
+    """Per-output-channel symmetric int8 quantisation of a [K, N] weight:
+    scale[n] = max_k |W[k, n]| / 127 (float32; 1 for an all-zero column),
+    W_q = clamp(rint(W / scale), -127, 127) (int8)."""
+    W = weight.to(torch.float32)
+    scale = W.abs().amax(dim=0) / 127.0
+    scale = torch.where(scale > 0, scale, torch.ones_like(scale))
+    return torch.clamp(torch.round(W / scale), -127, 127).to(torch.int8), scale
+
+
 def linear(x, weight, key, group, rank, sigma, activation=None, residual=None):
     if activation not in ACTIVATIONS:
         raise ValueError(f"unknown activation {activation!r}: expected one of None, 'gelu'")
