@@ -269,7 +269,8 @@ def lm_work(cfg=LM, P=None):
         "batched_u_pass": float(P * L * sum(tok * K * 2 + tok * 16 * 2 for K, N in projs)) + P * tok * E * 2.0,
         "rms_norm": float(P * (2 * L + 1) * tok * E * 2 * 2),
         "table_lookup": float(P * tok * E * 2 * 2),
-        "replay_gemm": 2.0 * (L * dense + V * E) * cfg["P"] * r,
+        # this rank's candidates: the exchanged update contracts only those
+        "replay_gemm": 2.0 * (L * dense + V * E) * P * r,
     }
     bound = {"batched_gemm": "tensor", "attention": "tensor", "tied_ce": "tensor", "replay_gemm": "tensor",
              "batched_u_pass": "hbm", "rms_norm": "hbm", "table_lookup": "hbm"}
@@ -322,8 +323,9 @@ def lm_config(world: int) -> dict:
     return {"workload": lm_workload_name(), "population": LM["P"], "rank": LM["rank"], "layers": LM["layers"],
             "width": LM["width"], "vocab": LM["vocab"], "batch": f"{LM['batch']}x{LM['seq']} tokens",
             "chunk_size": LM["chunk"],
-            "parallelism": (f"population shards x{world}, fitness all-gather, replicated update" if world > 1
-                            else "1 GPU"),
+            "parallelism": (f"population shards x{world}, fitness all-gather, exchanged update (each rank "
+                            "contracts its own candidates' factors; partial replays all-to-all, fixed-order sums, "
+                            "parameters all-gathered)" if world > 1 else "1 GPU"),
             "l2": "inputs larger than L2 (each chunk's activations are GBs); 256 MiB flush between generations",
             "sample_cpu": f"{CPU_SAMPLE} candidate(s) per step"}
 
@@ -434,10 +436,12 @@ def lm_section(args, R):
     opt = zg.ZeroGrad(manifest, zg.sgd(cfg["lr"]), P, r, cfg["sigma"], cfg["seed"], cfg["run_id"],
                       chunk_size=cfg["chunk"])
     gather = (lambda l: zg.allgather_losses(l, sizes)) if world > 1 else None
+    exchange = zg.ExchangedReplay(rank, world, a, P_local) if world > 1 else None
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     cg = zg.CapturedGeneration(opt, params, loss_fn, batch, state=opt.init(params),
-                               candidate_range=(a, P_local) if world > 1 else None, gather=gather)
+                               candidate_range=(a, P_local) if world > 1 else None, gather=gather,
+                               exchange=exchange)
     cstate = opt.init(params)
     pending = []
 
@@ -509,7 +513,7 @@ def lm_section(args, R):
     losses = opt.evaluate_shard(params, 300, loss_fn, batch, range(a, a + P_local))
     if world > 1:
         losses = zg.allgather_losses(losses, sizes)
-    opt.step_from_losses(zg.ZeroGradState(300, opt.init(params).opt_state), params, losses)
+    opt._step_from_losses(zg.ZeroGradState(300, opt.init(params).opt_state), params, losses, exchange=exchange)
     kernels = L.profile_end()
     R.barrier()
     return {"ms": ms, "e2e_ms": e2e_ms, "e2e_steps": e2e_steps, "clocks": clocks, "launches": launches,

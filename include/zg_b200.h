@@ -185,8 +185,14 @@ ZG_API int zg_forward_operands(const void* x, const void* W, int w_is_kn, const 
 
 /* Replay from operand factors (bf16, tcgen05):
  *   out[rows, cols] = inv_sqrt_rank * sum_q (w_{q/rank} A_op[:, q]) B_op[:, q]^T
- * (float32).  Replaces replay_entry (src/zerograd/_replay.py:44-51). */
-ZG_API size_t zg_replay_factors_workspace_size(int P, int64_t rows, int rank);
+ * (float32).  The sum over the P candidates runs as S =
+ * zg_replay_split_count(P, rank) groups of P / S consecutive candidates,
+ * each contracted on its own (float32 partial G_z), then added in group
+ * order: out = inv_sqrt_rank * (((G_0 + G_1) + G_2) + ...).  The fitness
+ * weight is applied to one operand, rounded to bf16 (the input-side factor
+ * when it is given transposed, else the smaller of the two).  Replaces
+ * replay_entry (src/zerograd/_replay.py:44-51). */
+ZG_API size_t zg_replay_factors_workspace_size(int P, int64_t rows, int64_t cols, int rank);
 ZG_API int zg_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P,
                              int64_t rows, int64_t cols, int rank, float inv_sqrt_rank, float* out,
                              void* workspace, size_t workspace_bytes, void* stream);
@@ -196,7 +202,7 @@ ZG_API int zg_replay_factors(const float* shaped, const void* A_op, const void* 
  * (cols a multiple of 8), which is how the per-candidate-input forward keeps
  * its input-side factor.  Replaces replay_entry
  * (src/zerograd/_replay.py:44-51). */
-ZG_API size_t zg_replay_operands_workspace_size(int P, int64_t rows, int rank);
+ZG_API size_t zg_replay_operands_workspace_size(int P, int64_t rows, int64_t cols, int rank);
 ZG_API int zg_replay_operands(const float* shaped, const void* A, int a_transposed, const void* B,
                               int b_transposed, int P, int64_t rows, int64_t cols, int rank,
                               float inv_sqrt_rank, float* out, void* workspace,
@@ -235,6 +241,36 @@ ZG_API int zg_replay_adamw(const float* shaped, const void* A, int a_transposed,
                            double lr, double b1, double b2, double eps, double weight_decay,
                            float* descent_out, const float* guard, const float* bias_corrections,
                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* The replay split over candidate groups, for a population spread over
+ * several GPUs (src/zerograd/_distributed.py:319-366 replays the whole
+ * population on every device; here each GPU contracts only the groups whose
+ * factors its forward drew, and the partials are exchanged and summed).
+ * zg_replay_split_count: S for a population of P candidates at this rank
+ * (the largest of 8, 4, 2 whose groups keep >= 4096 contraction columns, a
+ * multiple of 64; else 1).
+ * zg_replay_partials: `splits` consecutive groups (of the S = split_total
+ * groups of the population) from the factors of their P candidates, laid
+ * out as for zg_replay_operands, and the candidates' shaped weights:
+ * partials + z * partial_stride = G_z [rows, cols] float32 (unscaled), the
+ * same bits as the partial zg_replay_operands forms for that group.
+ * zg_replay_split_sum: out[e] = alpha * (((p_0 + p_1) + p_2) + ...) over S
+ * <= 8 partials, partial s of element e at partials[offsets[s] + e]
+ * (offsets: host array of S element offsets).
+ * zg_replay_split_sgd: the same sum d, then param_out = param + (-lr)(-d)
+ * (optax.sgd), nothing written when *guard != 0.  With the partials of all
+ * groups these give exactly the bits of zg_replay_operands / zg_replay_sgd. */
+ZG_API int zg_replay_split_count(int P, int rank);
+ZG_API size_t zg_replay_partials_workspace_size(int P, int64_t rows, int64_t cols, int rank);
+ZG_API int zg_replay_partials(const float* shaped, const void* A, int a_transposed, const void* B,
+                              int b_transposed, int P, int64_t rows, int64_t cols, int rank,
+                              int split_total, int splits, float* partials, int64_t partial_stride,
+                              void* workspace, size_t workspace_bytes, void* stream);
+ZG_API int zg_replay_split_sum(const float* partials, const int64_t* offsets, int S, int64_t n,
+                               float alpha, float* out, void* stream);
+ZG_API int zg_replay_split_sgd(const float* partials, const int64_t* offsets, int S, int64_t n,
+                               float alpha, const void* param, void* param_out, int dtype, double lr,
+                               const float* guard, void* stream);
 
 /* Tied logits fused with softmax cross-entropy (bf16, tcgen05): for each
  * candidate p and row m

@@ -56,40 +56,3 @@ def test_empty_shard():
     out = _run([0, 4])
     for rank, full, _ in out:
         assert full == [0.0, 10.0, 20.0, 30.0]
-
-
-def _row_worker(rank, world, port, rows, q):
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
-    try:
-        from zerograd_b200 import RowShard
-
-        block = rows // world
-        t = torch.full((rows, 3), -1.0)
-        r0 = rank * block
-        t[r0:r0 + block] = torch.arange(r0 * 3, (r0 + block) * 3, dtype=torch.float32).view(block, 3)
-        before = t.data_ptr()
-        RowShard(rank, world).gather(t, r0, r0 + block)
-        q.put((rank, t.tolist(), t.data_ptr() == before))
-    finally:
-        dist.destroy_process_group()
-
-
-def test_row_shard_gather_assembles_the_rows_in_place():
-    """The row-sharded update's parameter exchange: each rank's block of
-    rows, gathered in place, gives every rank the whole tensor."""
-    for world, rows in ((2, 8), (3, 6)):
-        ctx = mp.get_context("spawn")
-        q = ctx.Queue()
-        port = _free_port()
-        procs = [ctx.Process(target=_row_worker, args=(r, world, port, rows, q)) for r in range(world)]
-        for p in procs:
-            p.start()
-        out = [q.get(timeout=120) for _ in procs]
-        for p in procs:
-            p.join(60)
-            assert p.exitcode == 0
-        expect = torch.arange(rows * 3, dtype=torch.float32).view(rows, 3).tolist()
-        for rank, full, same_buffer in out:
-            assert full == expect and same_buffer, rank

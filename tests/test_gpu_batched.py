@@ -125,7 +125,7 @@ def test_replay_operands_transposed_matches_replay(cuda, oracle, layout):
     A = A_op.t().contiguous() if a_t else A_op
     B = B_op.t().contiguous() if b_t else B_op
     out = torch.empty((rows, cols), dtype=torch.float32, device=cuda)
-    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, r), cuda)
+    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, cols, r), cuda)
     L.call("zg_replay_operands", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r,
            _ops.scaled_factor_value(r, 1.0, torch.bfloat16), L.ptr(out), L.ptr(ws), ws.numel(), L.stream_ptr(cuda))
     assert L.load().zg_device_error(1) == 0

@@ -22,7 +22,7 @@ def _u32(a, dev):
 
 def _unfused(w, A, a_t, B, b_t, P, rows, cols, r, inv, dev):
     out = torch.empty((rows, cols), dtype=torch.float32, device=dev)
-    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, r), dev)
+    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, cols, r), dev)
     L.call("zg_replay_operands", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r, inv, L.ptr(out),
            L.ptr(ws), ws.numel(), L.stream_ptr(dev))
     return out
@@ -45,7 +45,7 @@ def test_fused_step_matches_replay_then_update(cuda, oracle, rows, cols, P, layo
     B = B_op.t().contiguous() if b_t else B_op
     inv = _ops.scaled_factor_value(r, 1.0, torch.bfloat16)
     d = _unfused(w, A, a_t, B, b_t, P, rows, cols, r, inv, cuda)
-    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, r), cuda)
+    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, cols, r), cuda)
     new = torch.empty_like(param)
     d2 = torch.empty_like(d)
     st = L.stream_ptr(cuda)

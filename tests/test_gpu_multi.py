@@ -144,7 +144,7 @@ def test_captured_process_group_generation():
         assert torch.equal(p0[k], p1[k]), k
 
 
-def _worker_row_sharded(rank, port, q):
+def _worker_exchanged(rank, port, q):
     import datetime
 
     import torch.distributed as dist
@@ -158,7 +158,8 @@ def _worker_row_sharded(rank, port, q):
                             device_id=dev)
     try:
         opt0, params0, x, loss_fn = _problem(dev)
-        opt = zg.ZeroGrad(opt0.manifest, zg.sgd(0.05), 48, 8, 0.02, 0, "multi-rows")
+        # P r = 32768: 8 candidate groups, 4 per rank
+        opt = zg.ZeroGrad(opt0.manifest, zg.sgd(0.05), 2048, 16, 0.02, 0, "multi-exchange")
         rep = zg.DistributedZeroGrad(opt, None, loss_fn)
         sh = zg.DistributedZeroGrad(opt, None, loss_fn, replay="sharded")
         cg = sh.capture(params0, x)
@@ -182,17 +183,14 @@ def _worker_row_sharded(rank, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_row_sharded_update_matches_replicated():
-    """Row-sharded update (each rank replays and updates its half of W's
-    rows, then the halves are all-gathered): every rank ends with the same
-    bits, the captured generation gives the eager step's bits, and the
-    result equals the replicated update within float tolerance (the GEMM
-    tiles of a half differ from the whole one's, so the sums round
-    differently)."""
+def test_exchanged_update_matches_replicated():
+    """Exchanged update (each rank contracts its own candidates' factors,
+    partials all-to-all, fixed-order sums, parameters all-gathered): every
+    rank ends with the bits of the replicated update, eager and captured."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_row_sharded, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker_exchanged, args=(r, port, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     out = sorted([q.get(timeout=300) for _ in procs], key=lambda t: t[0])
@@ -203,4 +201,5 @@ def test_row_sharded_update_matches_replicated():
     assert g0 and g1
     for k in s0:
         assert torch.equal(s0[k], s1[k]), k
-        torch.testing.assert_close(s0[k], r0[k], rtol=1e-2, atol=1e-2)
+        assert torch.equal(s0[k], r0[k]), k
+        assert torch.equal(r0[k], r1[k]), k

@@ -188,7 +188,7 @@ def test_replay_factors_matches_fp32(cuda, rows, cols, P, r):
     A = torch.randn(rows, q, generator=g).to(torch.bfloat16).to(cuda)
     B = torch.randn(cols, q, generator=g).to(torch.bfloat16).to(cuda)
     w = torch.randn(P, generator=g).to(cuda)
-    ws = L.workspace(L.query("zg_replay_factors_workspace_size", P, rows, r), cuda)
+    ws = L.workspace(L.query("zg_replay_factors_workspace_size", P, rows, cols, r), cuda)
 
     def run():
         out = torch.empty((rows, cols), dtype=torch.float32, device=cuda)

@@ -7,8 +7,9 @@ The public names mirror the reference package's hot-path exports
 """
 from ._candidate import (CandidateContext, perturbed_linear, perturbed_table_lookup, perturbed_tied_logits,
                          perturbed_vector)
-from ._distributed import (CalibrationResult, DeviceShard, DistributedZeroGrad, RowShard, ShardResult,
-                           allgather_losses, compute_partition_sizes)
+from ._distributed import (CalibrationResult, DeviceShard, DistributedZeroGrad, ShardResult, allgather_losses,
+                           compute_partition_sizes)
+from ._exchange import ExchangedReplay
 from ._factors import matrix_factors, scaled_factor, table_factors, vector_noise
 from ._fitness import shape_centered_loss, validate_losses
 from ._keys import candidate_key, group_key, step_key
@@ -24,8 +25,9 @@ from .checkpoint import load_checkpoint, save_checkpoint
 
 __all__ = [
     "attention", "load_checkpoint", "save_checkpoint", "checkpoint",
-    "CandidateContext", "CalibrationResult", "CapturedGeneration", "DeviceShard", "DistributedZeroGrad", "Manifest", "ManifestEntry",
-    "ParameterLayout", "ParameterPath", "ParameterTree", "RowShard", "ShardResult", "StepMetrics", "ZeroGrad",
+    "CandidateContext", "CalibrationResult", "CapturedGeneration", "DeviceShard", "DistributedZeroGrad", "ExchangedReplay",
+    "Manifest", "ManifestEntry",
+    "ParameterLayout", "ParameterPath", "ParameterTree", "ShardResult", "StepMetrics", "ZeroGrad",
     "ZeroGradState", "adamw", "allgather_losses", "apply_updates", "candidate_key", "compute_partition_sizes",
     "gelu", "quantize_int8_columns", "group_key", "layer_norm", "matrix_factors", "perturbed_linear", "perturbed_table_lookup", "perturbed_tied_logits",
     "perturbed_vector", "random", "replay", "replay_entry", "rms_norm", "scaled_factor", "sgd", "shape_centered_loss",

@@ -5,9 +5,12 @@ The population is the only sharded axis.  Two ways to run it:
 * one process per GPU (the B200 layout): ``DistributedZeroGrad`` with
   ``devices=None`` inside an initialised ``torch.distributed`` process group
   (NCCL).  Rank r evaluates its contiguous id range, the 1-D fitness array is
-  all-gathered (the ONLY collective), and every rank replays the identical
-  update -- the seed-derived replicated-replay protocol of
-  ``src/zerograd/_cluster.py:228-250`` -- so parameters never move.
+  all-gathered, and every rank replays the identical update -- the
+  seed-derived replicated-replay protocol of
+  ``src/zerograd/_cluster.py:228-250`` -- so parameters never move.  With
+  ``replay="sharded"`` (SGD) each rank contracts only its own candidates'
+  factors and the ranks exchange the partial replays and the new parameters
+  (``_exchange.py``): the same bits, 1/N of the replay and factor draws.
 * one process, several devices (the reference's layout): ``devices`` is a
   list of ``torch.device``; shards run on worker threads, losses are
   gathered to the coordinator device in shard order and the generation is
@@ -23,6 +26,7 @@ from typing import Any
 import torch
 import torch.distributed as dist
 
+from ._exchange import ExchangedReplay
 from ._keys import key as make_key
 from ._manifest import ParameterTree
 from ._optimizer import LossFn, StepMetrics, ZeroGrad, ZeroGradState, _materialize_tree
@@ -93,31 +97,6 @@ def allgather_losses(local: torch.Tensor, sizes: list[int], group=None) -> torch
     return torch.cat([gathered[r, : sizes[r]] for r in range(world)])
 
 
-@dataclass(frozen=True)
-class RowShard:
-    """The row-sharded update (an option beside the reference's replicated
-    replay): after the fitness all-gather, rank ``rank`` of ``world``
-    replays and updates rows [rank*R/world, (rank+1)*R/world) of each SGD
-    leaf, and ``gather`` all-gathers the row blocks in place, so every
-    rank holds the same parameters.  Each rank does 1/world of the replay
-    GEMM, its weighting pass and its update; the parameters cross NVLink
-    once per generation.  The blocks are computed by the same kernels as the
-    whole replay, on fewer rows; the GEMM's tile schedule differs, so
-    results agree with the replicated update to float32 rounding, not bit
-    for bit, while every rank ends bit-identical to every other."""
-
-    rank: int
-    world: int
-    group: Any = None
-
-    def gather(self, t: torch.Tensor, r0: int, r1: int) -> None:
-        """All-gather the row blocks of `t` ([rows, ...], contiguous; this
-        rank's block is rows r0..r1) in place."""
-        flat = t.view(-1)
-        per_row = flat.numel() // t.shape[0]
-        dist.all_gather_into_tensor(flat, flat[r0 * per_row:r1 * per_row], group=self.group)
-
-
 class DeviceShard:
     """Evaluates a population shard on one device (``_distributed.py:88-139``)."""
 
@@ -186,7 +165,7 @@ class DistributedZeroGrad:
         if replay not in ("replicated", "sharded"):
             raise ValueError("replay must be 'replicated' or 'sharded'")
         if replay == "sharded" and not self._pg_mode:
-            raise ValueError("the row-sharded update is for process-group mode (one process per GPU)")
+            raise ValueError("the exchanged update is for process-group mode (one process per GPU)")
         self._replay = replay
         if self._pg_mode:
             if not dist.is_initialized():
@@ -214,7 +193,10 @@ class DistributedZeroGrad:
                             for i, d in enumerate(self._devices)]
         self._partition_sizes = compute_partition_sizes(optimizer.population_size, self._weights)
         self._apply_partition()
-        self._row_shard = RowShard(self._rank, n, process_group) if replay == "sharded" else None
+        self._exchange = None
+        if replay == "sharded":
+            a, b = shard_ranges(self._partition_sizes)[self._rank]
+            self._exchange = ExchangedReplay(self._rank, n, a, b - a, process_group)
         self._executor = None if self._pg_mode else ThreadPoolExecutor(max_workers=n)
         self._closed = False
 
@@ -258,7 +240,7 @@ class DistributedZeroGrad:
         """The generation ``step`` runs in process-group mode, captured as a
         CUDA graph: this process's shard of the forward, the fitness
         all-gather (NCCL, in the graph) and the completion (replicated, or
-        row-sharded with the parameters' all-gather in the graph).  Every
+        exchanged, with its collectives in the graph).  Every
         rank must capture together.  Release the returned object before the
         process group is destroyed."""
         from ._graph import CapturedGeneration
@@ -272,7 +254,7 @@ class DistributedZeroGrad:
         return CapturedGeneration(self._optimizer, _to_device(_materialize_tree(params), self._devices[0]),
                                   self._loss_fn, batch, state=state, candidate_range=(a, b - a),
                                   gather=lambda local: allgather_losses(local, sizes, group), rng=rng,
-                                  warmup=warmup, slots=slots, draw_ahead=draw_ahead, row_shard=self._row_shard)
+                                  warmup=warmup, slots=slots, draw_ahead=draw_ahead, exchange=self._exchange)
 
     def step(self, state: ZeroGradState, params: ParameterTree, batch: Any, *, rng: torch.Tensor | None = None):
         if rng is None:
@@ -289,10 +271,10 @@ class DistributedZeroGrad:
                 local = torch.empty(0, dtype=torch.float32, device=shard.device)
             losses = allgather_losses(local.to(torch.float32), self._partition_sizes, self._group)
             params_c = _to_device(_materialize_tree(params), shard.device)
-            if self._row_shard is not None:
+            if self._exchange is not None:
                 opt = self._optimizer
                 opt._manifest.validate(params_c)
-                return opt._step_from_losses(state, params_c, losses, row_shard=self._row_shard)
+                return opt._step_from_losses(state, params_c, losses, exchange=self._exchange)
             return self._optimizer.step_from_losses(state, params_c, losses)
         futures = []
         for shard in self._shards:
@@ -340,6 +322,9 @@ class DistributedZeroGrad:
         self._weights = [1.0 / p for p in per]
         self._partition_sizes = compute_partition_sizes(pop, self._weights)
         self._apply_partition()
+        if self._exchange is not None:
+            a, b = shard_ranges(self._partition_sizes)[self._rank]
+            self._exchange = ExchangedReplay(self._rank, self._n, a, b - a, self._group)
         return results
 
     @property

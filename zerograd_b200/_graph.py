@@ -82,7 +82,7 @@ class CapturedGeneration:
                  candidate_range: tuple[int, int] | None = None,
                  gather: Callable[[torch.Tensor], torch.Tensor] | None = None,
                  rng: torch.Tensor | None = None, prefetch_replay: bool = False, warmup: int = 2,
-                 slots: int = 2, draw_ahead: bool = True, row_shard=None):
+                 slots: int = 2, draw_ahead: bool = True, exchange=None):
         from ._optimizer import ZeroGradState, _device_of, _materialize_tree
         from ._transforms import AdamWState, adamw, sgd
 
@@ -110,12 +110,18 @@ class CapturedGeneration:
         # (a parallel branch of the graph) during its forward; off by default,
         # since the draws and the forward's GEMMs contend for the same SMs
         self._prefetch = prefetch_replay
-        self._row_shard = row_shard  # the row-sharded update (RowShard), or None: replicated
+        self._exchange = exchange  # the exchanged update (ExchangedReplay), or None: replicated
         # a slot's per-generation inputs, one row of 8 words copied in by one
         # host-to-device copy: the base key (words 0-1), the next
         # generation's base key (2-3), AdamW's bias corrections (float32, 4-5)
         self._inputs = torch.zeros((slots, 8), dtype=torch.uint32, device=dev)
         self._ids = torch.arange(P, dtype=torch.int32, device=dev)
+        # the candidates whose factors this process draws ahead: all of them
+        # for a replicated replay, its own shard for the exchanged update
+        self._draw_range = (0, P)
+        if exchange is not None and isinstance(optimizer.transform, sgd) and \
+                exchange.applies(P, optimizer.rank):
+            self._draw_range = (exchange.start, exchange.count)
         g0 = state.generation if state is not None else 0
         opt_state0 = state.opt_state if state is not None else optimizer.init(self._params).opt_state
         self._state_cls = ZeroGradState
@@ -154,7 +160,7 @@ class CapturedGeneration:
         if slots == 2 and draw_ahead and torch.cuda.get_device_capability(dev) == (10, 0):
             self._entries = [e + ((_ops._T_TAG,) if e in t_entries and e[4] in (8, 16) else ())
                              for e in optimizer._factor_entries(self._params)]
-            need = sum((e[2] + e[3]) * P * e[4] * 2 for e in self._entries)
+            need = sum((e[2] + e[3]) * self._draw_range[1] * e[4] * 2 for e in self._entries)
             if need > _ops.CACHE._budget(dev):
                 self._entries = []  # over the factor-cache budget: drawn in the generation, as eagerly
         self._fbuf = [[self._factor_buffers(e) for e in self._entries] for _ in range(slots)]
@@ -167,13 +173,14 @@ class CapturedGeneration:
         pool = torch.cuda.graph_pool_handle()
         self._graphs, self._outs = [], []
         base0 = tuple(int(v) for v in optimizer.base_key(g0))
+        d0, dn = self._draw_range
         for slot in range(slots):
             graph = torch.cuda.CUDAGraph()
             self._set_inputs(g0, opt_state0, slot, False)
             for e, bufs in zip(self._entries, self._fbuf[slot]):
                 # the forward and the replay read the slot's factor buffers
-                _ops.CACHE.put((base0, 0, P) + e, bufs, dev)
-                _ops.CACHE.mark_drawn((base0, 0, P) + e)
+                _ops.CACHE.put((base0, d0, dn) + e, bufs, dev)
+                _ops.CACHE.mark_drawn((base0, d0, dn) + e)
             n0 = L.launch_count()
             with torch.cuda.graph(graph, pool=pool):
                 capture_stream = L.stream_ptr(dev).value
@@ -210,8 +217,8 @@ class CapturedGeneration:
 
     def _factor_buffers(self, e):
         """A buffer pair for entry `e` = (group, layout, rows, cols, rank[,
-        "t"]) of the whole population, in the factor cache's (A, B) order."""
-        P, dev = self._opt.population_size, self.device
+        "t"]) of the candidates drawn ahead, in the factor cache's (A, B) order."""
+        P, dev = self._draw_range[1], self.device
         _, layout, rows, cols, rank = e[:5]
         if len(e) == 6:  # per-candidate-input layout
             k_rows, n_rows = (rows, cols) if layout == L.ZG_MATRIX else (cols, rows)
@@ -222,10 +229,10 @@ class CapturedGeneration:
                 torch.empty((cols, P * rank), dtype=torch.bfloat16, device=dev))
 
     def _draw(self, base: torch.Tensor, bufs) -> None:
-        """Every entry's factors, for the whole population of the generation
-        with base key `base`, into `bufs` (current stream)."""
-        cks = _ops.launch_fold_in(base, self._ids)
-        P = self._opt.population_size
+        """Every entry's factors, for the candidates drawn ahead of the
+        generation with base key `base`, into `bufs` (current stream)."""
+        d0, P = self._draw_range
+        cks = _ops.launch_fold_in(base, self._ids[d0:d0 + P])
         for e, (A, B) in zip(self._entries, bufs):
             group, layout, rows, cols, rank = e[:5]
             if len(e) == 6:
@@ -279,7 +286,7 @@ class CapturedGeneration:
         # in the graph, fused steps update the captured parameters in place,
         # guarded by the non-finite count; the other leaves are copied back
         new_params, new_opt_state, metrics = opt._complete(state, self._params, losses, cand_keys=cks_all,
-                                                           inplace=copy_back, row_shard=self._row_shard)
+                                                           inplace=copy_back, exchange=self._exchange)
         if copy_back:
             flag = metrics[3:4]  # non-finite loss count
             pairs = [(t, tree_get(new_params, path)) for path, t in _leaves(self._params)]

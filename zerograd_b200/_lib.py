@@ -46,14 +46,20 @@ SIGNATURES = {
                                   _vp]),
     "zg_forward_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp,
                                    _vp, _sz, _vp]),
-    "zg_replay_factors_workspace_size": (_sz, [_i32, _i64, _i32]),
+    "zg_replay_factors_workspace_size": (_sz, [_i32, _i64, _i64, _i32]),
     "zg_replay_factors": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _sz, _vp]),
-    "zg_replay_operands_workspace_size": (_sz, [_i32, _i64, _i32]),
+    "zg_replay_operands_workspace_size": (_sz, [_i32, _i64, _i64, _i32]),
     "zg_replay_operands": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _sz, _vp]),
     "zg_replay_sgd": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _i32, _f64, _vp,
                              _vp, _vp, _sz, _vp]),
     "zg_replay_adamw": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _vp, _vp, _i32, _vp, _vp,
                                _vp, _vp, _i32, _f64, _f64, _f64, _f64, _f64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "zg_replay_split_count": (_i32, [_i32, _i32]),
+    "zg_replay_partials_workspace_size": (_sz, [_i32, _i64, _i64, _i32]),
+    "zg_replay_partials": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i64, _i64, _i32, _i32, _i32, _vp, _i64, _vp, _sz,
+                                  _vp]),
+    "zg_replay_split_sum": (_i32, [_vp, _vp, _i32, _i64, _f32, _vp, _vp]),
+    "zg_replay_split_sgd": (_i32, [_vp, _vp, _i32, _i64, _f32, _vp, _vp, _i32, _f64, _vp, _vp]),
     "zg_tied_logits_ce_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "zg_tied_logits_ce": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
                                  _vp]),

@@ -731,7 +731,7 @@ def launch_replay(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, lay
             # factors of a per-candidate-input forward: MATRIX keeps A^T, TABLE keeps B^T
             a_t = int(found[-1] == _T_TAG and layout == L.ZG_MATRIX)
             b_t = int(found[-1] == _T_TAG and layout == L.ZG_TABLE)
-            ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, r), dev)
+            ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, cols, r), dev)
             L.call("zg_replay_operands", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, r, inv, L.ptr(out),
                    L.ptr(ws), ws.numel(), L.stream_ptr(dev))
             return out
@@ -756,7 +756,7 @@ def _replay_operands_for(cand_keys, group, layout, rows, cols, rank, gen, cache)
 
 def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int, layout: int, param: torch.Tensor,
                        rank: int, step: dict, gen: _Generation | None = None, cache: FactorCache = CACHE,
-                       inplace_guard: torch.Tensor | None = None, row_range: tuple[int, int] | None = None):
+                       inplace_guard: torch.Tensor | None = None):
     """Replay of one MATRIX/TABLE entry with the optimizer step fused into the
     replay GEMM's epilogue (bf16 parameters on the tensor cores).  `step`:
     {"kind": "sgd", "lr"} or {"kind": "adamw", "lr", "b1", "b2", "eps",
@@ -764,11 +764,7 @@ def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int
     -- the moments None for SGD -- or None when the fused path does not apply
     (the caller then replays and updates separately, with identical results).
     With `inplace_guard` (a device float32 scalar) the step updates param and
-    the moments in place and writes nothing when the guard is non-zero.
-    With `row_range` (r0, r1) (SGD, input-side factor not transposed) only
-    rows r0..r1 of the result are computed and written; the other rows of
-    the returned tensor are left for the caller to fill (the row-sharded
-    update gathers them from the other ranks)."""
+    the moments in place and writes nothing when the guard is non-zero."""
     dev = L.require_cuda(shaped, cand_keys, param)
     k = _keys2d(cand_keys)
     P = k.shape[0]
@@ -779,30 +775,17 @@ def launch_replay_step(shaped: torch.Tensor, cand_keys: torch.Tensor, group: int
     w = shaped.to(torch.float32).contiguous()
     if w.numel() != P:
         raise ValueError("shaped weights and candidate keys differ in length")
-    if row_range is not None:
-        r0, r1 = (int(v) for v in row_range)
-        if step["kind"] != "sgd" or not 0 <= r0 < r1 <= rows:
-            return None
     A, a_t, B, b_t = _replay_operands_for(k, group, layout, rows, cols, rank, gen, cache)
     if b_t and cols % 8:
         return None
-    if row_range is not None and a_t:
-        return None  # the input-side factor is kept transposed: replayed whole by the caller
     inv = scaled_factor_value(rank, 1.0, param.dtype)
-    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, rank), dev)
+    ws = L.workspace(L.query("zg_replay_operands_workspace_size", P, rows, cols, rank), dev)
     inplace = inplace_guard is not None
     if inplace and (inplace_guard.dtype != torch.float32 or inplace_guard.device != dev):
         raise TypeError("the guard is a float32 scalar on the parameter's device")
     guard = L.ptr(inplace_guard) if inplace else None
     out = param if inplace else torch.empty_like(param)
     st = L.stream_ptr(dev)
-    if row_range is not None:
-        # rows r0..r1 only: the input-side operand's and the parameter's rows
-        # are contiguous row blocks
-        p_rows, o_rows = param[r0:r1], out[r0:r1]
-        L.call("zg_replay_sgd", L.ptr(w), L.ptr(A[r0:r1]), 0, L.ptr(B), b_t, P, r1 - r0, cols, rank, inv,
-               L.ptr(p_rows), L.ptr(o_rows), L.ZG_BF16, float(step["lr"]), None, guard, L.ptr(ws), ws.numel(), st)
-        return out, None, None
     if step["kind"] == "sgd":
         L.call("zg_replay_sgd", L.ptr(w), L.ptr(A), a_t, L.ptr(B), b_t, P, rows, cols, rank, inv, L.ptr(param),
                L.ptr(out), L.ZG_BF16, float(step["lr"]), None, guard, L.ptr(ws), ws.numel(), st)

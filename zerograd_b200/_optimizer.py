@@ -280,8 +280,8 @@ class ZeroGrad:
         if losses.shape[0] != self._population_size:
             raise ValueError(f"losses must have {self._population_size} entries, got {losses.shape[0]}")
 
-    def _step_from_losses(self, state, params, losses, cand_keys: torch.Tensor | None = None, row_shard=None):
-        new_params, new_opt_state, metrics = self._complete(state, params, losses, cand_keys, row_shard=row_shard)
+    def _step_from_losses(self, state, params, losses, cand_keys: torch.Tensor | None = None, exchange=None):
+        new_params, new_opt_state, metrics = self._complete(state, params, losses, cand_keys, exchange=exchange)
         # The one host sync of a generation, after all its work is queued.  The
         # update wrote new tensors only, so rejecting non-finite losses here
         # leaves params and state exactly as they were.
@@ -297,8 +297,33 @@ class ZeroGrad:
         return StepMetrics(generation=generation, mean_loss=float(m[0]), min_loss=float(m[1]),
                            max_loss=float(m[2]), population_size=self._population_size)
 
+    def _exchange_work(self, state, params, exchange, gen, cand_keys) -> list:
+        """(path, param, operands, lr) of the entries the exchanged update
+        takes: bf16 2-D MATRIX/TABLE leaves, their operand factors for this
+        rank's candidates (the forward's, from the factor cache, else drawn)."""
+        if not isinstance(self._transform, sgd) or not exchange.applies(self._population_size, self._rank):
+            return []
+        a, n = exchange.start, exchange.count
+        local = _ops._Generation(gen.base, a, n, cand_keys[a:a + n])
+        work = []
+        for entry in self._manifest.entries:
+            if entry.layout is ParameterLayout.VECTOR:
+                continue
+            leaf = self._manifest.resolve(params, entry.path)
+            if not (isinstance(leaf, torch.Tensor) and leaf.is_cuda and leaf.dtype == torch.bfloat16
+                    and leaf.ndim == 2 and leaf.is_contiguous() and (n * self._rank) % 8 == 0):
+                continue
+            rows, cols = (int(d) for d in leaf.shape)
+            layout = LAYOUT_CODE[entry.layout]
+            ops = _ops._replay_operands_for(local.cks, self._manifest.group_index(entry.group), layout, rows, cols,
+                                            self._rank, local, _ops.CACHE)
+            if ops[3] and cols % 8:
+                continue
+            work.append((tuple(entry.path), leaf, ops, self._transform.step_spec(state.opt_state, entry.path)["lr"]))
+        return work
+
     def _complete(self, state, params, losses, cand_keys: torch.Tensor | None = None, inplace: bool = False,
-                  row_shard=None):
+                  exchange=None):
         """Device part of a generation's completion, all queued on the
         current stream with no host synchronisation: shaping, replay and the
         optimizer step.  Returns (new params, new optimizer state, device
@@ -306,10 +331,10 @@ class ZeroGrad:
         step is fused into the replay are updated in place, and not at all
         when a loss is not finite (the metrics' non-finite count guards the
         writes); the other leaves still come back as new tensors.
-        `row_shard` (one process per GPU, SGD): each rank replays and updates
-        its block of rows of every bf16 MATRIX/TABLE leaf whose row count the
-        ranks divide, then the blocks are all-gathered (``row_shard.gather``),
-        so every rank ends with the same parameters."""
+        `exchange` (an ExchangedReplay; one process per GPU, SGD): the bf16
+        MATRIX/TABLE entries are replayed from this rank's candidates only and
+        the partials exchanged (``ExchangedReplay.update``), with the bits of
+        the replicated update; their new values come back as new tensors."""
         self._check_losses(losses)
         device = _device_of(params)
         losses = losses.to(device)
@@ -323,25 +348,23 @@ class ZeroGrad:
         descent: dict = {}
         fused = is_fused(self._transform)
         done: dict = {}
-        shard_rows = row_shard is not None and isinstance(self._transform, sgd)
+        guard = metrics[3:4] if inplace else None
+        if exchange is not None and fused:
+            work = self._exchange_work(state, params, exchange, gen, cand_keys)
+            if work:
+                inv = _ops.scaled_factor_value(self._rank, 1.0, torch.bfloat16)
+                new = exchange.update([(p, ops, lr) for _, p, ops, lr in work], shaped, self._population_size,
+                                      self._rank, inv, guard)
+                for (path, *_), t in zip(work, new):
+                    done[path] = (t, None, None)
         for entry in self._manifest.entries:
+            if tuple(entry.path) in done:
+                continue
             if fused:
                 # the optimizer step in the replay GEMM's epilogue (bf16 MATRIX/TABLE)
                 spec = self._transform.step_spec(state.opt_state, entry.path)
-                guard = metrics[3:4] if inplace else None
-                res = None
-                leaf = self._manifest.resolve(params, entry.path) if shard_rows else None
-                if shard_rows and isinstance(leaf, torch.Tensor) and leaf.ndim == 2 and \
-                        leaf.shape[0] % row_shard.world == 0:
-                    block = leaf.shape[0] // row_shard.world
-                    r0 = row_shard.rank * block
-                    res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank, spec,
-                                            gen, inplace_guard=guard, row_range=(r0, r0 + block))
-                    if res is not None:
-                        row_shard.gather(res[0], r0, r0 + block)
-                if res is None:
-                    res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank, spec,
-                                            gen, inplace_guard=guard)
+                res = replay_entry_step(params, self._manifest, entry.path, cand_keys, shaped, self._rank, spec,
+                                        gen, inplace_guard=guard)
                 if res is not None:
                     done[tuple(entry.path)] = res
                     continue

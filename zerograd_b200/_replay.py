@@ -37,7 +37,7 @@ def replay_entry_keys(params: ParameterTree, manifest: Manifest, path: Parameter
 
 def replay_entry_step(params: ParameterTree, manifest: Manifest, path: ParameterPath, cand_keys: torch.Tensor,
                       shaped_weights: torch.Tensor, rank: int, step: dict, gen=None,
-                      inplace_guard: torch.Tensor | None = None, row_range: tuple[int, int] | None = None):
+                      inplace_guard: torch.Tensor | None = None):
     """Replay of one entry with the optimizer step fused in: (param, mu, nu)
     or None where the fused form does not apply (VECTOR entries, float32
     leaves), in which case the caller replays and steps separately.  With
@@ -49,7 +49,7 @@ def replay_entry_step(params: ParameterTree, manifest: Manifest, path: Parameter
     parameter = manifest.resolve(params, path)
     return _ops.launch_replay_step(shaped_weights, cand_keys, manifest.group_index(entry.group),
                                    LAYOUT_CODE[entry.layout], parameter, rank, step, gen=gen,
-                                   inplace_guard=inplace_guard, row_range=row_range)
+                                   inplace_guard=inplace_guard)
 
 
 def replay_entry(params: ParameterTree, manifest: Manifest, path: ParameterPath, base_key: torch.Tensor,

@@ -45,6 +45,11 @@ struct TcArgs {
     int out_bf16;
     int tiles_m, tiles_n;
     zg::FusedStep step;  // optimizer step on the float32 result (kind 0: none)
+    // Split contraction: K is `splits` equal ranges of kb_split 64-deep
+    // blocks, each accumulated on its own into the partial output D +
+    // z * d_split (z = the range).  splits == 1: one range over all of K.
+    int splits, kb_split;
+    int64_t d_split;
 };
 
 // The optimizer step on d = alpha * v[0..n) of row `row`, columns col0..:
@@ -158,10 +163,11 @@ __device__ __forceinline__ void tc_step32(const TcArgs& args, int row, int col0,
 }
 
 // alpha * v[0..32) -> D[row, col0 .. col0+32), bounds-checked against M and N.
-__device__ __forceinline__ void tc_store32_d(const TcArgs& args, int row, int col0, const float (&v)[32]) {
+__device__ __forceinline__ void tc_store32_d(const TcArgs& args, int row, int col0, const float (&v)[32],
+                                             int64_t zoff) {
     if (row >= args.M || col0 >= args.N) return;
     if (args.out_bf16) {
-        __nv_bfloat16* d = static_cast<__nv_bfloat16*>(args.D) + (int64_t)row * args.ldd + col0;
+        __nv_bfloat16* d = static_cast<__nv_bfloat16*>(args.D) + zoff + (int64_t)row * args.ldd + col0;
         if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
@@ -176,7 +182,7 @@ __device__ __forceinline__ void tc_store32_d(const TcArgs& args, int row, int co
                 if (col0 + i < args.N) d[i] = __float2bfloat16_rn(args.alpha * v[i]);
         }
     } else {
-        float* d = static_cast<float*>(args.D) + (int64_t)row * args.ldd + col0;
+        float* d = static_cast<float*>(args.D) + zoff + (int64_t)row * args.ldd + col0;
         if (col0 + 32 <= args.N && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
@@ -191,10 +197,11 @@ __device__ __forceinline__ void tc_store32_d(const TcArgs& args, int row, int co
 
 // The epilogue's store of 32 columns: the fused optimizer step (if any) and
 // D (which may be null when the step consumes the result).
-__device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0, const float (&v)[32]) {
+__device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0, const float (&v)[32],
+                                           int64_t zoff) {
     if (row >= args.M || col0 >= args.N) return;
     if (args.step.kind != zg::ZG_STEP_NONE) tc_step32(args, row, col0, v);
-    if (args.D) tc_store32_d(args, row, col0, v);
+    if (args.D) tc_store32_d(args, row, col0, v, zoff);
 }
 
 // One tile row of an epilogue: TMEM columns [0, W) of this thread's lane ->
@@ -202,7 +209,8 @@ __device__ __forceinline__ void tc_store32(const TcArgs& args, int row, int col0
 // segment every parameter load of the row is issued before the first TMEM
 // read, so their latency is paid once per tile, not once per 32 columns.
 template <int W>
-__device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int col_base, uint32_t tacc) {
+__device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int col_base, uint32_t tacc,
+                                                int64_t zoff) {
     const zg::FusedStep& st = args.step;
     // a guarded step writes nothing at all when its guard is set (the same
     // value in every lane, so the warp stays on one path)
@@ -223,7 +231,7 @@ __device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int
         for (int c = 0; c < W / 32; ++c) {
             float v[32];
             tmem_ld32(tacc + c * 32, v);
-            if (args.D) tc_store32_d(args, row, col_base + c * 32, v);
+            if (args.D) tc_store32_d(args, row, col_base + c * 32, v, zoff);
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
                 const uint4 raw = pre[c * 4 + g];
@@ -245,7 +253,74 @@ __device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int
     for (int c0 = 0; c0 < W; c0 += 32) {
         float v[32];
         tmem_ld32(tacc + c0, v);
-        tc_store32(args, row, col_base + c0, v);
+        tc_store32(args, row, col_base + c0, v, zoff);
+    }
+}
+
+// Fixed-order sum of split partials and the step on it (split_reduce): one
+// thread per 8 consecutive elements, grid-stride.
+struct SplitParts {
+    const float* p[zg::kMaxSplits];
+    int S;
+};
+
+__global__ void __launch_bounds__(256)
+split_reduce_kernel(const SplitParts parts, int64_t n, float alpha, const zg::FusedStep step, float* out) {
+    if (step.guard != nullptr && !(*step.guard == 0.f)) return;
+    bool al = true;  // every partial 16-byte aligned: vector loads
+#pragma unroll
+    for (int s = 0; s < zg::kMaxSplits; ++s)
+        if (s < parts.S) al = al && ((reinterpret_cast<uintptr_t>(parts.p[s]) & 15) == 0);
+    const bool step_al = step.kind == zg::ZG_STEP_NONE ||
+                         ((((reinterpret_cast<uintptr_t>(step.param) | reinterpret_cast<uintptr_t>(step.param_out)) &
+                            15) == 0) &&
+                          (step.kind != zg::ZG_STEP_ADAMW ||
+                           ((reinterpret_cast<uintptr_t>(step.mu) | reinterpret_cast<uintptr_t>(step.nu) |
+                             reinterpret_cast<uintptr_t>(step.mu_out) | reinterpret_cast<uintptr_t>(step.nu_out)) &
+                            15) == 0));
+    const bool out_al = out == nullptr || (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
+    for (int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; e0 < n; e0 += stride) {
+        const int m = n - e0 < 8 ? (int)(n - e0) : 8;
+        const bool vec = m == 8 && al;
+        float acc[8];
+        if (vec) {
+            const float4 a = *reinterpret_cast<const float4*>(parts.p[0] + e0);
+            const float4 b = *reinterpret_cast<const float4*>(parts.p[0] + e0 + 4);
+            acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w; acc[4] = b.x; acc[5] = b.y; acc[6] = b.z;
+            acc[7] = b.w;
+#pragma unroll
+            for (int s = 1; s < zg::kMaxSplits; ++s) {
+                if (s >= parts.S) break;
+                const float4 c = *reinterpret_cast<const float4*>(parts.p[s] + e0);
+                const float4 d = *reinterpret_cast<const float4*>(parts.p[s] + e0 + 4);
+                acc[0] = __fadd_rn(acc[0], c.x); acc[1] = __fadd_rn(acc[1], c.y);
+                acc[2] = __fadd_rn(acc[2], c.z); acc[3] = __fadd_rn(acc[3], c.w);
+                acc[4] = __fadd_rn(acc[4], d.x); acc[5] = __fadd_rn(acc[5], d.y);
+                acc[6] = __fadd_rn(acc[6], d.z); acc[7] = __fadd_rn(acc[7], d.w);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = i < m ? parts.p[0][e0 + i] : 0.f;
+#pragma unroll
+            for (int s = 1; s < zg::kMaxSplits; ++s) {
+                if (s >= parts.S) break;
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (i < m) acc[i] = __fadd_rn(acc[i], parts.p[s][e0 + i]);
+            }
+        }
+        float d[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[i] = __fmul_rn(alpha, acc[i]);
+        if (step.kind != zg::ZG_STEP_NONE) {
+            tc_step8(step, e0, d, m, m == 8 && step_al);
+        } else if (m == 8 && out_al) {
+            *reinterpret_cast<float4*>(out + e0) = make_float4(d[0], d[1], d[2], d[3]);
+            *reinterpret_cast<float4*>(out + e0 + 4) = make_float4(d[4], d[5], d[6], d[7]);
+        } else {
+            for (int i = 0; i < m; ++i) out[e0 + i] = d[i];
+        }
     }
 }
 
@@ -265,8 +340,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num_tiles = args.tiles_m * args.tiles_n;
-    const int k_blocks = (args.K + BK - 1) / BK;
+    const int tiles_mn = args.tiles_m * args.tiles_n;
+    const int num_tiles = tiles_mn * args.splits;
+    const int k_blocks = args.kb_split;  // per tile: one split's K range
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -294,13 +370,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         uint32_t issue_parity = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            const int z = t / tiles_mn, tt = t % tiles_mn;
+            const int tm = tt / args.tiles_n, tn = tt % args.tiles_n;
             // Tiles start their K sweep at different blocks, so CTAs that share
             // an operand tile do not all request the same L2 lines at once.
-            const int k_start = t % k_blocks;
+            // The start depends on the tile's place in its output only, so a
+            // split's partial is the same whichever launch computes it.
+            const int k_start = tt % k_blocks;
             for (int kb = 0; kb < k_blocks; ++kb) {
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 1)) { ok = false; break; }
-                const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
+                const int kk = z * k_blocks + (kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks);
                 uint8_t* sa = smem + stage * STAGE_BYTES;
                 uint8_t* sb = sa + A_BYTES;
                 mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
@@ -373,9 +452,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             if (!mbar_wait(&tmem_full[acc], acc_phase, 4)) break;
             tc_fence_after();
-            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            const int z = t / tiles_mn, tt = t % tiles_mn;
+            const int tm = tt / args.tiles_n, tn = tt % args.tiles_n;
             const int row = tm * BM + quad * 32 + lane;
-            tc_epilogue_row<BN>(args, row, tn * BN, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN);
+            tc_epilogue_row<BN>(args, row, tn * BN, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN,
+                                z * args.d_split);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[acc]);
@@ -419,8 +500,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t rank = cluster_rank();
     const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
-    const int num_tiles = args.tiles_m * args.tiles_n;
-    const int k_blocks = (args.K + BK - 1) / BK;
+    const int tiles_mn = args.tiles_m * args.tiles_n;
+    const int num_tiles = tiles_mn * args.splits;
+    const int k_blocks = args.kb_split;  // per tile: one split's K range
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P2_STAGES; ++s) {
@@ -446,11 +528,12 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         uint32_t phase = 0, issued = 0, issue_parity = 0;
         bool ok = true;
         for (int t = pair; ok && t < num_tiles; t += pairs) {
-            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
-            const int k_start = t % k_blocks;
+            const int z = t / tiles_mn, tt = t % tiles_mn;
+            const int tm = tt / args.tiles_n, tn = tt % args.tiles_n;
+            const int k_start = tt % k_blocks;
             for (int kb = 0; kb < k_blocks; ++kb) {
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 21)) { ok = false; break; }
-                const int kk = kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks;
+                const int kk = z * k_blocks + (kb + k_start < k_blocks ? kb + k_start : kb + k_start - k_blocks);
                 uint8_t* sa = smem + stage * P2_STAGE;
                 uint8_t* sb = sa + P2_A;
                 if (rank == 0) mbar_expect_tx(&full_bar[stage], 2 * P2_STAGE);
@@ -521,9 +604,11 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int t = pair; t < num_tiles; t += pairs) {
             if (!mbar_wait(&tmem_full[acc], acc_phase, 24)) break;
             tc_fence_after();
-            const int tm = t / args.tiles_n, tn = t % args.tiles_n;
+            const int z = t / tiles_mn, tt = t % tiles_mn;
+            const int tm = tt / args.tiles_n, tn = tt % args.tiles_n;
             const int row = tm * 256 + (int)rank * 128 + quad * 32 + lane;
-            tc_epilogue_row<256>(args, row, tn * 256, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256);
+            tc_epilogue_row<256>(args, row, tn * 256, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256,
+                                 z * args.d_split);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(empty_leader + acc * (uint32_t)sizeof(uint64_t));
@@ -832,7 +917,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& a, cud
     if (cudaFuncSetAttribute(tc_gemm_kernel<BN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return zg::fail(ZG_ERR_CUDA, "tc_gemm: shared memory attribute");
-    int tiles = a.tiles_m * a.tiles_n;
+    int tiles = a.tiles_m * a.tiles_n * a.splits;
     int grid = tiles < num_sms() ? tiles : num_sms();
     zg::LaunchTimer zg_lt_(name, st);
     tc_gemm_kernel<BN, B_MN><<<grid, THREADS, smem, st>>>(ta, tb, a);
@@ -865,7 +950,7 @@ template <bool B_MN>
 int launch_tc_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& a, int slots, cudaStream_t st,
                    const char* name) {
     constexpr size_t smem = (size_t)P2_SMEM + 1024;
-    const int tiles = a.tiles_m * a.tiles_n;
+    const int tiles = a.tiles_m * a.tiles_n * a.splits;
     const int pairs = tiles < slots ? tiles : slots;
     zg::LaunchTimer zg_lt_(name, st);
     tc_gemm_pair_kernel<B_MN><<<2 * pairs, THREADS, smem, st>>>(ta, tb, a);
@@ -913,18 +998,27 @@ bool tensor_map_bf16_swz(CUtensorMap* m, const void* base, int rank, const uint6
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
-                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name,
-                 const FusedStep* step) {
-    if (M <= 0 || N <= 0 || K <= 0) return fail(ZG_ERR_INVALID, "tc_gemm: empty problem");
+// One GEMM launch: D = alpha * A B^T over `splits` of `split_total` equal K
+// ranges of k_split elements each (split z of the launch -> D + z * d_split).
+// The kernel and tile width are chosen from the split_total-range problem,
+// so a range computed alone (split_total > splits) runs the same kernel and
+// tile schedule, and gives the same bits, as in a launch of all of them.
+int tc_gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
+                 bool out_bf16, int M, int N, int splits, int split_total, int k_split, int64_t d_split, float alpha,
+                 cudaStream_t st, const char* name, const FusedStep* step) {
+    if (M <= 0 || N <= 0 || k_split <= 0 || splits < 1 || split_total < splits)
+        return fail(ZG_ERR_INVALID, "tc_gemm: empty problem");
     if (!D && !(step && step->kind != ZG_STEP_NONE)) return fail(ZG_ERR_INVALID, "tc_gemm: no output");
+    if (splits > 1 && (k_split % BK || (step && step->kind != ZG_STEP_NONE)))
+        return fail(ZG_ERR_INVALID, "tc_gemm: split ranges need K %% 64 == 0 and no fused step");
+    const int K = k_split * splits;
     const FusedStep no_step{};
     if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
         return fail(ZG_ERR_INVALID, "tc_gemm: operands need 16-byte aligned rows");
     // Tile width: the persistent grid finishes after ceil(tiles / SMs) tiles
     // per SM, each costing ~BN (narrower tiles re-read A more often, hence
     // the small penalty); take the cheapest.
-    auto tiles = [&](int b) { return (int64_t)((M + BM - 1) / BM) * ((N + b - 1) / b); };
+    auto tiles = [&](int b) { return (int64_t)((M + BM - 1) / BM) * ((N + b - 1) / b) * split_total; };
     auto cost = [&](int b, double pen) {
         return (double)((tiles(b) + num_sms() - 1) / num_sms()) * b * pen;
     };
@@ -932,22 +1026,25 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
     double best = cost(256, 1.0);
     if (cost(128, 1.3) < best) { bn = 128; best = cost(128, 1.3); }
     if (cost(64, 1.6) < best) { bn = 64; }
+    const int kb_split = (k_split + BK - 1) / BK;
     CUtensorMap ta, tb;
     if (!make_map(&ta, A, K, M, lda, BK, BM)) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map A");
     // At least one full wave of 256 x 256 tiles: CTA pairs (cta_group::2).
-    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const int64_t pair_tiles = (int64_t)((M + 255) / 256) * ((N + 255) / 256) * split_total;
     const int slots = b_mn_major ? pair_slots<true>() : pair_slots<false>();
     if (slots > 0 && pair_tiles >= slots) {
         bool okp = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, 128);
         if (!okp) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
-        TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + 255) / 256, (N + 255) / 256, no_step};
+        TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + 255) / 256, (N + 255) / 256, no_step,
+                 splits, kb_split, d_split};
         if (step) a.step = *step;
         return b_mn_major ? launch_tc_pair<true>(ta, tb, a, slots, st, name)
                           : launch_tc_pair<false>(ta, tb, a, slots, st, name);
     }
     bool okb = b_mn_major ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, bn);
     if (!okb) return fail(ZG_ERR_CUDA, "tc_gemm: tensor map B");
-    TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + BM - 1) / BM, (N + bn - 1) / bn, no_step};
+    TcArgs a{D, ldd, M, N, K, alpha, out_bf16 ? 1 : 0, (M + BM - 1) / BM, (N + bn - 1) / bn, no_step,
+             splits, kb_split, d_split};
     if (step) a.step = *step;
     if (b_mn_major) {
         if (bn == 256) return launch_tc<256, true>(ta, tb, a, st, name);
@@ -957,6 +1054,31 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
     if (bn == 256) return launch_tc<256, false>(ta, tb, a, st, name);
     if (bn == 128) return launch_tc<128, false>(ta, tb, a, st, name);
     return launch_tc<64, false>(ta, tb, a, st, name);
+}
+
+int split_reduce(const float* parts, const int64_t* offsets, int S, int64_t n, float alpha, const FusedStep* step,
+                 float* out, cudaStream_t st) {
+    if (S < 1 || S > kMaxSplits || n < 0 || !parts || !offsets) return fail(ZG_ERR_INVALID, "split reduce: bad splits");
+    const bool has_step = step && step->kind != ZG_STEP_NONE;
+    if (!has_step && !out) return fail(ZG_ERR_INVALID, "split reduce: no output");
+    if (n == 0) return ZG_OK;
+    SplitParts sp{};
+    sp.S = S;
+    for (int s = 0; s < S; ++s) sp.p[s] = parts + offsets[s];
+    const FusedStep none{};
+    const int64_t groups = (n + 7) / 8;
+    int64_t grid = (groups + 255) / 256;
+    const int64_t cap = (int64_t)num_sms() * 8;
+    if (grid > cap) grid = cap;
+    zg::LaunchTimer zg_lt_("replay_split_reduce", st);
+    split_reduce_kernel<<<(unsigned)grid, 256, 0, st>>>(sp, n, alpha, has_step ? *step : none, out);
+    return check_launch("replay_split_reduce");
+}
+
+int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
+                 bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name,
+                 const FusedStep* step) {
+    return tc_gemm_core(A, lda, B, ldb, b_mn_major, D, ldd, out_bf16, M, N, 1, 1, K, 0, alpha, st, name, step);
 }
 
 }  // namespace zg

@@ -60,6 +60,23 @@ int tc_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
                  bool out_bf16, int M, int N, int K, float alpha, cudaStream_t st, const char* name = "gemm",
                  const FusedStep* step = nullptr);
 
+// The same GEMM over `splits` equal K ranges of k_split elements (k_split %
+// 64 == 0 when splits > 1), each accumulated on its own into the partial
+// D + z * d_split (z = the range); no fused step.  The kernel and tile width
+// are those of the split_total-range problem, so ranges computed in separate
+// launches (or on separate GPUs) give the bits of one launch of all of them.
+int tc_gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_mn_major, void* D, int64_t ldd,
+                 bool out_bf16, int M, int N, int splits, int split_total, int k_split, int64_t d_split, float alpha,
+                 cudaStream_t st, const char* name, const FusedStep* step);
+
+// Fixed-order sum of S <= 8 float32 partials (partial s of element e at
+// parts + offsets[s] + e): d = alpha * (((p_0 + p_1) + p_2) + ...), then the
+// optimizer `step` on d (kind != NONE; param and moments at flat offsets e),
+// or d -> out.
+constexpr int kMaxSplits = 8;
+int split_reduce(const float* parts, const int64_t* offsets, int S, int64_t n, float alpha, const FusedStep* step,
+                 float* out, cudaStream_t st);
+
 // Factor fill in GEMM-operand layout: out[row * ld + p*r + j] =
 // scale_p * round_dtype(normal(key_p, ctr)), ctr = row*r + j (row-major) or
 // j*rows + row (col_major); which = 0 for the A factor key, 1 for B.  ld is
@@ -87,9 +104,17 @@ int tc_shared_forward(const void* x, const void* Wop, bool w_mn_major, int64_t l
                       int P, int M, int K, int N, int rank, int f1_which, int f1_col_major, int f2_which,
                       int f2_col_major, float s, void* y, Carver& cv, cudaStream_t st);
 
-// Replay of one MATRIX/TABLE entry as one GEMM over the P*r axis (bf16).
+// Replay of one MATRIX/TABLE entry as a GEMM over the P*r axis (bf16), split
+// into replay_split_count(P, rank) candidate groups summed in group order.
 bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype);
+int replay_split_count(int P, int rank);
+size_t tc_replay_operands_workspace(int P, int64_t rows, int64_t cols, int rank);
 size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank);
+// Partials of `splits` of `split_total` candidate groups from the factors of
+// those groups' P candidates: parts + z * part_stride = unscaled G_z [rows, cols].
+int tc_replay_partials(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
+                       int64_t cols, int rank, int split_total, int splits, float* parts, int64_t part_stride,
+                       Carver& cv, cudaStream_t st);
 int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
                       int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st,
                       const FusedStep* step = nullptr);

@@ -833,67 +833,144 @@ scale_operand_t_kernel(const __nv_bfloat16* __restrict__ AT, const float* __rest
     }
 }
 
-size_t tc_replay_factors_workspace(int P, int64_t rows, int rank) { return (size_t)rows * P * rank * 2 + 256; }
+// Row form of the weighting, for a factor kept [P r, cols] (the GEMM's
+// MN-major operand): out[q, c] = bf16(float(BT[q, c]) * w[q / rank]).
+// Thread = 8 consecutive columns of one row (cols % 8 == 0), grid-stride.
+__global__ void __launch_bounds__(256)
+scale_rows_kernel(const __nv_bfloat16* __restrict__ BT, const float* __restrict__ w, int rank, int64_t q,
+                  int64_t cols, __nv_bfloat16* __restrict__ out) {
+    const int64_t groups = q * (cols / 8);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += stride) {
+        const int64_t row = g / (cols / 8);
+        const float wr = w[row / rank];
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(BT + g * 8), f);
+        uint4 pk;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(__fmul_rn(f[2 * k], wr), __fmul_rn(f[2 * k + 1], wr));
+        *reinterpret_cast<uint4*>(out + g * 8) = pk;
+    }
+}
 
-// Replay from operand factors given in either layout: A [rows, P r] or, with
-// a_t, AT [P r, rows]; B [cols, P r] or, with b_t, BT [P r, cols] (then the
-// GEMM reads it as its MN-major operand).
-int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
-                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st,
-                       const FusedStep* step) {
+// Number of candidate groups the replay contraction is split into: the
+// largest S in {8, 4, 2} whose groups keep at least 4096 of the P r
+// contraction columns, a multiple of 64 (else 1).  A function of P and rank
+// only, so every entry of a model, on any number of GPUs, splits alike.
+int replay_split_count(int P, int rank) {
     const int64_t q = (int64_t)P * rank;
-    if (!a_t && !b_t) return tc_replay_factors(shaped, A, B, P, rows, cols, rank, inv_sqrt_rank, out, cv, st, step);
-    __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
-    if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
+    for (int S = kMaxSplits; S > 1; S /= 2)
+        if (q % S == 0 && (q / S) % 64 == 0 && q / S >= 4096) return S;
+    return 1;
+}
+
+// Bytes of the weighted operand (the side it scales) and of the split partials.
+size_t tc_replay_operands_workspace(int P, int64_t rows, int64_t cols, int rank) {
+    const size_t q = (size_t)P * rank;
+    const int S = replay_split_count(P, rank);
+    const size_t side = (size_t)(rows > cols ? rows : cols);
+    return Carver::need({side * q * 2, S > 1 ? (size_t)S * rows * cols * 4 : 0}) + 256;
+}
+
+namespace {
+
+// The replay's GEMM operands with the shaped fitness applied to one side:
+// the input-side factor when it has to be transposed anyway (a_t), else the
+// smaller side (the weighting pass then moves the fewest bytes).
+int weighted_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
+                      int64_t cols, int rank, Carver& cv, cudaStream_t st, const void** Aop, const void** Bop) {
+    const int64_t q = (int64_t)P * rank;
     if (q % 8 || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
         return fail(ZG_ERR_INVALID, "tc replay: operand alignment");
     if (b_t && cols % 8) return fail(ZG_ERR_INVALID, "tc replay: transposed B needs cols % 8 == 0");
     if (q > 2147483647 || rows > 2147483647 || cols > 2147483647)
         return fail(ZG_ERR_INVALID, "tc replay: sizes too large");
-    int rc;
+    *Aop = A;
+    *Bop = B;
+    const bool scale_b = !a_t && cols < rows;
+    __nv_bfloat16* W = cv.take<__nv_bfloat16>((size_t)(scale_b ? cols : rows) * q);
+    if (!W) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
+    zg::LaunchTimer zg_lt_("replay_scale", st);
     if (a_t) {
         const int64_t gx = (rows + 63) / 64, gy = (q + 63) / 64;
         if (gy > 65535 || gx > 2147483647) return fail(ZG_ERR_INVALID, "tc replay: transposed A too large");
-        zg::LaunchTimer zg_lt_("replay_scale", st);
         scale_operand_t_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(
-            static_cast<const __nv_bfloat16*>(A), shaped, rank, (int)q, rows, Aw);
-        rc = check_launch("replay_scale");
+            static_cast<const __nv_bfloat16*>(A), shaped, rank, (int)q, rows, W);
+        *Aop = W;
+    } else if (scale_b && b_t) {
+        const int64_t groups = q * (cols / 8);
+        int64_t grid = (groups + 255) / 256;
+        if (grid > (int64_t)sm_count() * 8) grid = (int64_t)sm_count() * 8;
+        scale_rows_kernel<<<(unsigned)grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(B), shaped, rank, q, cols,
+                                                          W);
+        *Bop = W;
     } else {
+        const int64_t n = scale_b ? cols : rows;
         const unsigned gx = (unsigned)((q / 8 + 255) / 256);
-        const int64_t gy = scale_grid_rows(gx, rows);
-        zg::LaunchTimer zg_lt_("replay_scale", st);
-        scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A), shaped,
-                                                                     rank, (int)q, rows, Aw);
-        rc = check_launch("replay_scale");
+        const int64_t gy = scale_grid_rows(gx, n);
+        scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(scale_b ? B : A), shaped, rank, (int)q, n, W);
+        if (scale_b) *Bop = W; else *Aop = W;
     }
+    return check_launch("replay_scale");
+}
+
+}  // namespace
+
+// Replay from operand factors given in either layout: A [rows, P r] or, with
+// a_t, AT [P r, rows]; B [cols, P r] or, with b_t, BT [P r, cols] (then the
+// GEMM reads it as its MN-major operand).  The contraction over the P
+// candidates runs as S = replay_split_count(P, rank) groups of P / S
+// candidates, each accumulated on its own, then summed in group order and
+// scaled: d = inv_sqrt_rank * (((G_0 + G_1) + G_2) + ...), so a GPU that
+// holds only some of the groups' factors computes the same partials
+// (zg_replay_partials) and the sum is the same bits on any number of GPUs.
+int tc_replay_operands(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
+                       int64_t cols, int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st,
+                       const FusedStep* step) {
+    const int64_t q = (int64_t)P * rank;
+    const void *Aop, *Bop;
+    int rc = weighted_operands(shaped, A, a_t, B, b_t, P, rows, cols, rank, cv, st, &Aop, &Bop);
     if (rc) return rc;
-    return tc_gemm_bf16(Aw, q, B, b_t ? cols : q, b_t, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank,
-                        st, "replay_gemm", step);
+    const int S = replay_split_count(P, rank);
+    const int64_t ldb = b_t ? cols : q;
+    if (S == 1)
+        return tc_gemm_core(Aop, q, Bop, ldb, b_t, out, cols, false, (int)rows, (int)cols, 1, 1, (int)q, 0,
+                            inv_sqrt_rank, st, "replay_gemm", step);
+    const int64_t n = rows * cols;
+    float* parts = cv.take<float>((size_t)S * n);
+    if (!parts) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small for the split partials");
+    rc = tc_gemm_core(Aop, q, Bop, ldb, b_t, parts, cols, false, (int)rows, (int)cols, S, S, (int)(q / S), n, 1.f, st,
+                      "replay_gemm", nullptr);
+    if (rc) return rc;
+    int64_t offs[kMaxSplits];
+    for (int s = 0; s < S; ++s) offs[s] = s * n;
+    return split_reduce(parts, offs, S, n, inv_sqrt_rank, step, out, st);
+}
+
+int tc_replay_partials(const float* shaped, const void* A, bool a_t, const void* B, bool b_t, int P, int64_t rows,
+                       int64_t cols, int rank, int split_total, int splits, float* parts, int64_t part_stride,
+                       Carver& cv, cudaStream_t st) {
+    const int64_t q = (int64_t)P * rank;
+    if (splits < 1 || split_total < splits || split_total > kMaxSplits || q % splits || (q / splits) % 64)
+        return fail(ZG_ERR_INVALID, "replay partials: each split needs a multiple of 64 contraction columns");
+    if (part_stride < rows * cols) return fail(ZG_ERR_INVALID, "replay partials: partials overlap");
+    const void *Aop, *Bop;
+    int rc = weighted_operands(shaped, A, a_t, B, b_t, P, rows, cols, rank, cv, st, &Aop, &Bop);
+    if (rc) return rc;
+    return tc_gemm_core(Aop, q, Bop, b_t ? cols : q, b_t, parts, cols, false, (int)rows, (int)cols, splits,
+                        split_total, (int)(q / splits), part_stride, 1.f, st, "replay_gemm", nullptr);
 }
 
 int tc_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows, int64_t cols,
                       int rank, float inv_sqrt_rank, float* out, Carver& cv, cudaStream_t st, const FusedStep* step) {
-    const int64_t q = (int64_t)P * rank;
-    __nv_bfloat16* Aw = cv.take<__nv_bfloat16>((size_t)rows * q);
-    if (!Aw) return fail(ZG_ERR_WORKSPACE, "tc replay: workspace too small");
-    if (q % 8 || (reinterpret_cast<uintptr_t>(A_op) & 15)) return fail(ZG_ERR_INVALID, "tc replay: operand alignment");
-    if (q > 2147483647) return fail(ZG_ERR_INVALID, "tc replay: P*rank too large");
-    const unsigned gx = (unsigned)((q / 8 + 255) / 256);
-    const int64_t gy = scale_grid_rows(gx, rows);
-    {
-        zg::LaunchTimer zg_lt_("replay_scale", st);
-        scale_operand_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(A_op), shaped,
-                                                                     rank, (int)q, rows, Aw);
-        int rc = check_launch("replay_scale");
-        if (rc) return rc;
-    }
-    return tc_gemm_bf16(Aw, q, B_op, q, false, out, cols, false, (int)rows, (int)cols, (int)q, inv_sqrt_rank, st,
-                        "replay_gemm", step);
+    return tc_replay_operands(shaped, A_op, false, B_op, false, P, rows, cols, rank, inv_sqrt_rank, out, cv, st, step);
 }
 
 size_t tc_replay_workspace(int P, int64_t rows, int64_t cols, int rank) {
     const size_t q = (size_t)P * rank;
-    return Carver::need({(size_t)rows * q * 2, (size_t)cols * q * 2}) + tc_replay_factors_workspace(P, rows, rank);
+    return Carver::need({(size_t)rows * q * 2, (size_t)cols * q * 2}) + tc_replay_operands_workspace(P, rows, cols, rank);
 }
 
 bool tc_replay_ok(int P, int64_t rows, int64_t cols, int rank, int dtype) {
@@ -989,9 +1066,9 @@ extern "C" int zg_forward_operands(const void* x, const void* W, int w_is_kn, co
                                    q, F2, q, P, M, K, N, rank, s, y, cv, zg::as_stream(stream));
 }
 
-extern "C" size_t zg_replay_factors_workspace_size(int P, int64_t rows, int rank) {
-    if (P < 1 || rows < 1 || rank < 1) return 0;
-    return zg::tc_replay_factors_workspace(P, rows, rank);
+extern "C" size_t zg_replay_factors_workspace_size(int P, int64_t rows, int64_t cols, int rank) {
+    if (P < 1 || rows < 1 || cols < 1 || rank < 1) return 0;
+    return zg::tc_replay_operands_workspace(P, rows, cols, rank);
 }
 
 extern "C" int zg_replay_factors(const float* shaped, const void* A_op, const void* B_op, int P, int64_t rows,
@@ -1002,7 +1079,7 @@ extern "C" int zg_replay_factors(const float* shaped, const void* A_op, const vo
     if (!shaped || !A_op || !B_op || !out) return zg::fail(ZG_ERR_INVALID, "zg_replay_factors: null pointer");
     if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
         return zg::fail(ZG_ERR_UNSUPPORTED, "zg_replay_factors: needs sm_100 and P*rank a multiple of 8");
-    size_t need = zg::tc_replay_factors_workspace(P, rows, rank);
+    size_t need = zg::tc_replay_operands_workspace(P, rows, cols, rank);
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "zg_replay_factors: workspace %zu < %zu bytes", workspace_bytes, need);
     zg::Carver cv(workspace, workspace_bytes);
@@ -1103,9 +1180,9 @@ extern "C" int zg_batched_forward_ex(const void* x, const void* W, int w_is_kn, 
                                N, rank, s, y, cv, zg::as_stream(stream), ld2, activation, residual);
 }
 
-extern "C" size_t zg_replay_operands_workspace_size(int P, int64_t rows, int rank) {
-    if (P < 1 || rows < 1 || rank < 1) return 0;
-    return zg::tc_replay_factors_workspace(P, rows, rank);
+extern "C" size_t zg_replay_operands_workspace_size(int P, int64_t rows, int64_t cols, int rank) {
+    if (P < 1 || rows < 1 || cols < 1 || rank < 1) return 0;
+    return zg::tc_replay_operands_workspace(P, rows, cols, rank);
 }
 
 extern "C" int zg_replay_operands(const float* shaped, const void* A, int a_transposed, const void* B,
@@ -1116,7 +1193,7 @@ extern "C" int zg_replay_operands(const float* shaped, const void* A, int a_tran
     if (!shaped || !A || !B || !out) return zg::fail(ZG_ERR_INVALID, "zg_replay_operands: null pointer");
     if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
         return zg::fail(ZG_ERR_UNSUPPORTED, "zg_replay_operands: needs sm_100 and P*rank a multiple of 8");
-    size_t need = zg::tc_replay_factors_workspace(P, rows, rank);
+    size_t need = zg::tc_replay_operands_workspace(P, rows, cols, rank);
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "zg_replay_operands: workspace %zu < %zu bytes", workspace_bytes, need);
     zg::Carver cv(workspace, workspace_bytes);
@@ -1137,7 +1214,7 @@ static int replay_step(const char* who, const float* shaped, const void* A, int 
     if (!shaped || !A || !B || !step.param || !step.param_out) return zg::fail(ZG_ERR_INVALID, "%s: null pointer", who);
     if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
         return zg::fail(ZG_ERR_UNSUPPORTED, "%s: needs sm_100 and P*rank a multiple of 8", who);
-    size_t need = zg::tc_replay_factors_workspace(P, rows, rank);
+    size_t need = zg::tc_replay_operands_workspace(P, rows, cols, rank);
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need);
     zg::Carver cv(workspace, workspace_bytes);
@@ -1187,4 +1264,59 @@ extern "C" int zg_replay_adamw(const float* shaped, const void* A, int a_transpo
     st.c = zg::adam_consts(count, lr, b1, b2, eps, weight_decay);
     return replay_step("zg_replay_adamw", shaped, A, a_transposed, B, b_transposed, P, rows, cols, rank,
                        inv_sqrt_rank, st, descent_out, workspace, workspace_bytes, stream);
+}
+
+// ===========================================================================
+// C ABI: the replay split over candidate groups (partials, fixed-order sum)
+// ===========================================================================
+
+extern "C" int zg_replay_split_count(int P, int rank) {
+    if (P < 1 || rank < 1) return 0;
+    return zg::replay_split_count(P, rank);
+}
+
+extern "C" size_t zg_replay_partials_workspace_size(int P, int64_t rows, int64_t cols, int rank) {
+    if (P < 1 || rows < 1 || cols < 1 || rank < 1) return 0;
+    const size_t q = (size_t)P * rank;
+    return zg::Carver::need({(size_t)(rows > cols ? rows : cols) * q * 2}) + 256;
+}
+
+extern "C" int zg_replay_partials(const float* shaped, const void* A, int a_transposed, const void* B,
+                                  int b_transposed, int P, int64_t rows, int64_t cols, int rank, int split_total,
+                                  int splits, float* partials, int64_t partial_stride, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    if (P < 1 || P > 65535 || rows < 1 || cols < 1 || rank < 1 || splits < 1 || split_total < splits ||
+        split_total > zg::kMaxSplits)
+        return zg::fail(ZG_ERR_INVALID, "zg_replay_partials: bad sizes or splits");
+    if (!shaped || !A || !B || !partials) return zg::fail(ZG_ERR_INVALID, "zg_replay_partials: null pointer");
+    if (!zg::tc_replay_ok(P, rows, cols, rank, ZG_BF16))
+        return zg::fail(ZG_ERR_UNSUPPORTED, "zg_replay_partials: needs sm_100 and P*rank a multiple of 8");
+    const size_t need = zg_replay_partials_workspace_size(P, rows, cols, rank);
+    if (!workspace || workspace_bytes < need)
+        return zg::fail(ZG_ERR_WORKSPACE, "zg_replay_partials: workspace %zu < %zu bytes", workspace_bytes, need);
+    zg::Carver cv(workspace, workspace_bytes);
+    return zg::tc_replay_partials(shaped, A, a_transposed != 0, B, b_transposed != 0, P, rows, cols, rank,
+                                  split_total, splits, partials, partial_stride, cv, zg::as_stream(stream));
+}
+
+extern "C" int zg_replay_split_sum(const float* partials, const int64_t* offsets, int S, int64_t n, float alpha,
+                                   float* out, void* stream) {
+    if (!out) return zg::fail(ZG_ERR_INVALID, "zg_replay_split_sum: null output");
+    return zg::split_reduce(partials, offsets, S, n, alpha, nullptr, out, zg::as_stream(stream));
+}
+
+extern "C" int zg_replay_split_sgd(const float* partials, const int64_t* offsets, int S, int64_t n, float alpha,
+                                   const void* param, void* param_out, int dtype, double lr, const float* guard,
+                                   void* stream) {
+    if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_replay_split_sgd: bad dtype");
+    if (!param || !param_out) return zg::fail(ZG_ERR_INVALID, "zg_replay_split_sgd: null parameter");
+    zg::FusedStep st{};
+    st.kind = zg::ZG_STEP_SGD;
+    st.guard = guard;
+    st.param_bf16 = dtype == ZG_BF16;
+    st.ldp = n;
+    st.param = param;
+    st.param_out = param_out;
+    st.c.neg_lr = (float)(-lr);
+    return zg::split_reduce(partials, offsets, S, n, alpha, &st, nullptr, zg::as_stream(stream));
 }
