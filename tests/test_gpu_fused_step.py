@@ -28,7 +28,8 @@ def _unfused(w, A, a_t, B, b_t, P, rows, cols, r, inv, dev):
     return out
 
 
-@pytest.mark.parametrize("rows,cols,P", [(520, 384, 48), (4096, 4096, 256)])   # one-SM / CTA-pair GEMM
+# one-SM GEMM / CTA-pair GEMM / the contraction split over 8 candidate groups (P r = 32768)
+@pytest.mark.parametrize("rows,cols,P", [(520, 384, 48), (4096, 4096, 256), (640, 384, 4096)])
 @pytest.mark.parametrize("layout,transposed", [("matrix", False), ("matrix", True), ("table", True)])
 @pytest.mark.parametrize("opt", ["sgd", "adamw"])
 def test_fused_step_matches_replay_then_update(cuda, oracle, rows, cols, P, layout, transposed, opt):

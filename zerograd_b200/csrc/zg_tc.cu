@@ -258,7 +258,8 @@ __device__ __forceinline__ void tc_epilogue_row(const TcArgs& args, int row, int
 }
 
 // Fixed-order sum of split partials and the step on it (split_reduce): one
-// thread per 8 consecutive elements, grid-stride.
+// thread per 8 consecutive elements, grid-stride; `out` (optional with a
+// step) receives the scaled sum.
 struct SplitParts {
     const float* p[zg::kMaxSplits];
     int S;
@@ -313,13 +314,15 @@ split_reduce_kernel(const SplitParts parts, int64_t n, float alpha, const zg::Fu
         float d[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[i] = __fmul_rn(alpha, acc[i]);
-        if (step.kind != zg::ZG_STEP_NONE) {
-            tc_step8(step, e0, d, m, m == 8 && step_al);
-        } else if (m == 8 && out_al) {
+        if (step.kind != zg::ZG_STEP_NONE) tc_step8(step, e0, d, m, m == 8 && step_al);
+        if (out == nullptr) continue;
+        if (m == 8 && out_al) {
             *reinterpret_cast<float4*>(out + e0) = make_float4(d[0], d[1], d[2], d[3]);
             *reinterpret_cast<float4*>(out + e0 + 4) = make_float4(d[4], d[5], d[6], d[7]);
         } else {
-            for (int i = 0; i < m; ++i) out[e0 + i] = d[i];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (i < m) out[e0 + i] = d[i];
         }
     }
 }

@@ -71,8 +71,8 @@ int tc_gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, bool b_
 
 // Fixed-order sum of S <= 8 float32 partials (partial s of element e at
 // parts + offsets[s] + e): d = alpha * (((p_0 + p_1) + p_2) + ...), then the
-// optimizer `step` on d (kind != NONE; param and moments at flat offsets e),
-// or d -> out.
+// optimizer `step` on d (kind != NONE; param and moments at flat offsets e)
+// and/or d -> out (out may be null when there is a step).
 constexpr int kMaxSplits = 8;
 int split_reduce(const float* parts, const int64_t* offsets, int S, int64_t n, float alpha, const FusedStep* step,
                  float* out, cudaStream_t st);
