@@ -190,6 +190,16 @@ __device__ __forceinline__ ZgKey zg_group_key(const uint32_t* cand_keys, int p, 
     return group >= 0 ? zg_fold(ck, (uint32_t)group) : ck;
 }
 
+// Eight bf16 values (one 16-byte load) as float32.
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Activation and residual epilogue of the population forward.
 // ---------------------------------------------------------------------------

@@ -140,7 +140,7 @@ __global__ void table_lookup_tiled_kernel(const T* __restrict__ table, const int
                                           int group, int64_t rows, int64_t cols, float s, const T* __restrict__ Bf,
                                           T* __restrict__ out) {
     constexpr int TB = 32;
-    __shared__ float a_s[TB][R];
+    __shared__ __align__(16) float a_s[TB][R];
     __shared__ int64_t row_s[TB];
     const int p = blockIdx.y;
     const int64_t t0 = (int64_t)blockIdx.x * TB;
@@ -164,9 +164,16 @@ __global__ void table_lookup_tiled_kernel(const T* __restrict__ table, const int
 #pragma unroll
         for (int j = 0; j < R; ++j) b[j] = zg_to_float(bp[c * R + j]);
         for (int tt = 0; tt < nt; ++tt) {
+            // the token's A row as 16-byte shared loads (the same value in every lane)
+            float a[R];
+#pragma unroll
+            for (int j = 0; j < R; j += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(&a_s[tt][j]);
+                a[j] = q.x; a[j + 1] = q.y; a[j + 2] = q.z; a[j + 3] = q.w;
+            }
             float lr = 0.f;
 #pragma unroll
-            for (int j = 0; j < R; ++j) lr = fmaf(a_s[tt][j], b[j], lr);
+            for (int j = 0; j < R; ++j) lr = fmaf(a[j], b[j], lr);
             ob[(int64_t)tt * cols + c] = zg_from_float<T>(fmaf(s, lr, zg_to_float(table[row_s[tt] * cols + c])));
         }
     }

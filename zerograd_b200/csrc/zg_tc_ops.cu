@@ -220,15 +220,6 @@ __global__ void fill_operand_kernel(const uint32_t* __restrict__ keys, int group
 // ---------------------------------------------------------------------------
 constexpr int EX_BM = 64, EX_BN = 128;
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        f[2 * i] = __uint_as_float(w[i] << 16);
-        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-    }
-}
-
 // Packed float32 pair FMA (sm_100): d = a * b + c on two lanes at once.
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     unsigned long long A = *reinterpret_cast<unsigned long long*>(&a), B = *reinterpret_cast<unsigned long long*>(&b),
