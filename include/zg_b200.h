@@ -363,10 +363,14 @@ ZG_API int zg_perturbed_linear(const void* x, int x_batched, const void* W, cons
 
 /* out[p, t, :] = T[idx[t]] + s * A_p[idx[t]] @ B_p^T, T [rows, cols],
  * idx [n_idx] (int32, shared by all candidates) or [P, n_idx]
- * (idx_batched = 1).  A rows are regenerated in-kernel at the gathered
- * rows.  Replaces perturbed_table_lookup / CandidateContext.table_lookup
+ * (idx_batched = 1).  A rows are drawn only at the gathered rows.  bf16
+ * with shared ids, rank 8 or 16 and cols a multiple of 8 runs on the
+ * tensor cores (the gathered rows and A rows staged in the workspace, one
+ * K = 16 MMA per candidate and 128 x 128 tile); otherwise CUDA cores.
+ * Replaces perturbed_table_lookup / CandidateContext.table_lookup
  * (src/zerograd/_candidate.py:25-30,68-73). */
-ZG_API size_t zg_table_lookup_workspace_size(int P, int64_t rows, int64_t cols, int rank, int dtype);
+ZG_API size_t zg_table_lookup_workspace_size(int P, int64_t n_idx, int64_t rows, int64_t cols, int rank,
+                                             int dtype);
 ZG_API int zg_table_lookup(const void* T, const int32_t* idx, int idx_batched, int64_t n_idx,
                     const uint32_t* keys, int group, int P, int64_t rows, int64_t cols,
                     int rank, float s, int dtype, void* out, void* workspace,

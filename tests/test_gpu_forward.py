@@ -94,6 +94,32 @@ def test_table_lookup(cuda, oracle, dtype, idx_batched):
         _check(out[p], want, dtype, base=Tn[ip], what=f"candidate {p}")
 
 
+@pytest.mark.parametrize("rank", [8, 16])
+def test_table_lookup_tensor_core_path(cuda, oracle, rank):
+    """bf16, ids shared by the candidates, cols a multiple of 8: the lookup
+    runs as an expansion on the tensor cores (gathered rows + A rows at the
+    ids staged, one K = 16 MMA per candidate and tile); odd P, ragged token
+    and column tiles, repeated and negative ids."""
+    from zerograd_b200 import _lib as L
+
+    P, rows, cols, sigma = 9, 500, 264, 0.05
+    cks, gks = _setup(oracle, P, group=3)
+    T = _rand((rows, cols), torch.bfloat16, cuda, 13, scale=0.1)
+    g = torch.Generator().manual_seed(14)
+    idx = torch.randint(-rows, rows, (3, 101), generator=g).to(torch.int32).to(cuda)
+    L.profile_begin()
+    out = _ops.launch_table_lookup(T, idx, _u32(cks, cuda), 3, rank, sigma, False)
+    prof = L.profile_end()
+    assert "lowrank_expand" not in prof and "table_lookup" in prof, prof
+    assert L.load().zg_device_error(1) == 0
+    ii = idx.cpu().numpy().astype(np.int64)
+    eff = np.where(ii < 0, ii + rows, ii)
+    Tn = T.float().cpu().numpy().astype(np.float64)
+    for p in (0, 4, P - 1):
+        want = oracle.perturbed_table_lookup(Tn, eff, gks[p], rank, sigma, "bfloat16")
+        _check(out[p], want, torch.bfloat16, base=Tn[eff], what=f"candidate {p}")
+
+
 def test_table_lookup_negative_and_out_of_range_indices(cuda, oracle):
     """jnp indexing: negative indices wrap, out-of-range gathers clamp."""
     P, rows, cols, rank, sigma = 2, 10, 16, 2, 0.1

@@ -78,7 +78,7 @@ SIGNATURES = {
     "zg_perturbed_linear_workspace_size":(_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "zg_perturbed_linear": (_i32, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32,
                                    _vp, _vp, _sz, _vp]),
-    "zg_table_lookup_workspace_size": (_sz, [_i32, _i64, _i64, _i32, _i32]),
+    "zg_table_lookup_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i32, _i32]),
     "zg_table_lookup": (_i32, [_vp, _vp, _i32, _i64, _vp, _i32, _i32, _i64, _i64, _i32, _f32, _i32, _vp,
                                _vp, _sz, _vp]),
     "zg_tied_logits_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),

@@ -668,7 +668,7 @@ def launch_table_lookup(table: torch.Tensor, indices: torch.Tensor, keys: torch.
         return out
     s = scaled_factor_value(rank, sigma, T.dtype)
     code = L.dtype_code(T.dtype)
-    ws = L.workspace(L.query("zg_table_lookup_workspace_size", P, rows, cols, rank, code), dev)
+    ws = L.workspace(L.query("zg_table_lookup_workspace_size", P, n_idx, rows, cols, rank, code), dev)
     L.call("zg_table_lookup", L.ptr(T), L.ptr(idx), int(idx_batched), n_idx, L.ptr(k), group, P, rows, cols,
            rank, s, code, L.ptr(out), L.ptr(ws), ws.numel(), L.stream_ptr(dev))
     return out

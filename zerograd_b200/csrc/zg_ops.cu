@@ -18,6 +18,8 @@ namespace zg {
 int launch_population_factors(const uint32_t* keys, int group, int P, int layout, int64_t rows,
                               int64_t cols, int rank, int dtype, void* A, void* B,
                               cudaStream_t st);
+int factor_operands(const uint32_t* keys, int group, int P, int layout, int64_t rows, int64_t cols, int rank,
+                    int dtype, void* A_op, void* B_op, cudaStream_t st);
 }
 
 namespace {
@@ -177,6 +179,71 @@ __global__ void table_lookup_tiled_kernel(const T* __restrict__ table, const int
             ob[(int64_t)tt * cols + c] = zg_from_float<T>(fmaf(s, lr, zg_to_float(table[row_s[tt] * cols + c])));
         }
     }
+}
+
+// Tensor-core lookup (bf16, ids shared by the candidates): the gathered
+// table rows once as float32 [n, cols] (the expansion's shared addend) and
+// the candidates' A rows at the gathered ids in the expansion's operand
+// layout U [n, P R]; then y = bf16(T[idx] + s U_p B_p^T) with one K = 16
+// MMA per candidate and tile (tc_expand), so the kernel is bound by its
+// output writes.  Ids wrap and clamp as in table_lookup_kernel.
+__device__ __forceinline__ int64_t lookup_row(const int32_t* idx, int64_t t, int64_t rows) {
+    int64_t row = idx[t];
+    if (row < 0) row += rows;
+    return row < 0 ? 0 : (row >= rows ? rows - 1 : row);
+}
+
+__global__ void gather_rows_f32_kernel(const __nv_bfloat16* __restrict__ T, const int32_t* __restrict__ idx, int64_t n,
+                                       int64_t rows, int64_t cols, float* __restrict__ out) {
+    const int64_t g8 = cols / 8;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * g8; e += stride) {
+        const int64_t t = e / g8, c = (e % g8) * 8;
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(T + lookup_row(idx, t, rows) * cols + c), f);
+        float4* o = reinterpret_cast<float4*>(out + t * cols + c);
+        o[0] = make_float4(f[0], f[1], f[2], f[3]);
+        o[1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+}
+
+// U[t, p R + j] = bf16(normal(A key of candidate p, idx_t R + j)): the
+// values table_lookup_kernel draws for the same rows.
+template <int R>
+__global__ void gather_a_rows_kernel(const uint32_t* __restrict__ keys, int group, int P,
+                                     const int32_t* __restrict__ idx, int64_t n, int64_t rows,
+                                     __nv_bfloat16* __restrict__ U) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * P; e += stride) {
+        const int64_t t = e / P;
+        const int p = (int)(e % P);
+        const uint64_t c0 = (uint64_t)lookup_row(idx, t, rows) * R;
+        const ZgFactorKeys fk = zg_factor_keys(keys, p, group);
+        uint4 o[R / 8];
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(o);
+#pragma unroll
+        for (int j = 0; j < R; ++j) h[j] = __float2bfloat16_rn(zg_normal(fk.a, c0 + j));
+        uint4* dst = reinterpret_cast<uint4*>(U + t * ((int64_t)P * R) + (int64_t)p * R);
+#pragma unroll
+        for (int i = 0; i < R / 8; ++i) dst[i] = o[i];
+    }
+}
+
+int sm_count_ops() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+    }
+    return n;
+}
+
+inline bool lookup_tc_ok(int P, int64_t n_idx, int64_t cols, int rank, int dtype, int idx_batched, const void* T,
+                         const void* out) {
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return dtype == ZG_BF16 && !idx_batched && (rank == 8 || rank == 16) && cols % 8 == 0 && n_idx >= 1 &&
+           n_idx <= 2147483647 && cols <= 2147483647 && zg::tc_available() && al(T) && al(out);
 }
 
 // ---------------------------------------------------------------------------
@@ -429,10 +496,15 @@ extern "C" int zg_tied_logits(const void* x, int x_batched, const void* T, const
     return dtype == ZG_BF16 ? run_low_rank<__nv_bfloat16>(q, st) : run_low_rank<float>(q, st);
 }
 
-extern "C" size_t zg_table_lookup_workspace_size(int P, int64_t rows, int64_t cols, int rank, int dtype) {
-    if (P < 1 || rows < 1 || cols < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
+extern "C" size_t zg_table_lookup_workspace_size(int P, int64_t n_idx, int64_t rows, int64_t cols, int rank,
+                                                 int dtype) {
+    if (P < 1 || n_idx < 0 || rows < 1 || cols < 1 || rank < 1 || !zg::dtype_ok(dtype)) return 0;
     // B factors for every candidate; the A factor of the unused slot is tiny.
-    return Carver::need({(size_t)P * cols * rank * zg::dtype_size(dtype), 256});
+    const size_t simt = Carver::need({(size_t)P * cols * rank * zg::dtype_size(dtype), 256});
+    // tensor-core path: gathered rows (float32), A rows at the ids, B operand
+    const size_t q = (size_t)P * rank;
+    const size_t tc = Carver::need({(size_t)n_idx * cols * 4, (size_t)n_idx * q * 2, (size_t)cols * q * 2});
+    return simt > tc ? simt : tc;
 }
 
 extern "C" int zg_table_lookup(const void* T, const int32_t* idx, int idx_batched, int64_t n_idx,
@@ -444,11 +516,36 @@ extern "C" int zg_table_lookup(const void* T, const int32_t* idx, int idx_batche
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "zg_table_lookup: bad dtype");
     if (n_idx == 0) return ZG_OK;
     if (!T || !idx || !keys || !out) return zg::fail(ZG_ERR_INVALID, "zg_table_lookup: null pointer");
-    size_t need = zg_table_lookup_workspace_size(P, rows, cols, rank, dtype);
+    size_t need = zg_table_lookup_workspace_size(P, n_idx, rows, cols, rank, dtype);
     if (!workspace || workspace_bytes < need)
         return zg::fail(ZG_ERR_WORKSPACE, "zg_table_lookup: workspace %zu < %zu bytes", workspace_bytes, need);
     cudaStream_t st = zg::as_stream(stream);
     Carver cv(workspace, workspace_bytes);
+    if (lookup_tc_ok(P, n_idx, cols, rank, dtype, idx_batched, T, out)) {
+        const int64_t q = (int64_t)P * rank;
+        float* Tg = cv.take<float>((size_t)n_idx * cols);
+        __nv_bfloat16* U = cv.take<__nv_bfloat16>((size_t)n_idx * q);
+        __nv_bfloat16* Bop = cv.take<__nv_bfloat16>((size_t)cols * q);
+        if (!Tg || !U || !Bop) return zg::fail(ZG_ERR_WORKSPACE, "zg_table_lookup: workspace too small");
+        int rc = zg::factor_operands(keys, group, P, ZG_TABLE, rows, cols, rank, ZG_BF16, nullptr, Bop, st);
+        if (rc) return rc;
+        const int64_t cap = (int64_t)sm_count_ops() * 8;
+        {
+            zg::LaunchTimer zg_lt_("table_lookup", st);
+            int64_t g1 = (n_idx * (cols / 8) + 255) / 256;
+            gather_rows_f32_kernel<<<(unsigned)(g1 < cap ? g1 : cap), 256, 0, st>>>(
+                static_cast<const __nv_bfloat16*>(T), idx, n_idx, rows, cols, Tg);
+            int64_t g2 = (n_idx * P + 255) / 256;
+            if (rank == 8)
+                gather_a_rows_kernel<8><<<(unsigned)(g2 < cap ? g2 : cap), 256, 0, st>>>(keys, group, P, idx, n_idx,
+                                                                                      rows, U);
+            else
+                gather_a_rows_kernel<16><<<(unsigned)(g2 < cap ? g2 : cap), 256, 0, st>>>(keys, group, P, idx, n_idx,
+                                                                                       rows, U);
+            if ((rc = zg::check_launch("zg_table_lookup(gather)"))) return rc;
+        }
+        return zg::tc_expand(Tg, U, Bop, q, P, (int)n_idx, (int)cols, rank, s, out, st, "table_lookup");
+    }
     char* fb = cv.take<char>((size_t)P * cols * rank * zg::dtype_size(dtype));
     // Fill only B_p [cols, rank]; A rows are regenerated at the gathered
     // rows inside the lookup kernel (rows = 0: no A elements are drawn).

@@ -665,6 +665,9 @@ __device__ __forceinline__ void ex_item_range(int items, int& t0, int& t1) {
     t1 = t0 + per + (b < rem ? 1 : 0);
 }
 
+// R = 8: the upper 8 K of each operand read a zero region; R = 16: they
+// read the second 8 factor columns, loaded beside the first.
+template <int R>
 __global__ void __launch_bounds__(EX_THREADS, 1)
 expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmY, const ExpandArgs a) {
@@ -678,12 +681,14 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
     int t_begin, t_end;
     ex_item_range(a.tiles_m * a.tiles_n * a.chunks, t_begin, t_end);
 
-    // zero halves of the K=16 operands (read through the descriptors' LBO)
-    for (uint32_t i = threadIdx.x; i < EX_LBO / 16; i += EX_THREADS) {
-        reinterpret_cast<uint4*>(smem + EX_AZ)[i] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(smem + EX_BZ)[i] = make_uint4(0, 0, 0, 0);
+    if constexpr (R == 8) {
+        // zero halves of the K=16 operands (read through the descriptors' LBO)
+        for (uint32_t i = threadIdx.x; i < EX_LBO / 16; i += EX_THREADS) {
+            reinterpret_cast<uint4*>(smem + EX_AZ)[i] = make_uint4(0, 0, 0, 0);
+            reinterpret_cast<uint4*>(smem + EX_BZ)[i] = make_uint4(0, 0, 0, 0);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < EX_STAGES; ++s) {
             mbar_init(&full_bar[s], 1);
@@ -717,9 +722,13 @@ expand_tc_kernel(const __grid_constant__ CUtensorMap tmU, const __grid_constant_
             const int p1 = min(a.P, (chunk + 1) * a.chunk);
             for (int p = chunk * a.chunk; p < p1; ++p) {
                 if (!mbar_wait(&empty_bar[stage], phase ^ 1, 11)) { ok = false; break; }
-                mbar_expect_tx(&full_bar[stage], 2 * EX_OP);
-                tma_load_2d(smem + EX_A + stage * EX_OP, &tmU, &full_bar[stage], p * 8, m0);
-                tma_load_2d(smem + EX_B + stage * EX_OP, &tmB, &full_bar[stage], p * 8, n0);
+                mbar_expect_tx(&full_bar[stage], (R / 8) * 2 * EX_OP);
+                tma_load_2d(smem + EX_A + stage * EX_OP, &tmU, &full_bar[stage], p * R, m0);
+                tma_load_2d(smem + EX_B + stage * EX_OP, &tmB, &full_bar[stage], p * R, n0);
+                if constexpr (R == 16) {
+                    tma_load_2d(smem + EX_AZ + stage * EX_OP, &tmU, &full_bar[stage], p * R + 8, m0);
+                    tma_load_2d(smem + EX_BZ + stage * EX_OP, &tmB, &full_bar[stage], p * R + 8, n0);
+                }
                 issued |= 1u << stage;
                 issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
                 if (++stage == EX_STAGES) { stage = 0; phase ^= 1; }
@@ -1096,8 +1105,14 @@ bool tc_expand_ok(int P, int M, int N, int rank, const void* XW, const void* U, 
 
 int tc_expand_r8(const float* XW, const void* U, const void* Bq, int64_t ldb, int P, int M, int N, float s, void* y,
                  cudaStream_t st) {
+    return tc_expand(XW, U, Bq, ldb, P, M, N, 8, s, y, st, "lowrank_expand");
+}
+
+int tc_expand(const float* XW, const void* U, const void* Bq, int64_t ldb, int P, int M, int N, int rank, float s,
+              void* y, cudaStream_t st, const char* name) {
+    if (rank != 8 && rank != 16) return fail(ZG_ERR_INVALID, "tc_expand: rank 8 or 16");
     CUtensorMap tu, tb, ty;
-    const uint64_t q = (uint64_t)P * 8;
+    const uint64_t q = (uint64_t)P * rank;
     if (!make_map_2d(&tu, U, q, M, q, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map_2d(&tb, Bq, q, N, (uint64_t)ldb, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) || !make_map_y(&ty, y, N, M, P))
         return fail(ZG_ERR_CUDA, "tc_expand: tensor maps");
@@ -1113,10 +1128,14 @@ int tc_expand_r8(const float* XW, const void* U, const void* Bq, int64_t ldb, in
     const int grid = items < num_sms() ? items : num_sms();
     // one CTA (and its 512 TMEM columns) per SM
     const size_t smem = EX_SMEM + 1024;
-    if (cudaFuncSetAttribute(expand_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(rank == 8 ? expand_tc_kernel<8> : expand_tc_kernel<16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return fail(ZG_ERR_CUDA, "tc_expand: shared memory attribute");
-    zg::LaunchTimer zg_lt_("lowrank_expand", st);
-    expand_tc_kernel<<<grid, EX_THREADS, smem, st>>>(tu, tb, ty, a);
+    zg::LaunchTimer zg_lt_(name, st);
+    if (rank == 8)
+        expand_tc_kernel<8><<<grid, EX_THREADS, smem, st>>>(tu, tb, ty, a);
+    else
+        expand_tc_kernel<16><<<grid, EX_THREADS, smem, st>>>(tu, tb, ty, a);
     return check_launch("tc_expand");
 }
 

@@ -90,6 +90,10 @@ int fill_operand(const uint32_t* keys, int group, int P, int rank, int64_t rows,
 // with rows ldb apart, XW float32 [M, N], y bf16 [P, M, N] written with TMA
 // bulk stores.
 bool tc_expand_ok(int P, int M, int N, int rank, const void* XW, const void* U, const void* Bq, const void* y);
+// y[p, m, n] = bf16(XW[m, n] + s (U_p B_p^T)[m, n]) for rank 8 or 16: U
+// [M, P r] bf16, Bq [N, P r] (row pitch ldb), XW [M, N] float32, y [P, M, N].
+int tc_expand(const float* XW, const void* U, const void* Bq, int64_t ldb, int P, int M, int N, int rank, float s,
+              void* y, cudaStream_t st, const char* name);
 int tc_expand_r8(const float* XW, const void* U, const void* Bq, int64_t ldb, int P, int M, int N, float s, void* y,
                  cudaStream_t st);
 
