@@ -689,6 +689,15 @@ extern "C" int zg_replay(const float* shaped, const uint32_t* keys, int group, i
     size_t es = zg::dtype_size(dtype);
     char* fa = cv.take<char>((size_t)P * rows * rank * es);
     char* fb = cv.take<char>((size_t)P * cols * rank * es);
+    if (dtype == ZG_F32 && ((int64_t)P * rank) % 4 == 0 && rows <= 2147483647 && cols <= 2147483647) {
+        // float32: the factors in operand layout (A_op [rows, P r], B_op
+        // [cols, P r], contraction columns contiguous) and one NT GEMM with
+        // the fitness weight applied to A as it is staged
+        int rc = zg::factor_operands(keys, group, P, layout, rows, cols, rank, ZG_F32, fa, fb, st);
+        if (rc) return rc;
+        return zg::launch_replay_sgemm(reinterpret_cast<const float*>(fa), reinterpret_cast<const float*>(fb), shaped,
+                                       rank, (int)rows, (int)cols, (int64_t)P * rank, inv_sqrt_rank, out, st);
+    }
     int rc = zg::launch_population_factors(keys, group, P, layout, rows, cols, rank, dtype, fa, fb, st);
     if (rc) return rc;
     SimtGemm g;

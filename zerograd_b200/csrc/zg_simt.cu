@@ -86,7 +86,113 @@ __global__ void __launch_bounds__(THREADS) simt_gemm_kernel(const SimtGemm g) {
     }
 }
 
+// ---- float32 NT replay GEMM ----
+constexpr int RS_BM = 128, RS_BN = 128, RS_BK = 16, RS_PAD = 4;
+
+__global__ void __launch_bounds__(256) replay_sgemm_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                           const float* __restrict__ w, int rank, int M, int N,
+                                                           int64_t K, float alpha, float* __restrict__ C) {
+    __shared__ __align__(16) float As[RS_BK][RS_BM + RS_PAD];
+    __shared__ __align__(16) float Bs[RS_BK][RS_BN + RS_PAD];
+    const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+    const int m0 = blockIdx.y * RS_BM, n0 = blockIdx.x * RS_BN;
+    // staging: thread -> (row lr = tid / 4 + 64 i, k chunk kc = tid % 4) for i = 0, 1
+    const int lr = tid / 4, kc = (tid % 4) * 4;
+    float4 ra[2], rb[2];
+    auto fetch = [&](int64_t k0) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int m = m0 + lr + 64 * i, n = n0 + lr + 64 * i;
+            const int64_t k = k0 + kc;
+            ra[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            rb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < K) {  // K % 4 == 0: a chunk is all in or all out
+                if (m < M) {
+                    ra[i] = *reinterpret_cast<const float4*>(A + (int64_t)m * K + k);
+                    const int64_t q = k / rank;  // the fitness weight of each contraction column
+                    if (rank % 4 == 0) {
+                        const float wq = w[q];
+                        ra[i].x *= wq; ra[i].y *= wq; ra[i].z *= wq; ra[i].w *= wq;
+                    } else {
+                        ra[i].x *= w[k / rank]; ra[i].y *= w[(k + 1) / rank];
+                        ra[i].z *= w[(k + 2) / rank]; ra[i].w *= w[(k + 3) / rank];
+                    }
+                }
+                if (n < N) rb[i] = *reinterpret_cast<const float4*>(B + (int64_t)n * K + k);
+            }
+        }
+    };
+    auto stash = [&]() {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int r = lr + 64 * i;
+            As[kc][r] = ra[i].x; As[kc + 1][r] = ra[i].y; As[kc + 2][r] = ra[i].z; As[kc + 3][r] = ra[i].w;
+            Bs[kc][r] = rb[i].x; Bs[kc + 1][r] = rb[i].y; Bs[kc + 2][r] = rb[i].z; Bs[kc + 3][r] = rb[i].w;
+        }
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    fetch(0);
+    for (int64_t k0 = 0; k0 < K; k0 += RS_BK) {
+        __syncthreads();  // the previous tile's reads are done
+        stash();
+        __syncthreads();
+        if (k0 + RS_BK < K) fetch(k0 + RS_BK);  // in flight during this tile's products
+#pragma unroll
+        for (int kk = 0; kk < RS_BK; ++kk) {
+            float a[8], b[8];
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + tx * 4]);
+            a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+            b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+        if (m >= M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int n = n0 + h * 64 + tx * 4;
+            float* c = C + (int64_t)m * N + n;
+            const float v0 = alpha * acc[i][4 * h], v1 = alpha * acc[i][4 * h + 1], v2 = alpha * acc[i][4 * h + 2],
+                        v3 = alpha * acc[i][4 * h + 3];
+            if (n + 4 <= N && (N % 4) == 0) {
+                *reinterpret_cast<float4*>(c) = make_float4(v0, v1, v2, v3);
+            } else {
+                if (n < N) c[0] = v0;
+                if (n + 1 < N) c[1] = v1;
+                if (n + 2 < N) c[2] = v2;
+                if (n + 3 < N) c[3] = v3;
+            }
+        }
+    }
+}
+
 }  // namespace
+
+int launch_replay_sgemm(const float* A, const float* B, const float* w, int rank, int M, int N, int64_t K, float alpha,
+                        float* C, cudaStream_t st, const char* name) {
+    if (M <= 0 || N <= 0) return ZG_OK;
+    if (K % 4 || rank < 1) return fail(ZG_ERR_INVALID, "replay sgemm: K %% 4 == 0 required");
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!al(A) || !al(B) || !al(C)) return fail(ZG_ERR_INVALID, "replay sgemm: operands must be 16-byte aligned");
+    const int64_t gy = (M + RS_BM - 1) / RS_BM;
+    if (gy > 65535) return fail(ZG_ERR_INVALID, "replay sgemm: M too large");
+    dim3 grid((unsigned)((N + RS_BN - 1) / RS_BN), (unsigned)gy);
+    zg::LaunchTimer zg_lt_(name, st);
+    replay_sgemm_kernel<<<grid, 256, 0, st>>>(A, B, w, rank, M, N, K, alpha, C);
+    return check_launch("replay_sgemm");
+}
 
 template <typename T, typename TO>
 int launch_simt_gemm(const SimtGemm& g, cudaStream_t st, const char* name) {

@@ -40,4 +40,13 @@ struct SimtGemm {
 template <typename T, typename TO>
 int launch_simt_gemm(const SimtGemm& g, cudaStream_t st, const char* name = "simt_gemm");
 
+// Float32 replay contraction on the CUDA cores, operands K-contiguous:
+//   C[m, n] = alpha * sum_k (A[m, k] * w[k / rank]) * B[n, k]
+// A [M, K] (row pitch K), B [N, K], C [M, N] float32; K % 4 == 0 and the
+// operands 16-byte aligned.  128 x 128 tiles, 8 x 8 outputs per thread, the
+// next K tile read into registers while the current one is multiplied; each
+// output's sum runs over k in order.
+int launch_replay_sgemm(const float* A, const float* B, const float* w, int rank, int M, int N, int64_t K, float alpha,
+                        float* C, cudaStream_t st, const char* name = "replay_gemm");
+
 }  // namespace zg
