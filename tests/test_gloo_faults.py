@@ -1,8 +1,9 @@
-"""Rank failures around the fitness all-gather, on CPU gloo ranks (no GPU
-is faulted): a rank that dies or raises before the collective makes the
-survivor's all-gather end with an error within the process group's short
-timeout, instead of hanging; the survivor then leaves without touching the
-group again."""
+"""Rank failures around the collectives of a generation, on CPU gloo ranks
+(no GPU is faulted): a rank that dies or raises before the fitness
+all-gather, or dies before the exchanged update's all-to-all of partial
+replays, makes the survivor's collective end with an error within the
+process group's short timeout, instead of hanging; the survivor then leaves
+without touching the group again."""
 import datetime
 import os
 import socket
@@ -33,7 +34,7 @@ def _worker(rank, port, mode, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=5))
     if rank == 1:
-        if mode == "exit":
+        if mode in ("exit", "exit_exchange"):
             os._exit(0)  # dies without joining the collective
         try:
             raise RuntimeError("loss function failed on this rank")
@@ -42,7 +43,13 @@ def _worker(rank, port, mode, q):
             _leave(q, 1)  # a failed rank leaves; it does not join the collective
     t0 = time.monotonic()
     try:
-        zg.allgather_losses(torch.ones(3), [3, 3])
+        if mode == "exit_exchange":
+            # the exchanged update's partial-replay all-to-all
+            from zerograd_b200._exchange import ExchangedReplay
+
+            ExchangedReplay(rank, 2, 0, 0).exchange(torch.ones(1, 16))
+        else:
+            zg.allgather_losses(torch.ones(3), [3, 3])
         q.put((rank, "completed", time.monotonic() - t0))
     except Exception as e:  # the collective reports the lost peer
         q.put((rank, "error", type(e).__name__, time.monotonic() - t0))
@@ -58,7 +65,7 @@ def _run(mode):
         p.start()
     out = {}
     deadline = time.monotonic() + 90
-    while len(out) < (1 if mode == "exit" else 2) and time.monotonic() < deadline:
+    while len(out) < (2 if mode == "raise" else 1) and time.monotonic() < deadline:
         try:
             item = q.get(timeout=5)
         except Exception:
@@ -81,3 +88,9 @@ def test_raising_rank_ends_the_allgather_with_an_error():
     out = _run("raise")
     assert out[1][0] == "raised", out
     assert out[0][0] == "error", out
+
+
+def test_dead_rank_ends_the_exchange_with_an_error():
+    out = _run("exit_exchange")
+    assert 0 in out and out[0][0] == "error", out
+    assert out[0][-1] < 60, out
