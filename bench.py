@@ -63,9 +63,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     # "headline": the decoder-LM generation alone; "all" adds the secondary
-    # workloads and the CPU baseline on one GPU; "profile": a small case for
+    # workloads and the CPU baseline on one GPU; "profile": small cases for
     # ncu captures (two evaluations of a 2-layer decoder-LM chunk of 16
-    # candidates at the LM's shapes), no JSON line
+    # candidates at the LM's shapes, then that model's replay for 2048
+    # candidates), no JSON line
     ap.add_argument("--sections", choices=["all", "headline", "profile"], default="all")
     return ap.parse_args()
 
@@ -559,9 +560,11 @@ def family_rates(kern: dict, P_local: int) -> dict:
 
 
 def profile_case(dev):
-    """Two evaluations of a 2-layer decoder-LM chunk (16 candidates, the LM's
-    shapes): every forward kernel of the headline at a size ncu captures
-    in seconds."""
+    """Small cases for ncu captures, at the decoder LM's shapes: two
+    evaluations of a 2-layer chunk of 16 candidates (every forward kernel of
+    the headline), then the replay and SGD step of the same 2-layer model for
+    the headline's population (2048 candidates, rank 16: the replay split
+    over candidate groups) from synthetic losses."""
     import torch
 
     import zerograd_b200 as zg
@@ -576,6 +579,13 @@ def profile_case(dev):
         losses = opt.evaluate_shard(params, gen, loss, batch, range(cfg["P"]))
         torch.cuda.synchronize()
     print("profile case done, mean loss", float(losses.mean()))
+    P = LM["P"]
+    ropt = zg.ZeroGrad(lm_manifest(cfg), zg.sgd(1e-3), P, cfg["rank"], cfg["sigma"], 0, "profile-replay")
+    g = torch.Generator(device=dev).manual_seed(1)
+    rlosses = torch.randn(P, generator=g, device=dev)
+    ropt.step_from_losses(ropt.init(params), params, rlosses)
+    torch.cuda.synchronize()
+    print("replay case done")
 
 
 def run_ours(args):
