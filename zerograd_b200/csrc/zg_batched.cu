@@ -588,8 +588,9 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
                             r0 = __bfloat162float(rr.x);
                             r1 = __bfloat162float(rr.y);
                         }
-                        h[j] = __floats2bfloat162_rn(zg_epilogue_value(v[8 * c + 2 * j], a.act, has_res, r0),
-                                                     zg_epilogue_value(v[8 * c + 2 * j + 1], a.act, has_res, r1));
+                        const float2 o = zg_epilogue_pair(v[8 * c + 2 * j], v[8 * c + 2 * j + 1], a.act, has_res,
+                                                          r0, r1);
+                        h[j] = __floats2bfloat162_rn(o.x, o.y);
                     }
                     *reinterpret_cast<uint4*>(buf + box64_off(lane, c)) = *reinterpret_cast<uint4*>(h);
                 }

@@ -226,6 +226,28 @@ __device__ __forceinline__ float zg_epilogue_value(float v, int act, bool has_re
     return has_res ? r + v : v;
 }
 
+// Two neighbouring outputs, the same values as zg_epilogue_value on each:
+// the intermediate bf16 roundings go through the paired conversion (one
+// instruction for both, off the special-function pipe that the single
+// conversion and the GELU's exp2 and reciprocal share).
+__device__ __forceinline__ float2 zg_round_pair(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return make_float2(__low2float(h), __high2float(h));
+}
+__device__ __forceinline__ float2 zg_epilogue_pair(float a, float b, int act, bool has_res, float ra, float rb) {
+    float2 v = (act || has_res) ? zg_round_pair(a, b) : make_float2(a, b);
+    if (act == ZG_ACT_GELU) {
+        v.x = zg_gelu_tanh(v.x);
+        v.y = zg_gelu_tanh(v.y);
+        if (has_res) v = zg_round_pair(v.x, v.y);
+    }
+    if (has_res) {
+        v.x = ra + v.x;
+        v.y = rb + v.y;
+    }
+    return v;
+}
+
 // One thread's 32 consecutive outputs of a row, written straight to global
 // memory (zg_epilogue_value per element).  d and r 16-byte aligned; `n`
 // valid columns (32 or more take the vector path).
@@ -248,8 +270,8 @@ __device__ __forceinline__ void zg_store_row32(const float (&v)[32], __nv_bfloat
                     r0 = __bfloat162float(rr.x);
                     r1 = __bfloat162float(rr.y);
                 }
-                h[j] = __floats2bfloat162_rn(zg_epilogue_value(v[i + 2 * j], act, r != nullptr, r0),
-                                             zg_epilogue_value(v[i + 2 * j + 1], act, r != nullptr, r1));
+                const float2 o = zg_epilogue_pair(v[i + 2 * j], v[i + 2 * j + 1], act, r != nullptr, r0, r1);
+                h[j] = __floats2bfloat162_rn(o.x, o.y);
             }
             *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<uint4*>(h);
         }
