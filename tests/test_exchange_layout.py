@@ -105,3 +105,23 @@ def test_all_to_all_delivers_every_group_in_order(world):
         assert p.exitcode == 0
     for rank, ok, shapes in out:
         assert ok and shapes, rank
+
+
+def test_exchange_applies_only_to_whole_candidate_groups():
+    """The exchanged update needs the population split into groups the ranks
+    hold whole (zg_replay_split_count(P, r) a multiple of the world size,
+    equal consecutive shards); otherwise the replicated update runs."""
+    from zerograd_b200 import _lib as L
+
+    lib = L.load()
+    assert lib.zg_replay_split_count(2048, 16) == 8
+    assert lib.zg_replay_split_count(256, 8) == 1  # 2048 contraction columns: too short to split
+    assert lib.zg_replay_split_count(1024, 16) == 4
+    for world in (2, 4, 8):
+        n = 2048 // world
+        assert all(ExchangedReplay(r, world, r * n, n).applies(2048, 16) for r in range(world))
+    assert not ExchangedReplay(0, 3, 0, 683).applies(2048, 16)      # 8 groups do not split over 3 ranks
+    assert not ExchangedReplay(1, 2, 1000, 1048).applies(2048, 16)  # uneven shards
+    assert not ExchangedReplay(0, 2, 0, 128).applies(256, 8)        # one group only
+    assert not ExchangedReplay(0, 8, 0, 128).applies(1024, 16)      # 4 groups over 8 ranks
+    assert not ExchangedReplay(0, 1, 0, 2048).applies(2048, 16)     # one process: the plain replay
