@@ -151,6 +151,105 @@ __global__ void __launch_bounds__(256) norm_reg_kernel(const NormArgs a) {
     }
 }
 
+// bf16 rows held packed: each lane keeps its chunks of R rows as raw 16-byte
+// words (12 registers per row at C = 768 instead of 24) and widens them to
+// float32 where the statistics and the output use them, so R = 4 rows per
+// warp fit in the registers the float form needs for two: twice the HBM
+// reads in flight.  Same per-lane arithmetic, in the same order, as
+// norm_reg_kernel (the same bits).
+template <int CH, int R>
+__global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const NormArgs a) {
+    const int lane = threadIdx.x % 32;
+    const int64_t rows = (int64_t)a.P * a.M;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const int64_t nwarps = (int64_t)gridDim.x * blockDim.x / 32;
+    const int chunks = a.C / 8;
+    for (int64_t g0 = warp0 * R; g0 < rows; g0 += nwarps * R) {
+        uint4 raw[R][CH];
+        float s2[R], mean[R], rinv[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t g = g0 + q;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) raw[q][j] = make_uint4(0, 0, 0, 0);
+            if (g >= rows) continue;
+            const int p = (int)(g / a.M);
+            const int64_t m = g % a.M;
+            const __nv_bfloat16* xr =
+                static_cast<const __nv_bfloat16*>(a.x) + ((a.x_batched ? (int64_t)p : 0) * a.M + m) * a.C;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+                const int c = lane + 32 * j;
+                if (c < chunks) raw[q][j] = *reinterpret_cast<const uint4*>(xr + 8 * c);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            float s1 = 0.f;
+            mean[q] = 0.f;
+            s2[q] = 0.f;
+            if (a.kind == NORM_LAYER) {
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                    if (lane + 32 * j < chunks) {
+                        float f[8];
+                        bf16x8_to_f32(raw[q][j], f);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) s1 += f[i];
+                    }
+                mean[q] = __fdiv_rn(warp_sum(s1), (float)a.C);
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                    if (lane + 32 * j < chunks) {
+                        float f[8];
+                        bf16x8_to_f32(raw[q][j], f);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float d = f[i] - mean[q];
+                            s2[q] = fmaf(d, d, s2[q]);
+                        }
+                    }
+            } else {
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                    if (lane + 32 * j < chunks) {
+                        float f[8];
+                        bf16x8_to_f32(raw[q][j], f);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) s2[q] = fmaf(f[i], f[i], s2[q]);
+                    }
+            }
+            rinv[q] = __fdiv_rn(1.f, __fsqrt_rn(__fdiv_rn(warp_sum(s2[q]), (float)a.C) + a.eps));
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t g = g0 + q;
+            if (g >= rows) continue;
+            const int p = (int)(g / a.M);
+            const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(a.scale) + (a.p_batched ? (int64_t)p : 0) * a.C;
+            const __nv_bfloat16* br =
+                a.bias ? static_cast<const __nv_bfloat16*>(a.bias) + (a.p_batched ? (int64_t)p : 0) * a.C : nullptr;
+            __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(a.y) + g * a.C;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+                const int c = lane + 32 * j;
+                if (c < chunks) {
+                    float f[8], sc[8], bi[8], o[8];
+                    bf16x8_to_f32(raw[q][j], f);
+                    load8(sr + 8 * c, sc);
+                    if (br) load8(br + 8 * c, bi);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        o[i] = __fmul_rn(__fmul_rn(f[i] - mean[q], rinv[q]), sc[i]);
+                        if (br) o[i] = __fadd_rn(o[i], bi[i]);
+                    }
+                    store8(yr + 8 * c, o);
+                }
+            }
+        }
+    }
+}
+
 // Any C and alignment: three passes over the row in global memory (the
 // second and third hit L1/L2).
 template <typename T>
@@ -210,6 +309,20 @@ int launch_norm(const NormArgs& a, cudaStream_t st, const char* name) {
     int64_t blocks = (rows + 8 * R - 1) / (8 * R);  // 8 warps per block
     if (blocks > (int64_t)sm_count_norm() * 16) blocks = (int64_t)sm_count_norm() * 16;
     if (blocks < 1) blocks = 1;
+    if constexpr (sizeof(T) == 2) {
+        if (vec && a.C <= 1024) {
+            // bf16: four rows per warp, held packed
+            int64_t b4 = (rows + 8 * 4 - 1) / (8 * 4);
+            if (b4 > (int64_t)sm_count_norm() * 16) b4 = (int64_t)sm_count_norm() * 16;
+            if (b4 < 1) b4 = 1;
+            zg::LaunchTimer zg_lt_(name, st);
+            if (a.C <= 256) norm_packed_kernel<1, 4><<<(unsigned)b4, 256, 0, st>>>(a);
+            else if (a.C <= 512) norm_packed_kernel<2, 4><<<(unsigned)b4, 256, 0, st>>>(a);
+            else if (a.C <= 768) norm_packed_kernel<3, 4><<<(unsigned)b4, 256, 0, st>>>(a);
+            else norm_packed_kernel<4, 4><<<(unsigned)b4, 256, 0, st>>>(a);
+            return zg::check_launch(name);
+        }
+    }
     zg::LaunchTimer zg_lt_(name, st);
     if (vec && a.C <= 256)
         norm_reg_kernel<T, 1, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
