@@ -82,6 +82,8 @@ def test_norm_ops_under_vmap(cuda, oracle):
     (4, 256, 2, 64, True, torch.bfloat16, "attention"),        # decoder LM: seq 256, causal
     (3, 100, 3, 64, True, torch.bfloat16, "attention"),        # ragged causal
     (2, 128, 4, 64, False, torch.bfloat16, "attention"),
+    (300, 65, 6, 64, False, torch.bfloat16, "attention"),      # 1800 (z, head) units: many per CTA, one tile each
+    (200, 200, 3, 64, True, torch.bfloat16, "attention"),      # 600 units of two tiles, ragged causal
     (5, 65, 4, 16, False, torch.bfloat16, "attention_simt"),   # the reference example's head dim 16
     (3, 50, 2, 64, True, torch.float32, "attention_simt"),
     (2, 300, 2, 64, True, torch.bfloat16, "attention_simt"),   # longer than one score row in TMEM

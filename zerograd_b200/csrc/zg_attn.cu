@@ -7,16 +7,18 @@
 // j > i masked).  q, k, v, o are [Z, S, H, D], the head-interleaved layout
 // the q/k/v projections produce, so no transpose is materialised.
 //
-// Tensor-core path (bf16, D = 64, S <= 256): one CTA per (128-query tile,
-// head, z).  TMA brings the query tile and the whole key and value sequence
-// (4-D tensor maps over [Z, S, H, D], 128-byte swizzle); one tcgen05 MMA
-// chain computes the scores S = Q K^T into TMEM (M=128, N=128 or 256); each
-// thread owns one query row, takes its max over the row in TMEM and writes
-// p = 2^(s * log2(e)/sqrt(D) - max) as bf16 into shared memory in the MMA's
-// K-major swizzled layout (over the finished Q and K tiles); a second MMA
-// chain computes O = P V (V as the MN-major operand) into the first 64 TMEM
-// columns; the epilogue divides by the row sum of the bf16 p and stores O.
-// The whole score row fits (S <= 256), so one pass suffices.
+// Tensor-core path (bf16, D = 64, S <= 256): a persistent kernel over the
+// (z, head) units.  TMA brings a unit's query tiles and its whole key and
+// value sequence (4-D tensor maps over [Z, S, H, D], 128-byte swizzle); one
+// tcgen05 MMA chain per 128-query tile computes the scores S = Q K^T into
+// TMEM (M=128, N = the keys the tile sees: a causal first tile stops at
+// 128); one thread per query row takes its max over the row in TMEM and
+// writes p = 2^(s * log2(e)/sqrt(D) - max) as bf16 back into TMEM over the
+// scores; a second MMA chain computes O = P V with P read from TMEM (V the
+// MN-major operand from shared memory); the epilogue divides by the row sum
+// of the bf16 p and stores O by TMA.  The whole score row fits (S <= 256),
+// so one pass suffices.  Two softmax groups alternate over the tiles, and
+// the next unit's loads overlap the current one's work.
 //
 // Other shapes (D != 64, S > 256, float32): a warp per query row with an
 // online softmax over the keys (float32 arithmetic).
@@ -27,13 +29,24 @@
 
 namespace {
 
-constexpr int AT_THREADS = 256;  // two threads per query row, each half of the key columns
-constexpr uint32_t AT_Q = 0;                // 16 KiB: 128 query rows x 128 B
-constexpr uint32_t AT_K = 16384;            // 32 KiB: up to 256 key rows
-constexpr uint32_t AT_V = 65536;            // 32 KiB: up to 256 value rows
-constexpr uint32_t AT_P = 0;                // 64 KiB over Q, K and the gap: P [128, 256] bf16, 4 K-blocks
-constexpr uint32_t AT_O = 0;                // 16 KiB over P once P V is done: the output tile [128, 64] bf16
-constexpr uint32_t AT_SMEM = 65536 + 32768; // 96 KiB
+// Persistent CTA (one per SM), 320 threads: warp 0 issues the TMA loads,
+// warp 1 the MMAs, warps 2-5 and 6-9 are two softmax groups of one thread
+// per query row.  Work unit = one (z, head): its query tiles (one or two of
+// 128 rows), keys and values land in one of two shared-memory buffers, so
+// the next unit loads while this one computes.  Tile j of the CTA's
+// sequence goes to group j % 2, which owns TMEM columns [256 g, 256 g + 256):
+// the scores S (up to 256 columns), then P written over them in place (each
+// half of the tile's keys at the start of its own score columns, key pair
+// (c, c+1) of a half as bf16x2 in its column c/2; the P V MMA reads it from
+// TMEM), and O in columns 192..255.  While one group runs its softmax, the other's
+// MMAs, output stores and the next loads proceed.
+constexpr int AT_THREADS = 320;
+constexpr uint32_t AT_Q = 0;         // 2 x 16 KiB: the unit's query tiles (then their output staging)
+constexpr uint32_t AT_K = 32768;     // 32 KiB: up to 256 key rows
+constexpr uint32_t AT_V = 65536;     // 32 KiB: up to 256 value rows
+constexpr uint32_t AT_BUF = 98304;   // one unit
+constexpr uint32_t AT_ONES = 2 * AT_BUF;  // 512 B of bf16 ones: the B operand of the row-sum MMA
+constexpr uint32_t AT_SMEM = AT_ONES + 512;
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -42,166 +55,286 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 struct AttnArgs {
-    __nv_bfloat16* o;
     int Z, S, H, s_pad, causal;
     float scale_log2;  // log2(e) / sqrt(D)
 };
 
-__global__ void __launch_bounds__(AT_THREADS, 2)
+// The query tile of the CTA's tile j (unit j / nq): with two tiles per unit
+// the order alternates between units, so each softmax group (j % 2) takes
+// the short causal tile and the long one in turn.
+__device__ __forceinline__ int tile_qt(int j, int nq) { return nq == 2 ? ((j & 1) ^ ((j >> 1) & 1)) : 0; }
+
+// keys a query tile sees: causal tiles stop at their last query
+__device__ __forceinline__ int tile_keys(const AttnArgs& a, int qt) {
+    const int q0 = qt * 128;
+    return a.causal && q0 + 128 < a.s_pad ? q0 + 128 : a.s_pad;
+}
+
+// Running maxima (8 independent chains) over a 32-key chunk of scores; only
+// a chunk that crosses the row's last visible key tests each key.
+__device__ __forceinline__ void chunk_max(const uint32_t (&r)[32], int c, int vis, float (&mx8)[8]) {
+    if (c + 32 <= vis) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx8[e % 8] = fmaxf(mx8[e % 8], __uint_as_float(r[e]));
+    } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+            if (c + e < vis) mx8[e % 8] = fmaxf(mx8[e % 8], __uint_as_float(r[e]));
+    }
+}
+
+// bf16 weights p = 2^(s * scale - mx) of a 32-key chunk as 16 packed pairs
+// (zero for keys past the row's last visible one, or for a chunk off).
+__device__ __forceinline__ void chunk_weights(const uint32_t (&r)[32], int c, int vis, bool on, float scale,
+                                              float mx, uint32_t (&pk)[16]) {
+    if (on && c + 32 <= vis) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const __nv_bfloat162 b2 =
+                __floats2bfloat162_rn(ex2_approx(fmaf(__uint_as_float(r[2 * e]), scale, -mx)),
+                                      ex2_approx(fmaf(__uint_as_float(r[2 * e + 1]), scale, -mx)));
+            pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+    } else if (on) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int col = c + 2 * e;
+            const float p0 = col < vis ? ex2_approx(fmaf(__uint_as_float(r[2 * e]), scale, -mx)) : 0.f;
+            const float p1 = col + 1 < vis ? ex2_approx(fmaf(__uint_as_float(r[2 * e + 1]), scale, -mx)) : 0.f;
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+            pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = 0u;  // masked keys: zero weight
+    }
+}
+
+// A bounded wait taken by every lane of a warp, with one outcome for all.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, code));
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
     extern __shared__ uint8_t dyn_smem[];
-    __shared__ __align__(8) uint64_t load_bar, mma_bar;
+    __shared__ __align__(8) uint64_t full_bar[2], empty_bar[2], s_full[2], p_full[2], o_full[2], t_empty[2], done_bar;
     __shared__ uint32_t tmem_base_sh;
-    __shared__ float s_red[2][128];  // the two column halves' row max, then row sum
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
-    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
-    const int quad = warp % 4, half = warp / 4;  // TMEM lane quadrant; key-column half
-    const int r = quad * 32 + lane;              // this thread's query row in the tile
-    const int qt = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
-    const int q0 = qt * 128;
-    // keys this query tile can see: causal tiles stop at their last query
-    const int n_keys = a.causal && q0 + 128 < a.s_pad ? q0 + 128 : a.s_pad;
-    const int kboxes = n_keys / 128;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nq = a.s_pad / 128;  // query tiles per unit; also the key/value boxes
+    const int64_t units = (int64_t)a.Z * a.H;
+    const int my_units = units > (int64_t)blockIdx.x ? (int)((units - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    const int tiles = my_units * nq;
 
-    if (t == 0) {
-        mbar_init(&load_bar, 1);
-        mbar_init(&mma_bar, 1);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&empty_bar[i], 4 * nq);  // the four warps of each of the unit's tiles
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&t_empty[i], 4);
+        }
+        mbar_init(&done_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) tmem_alloc(&tmem_base_sh, 256);
+    if (warp == 1) tmem_alloc(&tmem_base_sh, 512);
+    if (threadIdx.x < 128) reinterpret_cast<uint32_t*>(smem + AT_ONES)[threadIdx.x] = 0x3F803F80u;  // bf16 1.0 pairs
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the ones visible to the tensor cores
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
-    bool ok = true;
 
-    if (t == 0) {
-        mbar_expect_tx(&load_bar, (1 + 2 * kboxes) * 16384);
-        tma_load_4d(smem + AT_Q, &tmQ, &load_bar, 0, h, q0, z);
-        for (int b = 0; b < kboxes; ++b) {
-            tma_load_4d(smem + AT_K + b * 16384, &tmK, &load_bar, 0, h, b * 128, z);
-            tma_load_4d(smem + AT_V + b * 16384, &tmV, &load_bar, 0, h, b * 128, z);
-        }
-        if (mbar_wait(&load_bar, 0, 81)) {
-            tc_fence_after();
-            const uint32_t idesc = idesc_bf16(128, n_keys, 0);
-            const uint32_t qa = smem_u32(smem + AT_Q), ka = smem_u32(smem + AT_K);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                umma_bf16(tmem, smem_desc(qa + k * 32, 16, 1024), smem_desc(ka + k * 32, 16, 1024), idesc,
-                          k > 0 ? 1u : 0u);
-            umma_commit(&mma_bar);
-        }
-    }
-    ok = mbar_wait(&mma_bar, 0, 82);
-    tc_fence_after();
-
-    // ---- softmax: this thread's row, its half of the key columns ----
-    const int qi = q0 + r;
-    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-    // columns [0, vis) are visible to this query: the keys, up to the query when causal
-    const int vis = a.causal ? (qi + 1 < a.S ? qi + 1 : a.S) : a.S;
-    // the warp's last visible column (its last row sees the most): chunks past it hold no weight
-    const int wvis = __reduce_max_sync(0xffffffffu, vis);
-    const int hw = n_keys / 2, c_lo = half * hw, c_hi = c_lo + hw;
-    const int c_end = wvis < c_hi ? ((wvis - c_lo + 31) / 32) * 32 + c_lo : c_hi;  // chunks to evaluate
-    float mx = -INFINITY;
-    for (int c = c_lo; c < c_end; c += 32) {
-        float v[32];
-        tmem_ld32(trow + c, v);
-        if (c + 32 <= vis) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, v[j]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (c + j < vis) mx = fmaxf(mx, v[j]);
-        }
-    }
-    s_red[half][r] = mx;
-    __syncthreads();
-    mx = fmaxf(s_red[0][r], s_red[1][r]) * a.scale_log2;  // scale_log2 > 0: max(s) * scale = max(s * scale)
-    float sum = 0.f;
-    for (int c = c_lo; c < c_hi; c += 32) {
-        uint32_t pk[16];
-        if (c < c_end) {
-            float v[32];
-            tmem_ld32(trow + c, v);
-            const bool full = c + 32 <= vis;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                float pe[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int col = c + 2 * j + e;
-                    pe[e] = full || col < vis ? ex2_approx(fmaf(v[2 * j + e], a.scale_log2, -mx)) : 0.f;
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t issued = 0, issue_parity = 0;
+            for (int u = 0; u < my_units; ++u) {
+                const int b = u & 1;
+                const uint32_t m = (uint32_t)(u >> 1);
+                if (!mbar_wait(&empty_bar[b], (m & 1) ^ 1, 81)) break;
+                const int64_t U = blockIdx.x + (int64_t)u * gridDim.x;
+                const int z = (int)(U / a.H), h = (int)(U % a.H);
+                uint8_t* buf = smem + b * AT_BUF;
+                mbar_expect_tx(&full_bar[b], (uint32_t)(3 * nq) * 16384u);
+                for (int i = 0; i < nq; ++i) {
+                    tma_load_4d(buf + AT_Q + i * 16384, &tmQ, &full_bar[b], 0, h, i * 128, z);
+                    tma_load_4d(buf + AT_K + i * 16384, &tmK, &full_bar[b], 0, h, i * 128, z);
+                    tma_load_4d(buf + AT_V + i * 16384, &tmV, &full_bar[b], 0, h, i * 128, z);
                 }
-                const __nv_bfloat162 b2 = __floats2bfloat162_rn(pe[0], pe[1]);
-                sum += __low2float(b2) + __high2float(b2);  // the weights the PV product uses
-                pk[j] = *reinterpret_cast<const uint32_t*>(&b2);
+                issued |= 1u << b;
+                issue_parity = (issue_parity & ~(1u << b)) | ((m & 1) << b);
             }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) pk[j] = 0u;  // masked keys: zero weight
+            // loads still in flight (only after an abort) land before the CTA exits
+            for (int b = 0; b < 2; ++b)
+                if (issued >> b & 1)
+                    for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(&full_bar[b], issue_parity >> b & 1); ++i) {
+                    }
         }
-        // P is the K-major, 128-byte swizzled A operand: 64-column blocks of
-        // [128 rows x 128 B], 16-byte chunk ch of row r at (ch ^ (r & 7)) * 16
-        uint8_t* blk = smem + AT_P + (c / 64) * 16384 + r * 128;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // S(j) is issued before P V of tile j-1, so group j % 2 starts its
+            // softmax while the other group finishes its own
+            for (int j = 0; j <= tiles; ++j) {
+                if (j < tiles) {
+                    const int u = j / nq, qt = tile_qt(j, nq), g = j & 1, b = u & 1;
+                    const uint32_t n = (uint32_t)(j >> 1);
+                    if (j % nq == 0 && !mbar_wait(&full_bar[b], (uint32_t)(u >> 1) & 1, 82)) break;
+                    if (!mbar_wait(&t_empty[g], (n & 1) ^ 1, 83)) break;
+                    tc_fence_after();
+                    const uint32_t idesc = idesc_bf16(128, tile_keys(a, qt), 0);
+                    const uint32_t qa = smem_u32(smem + b * AT_BUF + AT_Q + qt * 16384);
+                    const uint32_t ka = smem_u32(smem + b * AT_BUF + AT_K);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int ch = (c % 64) / 8 + i;
-            *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) * 16)) =
-                make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                    for (int k = 0; k < 4; ++k)
+                        umma_bf16(tmem + g * 256, smem_desc(qa + k * 32, 16, 1024), smem_desc(ka + k * 32, 16, 1024),
+                                  idesc, k > 0 ? 1u : 0u);
+                    umma_commit(&s_full[g]);
+                }
+                if (j >= 1) {
+                    const int jp = j - 1;
+                    const int u = jp / nq, qt = tile_qt(jp, nq), g = jp & 1, b = u & 1;
+                    const uint32_t n = (uint32_t)(jp >> 1);
+                    if (!mbar_wait(&p_full[g], n & 1, 84)) break;
+                    tc_fence_after();
+                    const uint32_t idesc = idesc_bf16(128, 64, 1);
+                    const uint32_t va = smem_u32(smem + b * AT_BUF + AT_V);
+                    const uint32_t pt = tmem + g * 256;
+                    const int hw = tile_keys(a, qt) / 2, hk = hw / 16;  // each half's P at the start of its scores
+                    // the row sums of P: P times a [keys x 16] block of ones
+                    // (no swizzle, K-major; every address of the 512 B holds
+                    // 1.0), into columns hw/2 .. hw/2 + 15 (scores already read)
+                    const uint32_t idesc_sum = idesc_bf16(128, 16, 0);
+                    const uint64_t ones = smem_desc_noswizzle(smem_u32(smem + AT_ONES), 128, 256);
+                    for (int kk = 0; kk < 2 * hk; ++kk) {
+                        const uint32_t pa = pt + (kk < hk ? kk * 8 : hw + (kk - hk) * 8);
+                        umma_bf16_ts(pt + 192, pa, smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc,
+                                     kk > 0 ? 1u : 0u);
+                        umma_bf16_ts(pt + hw / 2, pa, ones, idesc_sum, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&o_full[g]);
+                }
+            }
+            // every MMA this thread issued has completed before TMEM is freed
+            umma_commit(&done_bar);
+            for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(&done_bar, 0); ++i) {
+            }
         }
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
-    tc_fence_before();
-    __syncthreads();  // every thread's max is read (s_red reusable), P complete
-    tc_fence_after();
-    s_red[half][r] = sum;
+    } else {
+        const int g = (warp - 2) / 4, quad = warp % 4;  // quad: this warp's TMEM lane quarter
+        const int r = quad * 32 + lane;                 // this thread's query row in the tile
+        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(g * 256);
+        for (int j = g; j < tiles; j += 2) {
+            const uint32_t n = (uint32_t)(j >> 1);
+            const int u = j / nq, qt = tile_qt(j, nq), b = u & 1;
+            const int64_t U = blockIdx.x + (int64_t)u * gridDim.x;
+            const int z = (int)(U / a.H), h = (int)(U % a.H);
+            const int q0 = qt * 128, n_keys = tile_keys(a, qt), hw = n_keys / 2;
+            if (!warp_wait(&s_full[g], n & 1, 85)) break;
+            tc_fence_after();
 
-    if (t == 0 && ok) {
-        const uint32_t idesc = idesc_bf16(128, 64, 1);
-        const uint32_t pa = smem_u32(smem + AT_P), va = smem_u32(smem + AT_V);
-        for (int kk = 0; kk < n_keys / 16; ++kk)
-            umma_bf16(tmem, smem_desc(pa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
-                      smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc, kk > 0 ? 1u : 0u);
-        umma_commit(&mma_bar);
-    }
-    ok = ok && mbar_wait(&mma_bar, 1, 83);
-    tc_fence_after();
-    __syncthreads();  // both halves' sums are in s_red; P is consumed by the MMA
-    {
-        // O / sum -> bf16 into the staging tile (over P; 128-byte swizzle,
-        // the layout of the output box), then one TMA store
-        float o[32];
-        tmem_ld32(trow + half * 32, o);
-        const float inv = 1.f / (s_red[0][r] + s_red[1][r]);
-        uint8_t* row = smem + AT_O + r * 128;
+            // columns [0, vis) are visible to this query: the keys, up to the query when causal
+            const int qi = q0 + r;
+            const int vis = a.causal ? (qi + 1 < a.S ? qi + 1 : a.S) : a.S;
+            // the warp's last visible column (its last row sees the most): chunks past it hold no weight
+            const int wvis = __reduce_max_sync(0xffffffffu, vis);
+            const int c_end = ((wvis + 31) / 32) * 32 < n_keys ? ((wvis + 31) / 32) * 32 : n_keys;
+            // The keys are taken as two halves [0, hw) and [hw, n_keys), chunk i
+            // of each side by side (two loads in flight).  Only chunks that
+            // cross this row's last visible key test each key.
+            float mx8[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            uint4 pk;
-            __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
+            for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+#pragma unroll 1
+            for (int i = 0; 32 * i < hw && 32 * i < c_end; ++i) {
+                const int cl = 32 * i, chi = hw + 32 * i;
+                const bool two = chi < c_end;
+                uint32_t rl[32], rh[32];
+                tmem_ld32_nowait(trow + cl, rl);
+                if (two) tmem_ld32_nowait(trow + chi, rh);
+                tmem_wait_ld32(rl);
+                if (two) tmem_wait_ld32(rh);
+                chunk_max(rl, cl, vis, mx8);
+                if (two) chunk_max(rh, chi, vis, mx8);
+            }
+            float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            mx *= a.scale_log2;  // scale_log2 > 0: max(s) * scale = max(s * scale)
+#pragma unroll 1
+            for (int i = 0; 32 * i < hw; ++i) {
+                const int cl = 32 * i, chi = hw + 32 * i;
+                const bool lo_on = cl < c_end, hi_on = chi < c_end;
+                uint32_t rl[32], rh[32];
+                if (lo_on) tmem_ld32_nowait(trow + cl, rl);
+                if (hi_on) tmem_ld32_nowait(trow + chi, rh);
+                if (lo_on) tmem_wait_ld32(rl);
+                if (hi_on) tmem_wait_ld32(rh);
+                // each half's weights at the start of its own scores, over
+                // columns this thread has already read: keys (2e, 2e+1) of
+                // chunk i in column 16 i + e of the half
+                uint32_t pk[16];
+                chunk_weights(rl, cl, vis, lo_on, a.scale_log2, mx, pk);
+                tmem_st16u(trow + cl / 2, pk);
+                chunk_weights(rh, chi, vis, hi_on, a.scale_log2, mx, pk);
+                tmem_st16u(trow + hw + cl / 2, pk);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full[g]);
+
+            if (!warp_wait(&o_full[g], n & 1, 86)) break;
+            tc_fence_after();
+            // O / sum -> bf16 into this warp's 32 rows of the query tile's
+            // (finished) buffer, 128-byte swizzled like the output box, in two
+            // halves of 32 columns; then one TMA store of the warp's rows
+            float sum[16];
+            tmem_ld16(trow + hw / 2, sum);  // the row sum of the bf16 weights (tensor cores, float32)
+            const float inv = 1.f / sum[0];
+            uint8_t* stage = smem + b * AT_BUF + AT_Q + qt * 16384 + quad * 4096;
+            uint8_t* row = stage + lane * 128;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) hp[e] = __floats2bfloat162_rn(o[8 * i + 2 * e] * inv, o[8 * i + 2 * e + 1] * inv);
-            const int ch = half * 4 + i;
-            *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) * 16)) = pk;
+            for (int half = 0; half < 2; ++half) {
+                float o[32];
+                tmem_ld32(trow + 192 + 32 * half, o);
+                if (half == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&t_empty[g]);  // the MMA warp may write this group's columns again
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint4 pk;
+                    __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        hp[e] = __floats2bfloat162_rn(o[8 * i + 2 * e] * inv, o[8 * i + 2 * e + 1] * inv);
+                    const int ch = 4 * half + i;
+                    *reinterpret_cast<uint4*>(row + ((ch ^ (lane & 7)) * 16)) = pk;
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the bulk store
+            __syncwarp();
+            if (lane == 0) {
+                if (q0 + quad * 32 < a.S) {  // rows past S are clipped; wholly past S, not stored
+                    tma_store_4d(&tmO, stage, 0, h, q0 + quad * 32, z);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                mbar_arrive(&empty_bar[b]);  // the unit's buffer may be loaded again
+            }
+            __syncwarp();
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the bulk store
     tc_fence_before();
     __syncthreads();
-    if (t == 0) {
-        if (ok) {
-            tma_store_4d(&tmO, smem + AT_O, 0, h, q0, z);  // rows past S are clipped
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        }
-        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
     }
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // Generic path: one warp per (z, query, head); lane d-slices of the head
@@ -268,7 +401,7 @@ int sm_count_attn() {
 
 namespace zg {
 
-// Timed-out waits of the tensor-core kernel (codes 81-83), 0 = none.
+// Timed-out waits of the tensor-core kernel (codes 81-86), 0 = none.
 int attn_error_word(int clear) { return ptx_error_word(clear); }
 
 }  // namespace zg
@@ -304,15 +437,15 @@ extern "C" int zg_attention_ex(const void* q, const void* k, const void* v, int6
         const uint64_t dims[4] = {64, (uint64_t)H, (uint64_t)S, (uint64_t)Z};
         const uint64_t strides[3] = {64 * 2, (uint64_t)ld * 2, (uint64_t)S * ld * 2};
         const uint64_t ostrides[3] = {64 * 2, (uint64_t)H * 64 * 2, (uint64_t)S * H * 64 * 2};
-        const uint32_t box[4] = {64, 1, 128, 1};
+        const uint32_t box[4] = {64, 1, 128, 1}, obox[4] = {64, 1, 32, 1};  // output: one warp's 32 rows
         if (!zg::tensor_map_bf16(&tq, q, 4, dims, strides, box, true) ||
             !zg::tensor_map_bf16(&tk, k, 4, dims, strides, box, true) ||
             !zg::tensor_map_bf16(&tv, v, 4, dims, strides, box, true) ||
-            !zg::tensor_map_bf16(&to, o, 4, dims, ostrides, box, true))
+            !zg::tensor_map_bf16(&to, o, 4, dims, ostrides, obox, true))
             return zg::fail(ZG_ERR_CUDA, "zg_attention: tensor maps");
-        AttnArgs a{static_cast<__nv_bfloat16*>(o), Z, S, H, S <= 128 ? 128 : 256, causal != 0,
-                   (float)(1.4426950408889634 / sqrt(64.0))};
-        dim3 grid((unsigned)((S + 127) / 128), (unsigned)H, (unsigned)Z);
+        AttnArgs a{Z, S, H, S <= 128 ? 128 : 256, causal != 0, (float)(1.4426950408889634 / sqrt(64.0))};
+        const int64_t units = (int64_t)Z * H;
+        const unsigned grid = (unsigned)(units < sm_count_attn() ? units : sm_count_attn());
         zg::LaunchTimer zg_lt_("attention", st);
         attn_tc_kernel<<<grid, AT_THREADS, smem, st>>>(tq, tk, tv, to, a);
         return zg::check_launch("zg_attention");
