@@ -29,23 +29,27 @@
 
 namespace {
 
-// Persistent CTA (one per SM), 320 threads: warp 0 issues the TMA loads,
-// warp 1 the MMAs, warps 2-5 and 6-9 are two softmax groups of one thread
-// per query row.  Work unit = one (z, head): its query tiles (one or two of
-// 128 rows), keys and values land in one of two shared-memory buffers, so
-// the next unit loads while this one computes.  Tile j of the CTA's
-// sequence goes to group j % 2, which owns TMEM columns [256 g, 256 g + 256):
-// the scores S (up to 256 columns), then P written over them in place (each
-// half of the tile's keys at the start of its own score columns, key pair
-// (c, c+1) of a half as bf16x2 in its column c/2; the P V MMA reads it from
-// TMEM), and O in columns 192..255.  While one group runs its softmax, the other's
-// MMAs, output stores and the next loads proceed.
-constexpr int AT_THREADS = 320;
-constexpr uint32_t AT_Q = 0;         // 2 x 16 KiB: the unit's query tiles (then their output staging)
+// Persistent CTA (one per SM), 352 threads: warp 0 issues the TMA loads,
+// warps 1 and 2 the MMAs of softmax group 0 and 1, warps 3-6 and 7-10 are
+// the two softmax groups, one thread per query row.  Work unit = one
+// (z, head): its query tiles (one or two of 128 rows), keys and values, in
+// one of two shared-memory buffers.  A buffer's queries and keys are loaded
+// again as soon as the unit's Q K^T MMAs have read them, its values once the
+// P V MMAs have, so the next units' loads run under this unit's softmax.
+// Tile j of the CTA's sequence goes to group j % 2, which owns TMEM columns
+// [256 g, 256 g + 256): the scores S (up to 256 columns), then P written
+// over them in place (each half of the tile's keys at the start of its own
+// score columns, key pair (c, c+1) of a half as bf16x2 in its column c/2;
+// the P V MMA reads it from TMEM), the row sums of P in columns hw/2.., and
+// O in columns 192..255, which the softmax warps normalise into their own
+// staging boxes for TMA stores.
+constexpr int AT_THREADS = 352;
+constexpr uint32_t AT_Q = 0;         // 2 x 16 KiB: the unit's query tiles
 constexpr uint32_t AT_K = 32768;     // 32 KiB: up to 256 key rows
 constexpr uint32_t AT_V = 65536;     // 32 KiB: up to 256 value rows
 constexpr uint32_t AT_BUF = 98304;   // one unit
-constexpr uint32_t AT_ONES = 2 * AT_BUF;  // 512 B of bf16 ones: the B operand of the row-sum MMA
+constexpr uint32_t AT_STAGE = 2 * AT_BUF;           // 8 x 4 KiB: each softmax warp's output box
+constexpr uint32_t AT_ONES = AT_STAGE + 8 * 4096;   // 512 B of bf16 ones: the B operand of the row-sum MMA
 constexpr uint32_t AT_SMEM = AT_ONES + 512;
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -119,7 +123,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
     extern __shared__ uint8_t dyn_smem[];
-    __shared__ __align__(8) uint64_t full_bar[2], empty_bar[2], s_full[2], p_full[2], o_full[2], t_empty[2], done_bar;
+    // per buffer: queries+keys and values loaded (full) / read by the MMAs
+    // (empty); per softmax group: scores ready, weights ready, O ready, O read
+    __shared__ __align__(8) uint64_t qk_full[2], v_full[2], qk_empty[2], v_empty[2], s_full[2], p_full[2],
+        o_full[2], t_empty[2], done_bar[2];
     __shared__ uint32_t tmem_base_sh;
     const uint32_t dyn_base = smem_u32(dyn_smem);
     uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
@@ -131,14 +138,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&full_bar[i], 1);
-            mbar_init(&empty_bar[i], 4 * nq);  // the four warps of each of the unit's tiles
+            mbar_init(&qk_full[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&qk_empty[i], nq);  // one commit per tile of the unit
+            mbar_init(&v_empty[i], nq);
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 128);
             mbar_init(&o_full[i], 1);
             mbar_init(&t_empty[i], 4);
+            mbar_init(&done_bar[i], 1);
         }
-        mbar_init(&done_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) tmem_alloc(&tmem_base_sh, 512);
@@ -151,85 +160,96 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t issued = 0, issue_parity = 0;
+            // unit u's values are loaded before unit u+1's queries and keys:
+            // the buffer's values are freed (P V of unit u-2) before its
+            // queries and keys are (Q K^T of unit u-1, issued after P V of u-2)
+            uint32_t issued = 0, issue_parity = 0;  // bit b: QK loads of buffer b; bit b+2: V loads
             for (int u = 0; u < my_units; ++u) {
                 const int b = u & 1;
                 const uint32_t m = (uint32_t)(u >> 1);
-                if (!mbar_wait(&empty_bar[b], (m & 1) ^ 1, 81)) break;
                 const int64_t U = blockIdx.x + (int64_t)u * gridDim.x;
                 const int z = (int)(U / a.H), h = (int)(U % a.H);
                 uint8_t* buf = smem + b * AT_BUF;
-                mbar_expect_tx(&full_bar[b], (uint32_t)(3 * nq) * 16384u);
+                if (!mbar_wait(&qk_empty[b], (m & 1) ^ 1, 81)) break;
+                mbar_expect_tx(&qk_full[b], (uint32_t)(2 * nq) * 16384u);
                 for (int i = 0; i < nq; ++i) {
-                    tma_load_4d(buf + AT_Q + i * 16384, &tmQ, &full_bar[b], 0, h, i * 128, z);
-                    tma_load_4d(buf + AT_K + i * 16384, &tmK, &full_bar[b], 0, h, i * 128, z);
-                    tma_load_4d(buf + AT_V + i * 16384, &tmV, &full_bar[b], 0, h, i * 128, z);
+                    tma_load_4d(buf + AT_Q + i * 16384, &tmQ, &qk_full[b], 0, h, i * 128, z);
+                    tma_load_4d(buf + AT_K + i * 16384, &tmK, &qk_full[b], 0, h, i * 128, z);
                 }
                 issued |= 1u << b;
                 issue_parity = (issue_parity & ~(1u << b)) | ((m & 1) << b);
+                if (!mbar_wait(&v_empty[b], (m & 1) ^ 1, 88)) break;
+                mbar_expect_tx(&v_full[b], (uint32_t)nq * 16384u);
+                for (int i = 0; i < nq; ++i)
+                    tma_load_4d(buf + AT_V + i * 16384, &tmV, &v_full[b], 0, h, i * 128, z);
+                issued |= 4u << b;
+                issue_parity = (issue_parity & ~(4u << b)) | ((m & 1) << (b + 2));
             }
             // loads still in flight (only after an abort) land before the CTA exits
-            for (int b = 0; b < 2; ++b)
-                if (issued >> b & 1)
-                    for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(&full_bar[b], issue_parity >> b & 1); ++i) {
+            for (int i = 0; i < 4; ++i)
+                if (issued >> i & 1) {
+                    uint64_t* bar = i < 2 ? &qk_full[i] : &v_full[i - 2];
+                    for (uint32_t t = 0; t < kSpinLimit && !mbar_try_wait(bar, issue_parity >> i & 1); ++t) {
                     }
+                }
         }
-    } else if (warp == 1) {
+    } else if (warp <= 2) {
         if (lane == 0) {
-            // S(j) is issued before P V of tile j-1, so group j % 2 starts its
-            // softmax while the other group finishes its own
-            for (int j = 0; j <= tiles; ++j) {
-                if (j < tiles) {
-                    const int u = j / nq, qt = tile_qt(j, nq), g = j & 1, b = u & 1;
-                    const uint32_t n = (uint32_t)(j >> 1);
-                    if (j % nq == 0 && !mbar_wait(&full_bar[b], (uint32_t)(u >> 1) & 1, 82)) break;
-                    if (!mbar_wait(&t_empty[g], (n & 1) ^ 1, 83)) break;
-                    tc_fence_after();
-                    const uint32_t idesc = idesc_bf16(128, tile_keys(a, qt), 0);
-                    const uint32_t qa = smem_u32(smem + b * AT_BUF + AT_Q + qt * 16384);
-                    const uint32_t ka = smem_u32(smem + b * AT_BUF + AT_K);
+            // one MMA issuer per softmax group: S = Q K^T of the group's next
+            // tile once it has read the previous tile's O, then P V and the
+            // row sums once its weights are in TMEM
+            const int g = warp - 1;
+            const uint32_t pt = tmem + g * 256;
+            for (int j = g; j < tiles; j += 2) {
+                const int u = j / nq, qt = tile_qt(j, nq), b = u & 1;
+                const uint32_t n = (uint32_t)(j >> 1), m = (uint32_t)(u >> 1);
+                if (!mbar_wait(&qk_full[b], m & 1, 82)) break;
+                if (!mbar_wait(&t_empty[g], (n & 1) ^ 1, 83)) break;
+                tc_fence_after();
+                const uint32_t qa = smem_u32(smem + b * AT_BUF + AT_Q + qt * 16384);
+                const uint32_t ka = smem_u32(smem + b * AT_BUF + AT_K);
+                const uint32_t idesc_s = idesc_bf16(128, tile_keys(a, qt), 0);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        umma_bf16(tmem + g * 256, smem_desc(qa + k * 32, 16, 1024), smem_desc(ka + k * 32, 16, 1024),
-                                  idesc, k > 0 ? 1u : 0u);
-                    umma_commit(&s_full[g]);
+                for (int k = 0; k < 4; ++k)
+                    umma_bf16(pt, smem_desc(qa + k * 32, 16, 1024), smem_desc(ka + k * 32, 16, 1024), idesc_s,
+                              k > 0 ? 1u : 0u);
+                umma_commit(&s_full[g]);
+                umma_commit(&qk_empty[b]);  // this tile's queries and keys are read
+
+                if (!mbar_wait(&p_full[g], n & 1, 84)) break;
+                if (!mbar_wait(&v_full[b], m & 1, 89)) break;
+                tc_fence_after();
+                const uint32_t idesc = idesc_bf16(128, 64, 1);
+                const uint32_t va = smem_u32(smem + b * AT_BUF + AT_V);
+                const int hw = tile_keys(a, qt) / 2, hk = hw / 16;  // each half's P at the start of its scores
+                // the row sums of P: P times a [keys x 16] block of ones
+                // (no swizzle, K-major; every address of the 512 B holds
+                // 1.0), into columns hw/2 .. hw/2 + 15 (scores already read)
+                const uint32_t idesc_sum = idesc_bf16(128, 16, 0);
+                const uint64_t ones = smem_desc_noswizzle(smem_u32(smem + AT_ONES), 128, 256);
+                for (int kk = 0; kk < 2 * hk; ++kk) {
+                    const uint32_t pa = pt + (kk < hk ? kk * 8 : hw + (kk - hk) * 8);
+                    umma_bf16_ts(pt + 192, pa, smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc,
+                                 kk > 0 ? 1u : 0u);
+                    umma_bf16_ts(pt + hw / 2, pa, ones, idesc_sum, kk > 0 ? 1u : 0u);
                 }
-                if (j >= 1) {
-                    const int jp = j - 1;
-                    const int u = jp / nq, qt = tile_qt(jp, nq), g = jp & 1, b = u & 1;
-                    const uint32_t n = (uint32_t)(jp >> 1);
-                    if (!mbar_wait(&p_full[g], n & 1, 84)) break;
-                    tc_fence_after();
-                    const uint32_t idesc = idesc_bf16(128, 64, 1);
-                    const uint32_t va = smem_u32(smem + b * AT_BUF + AT_V);
-                    const uint32_t pt = tmem + g * 256;
-                    const int hw = tile_keys(a, qt) / 2, hk = hw / 16;  // each half's P at the start of its scores
-                    // the row sums of P: P times a [keys x 16] block of ones
-                    // (no swizzle, K-major; every address of the 512 B holds
-                    // 1.0), into columns hw/2 .. hw/2 + 15 (scores already read)
-                    const uint32_t idesc_sum = idesc_bf16(128, 16, 0);
-                    const uint64_t ones = smem_desc_noswizzle(smem_u32(smem + AT_ONES), 128, 256);
-                    for (int kk = 0; kk < 2 * hk; ++kk) {
-                        const uint32_t pa = pt + (kk < hk ? kk * 8 : hw + (kk - hk) * 8);
-                        umma_bf16_ts(pt + 192, pa, smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc,
-                                     kk > 0 ? 1u : 0u);
-                        umma_bf16_ts(pt + hw / 2, pa, ones, idesc_sum, kk > 0 ? 1u : 0u);
-                    }
-                    umma_commit(&o_full[g]);
-                }
+                umma_commit(&o_full[g]);
+                umma_commit(&v_empty[b]);  // this tile's values are read
             }
             // every MMA this thread issued has completed before TMEM is freed
-            umma_commit(&done_bar);
-            for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(&done_bar, 0); ++i) {
+            umma_commit(&done_bar[g]);
+            for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(&done_bar[g], 0); ++i) {
             }
         }
     } else {
-        const int g = (warp - 2) / 4, quad = warp % 4;  // quad: this warp's TMEM lane quarter
+        // softmax: one thread per query row
+        const int g = (warp - 3) / 4, quad = warp % 4;  // quad: this warp's TMEM lane quarter
         const int r = quad * 32 + lane;                 // this thread's query row in the tile
         const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(g * 256);
+        uint8_t* stage = smem + AT_STAGE + (warp - 3) * 4096;  // this warp's output box: 32 rows x 128 B
         for (int j = g; j < tiles; j += 2) {
             const uint32_t n = (uint32_t)(j >> 1);
-            const int u = j / nq, qt = tile_qt(j, nq), b = u & 1;
+            const int u = j / nq, qt = tile_qt(j, nq);
             const int64_t U = blockIdx.x + (int64_t)u * gridDim.x;
             const int z = (int)(U / a.H), h = (int)(U % a.H);
             const int q0 = qt * 128, n_keys = tile_keys(a, qt), hw = n_keys / 2;
@@ -242,27 +262,29 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             // the warp's last visible column (its last row sees the most): chunks past it hold no weight
             const int wvis = __reduce_max_sync(0xffffffffu, vis);
             const int c_end = ((wvis + 31) / 32) * 32 < n_keys ? ((wvis + 31) / 32) * 32 : n_keys;
-            // The keys are taken as two halves [0, hw) and [hw, n_keys), chunk i
-            // of each side by side (two loads in flight).  Only chunks that
-            // cross this row's last visible key test each key.
+            // the maximum (8 independent chains; only chunks that cross the
+            // row's last visible key test each key), two chunks per wait
             float mx8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
 #pragma unroll 1
-            for (int i = 0; 32 * i < hw && 32 * i < c_end; ++i) {
-                const int cl = 32 * i, chi = hw + 32 * i;
-                const bool two = chi < c_end;
-                uint32_t rl[32], rh[32];
-                tmem_ld32_nowait(trow + cl, rl);
-                if (two) tmem_ld32_nowait(trow + chi, rh);
-                tmem_wait_ld32(rl);
-                if (two) tmem_wait_ld32(rh);
-                chunk_max(rl, cl, vis, mx8);
-                if (two) chunk_max(rh, chi, vis, mx8);
+            for (int c0 = 0; c0 < c_end; c0 += 64) {
+                uint32_t r0[32], r1[32];
+                const bool two = c0 + 32 < c_end;
+                tmem_ld32_nowait(trow + c0, r0);
+                if (two) tmem_ld32_nowait(trow + c0 + 32, r1);
+                tmem_wait_ld32(r0);
+                if (two) tmem_wait_ld32(r1);
+                chunk_max(r0, c0, vis, mx8);
+                if (two) chunk_max(r1, c0 + 32, vis, mx8);
             }
             float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             mx *= a.scale_log2;  // scale_log2 > 0: max(s) * scale = max(s * scale)
+            // the weights: the keys as two halves [0, hw) and [hw, n_keys),
+            // chunk i of each side by side (two loads in flight); each half's
+            // weights at the start of its own scores, over columns this thread
+            // has already read: keys (2e, 2e+1) of chunk i in column 16 i + e
 #pragma unroll 1
             for (int i = 0; 32 * i < hw; ++i) {
                 const int cl = 32 * i, chi = hw + 32 * i;
@@ -272,9 +294,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (hi_on) tmem_ld32_nowait(trow + chi, rh);
                 if (lo_on) tmem_wait_ld32(rl);
                 if (hi_on) tmem_wait_ld32(rh);
-                // each half's weights at the start of its own scores, over
-                // columns this thread has already read: keys (2e, 2e+1) of
-                // chunk i in column 16 i + e of the half
                 uint32_t pk[16];
                 chunk_weights(rl, cl, vis, lo_on, a.scale_log2, mx, pk);
                 tmem_st16u(trow + cl / 2, pk);
@@ -287,19 +306,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
             if (!warp_wait(&o_full[g], n & 1, 86)) break;
             tc_fence_after();
-            // O / sum -> bf16 into this warp's 32 rows of the query tile's
-            // (finished) buffer, 128-byte swizzled like the output box, in two
-            // halves of 32 columns; then one TMA store of the warp's rows
-            float sum[16];
-            tmem_ld16(trow + hw / 2, sum);  // the row sum of the bf16 weights (tensor cores, float32)
-            const float inv = 1.f / sum[0];
-            uint8_t* stage = smem + b * AT_BUF + AT_Q + qt * 16384 + quad * 4096;
+            // O / sum -> bf16 into the warp's staging box (128-byte swizzle,
+            // the output box's layout) in two halves of 32 columns, then one
+            // TMA store of the warp's 32 rows
+            const float inv = 1.f / tmem_ld1(trow + hw / 2);  // the row sum of the bf16 weights (tensor cores)
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // last box read out
+            __syncwarp();
             uint8_t* row = stage + lane * 128;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            for (int hf = 0; hf < 2; ++hf) {
                 float o[32];
-                tmem_ld32(trow + 192 + 32 * half, o);
-                if (half == 1) {
+                tmem_ld32(trow + 192 + 32 * hf, o);
+                if (hf == 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&t_empty[g]);  // the MMA warp may write this group's columns again
@@ -311,19 +329,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
                         hp[e] = __floats2bfloat162_rn(o[8 * i + 2 * e] * inv, o[8 * i + 2 * e + 1] * inv);
-                    const int ch = 4 * half + i;
+                    const int ch = 4 * hf + i;
                     *reinterpret_cast<uint4*>(row + ((ch ^ (lane & 7)) * 16)) = pk;
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the bulk store
             __syncwarp();
-            if (lane == 0) {
-                if (q0 + quad * 32 < a.S) {  // rows past S are clipped; wholly past S, not stored
-                    tma_store_4d(&tmO, stage, 0, h, q0 + quad * 32, z);
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                }
-                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-                mbar_arrive(&empty_bar[b]);  // the unit's buffer may be loaded again
+            if (lane == 0 && q0 + quad * 32 < a.S) {  // rows past S are clipped; wholly past S, not stored
+                tma_store_4d(&tmO, stage, 0, h, q0 + quad * 32, z);
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             }
             __syncwarp();
         }
