@@ -16,7 +16,7 @@
 // writes p = 2^(s * log2(e)/sqrt(D) - max) as bf16 back into TMEM over the
 // scores; a second MMA chain computes O = P V with P read from TMEM (V the
 // MN-major operand from shared memory); the epilogue divides by the row sum
-// of the bf16 p and stores O by TMA.  The whole score row fits (S <= 256),
+// of p (float32) and stores O by TMA.  The whole score row fits (S <= 256),
 // so one pass suffices.  Two softmax groups alternate over the tiles, and
 // the next unit's loads overlap the current one's work.
 //
@@ -40,17 +40,16 @@ namespace {
 // [256 g, 256 g + 256): the scores S (up to 256 columns), then P written
 // over them in place (each half of the tile's keys at the start of its own
 // score columns, key pair (c, c+1) of a half as bf16x2 in its column c/2;
-// the P V MMA reads it from TMEM), the row sums of P in columns hw/2.., and
-// O in columns 192..255, which the softmax warps normalise into their own
-// staging boxes for TMA stores.
+// the P V MMA reads it from TMEM), and O in columns 192..255, which the
+// softmax warps divide by their rows' sums of p and stage into their own
+// boxes for TMA stores.
 constexpr int AT_THREADS = 352;
 constexpr uint32_t AT_Q = 0;         // 2 x 16 KiB: the unit's query tiles
 constexpr uint32_t AT_K = 32768;     // 32 KiB: up to 256 key rows
 constexpr uint32_t AT_V = 65536;     // 32 KiB: up to 256 value rows
 constexpr uint32_t AT_BUF = 98304;   // one unit
 constexpr uint32_t AT_STAGE = 2 * AT_BUF;           // 8 x 4 KiB: each softmax warp's output box
-constexpr uint32_t AT_ONES = AT_STAGE + 8 * 4096;   // 512 B of bf16 ones: the B operand of the row-sum MMA
-constexpr uint32_t AT_SMEM = AT_ONES + 512;
+constexpr uint32_t AT_SMEM = AT_STAGE + 8 * 4096;
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -67,6 +66,13 @@ struct AttnArgs {
 // the order alternates between units, so each softmax group (j % 2) takes
 // the short causal tile and the long one in turn.
 __device__ __forceinline__ int tile_qt(int j, int nq) { return nq == 2 ? ((j & 1) ^ ((j >> 1) & 1)) : 0; }
+
+// The 32-row block of query tile qt held in TMEM lane quarter `quad` (MMA
+// rows 32 quad ..): the first tile in order, the second reversed.  Lane
+// quarter q is read only by the warps of SM sub-partition q, and under the
+// causal mask a tile's later rows see more keys, so the reversal gives each
+// sub-partition one short and one long block of the unit's two tiles.
+__device__ __forceinline__ int tile_block(int qt, int quad) { return qt == 1 ? 3 - quad : quad; }
 
 // keys a query tile sees: causal tiles stop at their last query
 __device__ __forceinline__ int tile_keys(const AttnArgs& a, int qt) {
@@ -88,15 +94,19 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&r)[32], int c, int vi
 }
 
 // bf16 weights p = 2^(s * scale - mx) of a 32-key chunk as 16 packed pairs
-// (zero for keys past the row's last visible one, or for a chunk off).
+// (zero for keys past the row's last visible one, or for a chunk off), and
+// their float32 values added pairwise into two running sums (packed f32x2
+// adds on the FMA pipe).
 __device__ __forceinline__ void chunk_weights(const uint32_t (&r)[32], int c, int vis, bool on, float scale,
-                                              float mx, uint32_t (&pk)[16]) {
+                                              float mx, uint32_t (&pk)[16], float2 (&acc)[2]) {
+    const float2 one = make_float2(1.f, 1.f);
     if (on && c + 32 <= vis) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-            const __nv_bfloat162 b2 =
-                __floats2bfloat162_rn(ex2_approx(fmaf(__uint_as_float(r[2 * e]), scale, -mx)),
-                                      ex2_approx(fmaf(__uint_as_float(r[2 * e + 1]), scale, -mx)));
+            const float p0 = ex2_approx(fmaf(__uint_as_float(r[2 * e]), scale, -mx));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(r[2 * e + 1]), scale, -mx));
+            acc[e & 1] = ffma2_tc(make_float2(p0, p1), one, acc[e & 1]);
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
             pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
         }
     } else if (on) {
@@ -105,6 +115,7 @@ __device__ __forceinline__ void chunk_weights(const uint32_t (&r)[32], int c, in
             const int col = c + 2 * e;
             const float p0 = col < vis ? ex2_approx(fmaf(__uint_as_float(r[2 * e]), scale, -mx)) : 0.f;
             const float p1 = col + 1 < vis ? ex2_approx(fmaf(__uint_as_float(r[2 * e + 1]), scale, -mx)) : 0.f;
+            acc[e & 1] = ffma2_tc(make_float2(p0, p1), one, acc[e & 1]);
             const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
             pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
         }
@@ -151,8 +162,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) tmem_alloc(&tmem_base_sh, 512);
-    if (threadIdx.x < 128) reinterpret_cast<uint32_t*>(smem + AT_ONES)[threadIdx.x] = 0x3F803F80u;  // bf16 1.0 pairs
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the ones visible to the tensor cores
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -173,7 +182,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (!mbar_wait(&qk_empty[b], (m & 1) ^ 1, 81)) break;
                 mbar_expect_tx(&qk_full[b], (uint32_t)(2 * nq) * 16384u);
                 for (int i = 0; i < nq; ++i) {
-                    tma_load_4d(buf + AT_Q + i * 16384, &tmQ, &qk_full[b], 0, h, i * 128, z);
+                    // query tile i as four 32-row blocks, the second tile's in
+                    // reverse order (tile_block)
+                    for (int blk = 0; blk < 4; ++blk)
+                        tma_load_4d(buf + AT_Q + i * 16384 + blk * 4096, &tmQ, &qk_full[b], 0, h,
+                                    i * 128 + 32 * tile_block(i, blk), z);
                     tma_load_4d(buf + AT_K + i * 16384, &tmK, &qk_full[b], 0, h, i * 128, z);
                 }
                 issued |= 1u << b;
@@ -196,8 +209,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     } else if (warp <= 2) {
         if (lane == 0) {
             // one MMA issuer per softmax group: S = Q K^T of the group's next
-            // tile once it has read the previous tile's O, then P V and the
-            // row sums once its weights are in TMEM
+            // tile once it has read the previous tile's O, then P V once its
+            // weights are in TMEM
             const int g = warp - 1;
             const uint32_t pt = tmem + g * 256;
             for (int j = g; j < tiles; j += 2) {
@@ -222,17 +235,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 const uint32_t idesc = idesc_bf16(128, 64, 1);
                 const uint32_t va = smem_u32(smem + b * AT_BUF + AT_V);
                 const int hw = tile_keys(a, qt) / 2, hk = hw / 16;  // each half's P at the start of its scores
-                // the row sums of P: P times a [keys x 16] block of ones
-                // (no swizzle, K-major; every address of the 512 B holds
-                // 1.0), into columns hw/2 .. hw/2 + 15 (scores already read)
-                const uint32_t idesc_sum = idesc_bf16(128, 16, 0);
-                const uint64_t ones = smem_desc_noswizzle(smem_u32(smem + AT_ONES), 128, 256);
-                for (int kk = 0; kk < 2 * hk; ++kk) {
-                    const uint32_t pa = pt + (kk < hk ? kk * 8 : hw + (kk - hk) * 8);
-                    umma_bf16_ts(pt + 192, pa, smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc,
-                                 kk > 0 ? 1u : 0u);
-                    umma_bf16_ts(pt + hw / 2, pa, ones, idesc_sum, kk > 0 ? 1u : 0u);
-                }
+                for (int kk = 0; kk < 2 * hk; ++kk)
+                    umma_bf16_ts(pt + 192, pt + (kk < hk ? kk * 8 : hw + (kk - hk) * 8),
+                                 smem_desc(va + kk * 2048, 64 * 256 * 2, 1024), idesc, kk > 0 ? 1u : 0u);
                 umma_commit(&o_full[g]);
                 umma_commit(&v_empty[b]);  // this tile's values are read
             }
@@ -244,7 +249,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     } else {
         // softmax: one thread per query row
         const int g = (warp - 3) / 4, quad = warp % 4;  // quad: this warp's TMEM lane quarter
-        const int r = quad * 32 + lane;                 // this thread's query row in the tile
         const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(g * 256);
         uint8_t* stage = smem + AT_STAGE + (warp - 3) * 4096;  // this warp's output box: 32 rows x 128 B
         for (int j = g; j < tiles; j += 2) {
@@ -257,7 +261,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             tc_fence_after();
 
             // columns [0, vis) are visible to this query: the keys, up to the query when causal
-            const int qi = q0 + r;
+            const int row0 = q0 + 32 * tile_block(qt, quad);  // the warp's first query row
+            const int qi = row0 + lane;
             const int vis = a.causal ? (qi + 1 < a.S ? qi + 1 : a.S) : a.S;
             // the warp's last visible column (its last row sees the most): chunks past it hold no weight
             const int wvis = __reduce_max_sync(0xffffffffu, vis);
@@ -285,6 +290,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             // chunk i of each side by side (two loads in flight); each half's
             // weights at the start of its own scores, over columns this thread
             // has already read: keys (2e, 2e+1) of chunk i in column 16 i + e
+            float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll 1
             for (int i = 0; 32 * i < hw; ++i) {
                 const int cl = 32 * i, chi = hw + 32 * i;
@@ -295,9 +301,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 if (lo_on) tmem_wait_ld32(rl);
                 if (hi_on) tmem_wait_ld32(rh);
                 uint32_t pk[16];
-                chunk_weights(rl, cl, vis, lo_on, a.scale_log2, mx, pk);
+                chunk_weights(rl, cl, vis, lo_on, a.scale_log2, mx, pk, acc);
                 tmem_st16u(trow + cl / 2, pk);
-                chunk_weights(rh, chi, vis, hi_on, a.scale_log2, mx, pk);
+                chunk_weights(rh, chi, vis, hi_on, a.scale_log2, mx, pk, acc);
                 tmem_st16u(trow + hw + cl / 2, pk);
             }
             tmem_wait_st();
@@ -309,7 +315,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             // O / sum -> bf16 into the warp's staging box (128-byte swizzle,
             // the output box's layout) in two halves of 32 columns, then one
             // TMA store of the warp's 32 rows
-            const float inv = 1.f / tmem_ld1(trow + hw / 2);  // the row sum of the bf16 weights (tensor cores)
+            const float inv = 1.f / ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));  // 1 / the row sum of p
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // last box read out
             __syncwarp();
             uint8_t* row = stage + lane * 128;
@@ -335,8 +341,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the bulk store
             __syncwarp();
-            if (lane == 0 && q0 + quad * 32 < a.S) {  // rows past S are clipped; wholly past S, not stored
-                tma_store_4d(&tmO, stage, 0, h, q0 + quad * 32, z);
+            if (lane == 0 && row0 < a.S) {  // rows past S are clipped; wholly past S, not stored
+                tma_store_4d(&tmO, stage, 0, h, row0, z);
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             }
             __syncwarp();
@@ -451,11 +457,12 @@ extern "C" int zg_attention_ex(const void* q, const void* k, const void* v, int6
         const uint64_t dims[4] = {64, (uint64_t)H, (uint64_t)S, (uint64_t)Z};
         const uint64_t strides[3] = {64 * 2, (uint64_t)ld * 2, (uint64_t)S * ld * 2};
         const uint64_t ostrides[3] = {64 * 2, (uint64_t)H * 64 * 2, (uint64_t)S * H * 64 * 2};
-        const uint32_t box[4] = {64, 1, 128, 1}, obox[4] = {64, 1, 32, 1};  // output: one warp's 32 rows
-        if (!zg::tensor_map_bf16(&tq, q, 4, dims, strides, box, true) ||
+        // queries and outputs in 32-row boxes (one TMEM lane quarter), keys and values in 128
+        const uint32_t box[4] = {64, 1, 128, 1}, qbox[4] = {64, 1, 32, 1};
+        if (!zg::tensor_map_bf16(&tq, q, 4, dims, strides, qbox, true) ||
             !zg::tensor_map_bf16(&tk, k, 4, dims, strides, box, true) ||
             !zg::tensor_map_bf16(&tv, v, 4, dims, strides, box, true) ||
-            !zg::tensor_map_bf16(&to, o, 4, dims, ostrides, obox, true))
+            !zg::tensor_map_bf16(&to, o, 4, dims, ostrides, qbox, true))
             return zg::fail(ZG_ERR_CUDA, "zg_attention: tensor maps");
         AttnArgs a{Z, S, H, S <= 128 ? 128 : 256, causal != 0, (float)(1.4426950408889634 / sqrt(64.0))};
         const int64_t units = (int64_t)Z * H;
