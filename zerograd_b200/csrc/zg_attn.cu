@@ -43,13 +43,26 @@ namespace {
 // the P V MMA reads it from TMEM), and O in columns 192..255, which the
 // softmax warps divide by their rows' sums of p and stage into their own
 // boxes for TMA stores.
-constexpr int AT_THREADS = 352;
+constexpr int AT_THREADS = 608;
 constexpr uint32_t AT_Q = 0;         // 2 x 16 KiB: the unit's query tiles
 constexpr uint32_t AT_K = 32768;     // 32 KiB: up to 256 key rows
 constexpr uint32_t AT_V = 65536;     // 32 KiB: up to 256 value rows
 constexpr uint32_t AT_BUF = 98304;   // one unit
-constexpr uint32_t AT_STAGE = 2 * AT_BUF;           // 8 x 4 KiB: each softmax warp's output box
-constexpr uint32_t AT_SMEM = AT_STAGE + 8 * 4096;
+constexpr uint32_t AT_STAGE = 2 * AT_BUF;           // 16 x 2 KiB: each softmax warp's output box
+constexpr uint32_t AT_SUM = AT_STAGE + 16 * 2048;   // float [group][half][row]: the halves' sums of p
+constexpr uint32_t AT_CTRL = AT_SUM + 2048;         // AttnCtrl
+constexpr uint32_t AT_SMEM = AT_CTRL + 256;         // all of the kernel's shared memory (none static)
+
+// mbarriers and the TMEM base, at AT_CTRL.  Per buffer: queries+keys and
+// values loaded (full) / read by the MMAs (empty); per softmax group: scores
+// ready, weights ready, O ready, O read, MMAs done at exit, the halves'
+// maxima passed, the halves' sums passed.
+struct AttnCtrl {
+    uint64_t qk_full[2], v_full[2], qk_empty[2], v_empty[2], s_full[2], p_full[2], o_full[2], t_empty[2],
+        done_bar[2], mx_bar[2], sum_bar[2];
+    uint32_t tmem_base;
+};
+static_assert(sizeof(AttnCtrl) <= 256, "control block");
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -133,14 +146,20 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsign
 __global__ void __launch_bounds__(AT_THREADS, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs a) {
-    extern __shared__ uint8_t dyn_smem[];
-    // per buffer: queries+keys and values loaded (full) / read by the MMAs
-    // (empty); per softmax group: scores ready, weights ready, O ready, O read
-    __shared__ __align__(8) uint64_t qk_full[2], v_full[2], qk_empty[2], v_empty[2], s_full[2], p_full[2],
-        o_full[2], t_empty[2], done_bar[2];
-    __shared__ uint32_t tmem_base_sh;
-    const uint32_t dyn_base = smem_u32(dyn_smem);
-    uint8_t* smem = dyn_smem + (((dyn_base + 1023u) & ~1023u) - dyn_base);
+    // The kernel declares no static shared memory, so the dynamic block
+    // starts at the CTA's first shared byte; the 128-byte-swizzled tiles need
+    // it 1024-aligned, which is checked (error 90, every thread returns)
+    // rather than padded for: the block fills the 227 KiB a CTA may hold.
+    extern __shared__ __align__(1024) uint8_t smem[];
+    if (smem_u32(smem) & 1023u) {
+        if (threadIdx.x == 0) atomicCAS(&g_zg_tc_error, 0u, 90u);
+        return;
+    }
+    AttnCtrl& cs = *reinterpret_cast<AttnCtrl*>(smem + AT_CTRL);
+    uint64_t *qk_full = cs.qk_full, *v_full = cs.v_full, *qk_empty = cs.qk_empty, *v_empty = cs.v_empty,
+             *s_full = cs.s_full, *p_full = cs.p_full, *o_full = cs.o_full, *t_empty = cs.t_empty,
+             *done_bar = cs.done_bar, *mx_bar = cs.mx_bar, *sum_bar = cs.sum_bar;
+    float* s_sum = reinterpret_cast<float*>(smem + AT_SUM);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int nq = a.s_pad / 128;  // query tiles per unit; also the key/value boxes
     const int64_t units = (int64_t)a.Z * a.H;
@@ -154,18 +173,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             mbar_init(&qk_empty[i], nq);  // one commit per tile of the unit
             mbar_init(&v_empty[i], nq);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&p_full[i], 256);
             mbar_init(&o_full[i], 1);
-            mbar_init(&t_empty[i], 4);
+            mbar_init(&t_empty[i], 8);
             mbar_init(&done_bar[i], 1);
+            mbar_init(&mx_bar[i], 256);
+            mbar_init(&sum_bar[i], 256);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) tmem_alloc(&tmem_base_sh, 512);
+    if (warp == 1) tmem_alloc(&cs.tmem_base, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = tmem_base_sh;
+    const uint32_t tmem = cs.tmem_base;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -247,16 +268,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
         }
     } else {
-        // softmax: one thread per query row
-        const int g = (warp - 3) / 4, quad = warp % 4;  // quad: this warp's TMEM lane quarter
+        // softmax: two threads per query row, each one half of the tile's keys
+        const int g = (warp - 3) / 8, half = ((warp - 3) % 8) / 4, quad = warp % 4;  // quad: TMEM lane quarter
         const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(g * 256);
-        uint8_t* stage = smem + AT_STAGE + (warp - 3) * 4096;  // this warp's output box: 32 rows x 128 B
+        // this warp's output box (32 rows x 64 B); its first 128 B also pass
+        // the rows' partial maxima to the other half's warp (warp -/+ 4)
+        uint8_t* stage = smem + AT_STAGE + (warp - 3) * 2048;
+        const float* partner_mx = reinterpret_cast<const float*>(stage + (half ? -4 : 4) * 2048);
         for (int j = g; j < tiles; j += 2) {
             const uint32_t n = (uint32_t)(j >> 1);
             const int u = j / nq, qt = tile_qt(j, nq);
-            const int64_t U = blockIdx.x + (int64_t)u * gridDim.x;
-            const int z = (int)(U / a.H), h = (int)(U % a.H);
+            const uint32_t U = blockIdx.x + (uint32_t)u * gridDim.x;
+            const int z = (int)(U / (uint32_t)a.H), h = (int)(U % (uint32_t)a.H);
             const int q0 = qt * 128, n_keys = tile_keys(a, qt), hw = n_keys / 2;
+            const int k0 = half * hw;  // this thread's keys: [k0, k0 + hw)
             if (!warp_wait(&s_full[g], n & 1, 85)) break;
             tc_fence_after();
 
@@ -267,82 +292,80 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             // the warp's last visible column (its last row sees the most): chunks past it hold no weight
             const int wvis = __reduce_max_sync(0xffffffffu, vis);
             const int c_end = ((wvis + 31) / 32) * 32 < n_keys ? ((wvis + 31) / 32) * 32 : n_keys;
-            // the maximum (8 independent chains; only chunks that cross the
-            // row's last visible key test each key), two chunks per wait
+            const int c_stop = k0 + hw < c_end ? k0 + hw : c_end;  // this half's chunks that hold weight
+            // the maximum over this half (8 independent chains; only chunks
+            // that cross the row's last visible key test each key)
             float mx8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
 #pragma unroll 1
-            for (int c0 = 0; c0 < c_end; c0 += 64) {
-                uint32_t r0[32], r1[32];
-                const bool two = c0 + 32 < c_end;
-                tmem_ld32_nowait(trow + c0, r0);
-                if (two) tmem_ld32_nowait(trow + c0 + 32, r1);
-                tmem_wait_ld32(r0);
-                if (two) tmem_wait_ld32(r1);
-                chunk_max(r0, c0, vis, mx8);
-                if (two) chunk_max(r1, c0 + 32, vis, mx8);
+            for (int c = k0; c < c_stop; c += 32) {
+                uint32_t rc[32];
+                tmem_ld32_nowait(trow + c, rc);
+                tmem_wait_ld32(rc);
+                chunk_max(rc, c, vis, mx8);
             }
-            float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            mx *= a.scale_log2;  // scale_log2 > 0: max(s) * scale = max(s * scale)
-            // the weights: the keys as two halves [0, hw) and [hw, n_keys),
-            // chunk i of each side by side (two loads in flight); each half's
-            // weights at the start of its own scores, over columns this thread
-            // has already read: keys (2e, 2e+1) of chunk i in column 16 i + e
+            // the row's maximum over both halves: this half's through the
+            // staging box (read out by the last output store before)
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
+            reinterpret_cast<float*>(stage)[lane] = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            mbar_arrive(&mx_bar[g]);
+            if (!warp_wait(&mx_bar[g], n & 1, 87)) break;
+            // scale_log2 > 0: max(s) * scale = max(s * scale)
+            const float mx = fmaxf(reinterpret_cast<const float*>(stage)[lane], partner_mx[lane]) * a.scale_log2;
+            // the weights of this half at the start of its own scores, over
+            // columns this thread has already read: keys (2e, 2e+1) of chunk
+            // i in column 16 i + e of the half
             float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll 1
-            for (int i = 0; 32 * i < hw; ++i) {
-                const int cl = 32 * i, chi = hw + 32 * i;
-                const bool lo_on = cl < c_end, hi_on = chi < c_end;
-                uint32_t rl[32], rh[32];
-                if (lo_on) tmem_ld32_nowait(trow + cl, rl);
-                if (hi_on) tmem_ld32_nowait(trow + chi, rh);
-                if (lo_on) tmem_wait_ld32(rl);
-                if (hi_on) tmem_wait_ld32(rh);
+            for (int c = k0; c < k0 + hw; c += 32) {
+                const bool on = c < c_stop;
+                uint32_t rc[32];
+                if (on) {
+                    tmem_ld32_nowait(trow + c, rc);
+                    tmem_wait_ld32(rc);
+                }
                 uint32_t pk[16];
-                chunk_weights(rl, cl, vis, lo_on, a.scale_log2, mx, pk, acc);
-                tmem_st16u(trow + cl / 2, pk);
-                chunk_weights(rh, chi, vis, hi_on, a.scale_log2, mx, pk, acc);
-                tmem_st16u(trow + hw + cl / 2, pk);
+                chunk_weights(rc, c, vis, on, a.scale_log2, mx, pk, acc);
+                tmem_st16u(trow + k0 + (c - k0) / 2, pk);
             }
+            // this half's sum of p for the other half's epilogue
+            float* my_sum = s_sum + (g * 2 + half) * 128 + 32 * quad + lane;
+            *my_sum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
+            mbar_arrive(&sum_bar[g]);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&p_full[g]);
 
             if (!warp_wait(&o_full[g], n & 1, 86)) break;
             tc_fence_after();
-            // O / sum -> bf16 into the warp's staging box (128-byte swizzle,
-            // the output box's layout) in two halves of 32 columns, then one
-            // TMA store of the warp's 32 rows
-            const float inv = 1.f / ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));  // 1 / the row sum of p
-            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // last box read out
+            // this half's 32 columns of O / sum -> bf16 into the warp's box
+            // (64-byte swizzle: 16-byte chunk i of row l at
+            // (i ^ ((l >> 1) & 3)) * 16), then one TMA store of the box
+            if (!warp_wait(&sum_bar[g], n & 1, 91)) break;
+            const float* row_sums = s_sum + g * 256 + 32 * quad + lane;
+            const float inv = 1.f / (row_sums[0] + row_sums[128]);  // the halves' sums of p, in half order
+            float o[32];
+            tmem_ld32(trow + 192 + 32 * half, o);
+            tc_fence_before();
             __syncwarp();
-            uint8_t* row = stage + lane * 128;
+            if (lane == 0) mbar_arrive(&t_empty[g]);  // the MMA warp may write this group's columns again
+            uint8_t* row = stage + lane * 64;
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                float o[32];
-                tmem_ld32(trow + 192 + 32 * hf, o);
-                if (hf == 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&t_empty[g]);  // the MMA warp may write this group's columns again
-                }
+            for (int i = 0; i < 4; ++i) {
+                uint4 pk;
+                __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint4 pk;
-                    __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        hp[e] = __floats2bfloat162_rn(o[8 * i + 2 * e] * inv, o[8 * i + 2 * e + 1] * inv);
-                    const int ch = 4 * hf + i;
-                    *reinterpret_cast<uint4*>(row + ((ch ^ (lane & 7)) * 16)) = pk;
-                }
+                for (int e = 0; e < 4; ++e)
+                    hp[e] = __floats2bfloat162_rn(o[8 * i + 2 * e] * inv, o[8 * i + 2 * e + 1] * inv);
+                *reinterpret_cast<uint4*>(row + ((i ^ ((lane >> 1) & 3)) * 16)) = pk;
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the bulk store
             __syncwarp();
             if (lane == 0 && row0 < a.S) {  // rows past S are clipped; wholly past S, not stored
-                tma_store_4d(&tmO, stage, 0, h, row0, z);
+                tma_store_4d(&tmO, stage, 32 * half, h, row0, z);
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             }
             __syncwarp();
@@ -421,7 +444,8 @@ int sm_count_attn() {
 
 namespace zg {
 
-// Timed-out waits of the tensor-core kernel (codes 81-86), 0 = none.
+// Timed-out waits of the tensor-core kernel (codes 81-89, 91) or its shared
+// memory not 1024-aligned (90); 0 = none.
 int attn_error_word(int clear) { return ptx_error_word(clear); }
 
 }  // namespace zg
@@ -446,7 +470,7 @@ extern "C" int zg_attention_ex(const void* q, const void* k, const void* v, int6
                     al(q) && al(k) && al(v) && al(o) && (ld * 2) % 16 == 0;
     if (tc) {
         static bool attr = false;
-        const size_t smem = AT_SMEM + 1024;
+        const size_t smem = AT_SMEM;
         if (!attr) {
             if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
                 cudaSuccess)
@@ -457,12 +481,13 @@ extern "C" int zg_attention_ex(const void* q, const void* k, const void* v, int6
         const uint64_t dims[4] = {64, (uint64_t)H, (uint64_t)S, (uint64_t)Z};
         const uint64_t strides[3] = {64 * 2, (uint64_t)ld * 2, (uint64_t)S * ld * 2};
         const uint64_t ostrides[3] = {64 * 2, (uint64_t)H * 64 * 2, (uint64_t)S * H * 64 * 2};
-        // queries and outputs in 32-row boxes (one TMEM lane quarter), keys and values in 128
-        const uint32_t box[4] = {64, 1, 128, 1}, qbox[4] = {64, 1, 32, 1};
+        // queries in 32-row boxes (one TMEM lane quarter), keys and values in
+        // 128; outputs in boxes of 32 rows x 32 columns (one warp's half rows)
+        const uint32_t box[4] = {64, 1, 128, 1}, qbox[4] = {64, 1, 32, 1}, obox[4] = {32, 1, 32, 1};
         if (!zg::tensor_map_bf16(&tq, q, 4, dims, strides, qbox, true) ||
             !zg::tensor_map_bf16(&tk, k, 4, dims, strides, box, true) ||
             !zg::tensor_map_bf16(&tv, v, 4, dims, strides, box, true) ||
-            !zg::tensor_map_bf16(&to, o, 4, dims, ostrides, qbox, true))
+            !zg::tensor_map_bf16_swz(&to, o, 4, dims, ostrides, obox, 64))
             return zg::fail(ZG_ERR_CUDA, "zg_attention: tensor maps");
         AttnArgs a{Z, S, H, S <= 128 ? 128 : 256, causal != 0, (float)(1.4426950408889634 / sqrt(64.0))};
         const int64_t units = (int64_t)Z * H;

@@ -151,6 +151,21 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
         : "memory");
 }
 
+// 32 lanes x 1 column from a register.
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+    __syncwarp();
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "f"(v) : "memory");
+}
+
+// 32 lanes x 2 columns (waits for the load).
+__device__ __forceinline__ float2 tmem_ld2(uint32_t taddr) {
+    uint32_t r0, r1;
+    __syncwarp();
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return make_float2(__uint_as_float(r0), __uint_as_float(r1));
+}
+
 __device__ __forceinline__ void tmem_wait_st() {
     __syncwarp();
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
