@@ -256,7 +256,8 @@ def lm_work(cfg=LM, P=None):
     the projections (dense x W plus the rank-r term U F2^T), of attention
     (the causal pairs only: q.k and p.v over the S(S+1)/2 visible pairs),
     of the tied logits (dense + rank-r) and of the replay GEMMs; bytes of
-    the norms, the lookup and the low-rank u passes."""
+    the norms, the lookup, the low-rank u passes and attention (q, k, v read,
+    o written)."""
     P = cfg["P"] if P is None else P
     tok = cfg["batch"] * cfg["seq"]
     E, F, L, V, r, S, H = cfg["width"], cfg["mlp"], cfg["layers"], cfg["vocab"], cfg["rank"], cfg["seq"], cfg["heads"]
@@ -272,6 +273,8 @@ def lm_work(cfg=LM, P=None):
         "table_lookup": float(P * tok * E * 2 * 2),
         # this rank's candidates: the exchanged update contracts only those
         "replay_gemm": 2.0 * (L * dense + V * E) * P * r,
+        # attention's HBM bytes: q, k and v read, o written
+        "attention_bytes": float(4 * P * L * tok * E * 2),
     }
     bound = {"batched_gemm": "tensor", "attention": "tensor", "tied_ce": "tensor", "replay_gemm": "tensor",
              "batched_u_pass": "hbm", "rms_norm": "hbm", "table_lookup": "hbm"}
@@ -556,6 +559,9 @@ def family_rates(kern: dict, P_local: int) -> dict:
         else:
             out[name] = {"TFLOP/s": work[name] / sec / 1e12,
                          "frac_sustained": work[name] / sec / 1e12 / pk["bf16_tflops_sustained"], "ms": tot}
+        if name == "attention":  # bound by its loads and softmax latency more than by the tensor cores
+            gbs = work["attention_bytes"] / sec / 1e9
+            out[name].update({"GB/s": gbs, "frac_hbm": gbs / pk["hbm_gbs"]})
     return out
 
 
