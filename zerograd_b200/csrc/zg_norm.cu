@@ -6,8 +6,10 @@
 //   layer_norm: y = (x - mean) / sqrt(var + eps) * scale + bias
 //               (biased variance; examples/train_vit_cifar10.py:76-79)
 //   rms_norm:   y = x / sqrt(mean(x^2) + eps) * scale
-// The division is one correctly rounded reciprocal per row and a multiply
-// per element (within 1.5 float32 ulp of dividing).
+// Per row: the means as sums times 1/C (float32), one reciprocal square
+// root (rsqrtf, within 2 ulp), a multiply per element (within a few float32
+// ulp of the divisions; the per-row statistics are executed by every lane of
+// the row's warp, so their cost weighs most on short rows).
 //
 // Statistics in float32 over the last axis (C); output rounded to x's dtype.
 // x [P, M, C] (x_batched) or [M, C] shared by the candidates; scale, bias
@@ -64,6 +66,7 @@ struct NormArgs {
     int64_t M;
     int P, C, x_batched, p_batched, kind;
     float eps;
+    float inv_c;  // 1/C rounded to float32: means are sums times it
 };
 
 // Rows held in registers: CH chunks of 8 values per lane (C <= 256 * CH, C a
@@ -105,7 +108,7 @@ __global__ void __launch_bounds__(256) norm_reg_kernel(const NormArgs a) {
                     if (lane + 32 * j < chunks)
 #pragma unroll
                         for (int i = 0; i < 8; ++i) s1[q] += v[q][j][i];
-                mean[q] = __fdiv_rn(warp_sum(s1[q]), (float)a.C);
+                mean[q] = warp_sum(s1[q]) * a.inv_c;
 #pragma unroll
                 for (int j = 0; j < CH; ++j)
                     if (lane + 32 * j < chunks)
@@ -122,7 +125,7 @@ __global__ void __launch_bounds__(256) norm_reg_kernel(const NormArgs a) {
                         for (int i = 0; i < 8; ++i) s2[q] = fmaf(v[q][j][i], v[q][j][i], s2[q]);
             }
             // one division per row
-            rinv[q] = __fdiv_rn(1.f, __fsqrt_rn(__fdiv_rn(warp_sum(s2[q]), (float)a.C) + a.eps));
+            rinv[q] = rsqrtf(warp_sum(s2[q]) * a.inv_c + a.eps);
         }
 #pragma unroll
         for (int q = 0; q < R; ++q) {
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const
 #pragma unroll
                         for (int i = 0; i < 8; ++i) s1 += f[i];
                     }
-                mean[q] = __fdiv_rn(warp_sum(s1), (float)a.C);
+                mean[q] = warp_sum(s1) * a.inv_c;
 #pragma unroll
                 for (int j = 0; j < CH; ++j)
                     if (lane + 32 * j < chunks) {
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const
                         for (int i = 0; i < 8; ++i) s2[q] = fmaf(f[i], f[i], s2[q]);
                     }
             }
-            rinv[q] = __fdiv_rn(1.f, __fsqrt_rn(__fdiv_rn(warp_sum(s2[q]), (float)a.C) + a.eps));
+            rinv[q] = rsqrtf(warp_sum(s2[q]) * a.inv_c + a.eps);
         }
 #pragma unroll
         for (int q = 0; q < R; ++q) {
@@ -269,7 +272,7 @@ __global__ void norm_any_kernel(const NormArgs a) {
         if (a.kind == NORM_LAYER) {
             float s1 = 0.f;
             for (int c = lane; c < a.C; c += 32) s1 += zg_to_float(xr[c]);
-            mean = __fdiv_rn(warp_sum(s1), (float)a.C);
+            mean = warp_sum(s1) * a.inv_c;
             for (int c = lane; c < a.C; c += 32) {
                 const float d = zg_to_float(xr[c]) - mean;
                 s2 = fmaf(d, d, s2);
@@ -280,7 +283,7 @@ __global__ void norm_any_kernel(const NormArgs a) {
                 s2 = fmaf(xv, xv, s2);
             }
         }
-        const float rinv = __fdiv_rn(1.f, __fsqrt_rn(__fdiv_rn(warp_sum(s2), (float)a.C) + a.eps));
+        const float rinv = rsqrtf(warp_sum(s2) * a.inv_c + a.eps);
         for (int c = lane; c < a.C; c += 32) {
             float o = __fmul_rn(__fmul_rn(zg_to_float(xr[c]) - mean, rinv), zg_to_float(sr[c]));
             if (br) o = __fadd_rn(o, zg_to_float(br[c]));
@@ -346,7 +349,7 @@ int norm_entry(const char* who, int kind, const void* x, int x_batched, const vo
     if (!zg::dtype_ok(dtype)) return zg::fail(ZG_ERR_INVALID, "%s: bad dtype", who);
     if (M == 0) return ZG_OK;
     if (!x || !scale || !y) return zg::fail(ZG_ERR_INVALID, "%s: null pointer", who);
-    NormArgs a{x, scale, bias, y, M, P, C, x_batched != 0, p_batched != 0, kind, eps};
+    NormArgs a{x, scale, bias, y, M, P, C, x_batched != 0, p_batched != 0, kind, eps, 1.f / (float)C};
     cudaStream_t st = zg::as_stream(stream);
     return dtype == ZG_BF16 ? launch_norm<__nv_bfloat16>(a, st, who) : launch_norm<float>(a, st, who);
 }
