@@ -508,8 +508,9 @@ ZG_API int zg_rms_norm(const void* x, int x_batched, const void* scale, int p_ba
  * q, k, v, o [Z, S, H, D] contiguous (Z = candidates x batch rows; the
  * q/k/v projections' head-interleaved layout); causal != 0 masks keys j > i.
  * bf16 with D = 64 and S <= 256 runs on the tensor cores (scores and P V
- * accumulated in float32, P rounded to bf16, normalised by the sum of the
- * rounded P); other shapes and float32 run a warp-per-row kernel in float32.
+ * accumulated in float32, P rounded to bf16, normalised by the float32 sum
+ * of P; a persistent kernel holding one CTA per SM); other shapes and
+ * float32 run a warp-per-row kernel in float32.
  * D <= 256.  Replaces softmax(einsum(q, k) / sqrt(D)) @ v of the reference's
  * ViT block (examples/train_vit_cifar10.py:166-172) under jax.vmap. */
 ZG_API int zg_attention(const void* q, const void* k, const void* v, int Z, int S, int H, int D, int causal,
