@@ -32,7 +32,7 @@ def _close(got, want, dtype):
         assert_bf16_close(got, want)
 
 
-@pytest.mark.parametrize("C", [64, 384, 768, 1536, 3000])
+@pytest.mark.parametrize("C", [64, 200, 384, 512, 768, 1536, 3000])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("x_batched,p_batched", [(True, True), (False, True), (True, False)])
 def test_layer_norm_matches_oracle(cuda, oracle, C, dtype, x_batched, p_batched):

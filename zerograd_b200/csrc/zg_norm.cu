@@ -160,19 +160,33 @@ __global__ void __launch_bounds__(256) norm_reg_kernel(const NormArgs a) {
 // warp fit in the registers the float form needs for two: twice the HBM
 // reads in flight.  Same per-lane arithmetic, in the same order, as
 // norm_reg_kernel (the same bits).
-template <int CH, int R>
+//
+// LW = 16 gives each row half a warp (two rows side by side in one warp),
+// so each per-row instruction of the statistics (reductions, rsqrtf) serves
+// two rows: for short rows (C <= 512) those dominate, and 384 columns split
+// evenly over 16 lanes (3 chunks each) where 32 lanes leave half of them
+// idle in the second chunk.
+template <int LW>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = LW / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int CH, int R, int LW = 32>
 __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const NormArgs a) {
-    const int lane = threadIdx.x % 32;
+    const int lane = threadIdx.x % LW, slot = (threadIdx.x % 32) / LW;  // lane in the row's group; which row
+    constexpr int RW = R * (32 / LW);                                     // rows per warp per pass
     const int64_t rows = (int64_t)a.P * a.M;
     const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
     const int64_t nwarps = (int64_t)gridDim.x * blockDim.x / 32;
     const int chunks = a.C / 8;
-    for (int64_t g0 = warp0 * R; g0 < rows; g0 += nwarps * R) {
+    for (int64_t g0 = warp0 * RW; g0 < rows; g0 += nwarps * RW) {
         uint4 raw[R][CH];
         float s2[R], mean[R], rinv[R];
 #pragma unroll
         for (int q = 0; q < R; ++q) {
-            const int64_t g = g0 + q;
+            const int64_t g = g0 + q * (32 / LW) + slot;
 #pragma unroll
             for (int j = 0; j < CH; ++j) raw[q][j] = make_uint4(0, 0, 0, 0);
             if (g >= rows) continue;
@@ -182,7 +196,7 @@ __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const
                 static_cast<const __nv_bfloat16*>(a.x) + ((a.x_batched ? (int64_t)p : 0) * a.M + m) * a.C;
 #pragma unroll
             for (int j = 0; j < CH; ++j) {
-                const int c = lane + 32 * j;
+                const int c = lane + LW * j;
                 if (c < chunks) raw[q][j] = *reinterpret_cast<const uint4*>(xr + 8 * c);
             }
         }
@@ -194,16 +208,16 @@ __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const
             if (a.kind == NORM_LAYER) {
 #pragma unroll
                 for (int j = 0; j < CH; ++j)
-                    if (lane + 32 * j < chunks) {
+                    if (lane + LW * j < chunks) {
                         float f[8];
                         bf16x8_to_f32(raw[q][j], f);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) s1 += f[i];
                     }
-                mean[q] = warp_sum(s1) * a.inv_c;
+                mean[q] = group_sum<LW>(s1) * a.inv_c;
 #pragma unroll
                 for (int j = 0; j < CH; ++j)
-                    if (lane + 32 * j < chunks) {
+                    if (lane + LW * j < chunks) {
                         float f[8];
                         bf16x8_to_f32(raw[q][j], f);
 #pragma unroll
@@ -215,18 +229,18 @@ __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const
             } else {
 #pragma unroll
                 for (int j = 0; j < CH; ++j)
-                    if (lane + 32 * j < chunks) {
+                    if (lane + LW * j < chunks) {
                         float f[8];
                         bf16x8_to_f32(raw[q][j], f);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) s2[q] = fmaf(f[i], f[i], s2[q]);
                     }
             }
-            rinv[q] = rsqrtf(warp_sum(s2[q]) * a.inv_c + a.eps);
+            rinv[q] = rsqrtf(group_sum<LW>(s2[q]) * a.inv_c + a.eps);
         }
 #pragma unroll
         for (int q = 0; q < R; ++q) {
-            const int64_t g = g0 + q;
+            const int64_t g = g0 + q * (32 / LW) + slot;
             if (g >= rows) continue;
             const int p = (int)(g / a.M);
             const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(a.scale) + (a.p_batched ? (int64_t)p : 0) * a.C;
@@ -235,7 +249,7 @@ __global__ void __launch_bounds__(256, CH >= 4 ? 2 : 3) norm_packed_kernel(const
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(a.y) + g * a.C;
 #pragma unroll
             for (int j = 0; j < CH; ++j) {
-                const int c = lane + 32 * j;
+                const int c = lane + LW * j;
                 if (c < chunks) {
                     float f[8], sc[8], bi[8], o[8];
                     bf16x8_to_f32(raw[q][j], f);
@@ -314,13 +328,15 @@ int launch_norm(const NormArgs& a, cudaStream_t st, const char* name) {
     if (blocks < 1) blocks = 1;
     if constexpr (sizeof(T) == 2) {
         if (vec && a.C <= 1024) {
-            // bf16: four rows per warp, held packed
+            // bf16 rows held packed: up to C = 512 half a warp per row (four
+            // or eight rows per warp), above it a whole warp (four rows)
             int64_t b4 = (rows + 8 * 4 - 1) / (8 * 4);
             if (b4 > (int64_t)sm_count_norm() * 16) b4 = (int64_t)sm_count_norm() * 16;
             if (b4 < 1) b4 = 1;
             zg::LaunchTimer zg_lt_(name, st);
-            if (a.C <= 256) norm_packed_kernel<1, 4><<<(unsigned)b4, 256, 0, st>>>(a);
-            else if (a.C <= 512) norm_packed_kernel<2, 4><<<(unsigned)b4, 256, 0, st>>>(a);
+            if (a.C <= 256) norm_packed_kernel<2, 4, 16><<<(unsigned)b4, 256, 0, st>>>(a);
+            else if (a.C <= 384) norm_packed_kernel<3, 2, 16><<<(unsigned)b4, 256, 0, st>>>(a);
+            else if (a.C <= 512) norm_packed_kernel<4, 2, 16><<<(unsigned)b4, 256, 0, st>>>(a);
             else if (a.C <= 768) norm_packed_kernel<3, 4><<<(unsigned)b4, 256, 0, st>>>(a);
             else norm_packed_kernel<4, 4><<<(unsigned)b4, 256, 0, st>>>(a);
             return zg::check_launch(name);
