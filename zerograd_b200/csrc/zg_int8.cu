@@ -62,18 +62,22 @@ template <int R>
 __global__ void __launch_bounds__(U_ROWS)
 int8_u_tile_kernel(const int8_t* __restrict__ x, int x_batched, const float* __restrict__ A, int M, int K,
                    float* __restrict__ U) {
+    constexpr int XV = U_ROWS * (U_SLAB / 16) / U_ROWS;  // 16-byte pieces of a slab per thread (8)
     __shared__ __align__(16) int8_t xs[U_ROWS][U_PITCH];
     __shared__ __align__(16) float as[U_SLAB][R];
     const int p = blockIdx.y, m0 = blockIdx.x * U_ROWS, tid = threadIdx.x;
     const int8_t* xp = x + (x_batched ? (int64_t)p * M * K : 0);
     const float* ap = A + (int64_t)p * K * R;
     const bool vec = (K % 16) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    float acc[R];
+    const bool avec = R % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
+    // The next slab is fetched into registers while this one is summed:
+    // all of a thread's pieces are requested before any is needed.
+    uint4 nx[XV];
+    float4 na[R % 4 == 0 ? R / 4 : 1];
+    auto fetch = [&](int k0) {
 #pragma unroll
-    for (int j = 0; j < R; ++j) acc[j] = 0.f;
-    for (int k0 = 0; k0 < K; k0 += U_SLAB) {
-        __syncthreads();
-        for (int c = tid; c < U_ROWS * (U_SLAB / 16); c += U_ROWS) {
+        for (int i = 0; i < XV; ++i) {
+            const int c = tid + i * U_ROWS;
             const int r = c / (U_SLAB / 16), q = c % (U_SLAB / 16);
             const int m = m0 + r, k = k0 + q * 16;
             uint4 v = make_uint4(0, 0, 0, 0);
@@ -84,28 +88,66 @@ int8_u_tile_kernel(const int8_t* __restrict__ x, int x_batched, const float* __r
                 } else {
                     int8_t tmp[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) tmp[i] = k + i < K ? src[i] : (int8_t)0;
+                    for (int e = 0; e < 16; ++e) tmp[e] = k + e < K ? src[e] : (int8_t)0;
                     v = *reinterpret_cast<const uint4*>(tmp);
                 }
             }
-            *reinterpret_cast<uint4*>(&xs[r][q * 16]) = v;
+            nx[i] = v;
         }
-        for (int e = tid; e < U_SLAB * R; e += U_ROWS) {
-            const int kk = e / R, j = e % R;
-            as[kk][j] = k0 + kk < K ? ap[(int64_t)(k0 + kk) * R + j] : 0.f;
+        if (avec) {  // this thread's A row of the slab (k0 + tid), R floats as float4s
+#pragma unroll
+            for (int i = 0; i < (R % 4 == 0 ? R / 4 : 1); ++i)
+                na[i] = k0 + tid < K ? *reinterpret_cast<const float4*>(ap + (int64_t)(k0 + tid) * R + 4 * i)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    float acc[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) acc[j] = 0.f;
+    fetch(0);
+    for (int k0 = 0; k0 < K; k0 += U_SLAB) {
+        __syncthreads();  // the last slab is summed: its buffers may be overwritten
+#pragma unroll
+        for (int i = 0; i < XV; ++i) {
+            const int c = tid + i * U_ROWS;
+            *reinterpret_cast<uint4*>(&xs[c / (U_SLAB / 16)][(c % (U_SLAB / 16)) * 16]) = nx[i];
+        }
+        if (avec) {
+#pragma unroll
+            for (int i = 0; i < (R % 4 == 0 ? R / 4 : 1); ++i) *reinterpret_cast<float4*>(&as[tid][4 * i]) = na[i];
+        } else {
+            for (int e = tid; e < U_SLAB * R; e += U_ROWS) {
+                const int kk = e / R, j = e % R;
+                as[kk][j] = k0 + kk < K ? ap[(int64_t)(k0 + kk) * R + j] : 0.f;
+            }
         }
         __syncthreads();
+        if (k0 + U_SLAB < K) fetch(k0 + U_SLAB);
         const int kw = K - k0 < U_SLAB ? K - k0 : U_SLAB;
-        // zero-padded bytes past K are never folded in: the loop stops at kw
-        for (int kk0 = 0; kk0 < kw; kk0 += 16) {
-            const uint4 v = *reinterpret_cast<const uint4*>(&xs[tid][kk0]);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        if (kw == U_SLAB) {  // a full slab: no per-byte test
+#pragma unroll 2
+            for (int kk0 = 0; kk0 < U_SLAB; kk0 += 16) {
+                const uint4 v = *reinterpret_cast<const uint4*>(&xs[tid][kk0]);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                if (kk0 + i < kw) {
+                for (int i = 0; i < 16; ++i) {
                     const float xv = s8_to_f32(w[i / 4], i % 4);
 #pragma unroll
                     for (int j = 0; j < R; ++j) acc[j] = __fmaf_rn(xv, as[kk0 + i][j], acc[j]);
+                }
+            }
+        } else {
+            // zero-padded bytes past K are never folded in: the loop stops at kw
+            for (int kk0 = 0; kk0 < kw; kk0 += 16) {
+                const uint4 v = *reinterpret_cast<const uint4*>(&xs[tid][kk0]);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    if (kk0 + i < kw) {
+                        const float xv = s8_to_f32(w[i / 4], i % 4);
+#pragma unroll
+                        for (int j = 0; j < R; ++j) acc[j] = __fmaf_rn(xv, as[kk0 + i][j], acc[j]);
+                    }
                 }
             }
         }
