@@ -89,7 +89,14 @@ __global__ void __launch_bounds__(THREADS) simt_gemm_kernel(const SimtGemm g) {
 // ---- float32 NT replay GEMM ----
 constexpr int RS_BM = 128, RS_BN = 128, RS_BK = 16, RS_PAD = 4;
 
-__global__ void __launch_bounds__(256) replay_sgemm_kernel(const float* __restrict__ A, const float* __restrict__ B,
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+    unsigned long long A = *reinterpret_cast<unsigned long long*>(&a), B = *reinterpret_cast<unsigned long long*>(&b),
+                       C = *reinterpret_cast<unsigned long long*>(&c), D;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D) : "l"(A), "l"(B), "l"(C));
+    return *reinterpret_cast<float2*>(&D);
+}
+
+__global__ void __launch_bounds__(256, 2) replay_sgemm_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                            const float* __restrict__ w, int rank, int M, int N,
                                                            int64_t K, float alpha, float* __restrict__ C) {
     __shared__ __align__(16) float As[RS_BK][RS_BM + RS_PAD];
@@ -130,11 +137,13 @@ __global__ void __launch_bounds__(256) replay_sgemm_kernel(const float* __restri
             Bs[kc][r] = rb[i].x; Bs[kc + 1][r] = rb[i].y; Bs[kc + 2][r] = rb[i].z; Bs[kc + 3][r] = rb[i].w;
         }
     };
-    float acc[8][8];
+    // acc[i][jj]: outputs (i, 2 jj) and (i, 2 jj + 1), a register pair for
+    // the packed float32x2 FMA
+    float2 acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj] = make_float2(0.f, 0.f);
     fetch(0);
     for (int64_t k0 = 0; k0 < K; k0 += RS_BK) {
         __syncthreads();  // the previous tile's reads are done
@@ -143,17 +152,21 @@ __global__ void __launch_bounds__(256) replay_sgemm_kernel(const float* __restri
         if (k0 + RS_BK < K) fetch(k0 + RS_BK);  // in flight during this tile's products
 #pragma unroll
         for (int kk = 0; kk < RS_BK; ++kk) {
-            float a[8], b[8];
             const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
             const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][64 + ty * 4]);
             const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
             const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][64 + tx * 4]);
-            a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
-            b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                 make_float2(b1.z, b1.w)};
+            // two adjacent outputs per packed float32x2 FMA (each lane an
+            // IEEE fma: the same value and order as one fmaf per output)
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < 8; ++i) {
+                const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fma_f32x2(ai, b[jj], acc[i][jj]);
+            }
         }
     }
 #pragma unroll
@@ -164,8 +177,8 @@ __global__ void __launch_bounds__(256) replay_sgemm_kernel(const float* __restri
         for (int h = 0; h < 2; ++h) {
             const int n = n0 + h * 64 + tx * 4;
             float* c = C + (int64_t)m * N + n;
-            const float v0 = alpha * acc[i][4 * h], v1 = alpha * acc[i][4 * h + 1], v2 = alpha * acc[i][4 * h + 2],
-                        v3 = alpha * acc[i][4 * h + 3];
+            const float v0 = alpha * acc[i][2 * h].x, v1 = alpha * acc[i][2 * h].y, v2 = alpha * acc[i][2 * h + 1].x,
+                        v3 = alpha * acc[i][2 * h + 1].y;
             if (n + 4 <= N && (N % 4) == 0) {
                 *reinterpret_cast<float4*>(c) = make_float4(v0, v1, v2, v3);
             } else {
