@@ -12,13 +12,14 @@
 // value sequence (4-D tensor maps over [Z, S, H, D], 128-byte swizzle); one
 // tcgen05 MMA chain per 128-query tile computes the scores S = Q K^T into
 // TMEM (M=128, N = the keys the tile sees: a causal first tile stops at
-// 128); one thread per query row takes its max over the row in TMEM and
-// writes p = 2^(s * log2(e)/sqrt(D) - max) as bf16 back into TMEM over the
-// scores; a second MMA chain computes O = P V with P read from TMEM (V the
-// MN-major operand from shared memory); the epilogue divides by the row sum
-// of p (float32) and stores O by TMA.  The whole score row fits (S <= 256),
-// so one pass suffices.  Two softmax groups alternate over the tiles, and
-// the next unit's loads overlap the current one's work.
+// 128); two threads per query row, each over half of the keys, take the
+// row's max over the scores in TMEM and write p = 2^(s * log2(e)/sqrt(D) -
+// max) as bf16 back into TMEM over them; a second MMA chain computes O = P V
+// with P read from TMEM (V the MN-major operand from shared memory); the
+// epilogue divides by the row sum of p (float32) and stores O by TMA.  The
+// whole score row fits (S <= 256), so one pass suffices.  Two softmax
+// groups alternate over the tiles, and the next unit's loads overlap the
+// current one's work.
 //
 // Other shapes (D != 64, S > 256, float32): a warp per query row with an
 // online softmax over the keys (float32 arithmetic).
@@ -29,9 +30,10 @@
 
 namespace {
 
-// Persistent CTA (one per SM), 352 threads: warp 0 issues the TMA loads,
-// warps 1 and 2 the MMAs of softmax group 0 and 1, warps 3-6 and 7-10 are
-// the two softmax groups, one thread per query row.  Work unit = one
+// Persistent CTA (one per SM), 608 threads: warp 0 issues the TMA loads,
+// warps 1 and 2 the MMAs of softmax group 0 and 1, warps 3-10 and 11-18 are
+// the two softmax groups, two threads per query row (warps w and w + 4: the
+// first and second half of the keys).  Work unit = one
 // (z, head): its query tiles (one or two of 128 rows), keys and values, in
 // one of two shared-memory buffers.  A buffer's queries and keys are loaded
 // again as soon as the unit's Q K^T MMAs have read them, its values once the
@@ -42,7 +44,8 @@ namespace {
 // score columns, key pair (c, c+1) of a half as bf16x2 in its column c/2;
 // the P V MMA reads it from TMEM), and O in columns 192..255, which the
 // softmax warps divide by their rows' sums of p and stage into their own
-// boxes for TMA stores.
+// boxes (32 rows x 32 columns) for TMA stores.  A unit's second query tile
+// is loaded in reversed 32-row blocks (tile_block).
 constexpr int AT_THREADS = 608;
 constexpr uint32_t AT_Q = 0;         // 2 x 16 KiB: the unit's query tiles
 constexpr uint32_t AT_K = 32768;     // 32 KiB: up to 256 key rows
