@@ -371,7 +371,12 @@ batched_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
 // has read it.
 // ---------------------------------------------------------------------------
 constexpr int BP_THREADS = 320;                                    // warp 0 TMA, 1 MMA, 2..9 epilogue
-constexpr int BP_STAGES = 5;
+// NB staging boxes per epilogue warp: 2 (double-buffered; the residual's
+// TMA load into the next box runs while the last box is stored) or 1 for
+// GEMMs without a residual, whose freed 16 KiB buy a sixth operand stage:
+// the main loop waits on operand loads for about a third of its time with
+// five (the tile's L2 demand, 32 KiB per CTA per 64-deep K block).
+__host__ __device__ constexpr int bp_stages(int nb) { return nb == 1 ? 6 : 5; }
 constexpr uint32_t BP_A = BM * BK * 2;                             // 16 KiB: 128 rows of x
 constexpr uint32_t BP_B = 128 * BK * 2;                            // 16 KiB: 128 columns of Wop
 constexpr uint32_t BP_STAGE = BP_A + BP_B;                         // 32 KiB
@@ -379,20 +384,22 @@ constexpr uint32_t BP_CU = 128 * 16;                               // 8 K column
 constexpr uint32_t BP_CF = 128 * 16;                               // 8 K columns of 128 F2 rows
 constexpr uint32_t BP_CORR = 2 * BP_CU + 2 * BP_CF;                // 8 KiB per accumulator
 constexpr uint32_t BP_BOX = 32 * 32 * 2;                           // 2 KiB: 32 rows x 32 bf16 columns
-constexpr uint32_t BP_STG = BP_STAGES * BP_STAGE + 2 * BP_CORR;    // staging buffers' offset (1 KiB aligned)
-constexpr uint32_t BP_SMEM = BP_STG + 8 * 2 * BP_BOX;              // 208 KiB
+__host__ __device__ constexpr uint32_t bp_stg(int nb) { return bp_stages(nb) * BP_STAGE + 2 * BP_CORR; }  // staging offset (1 KiB aligned)
+__host__ __device__ constexpr uint32_t bp_smem(int nb) { return bp_stg(nb) + 8 * nb * BP_BOX; }            // 208 / 224 KiB
 
 // Byte offset of the 16-byte chunk `c` (0..3) of row `r` (0..31) in a
 // 32 x 32 bf16 box with 64-byte swizzle: chunk bits [4,6) ^= address bits [7,9).
 __device__ __forceinline__ uint32_t box64_off(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
-template <bool B_MN>
+template <bool B_MN, int NB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BP_THREADS, 1)
 batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                          const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmF,
                          const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                          const GemmArgs a) {
     extern __shared__ uint8_t dyn_smem[];
+    constexpr int BP_STAGES = bp_stages(NB);
+    constexpr uint32_t BP_STG = bp_stg(NB);
     __shared__ __align__(8) uint64_t full_bar[BP_STAGES], empty_bar[BP_STAGES], tmem_full[2], tmem_empty[2],
         corr_full[2], corr_empty[2], mma_done, res_bar[16];
     __shared__ uint32_t tmem_base_sh;
@@ -533,7 +540,7 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
         const int quad = warp % 4;             // TMEM lanes 32*quad .. 32*quad + 31
         const int half = ew / 4;               // tile columns 128*half .. 128*half + 127
         const uint32_t empty_leader = cluster_addr(&tmem_empty[0], 0);
-        uint8_t* stg = smem + BP_STG + ew * 2 * BP_BOX;
+        uint8_t* stg = smem + BP_STG + ew * NB * BP_BOX;
         uint64_t* rbar = &res_bar[ew * 2];
         const bool has_res = a.res != nullptr;
         int acc = 0;
@@ -548,13 +555,14 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
             const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 256 + half * 128;
 #pragma unroll 1
             for (int ch = 0; ch < 4; ++ch, ++box) {
-                const int b = (int)(box & 1);
+                const int b = (int)(box % NB);
                 uint8_t* buf = stg + b * BP_BOX;
                 const int col0 = tn * 256 + half * 128 + ch * 32;
                 const bool active = row0 < a.M && col0 < a.N;  // warp-uniform; TMA clips partial boxes
                 if (lane == 0) {
-                    // the store issued from this buffer two boxes ago has read it
-                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    // the store issued from this buffer NB boxes ago has read it
+                    if constexpr (NB == 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    else asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                     if (has_res && active) {
                         mbar_expect_tx(&rbar[b], BP_BOX);
                         tma_load_3d(buf, &tmR, &rbar[b], col0, row0, p);
@@ -613,20 +621,20 @@ batched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_c
 }
 
 // CTA pairs that can be resident at once for the pair kernel (0 if unknown).
-template <bool B_MN>
+template <bool B_MN, int NB>
 int batched_pair_slots() {
     static int n = -1;
     if (n < 0) {
-        constexpr size_t smem = (size_t)BP_SMEM + 1024;
+        constexpr size_t smem = (size_t)bp_smem(NB) + 1024;
         n = 0;
-        if (cudaFuncSetAttribute(batched_gemm_pair_kernel<B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(batched_gemm_pair_kernel<B_MN, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem) == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(2 * 74, 1, 1);
             cfg.blockDim = dim3(BP_THREADS, 1, 1);
             cfg.dynamicSmemBytes = smem;
             int clusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&clusters, batched_gemm_pair_kernel<B_MN>, &cfg) == cudaSuccess)
+            if (cudaOccupancyMaxActiveClusters(&clusters, batched_gemm_pair_kernel<B_MN, NB>, &cfg) == cudaSuccess)
                 n = clusters;
         }
         cudaGetLastError();
@@ -700,7 +708,9 @@ int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U,
     const uint32_t bf[2] = {8, BG_BN};
     ok = ok && tensor_map_bf16(&tu, U, 3, du, su, bu, false) && tensor_map_bf16(&tf, F2, 2, df, sf, bf, false);
     if (!ok) return fail(ZG_ERR_CUDA, "batched_gemm: tensor maps");
-    const int slots = w_mn_major ? batched_pair_slots<true>() : batched_pair_slots<false>();
+    const bool one_box = resb == nullptr;  // no residual: single-buffered staging, six stages
+    const int slots = w_mn_major ? (one_box ? batched_pair_slots<true, 1>() : batched_pair_slots<true, 2>())
+                                 : (one_box ? batched_pair_slots<false, 1>() : batched_pair_slots<false, 2>());
     const int64_t pair_tiles = (int64_t)P * ((M + 255) / 256) * ((N + 255) / 256);
     if (slots > 0 && pair_tiles >= slots && pair_tiles <= INT_MAX) {
         // CTA pairs: each CTA loads 128 of the 256 x / U rows and 128 of the 256 Wop / F2 columns
@@ -731,12 +741,16 @@ int batched_gemm(const void* x, const void* Wop, bool w_mn_major, const void* U,
         if (!ok2) return fail(ZG_ERR_CUDA, "batched_gemm: tensor maps");
         GemmArgs a2{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + 255) / 256, (N + 255) / 256, resb, act};
         const int pairs = pair_tiles < slots ? (int)pair_tiles : slots;
-        const size_t smem2 = BP_SMEM + 1024;
+        const size_t smem2 = (size_t)bp_smem(one_box ? 1 : 2) + 1024;
         zg::LaunchTimer zg_lt_("batched_gemm", st);
-        if (w_mn_major)
-            batched_gemm_pair_kernel<true><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
+        if (w_mn_major && one_box)
+            batched_gemm_pair_kernel<true, 1><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
+        else if (w_mn_major)
+            batched_gemm_pair_kernel<true, 2><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
+        else if (one_box)
+            batched_gemm_pair_kernel<false, 1><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
         else
-            batched_gemm_pair_kernel<false><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
+            batched_gemm_pair_kernel<false, 2><<<2 * pairs, BP_THREADS, smem2, st>>>(tx2, tw2, tu2, tf2, ty, tr, a2);
         return check_launch("batched_gemm");
     }
     GemmArgs a{static_cast<__nv_bfloat16*>(y), M, N, K, P, rank, (M + BM - 1) / BM, (N + BG_BN - 1) / BG_BN, resb, act};
