@@ -52,6 +52,18 @@ def test_argument_errors_need_no_gpu():
     assert lib.zg_perturbed_linear(None, 0, None, None, 0, 0, 1, 1, 1, 1, 0.1, 0, None, None, 0, None) == \
         _lib.ZG_ERR_INVALID
     assert lib.zg_replay(None, None, 0, 4, 7, 4, 4, 2, 1.0, 0, None, None, 0, None) == _lib.ZG_ERR_INVALID
+    # block ops: sizes, eps, head dim and row pitch are checked before any launch
+    bf = _lib.ZG_BF16
+    assert lib.zg_rms_norm(None, 1, None, 1, 0, 1, 8, 1e-6, bf, None, None) == _lib.ZG_ERR_INVALID
+    assert b"bad sizes" in lib.zg_last_error()
+    assert lib.zg_layer_norm(None, 1, None, None, 1, 1, 1, 8, -1.0, bf, None, None) == _lib.ZG_ERR_INVALID
+    assert b"eps" in lib.zg_last_error()
+    assert lib.zg_rms_norm(None, 1, None, 1, 2, 0, 8, 1e-6, bf, None, None) == _lib.ZG_OK  # no rows: no work
+    assert lib.zg_attention(None, None, None, -1, 4, 2, 64, 1, bf, None, None) == _lib.ZG_ERR_INVALID
+    assert lib.zg_attention(None, None, None, 1, 4, 2, 300, 1, bf, None, None) == _lib.ZG_ERR_UNSUPPORTED
+    assert lib.zg_attention_ex(None, None, None, 100, 1, 4, 2, 64, 1, bf, None, None) == _lib.ZG_ERR_INVALID
+    assert b"row pitch" in lib.zg_last_error()
+    assert lib.zg_attention(None, None, None, 0, 4, 2, 64, 1, bf, None, None) == _lib.ZG_OK  # no rows
 
 
 def test_workspace_queries():
