@@ -57,6 +57,45 @@ def test_batched_linear_matches_oracle(cuda, oracle, P, M, K, N, r):
         _check_candidate(y[p].float().cpu().numpy(), want, xs[p] @ Ws)
 
 
+@pytest.mark.parametrize("act,res", [(0, False), (1, False), (0, True), (1, True)])
+def test_pair_kernel_ragged_epilogues(cuda, oracle, act, res):
+    """Enough tiles for the CTA-pair kernel (>= 74 pair tiles) with every
+    tile edge ragged (M, K, N not multiples of 256 / 64), each epilogue:
+    plain and GELU (one staging box per warp, six stages) and with a
+    residual (two boxes, five stages)."""
+    from oracle.lm import gelu_tanh
+
+    P, M, K, N, r, sigma, group = 40, 300, 200, 600, 8, 0.02, 2
+    base = oracle.step_key(5, "pair-edges", 0, 1)
+    cks = oracle.candidate_keys(base, range(P))
+    g = torch.Generator().manual_seed(act * 2 + int(res))
+    x = torch.randn(P, M, K, generator=g).to(torch.bfloat16).to(cuda)
+    W = (torch.randn(K, N, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
+    rs = torch.randn(P, M, N, generator=g).to(torch.bfloat16).to(cuda) if res else None
+    L.profile_begin()
+    y = _ops.launch_linear(x, W, _u32(cks, cuda), group, r, sigma, True, act, rs)
+    prof = L.profile_end()
+    assert L.load().zg_device_error(1) == 0
+    assert "batched_gemm" in prof, prof
+    xs, Ws = x.float().cpu().numpy().astype(np.float64), W.float().cpu().numpy().astype(np.float64)
+    for p in range(0, P, 13):
+        v = oracle.perturbed_linear(xs[p], Ws, oracle.fold_in(cks[p], group), r, sigma, "bfloat16")
+        if act:
+            v = gelu_tanh(v)
+        got = y[p].float().cpu().numpy()
+        if not res:
+            assert_bf16_close(got, v, floor=rms_floor(v), what="epilogue output")
+            continue
+        # the residual is added to the bf16-rounded product (the unfused ops'
+        # roundings): the sum keeps that intermediate's rounding error, up to
+        # one bf16 ulp of |v| (two half-ulp roundings), which cancellation
+        # against the residual does not shrink
+        want = v + rs[p].float().cpu().numpy().astype(np.float64)
+        bound = 2e-2 * np.maximum(np.abs(want), rms_floor(want)) + 2.0 ** -7 * np.abs(v)
+        err = np.abs(got - want)
+        assert (err <= bound).all(), (float((err / bound).max()), int((err > bound).sum()))
+
+
 def test_batched_tied_logits_matches_oracle(cuda, oracle):
     P, M, V, C, r, sigma, group = 6, 100, 1000, 256, 8, 0.02, 2
     base = oracle.step_key(4, "batched-tied", 0, 1)
