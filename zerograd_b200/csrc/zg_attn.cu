@@ -193,9 +193,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
     if (warp == 0) {
         if (lane == 0) {
-            // unit u's values are loaded before unit u+1's queries and keys:
-            // the buffer's values are freed (P V of unit u-2) before its
-            // queries and keys are (Q K^T of unit u-1, issued after P V of u-2)
+            // unit u's values are loaded before unit u+1's queries and keys.
+            // With two tiles per unit, u's buffer has its values freed (P V of
+            // unit u-2) before u+1's buffer has its queries and keys freed
+            // (Q K^T of unit u-1, issued by each group after its P V of u-2).
+            // With one tile per unit those come from different groups, and
+            // the fixed order can only delay a load: no P V waits on a later
+            // unit's loads.
             uint32_t issued = 0, issue_parity = 0;  // bit b: QK loads of buffer b; bit b+2: V loads
             for (int u = 0; u < my_units; ++u) {
                 const int b = u & 1;
